@@ -1,0 +1,69 @@
+"""Builds libfgs_b200.so (all CUDA sources of csrc/) for sm_100a with nvcc, in parallel, in-tree.
+
+Usage: python build.py [--force]. The shared library lands in FasterGSVDACudaBackend/lib/ so that it
+travels with the source tree; objects go to _build/ next to this file.
+"""
+import concurrent.futures
+import hashlib
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / 'csrc'
+BUILD = HERE / '_build'
+LIB = HERE / 'FasterGSVDACudaBackend' / 'lib' / 'libfgs_b200.so'
+NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
+ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
+# -fmad=false: no implicit contraction of a*b+c (the arithmetic contract of fgs_common.cuh);
+# IEEE division / square root and denormals are nvcc's defaults without --use_fast_math.
+FLAGS = ['-O3', '-std=c++17', '-lineinfo', '-fmad=false', '-Xcompiler', '-fPIC', '--expt-relaxed-constexpr',
+         '-Xptxas', '-warn-spills']
+
+
+def _digest(paths):
+    h = hashlib.sha256()
+    for p in sorted(paths):
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    h.update(' '.join(FLAGS + ARCH).encode())
+    return h.hexdigest()
+
+
+def _compile(src: Path, headers_digest: str) -> Path:
+    obj = BUILD / (src.stem + '.o')
+    stamp = BUILD / (src.stem + '.stamp')
+    key = headers_digest + hashlib.sha256(src.read_bytes()).hexdigest()
+    if obj.exists() and stamp.exists() and stamp.read_text() == key:
+        return obj
+    cmd = [NVCC, *ARCH, *FLAGS, '-c', str(src), '-o', str(obj)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f'nvcc failed for {src.name}:\n{res.stdout}\n{res.stderr}')
+    if res.stderr.strip():
+        sys.stderr.write(res.stderr)
+    stamp.write_text(key)
+    return obj
+
+
+def build(force: bool = False) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    LIB.parent.mkdir(parents=True, exist_ok=True)
+    sources = sorted(CSRC.glob('*.cu'))
+    headers = sorted(list(CSRC.glob('*.cuh')) + list(CSRC.glob('*.h')) + list((HERE.parent / 'include').glob('*.h')))
+    hd = _digest(headers)
+    if force:
+        for f in BUILD.glob('*.stamp'):
+            f.unlink()
+    with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, hd), sources))
+    cmd = [NVCC, *ARCH, '-shared', '-o', str(LIB), *map(str, objs), '-lcudart']
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f'link failed:\n{res.stdout}\n{res.stderr}')
+    return LIB
+
+
+if __name__ == '__main__':
+    print(build(force='--force' in sys.argv))

@@ -1,0 +1,73 @@
+// Host-side launchers of the kernel translation units (called by the C-ABI layer in capi.cu).
+#pragma once
+
+#include "preprocess.cuh"
+
+namespace fgs {
+
+struct GradOut;
+
+// preprocess.cu
+cudaError_t launch_preprocess_fwd(const Params& P, const AppearanceConfig& A, const View& v, const PrimBuffers& B, bool precomputed,
+                                  cudaStream_t s);
+cudaError_t launch_compaction(const PrimBuffers& B, uint32_t n, cudaStream_t s);
+cudaError_t launch_reorder(const PrimBuffers& B, uint32_t n_visible, cudaStream_t s);
+cudaError_t launch_preprocess_bwd(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* rank_of,
+                                  const Record* sorted_rec, const GradRecord* grads, const GradOut& O, bool precomputed,
+                                  cudaStream_t s);
+
+// neural.cu
+cudaError_t launch_preprocess_fwd_neural(const Params& P, const AppearanceConfig& A, const View& v, const PrimBuffers& B, cudaStream_t s);
+cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* rank_of,
+                                         const Record* sorted_rec, const GradRecord* grads, const GradOut& O, cudaStream_t s);
+size_t neural_grad_scratch_floats(const AppearanceConfig& A);
+
+// sort.cu (depth sort, instance offsets, tile sort, scans)
+size_t depth_sort_temp_bytes(uint32_t n);
+cudaError_t depth_sort(PrimBuffers& B, uint32_t n_visible, cudaStream_t s);  // sets B.sorted_idx, fills B.inst_off via scan
+size_t tile_sort_temp_bytes(uint64_t n_instances, int end_bit, bool wide);
+cudaError_t tile_sort(void* keys_a, void* keys_b, uint32_t* vals_a, uint32_t* vals_b, uint64_t n, int end_bit, bool wide,
+                      void* temp, size_t temp_bytes, const void** keys_out, const uint32_t** vals_out, cudaStream_t s);
+cudaError_t exclusive_scan_u32(uint32_t* data, uint32_t n, void* temp, size_t temp_bytes, cudaStream_t s);
+size_t exclusive_scan_temp_bytes(uint32_t n);
+
+// binning.cu
+struct TileBuffers {
+    uint2* ranges;          // [T] instance range per tile
+    uint32_t* bucket_off;   // [T] inclusive bucket offsets
+    uint32_t* tile_max;     // [T] max contributor count per tile
+    float* final_T;         // [T * 192] tile-local layout
+    uint32_t* n_contrib;    // [T * 192]
+};
+cudaError_t launch_emit(const Record* sorted_rec, const uint32_t* inst_off, void* keys, uint32_t* vals, uint32_t n_visible,
+                        int grid_w, bool wide, cudaStream_t s);
+cudaError_t launch_ranges(const void* keys, uint64_t n_instances, bool wide, const TileBuffers& T, int n_tiles, cudaStream_t s);
+
+// blend.cu
+struct BlendArgs {
+    const uint2* ranges;
+    const uint32_t* bucket_off;
+    const uint32_t* vals;        // instance -> depth rank
+    const Record* rec;           // depth-ordered records
+    const float* bg;
+    int width, height, grid_w, grid_h;
+};
+cudaError_t launch_blend_train(const BlendArgs& a, float* image, const TileBuffers& T, uint32_t* bucket_tile, float4* ckpt,
+                               cudaStream_t s);
+cudaError_t launch_blend_inference(const BlendArgs& a, float* image, int chw, int clamp, cudaStream_t s);
+cudaError_t launch_blend_backward(const BlendArgs& a, const float* image, const float* grad_image, const TileBuffers& T,
+                                  const uint32_t* bucket_tile, const float4* ckpt, uint32_t n_buckets_max, GradRecord* grads,
+                                  int proper_aa, int abs_grad, cudaStream_t s);
+
+// adam.cu
+struct AdamSegment {
+    float* param; const float* grad; float* m; float* v;
+    uint64_t n;            // elements
+    uint64_t col_offset;   // index of the first element within its tensor (selects the per-column lr)
+    float lr[7]; int n_lr;
+    float beta1, beta2, eps, bc2_sqrt_rcp;
+};
+constexpr int kMaxAdamSegments = 12;
+cudaError_t launch_adam(const AdamSegment* segs, int n_segs, cudaStream_t s);
+
+}  // namespace fgs

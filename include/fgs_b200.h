@@ -1,0 +1,194 @@
+/*
+ * C-ABI of the B200-native fused-appearance Gaussian-splatting rasterizer (libfgs_b200.so).
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer owned by the caller, every
+ * workspace is a caller-allocated device buffer whose size the *_bytes queries return, and `stream` is a
+ * cudaStream_t passed as void*. Functions return FGS_OK (0) or an error code; fgs_last_error() returns
+ * the message of the last failure on the calling thread. Nothing throws across this boundary.
+ *
+ * The entry points replace the pybind module of the reference backend
+ * (FasterGSVDACudaBackend/FasterGSVDACudaBackend/torch_bindings/bindings.cu:14-28):
+ *   _C.Rasterizer / set_appearance / set_residual_mlp -> fgs_rasterizer_create, fgs_set_appearance, fgs_set_residual_mlp
+ *   _C.forward   (rasterization/src/rasterization_api.cu:16-123)  -> fgs_forward_preprocess + fgs_forward_render
+ *   _C.backward  (rasterization/src/rasterization_api.cu:125-247) -> fgs_backward
+ *   _C.inference (rasterization/src/rasterization_api.cu:249-335) -> fgs_forward_preprocess + fgs_inference_render
+ *   _C.adam_step (adam/src/adam.cu:44-87)                          -> fgs_adam_step (several tensors per launch)
+ * The reference's forward reads the visible-primitive and instance counts back to the host in the middle
+ * of the call (rasterization/src/forward.cu:82-85) to size its buffers; here that point is the boundary
+ * between fgs_forward_preprocess and fgs_forward_render, so the caller allocates the instance and bucket
+ * workspaces in between.
+ */
+#ifndef FGS_B200_H
+#define FGS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    FGS_OK = 0,
+    FGS_ERR_INVALID_ARGUMENT = 1,
+    FGS_ERR_NOT_CONFIGURED = 2,
+    FGS_ERR_UNSUPPORTED = 3,
+    FGS_ERR_CUDA = 4,
+    FGS_ERR_WORKSPACE = 5
+};
+
+/* appearance model ids (rasterization/include/appearance.h:110; torch_bindings/rasterization.py:21) */
+enum { FGS_MODEL_PRECOMPUTED = 0, FGS_MODEL_SH = 1, FGS_MODEL_SV = 2, FGS_MODEL_NASG = 3, FGS_MODEL_NASGABOR = 4, FGS_MODEL_NEURAL = 5 };
+
+typedef struct fgs_rasterizer fgs_rasterizer;
+
+/* Per-Gaussian inputs, all fp32 device pointers, rows contiguous (replaces the tensor arguments of
+ * rasterization.py:86-99). Unused appearance pointers are NULL. mlp_weights is the fp32 master copy;
+ * the kernels round it to fp16 when staging (the reference casts with .half() in rasterization.py:101). */
+typedef struct {
+    const float* means;              /* [N,3] */
+    const float* scales;             /* [N,3] log scales */
+    const float* rotations;          /* [N,4] unnormalised quaternions (w,x,y,z) */
+    const float* opacities;          /* [N,1] logits */
+    const float* precomputed_colors; /* [N,3] or NULL */
+    const float* base_colors;        /* [N,3] or NULL */
+    const float* residual_params;    /* [N,R] or NULL */
+    const float* mlp_weights;        /* [P] or NULL */
+    int64_t n_primitives;
+} fgs_primitives;
+
+/* RasterizerSettings (torch_bindings/rasterization.py:49-83); w2c, cam_position and bg_color are
+ * device pointers (16, 3 and 3 floats), the rest are values. */
+typedef struct {
+    const float* w2c;
+    const float* cam_position;
+    const float* bg_color;
+    int appearance_degree;
+    int width;
+    int height;
+    float focal_x;
+    float focal_y;
+    float center_x;
+    float center_y;
+    float near_plane;
+    float far_plane;
+    int proper_antialiasing;
+    int render_base;
+    int render_residual;
+} fgs_settings;
+
+/* Host-side record of one forward pass; filled by fgs_forward_preprocess / fgs_forward_render and read
+ * by fgs_backward (replaces the (n_instances, n_buckets, selector) ints the reference returns). */
+typedef struct {
+    int64_t n_primitives;
+    int64_t n_visible;
+    int64_t n_instances;
+    int64_t n_buckets;   /* upper bound n_instances / 32 + n_tiles, as in forward.cu:221 */
+    int32_t width, height, grid_w, grid_h, end_bit, wide_keys;
+    int32_t depth_selector;  /* which half of the depth double buffer holds the sorted indices */
+    int32_t tile_selector;   /* which half of the tile double buffer holds the sorted instances */
+    int32_t precomputed;
+    int32_t reserved;
+} fgs_frame;
+
+/* Gradient outputs (rasterization_api.cu:170-183). Arrays are overwritten (or added to when
+ * `accumulate` is set); NULL entries that the model does not use are ignored. */
+typedef struct {
+    float* means;
+    float* scales;
+    float* rotations;
+    float* opacities;
+    float* precomputed_colors;
+    float* base_colors;
+    float* residual_params;
+    float* mlp_weights;  /* fp32, unscaled */
+} fgs_gradients;
+
+/* Device pointers into the workspaces of a frame, for inspection and tests. */
+typedef struct {
+    const uint32_t* n_touched;     /* [N] tiles touched per primitive (0 = culled) */
+    const uint32_t* depth_keys;    /* [N] float bits of the view depth (valid where n_touched > 0) */
+    const uint32_t* sorted_indices;/* [V] primitive index per depth rank */
+    const uint32_t* rank_of;       /* [N] depth rank per primitive or 0xffffffff */
+    const void* sorted_records;    /* [V] 48-byte render records in depth order */
+    const uint32_t* instance_offsets; /* [V] exclusive instance offsets in depth order */
+    const void* instance_keys;     /* [I] tile index per instance, uint16 or uint32 (wide_keys) */
+    const uint32_t* instance_ranks;/* [I] depth rank per instance */
+    const uint32_t* tile_ranges;   /* [T][2] instance range per tile */
+    const uint32_t* bucket_offsets;/* [T] inclusive bucket offsets */
+    const uint32_t* tile_max_contributors; /* [T] */
+    const float* final_transmittance;      /* [T*192] tile-local pixel order */
+    const uint32_t* n_contributors;        /* [T*192] */
+} fgs_frame_views;
+
+typedef struct {
+    float* param;
+    const float* grad;
+    float* exp_avg;
+    float* exp_avg_sq;
+    int64_t n_elements;
+    int64_t column_offset;   /* index of param[0] within its tensor (selects the per-column learning rate) */
+    int64_t step;            /* step count after this update (>= 1) */
+    double learning_rates[7];
+    int32_t n_learning_rates;/* 1..7, cycled per element */
+    double beta1, beta2, eps;
+} fgs_adam_segment;
+
+const char* fgs_last_error(void);
+int fgs_version(void);
+
+/* _C.Rasterizer() and its set_appearance / set_residual_mlp (rasterization/src/appearance.cu:166-201) */
+int fgs_rasterizer_create(fgs_rasterizer** out);
+int fgs_rasterizer_destroy(fgs_rasterizer* r);
+int fgs_set_appearance(fgs_rasterizer* r, int model, int max_degree, int base_activation, int residual_activation,
+                       int color_activation, int direction_gradient);
+/* tinycudann FullyFusedMLP with Identity encoding and no output activation (Appearance/Neural.py:40-51):
+ * hidden_activation 0 = none, 1 = ReLU; sh_degree_mask bit l = SH band l is an input (rasterization.py:45) */
+int fgs_set_residual_mlp(fgs_rasterizer* r, int n_input_dims, int n_output_dims, int n_neurons, int n_hidden_layers,
+                         int hidden_activation, int base_input, int n_frequencies, int sh_degree_mask);
+int fgs_mlp_param_count(const fgs_rasterizer* r, int64_t* out);
+int fgs_residual_stride(const fgs_rasterizer* r, int64_t* out);
+
+/* workspace sizes (the reference's grow-on-demand blobs, rasterization/include/buffer_utils.h:35-152) */
+int fgs_primitive_workspace_bytes(const fgs_rasterizer* r, int64_t n_primitives, size_t* out);
+int fgs_tile_workspace_bytes(int width, int height, size_t* out);
+int fgs_instance_workspace_bytes(int64_t n_instances, int width, int height, size_t* out);
+int fgs_bucket_workspace_bytes(int64_t n_buckets, size_t* out);
+int fgs_gradient_workspace_bytes(const fgs_rasterizer* r, int64_t n_primitives, size_t* out);
+
+/* forward, stage 1: preprocess with the fused appearance, order-preserving compaction of the visible
+ * primitives, stable depth sort, depth-ordered render records and instance offsets. Synchronises
+ * `stream` once to read the visible-primitive and instance counts into `frame`. */
+int fgs_forward_preprocess(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_settings* settings, void* prim_ws,
+                           size_t prim_ws_bytes, void* stream, fgs_frame* frame);
+/* forward, stage 2 (training): instance emission, stable tile sort, ranges, buckets, blend with
+ * per-bucket checkpoints; image is [3,H,W] fp32 */
+int fgs_forward_render(fgs_rasterizer* r, const fgs_settings* settings, fgs_frame* frame, void* prim_ws, void* tile_ws,
+                       size_t tile_ws_bytes, void* inst_ws, size_t inst_ws_bytes, void* bucket_ws, size_t bucket_ws_bytes,
+                       float* image, void* stream);
+/* forward, stage 2 (inference): as above without checkpoints; image is [H,W,3] or [3,H,W] */
+int fgs_inference_render(fgs_rasterizer* r, const fgs_settings* settings, fgs_frame* frame, void* prim_ws, void* tile_ws,
+                         size_t tile_ws_bytes, void* inst_ws, size_t inst_ws_bytes, float* image, int to_chw, int clamp_output,
+                         void* stream);
+/* backward of a training forward. densification_info is [2 or 3, N] (updated in place) or NULL. */
+int fgs_backward(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_settings* settings, const fgs_frame* frame,
+                 void* prim_ws, void* tile_ws, void* inst_ws, void* bucket_ws, void* grad_ws, size_t grad_ws_bytes,
+                 const float* image, const float* grad_image, const fgs_gradients* grads, float* densification_info,
+                 int densification_rows, int accumulate, void* stream);
+int fgs_frame_buffers(const fgs_frame* frame, void* prim_ws, void* tile_ws, void* inst_ws, fgs_frame_views* out);
+
+/* fused Adam over up to 12 segments in one launch (adam/src/adam.cu:18-42 per element) */
+int fgs_adam_step(const fgs_adam_segment* segments, int n_segments, void* stream);
+
+/* Optional per-stage timing: while enabled, every stage above records a CUDA event pair on its stream;
+ * fgs_profile_collect waits for them, returns the summed milliseconds per stage since the last collect
+ * (names comma-separated in `names`) and resets the totals. No counterpart in the reference, which has
+ * none (its timing is NeRFICG wall clock). */
+int fgs_profile_enable(int enabled);
+int fgs_profile_collect(char* names, size_t names_bytes, double* ms, int max_entries, int* n_entries);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FGS_B200_H */

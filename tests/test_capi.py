@@ -1,0 +1,61 @@
+"""The C-ABI library loads without a GPU, exports every symbol include/fgs_b200.h declares, and validates its
+arguments with error codes and messages (no compute calls)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared_symbols():
+    text = (ROOT / 'include' / 'fgs_b200.h').read_text()
+    return sorted(set(re.findall(r'^\s*(?:int|const char\*|void)\s+(fgs_\w+)\s*\(', text, re.M)))
+
+
+def test_library_exports_header_symbols():
+    from FasterGSVDACudaBackend import _lib
+    names = _declared_symbols()
+    assert len(names) >= 18
+    for n in names:
+        assert hasattr(_lib.lib, n), n
+
+
+def test_argument_validation_without_gpu():
+    import FasterGSVDACudaBackend as F
+    from FasterGSVDACudaBackend import rasterization as R
+    with pytest.raises(RuntimeError, match='invalid appearance model id'):
+        R._rasterizer.set_appearance(9, 3, 0, 0, 1, True)
+    with pytest.raises(RuntimeError, match='invalid color activation id'):
+        R._rasterizer.set_appearance(1, 3, 0, 0, 9, True)
+    with pytest.raises(RuntimeError, match='must select the neural appearance'):
+        F.initialize_appearance('sh', 3, 'none', 'none', 'relu', True)
+        F.initialize_residual_mlp(32, 3, {'otype': 'Identity'}, {'otype': 'FullyFusedMLP', 'activation': 'ReLU', 'output_activation': 'None',
+                                                                  'n_neurons': 16, 'n_hidden_layers': 2}, False, 1, [0, 1, 2, 3])
+    F.initialize_appearance('neural', 0, 'none', 'tanh', 'relu', True)
+    F.initialize_residual_mlp(32, 3, {'otype': 'Identity'}, {'otype': 'FullyFusedMLP', 'activation': 'ReLU', 'output_activation': 'None',
+                                                              'n_neurons': 16, 'n_hidden_layers': 2}, False, 1, [0, 1, 2, 3])
+    assert R._rasterizer.n_mlp_params == 16 * 32 + 16 * 16 + 16 * 16
+    assert R._rasterizer.residual_stride == 8
+    F.initialize_appearance('sv', 7, 'none', 'none', 'relu', True)
+    assert R._rasterizer.residual_stride == 49
+
+
+def test_workspace_queries():
+    from FasterGSVDACudaBackend._lib import lib, size_out
+    from FasterGSVDACudaBackend import rasterization as R
+    a = size_out(lib.fgs_primitive_workspace_bytes, R._rasterizer.handle, 1000)
+    b = size_out(lib.fgs_primitive_workspace_bytes, R._rasterizer.handle, 2000)
+    assert 0 < a < b
+    assert size_out(lib.fgs_tile_workspace_bytes, 1920, 1080) > 120 * 90 * 192 * 8
+    assert size_out(lib.fgs_instance_workspace_bytes, 10, 64, 48) > 0
+    with pytest.raises(RuntimeError):
+        size_out(lib.fgs_tile_workspace_bytes, 0, 10)
+
+
+def test_settings_field_order_matches_reference():
+    import FasterGSVDACudaBackend as F
+    assert F.RasterizerSettings._fields == ('w2c', 'cam_position', 'bg_color', 'appearance_degree', 'width', 'height', 'focal_x', 'focal_y',
+                                            'center_x', 'center_y', 'near_plane', 'far_plane', 'proper_antialiasing', 'render_base',
+                                            'render_residual')

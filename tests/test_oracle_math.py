@@ -1,0 +1,41 @@
+"""The deterministic exp / log used on both sides of the parity checks stay within a few ulp of the exact
+functions, and the oracle's binning invariants hold (ranges partition the instance list, lists sorted by tile,
+depth order inside a tile)."""
+import numpy as np
+import torch
+
+import synthetic as S
+from oracle import oracle as O
+from fgs_testutil import scene
+
+
+def test_det_exp_log_accuracy():
+    lib = O.load(False)
+    xs = np.concatenate([np.linspace(-86, 87, 20001), np.linspace(-6, 0, 5001)]).astype(np.float32)
+    e = np.array([lib.orc_det_exp(float(x)) for x in xs], np.float64)
+    ref = np.exp(xs.astype(np.float64))
+    assert np.max(np.abs(e - ref) / ref) < 3e-7
+    xb = np.linspace(-6, 0, 5001).astype(np.float32)
+    eb = np.array([lib.orc_det_exp_blend(float(x)) for x in xb], np.float64)
+    assert np.max(np.abs(eb - np.exp(xb.astype(np.float64))) / np.exp(xb.astype(np.float64))) < 5e-7
+    ys = np.concatenate([np.geomspace(1e-30, 1e30, 20001), np.linspace(0.9, 300, 5001)]).astype(np.float32)
+    lg = np.array([lib.orc_det_log(float(y)) for y in ys], np.float64)
+    ref = np.log(ys.astype(np.float64))
+    assert np.max(np.abs(lg - ref) / np.maximum(np.abs(ref), 1.0)) < 3e-7
+
+
+def test_binning_invariants():
+    n, W, H = 5000, 160, 120
+    prims = scene('sh', n, 3, seed=2, scale_shift=1.0)
+    cam = S.ring_cameras(2, W, H)[0]
+    o = O.run(O.make_appearance('sh', 3, 0, 0, 1, True), O.make_view(cam, 3), prims)
+    keys, ranks, ranges = o['tile_keys'], o['ranks'], o['ranges']
+    assert np.all(np.diff(keys.astype(np.int64)) >= 0)
+    for t in np.unique(keys):
+        s, e = ranges[t]
+        assert np.all(keys[s:e] == t)
+        assert np.all(np.diff(ranks[s:e].astype(np.int64)) > 0)
+    assert ranges[:, 1].max() == len(keys)
+    assert o['n_instances'] == int(o['n_touched'].sum())
+    d = o['depth_key'][o['sorted_idx']].view(np.float32)
+    assert np.all(np.diff(d) >= 0)
