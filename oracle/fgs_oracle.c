@@ -233,8 +233,8 @@ static int tile_overlaps_r(real mx, real my, real cx, real cy, real cz, uint32_t
     const real dfx = mx - kx, dfy = my - ky;
     const real dx = copysign((real)(TILE_W - 1), xmd);
     const real dy = copysign((real)(TILE_H - 1), ymd);
-    const real tx_ = nx * sat_r((dx * cx * dfx + dx * cy * dfy) / (dx * cx * dx));
-    const real ty_ = ny * sat_r((dy * cy * dfx + dy * cz * dfy) / (dy * cz * dy));
+    const real tx_ = ny * sat_r((dx * cx * dfx + dx * cy * dfy) / (dx * cx * dx));
+    const real ty_ = nx * sat_r((dy * cy * dfx + dy * cz * dfy) / (dy * cz * dy));
     const real px = kx + tx_ * dx, py = ky + ty_ * dy;
     const real ex = mx - px, ey = my - py;
     const real maxp = R(0.5) * (cx * ex * ex + cz * ey * ey) + cy * ex * ey;
@@ -262,6 +262,11 @@ static v3_r fused_color(const orc_appearance* A, const orc_view* v, int64_t i, c
                         const inreal* residual, const inreal* mlp);
 
 /* returns n_touched (0 = culled); fills rec and depth */
+/* optional trace of the intermediate values of one primitive (debugging aid): depth, opacity, det, a, b, c, x, y,
+ * mx, my, thr, xmin, xmax, ymin, ymax, nmax, count, stage reached */
+static double* g_trace = 0;
+#define TRACE(k, val) do { if (g_trace) g_trace[k] = (double)(val); } while (0)
+
 static uint32_t preprocess_one(const orc_appearance* A, const orc_view* v, int64_t i, const inreal* means, const inreal* scales,
                                const inreal* rots, const inreal* opac, orc_rec* out, real* depth_out) {
     const real* w;
@@ -271,6 +276,8 @@ static uint32_t preprocess_one(const orc_appearance* A, const orc_view* v, int64
     const real mx3 = means[3 * i], my3 = means[3 * i + 1], mz3 = means[3 * i + 2];
     const real depth = w[8] * mx3 + w[9] * my3 + w[10] * mz3 + w[11];
     *depth_out = depth;
+    TRACE(0, depth);
+    TRACE(17, 0);
     if (depth < (real)v->near_plane || depth > (real)v->far_plane) return 0;
     real opacity = sigmoid_r(opac[i]);
     int active = 1;
@@ -312,6 +319,7 @@ static uint32_t preprocess_one(const orc_appearance* A, const orc_view* v, int64
         opacity = opacity * sqrt(fmax(det_raw / det, R(0.0)));
         if (opacity < R(1.0) / R(255.0)) active = 0;
     }
+    TRACE(1, opacity); TRACE(2, det); TRACE(3, a); TRACE(4, b); TRACE(5, c); TRACE(6, x); TRACE(7, y); TRACE(17, 1);
     if (!active) return 0;
     const real mx = x * fx + cx, my = y * fy + cy;
     const real thr = DLOG(opacity * R(255.0));
@@ -324,11 +332,13 @@ static uint32_t preprocess_one(const orc_appearance* A, const orc_view* v, int64
     const uint32_t ymin = floor_clamped(my - ey, ph), ymax = ceil_clamped(my + ey, ph);
     const uint32_t tx0 = xmin / TILE_W, tx1 = (xmax + TILE_W - 1) / TILE_W, ty0 = ymin / TILE_H, ty1 = (ymax + TILE_H - 1) / TILE_H;
     const uint32_t bw = tx1 - tx0, nmax = bw * (ty1 - ty0);
+    TRACE(8, mx); TRACE(9, my); TRACE(10, thr); TRACE(11, xmin); TRACE(12, xmax); TRACE(13, ymin); TRACE(14, ymax); TRACE(15, nmax); TRACE(17, 2);
     if (nmax == 0) return 0;
     uint32_t count = 0;
     const real sx = mx - R(0.5), sy = my - R(0.5);
     for (uint32_t t = 0; t < nmax; t++)
         if (tile_overlaps_r(sx, sy, ca, cb, cc, tx0 + t % bw, ty0 + t / bw, thr)) count++;
+    TRACE(16, count); TRACE(17, 3);
     if (count == 0) return 0;
     out->mx = mx; out->my = my; out->opacity = opacity; out->thr = thr;
     out->ca = ca; out->cb = cb; out->cc = cc;
@@ -880,4 +890,16 @@ int orc_appearance_grad(const orc_appearance* A, int64_t n, const inreal* means,
         g_means[3 * i] = gm.x; g_means[3 * i + 1] = gm.y; g_means[3 * i + 2] = gm.z;
     }
     return 0;
+}
+
+/* trace of the preprocess intermediates of primitive i into out[18] (debugging aid) */
+int orc_preprocess_trace(const orc_appearance* A, const orc_view* v, int64_t i, const inreal* means, const inreal* scales, const inreal* rots,
+                         const inreal* opac, double* out) {
+    orc_rec q;
+    real depth;
+    for (int k = 0; k < 18; k++) out[k] = -1.0;
+    g_trace = out;
+    const uint32_t c = preprocess_one(A, v, i, means, scales, rots, opac, &q, &depth);
+    g_trace = 0;
+    return (int)c;
 }
