@@ -9,28 +9,56 @@ namespace fgs {
 
 struct AdamTable {
     AdamSegment seg[kMaxAdamSegments];
-    uint64_t start[kMaxAdamSegments + 1];
     int n;
 };
 
+__device__ inline void adam_one(const AdamSegment& S, float& p, float g, float& m, float& v, float lr) {
+    const float g2 = g * g;
+    const float mm = fmaf(S.beta1, m - g, g);
+    const float vv = fmaf(S.beta2, v - g2, g2);
+    const float denom = sqrtf(vv) * S.bc2_sqrt_rcp + S.eps;
+    p -= lr * mm / denom;
+    m = mm;
+    v = vv;
+}
+
+// blockIdx.y selects the segment; the x blocks stride over it, four elements per thread when the four arrays
+// are 16-byte aligned
 __global__ void __launch_bounds__(256) adam_kernel(const AdamTable tab) {
-    const uint64_t total = tab.start[tab.n];
+    if (static_cast<int>(blockIdx.y) >= tab.n) return;
+    const AdamSegment& S = tab.seg[blockIdx.y];
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-    int s = 0;
-    for (uint64_t e = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += stride) {
-        while (e >= tab.start[s + 1]) s++;
-        const AdamSegment& S = tab.seg[s];
-        const uint64_t j = e - tab.start[s];
-        const float g = S.grad[j];
-        const float m0 = S.m[j], v0 = S.v[j];
-        const float g2 = g * g;
-        const float m = fmaf(S.beta1, m0 - g, g);
-        const float v = fmaf(S.beta2, v0 - g2, g2);
-        const float denom = sqrtf(v) * S.bc2_sqrt_rcp + S.eps;
-        const float lr = S.lr[(S.col_offset + j) % static_cast<uint64_t>(S.n_lr)];
-        S.param[j] -= lr * m / denom;
-        S.m[j] = m;
-        S.v[j] = v;
+    const uint64_t tid = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint32_t nl = static_cast<uint32_t>(S.n_lr);
+    const bool vec = ((reinterpret_cast<uintptr_t>(S.param) | reinterpret_cast<uintptr_t>(S.grad) | reinterpret_cast<uintptr_t>(S.m) |
+                       reinterpret_cast<uintptr_t>(S.v)) & 15u) == 0;
+    uint64_t done = 0;
+    if (vec) {
+        const uint64_t n4 = S.n / 4;
+        float4* P4 = reinterpret_cast<float4*>(S.param);
+        const float4* G4 = reinterpret_cast<const float4*>(S.grad);
+        float4* M4 = reinterpret_cast<float4*>(S.m);
+        float4* V4 = reinterpret_cast<float4*>(S.v);
+        for (uint64_t q = tid; q < n4; q += stride) {
+            float4 p = P4[q], m = M4[q], v = V4[q];
+            const float4 g = G4[q];
+            uint32_t c = nl == 1 ? 0u : static_cast<uint32_t>((S.col_offset + 4 * q) % nl);
+            adam_one(S, p.x, g.x, m.x, v.x, S.lr[c]);
+            c = c + 1 == nl ? 0u : c + 1;
+            adam_one(S, p.y, g.y, m.y, v.y, S.lr[c]);
+            c = c + 1 == nl ? 0u : c + 1;
+            adam_one(S, p.z, g.z, m.z, v.z, S.lr[c]);
+            c = c + 1 == nl ? 0u : c + 1;
+            adam_one(S, p.w, g.w, m.w, v.w, S.lr[c]);
+            P4[q] = p;
+            M4[q] = m;
+            V4[q] = v;
+        }
+        done = 4 * n4;
+    }
+    for (uint64_t j = done + tid; j < S.n; j += stride) {
+        const uint32_t c = nl == 1 ? 0u : static_cast<uint32_t>((S.col_offset + j) % nl);
+        adam_one(S, S.param[j], S.grad[j], S.m[j], S.v[j], S.lr[c]);
     }
 }
 
@@ -39,19 +67,18 @@ cudaError_t launch_adam(const AdamSegment* segs, int n_segs, cudaStream_t s) {
     if (n_segs > kMaxAdamSegments) return cudaErrorInvalidValue;
     AdamTable tab;
     tab.n = n_segs;
-    tab.start[0] = 0;
+    uint64_t largest = 0;
     for (int i = 0; i < n_segs; i++) {
         tab.seg[i] = segs[i];
-        tab.start[i + 1] = tab.start[i] + segs[i].n;
+        largest = segs[i].n > largest ? segs[i].n : largest;
     }
-    for (int i = n_segs; i < kMaxAdamSegments; i++) tab.start[i + 1] = tab.start[n_segs];
-    const uint64_t total = tab.start[n_segs];
-    if (total == 0) return cudaSuccess;
+    if (largest == 0) return cudaSuccess;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const uint64_t want = (total + 255) / 256;
-    const int grid = static_cast<int>(want < static_cast<uint64_t>(sms) * 8 ? want : static_cast<uint64_t>(sms) * 8);
+    const uint64_t want = (largest / 4 + 255) / 256 + 1;
+    const uint64_t cap = static_cast<uint64_t>(sms) * 4;
+    const dim3 grid(static_cast<unsigned>(want < cap ? want : cap), static_cast<unsigned>(n_segs));
     adam_kernel<<<grid, 256, 0, s>>>(tab);
     return cudaGetLastError();
 }

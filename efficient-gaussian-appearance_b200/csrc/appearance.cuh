@@ -316,6 +316,8 @@ __device__ inline f3 lobes_backward(const float* p, f3 g, f3 d, int n_lobes, int
     return gd;
 }
 
+constexpr int kMaxResidualStride = 90;  // 10 NASGabor lobes
+
 // number of raw residual floats per Gaussian and of those active at the given degree
 __host__ __device__ inline int residual_stride(int model, int max_degree, int feature_dim) {
     switch (model) {

@@ -127,16 +127,6 @@ InstBuffers carve_inst(void* ws, uint64_t n, const Grid& g, size_t* bytes) {
     return I;
 }
 
-struct BucketBuffers { uint32_t* tile; float4* ckpt; };
-BucketBuffers carve_bucket(void* ws, uint64_t nb, size_t* bytes) {
-    Carver c(ws);
-    BucketBuffers b{};
-    b.tile = c.take<uint32_t>(nb);
-    b.ckpt = c.take<float4>(nb * fgs::kTilePixels);
-    if (bytes) *bytes = c.off;
-    return b;
-}
-
 struct GradBuffers { fgs::GradRecord* rec; float* mlp_scratch; };
 GradBuffers carve_grad(void* ws, uint64_t n, uint64_t n_mlp, size_t* bytes) {
     Carver c(ws);
@@ -354,7 +344,7 @@ int fgs_instance_workspace_bytes(int64_t n, int width, int height, size_t* out) 
 
 int fgs_bucket_workspace_bytes(int64_t n, size_t* out) {
     if (!out || n < 0) return fail(FGS_ERR_INVALID_ARGUMENT, "bad argument");
-    carve_bucket(nullptr, static_cast<uint64_t>(n), out);
+    *out = 0;  // the backward re-derives fragments per pixel; no per-bucket checkpoints are stored
     return FGS_OK;
 }
 
@@ -468,16 +458,16 @@ int fgs_forward_render(fgs_rasterizer* r, const fgs_settings* settings, fgs_fram
     if (!r || !frame || !image) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const Grid g = grid_of(frame->width, frame->height);
-    frame->n_buckets = frame->n_instances / 32 + g.tiles;
-    size_t need = 0;
-    BucketBuffers bb = carve_bucket(bucket_ws, static_cast<uint64_t>(frame->n_buckets), &need);
-    if (!bucket_ws || bucket_ws_bytes < need) return fail(FGS_ERR_WORKSPACE, "bucket workspace too small");
+    (void)bucket_ws;
+    (void)bucket_ws_bytes;
+    (void)g;
+    frame->n_buckets = 0;
     fgs::BlendArgs a;
     fgs::TileBuffers T;
     int rc = render_common(settings, frame, prim_ws, tile_ws, tile_ws_bytes, inst_ws, inst_ws_bytes, s, &a, &T);
     if (rc) return rc;
     ProfScope p_("blend_forward", s);
-    FGS_CUDA(fgs::launch_blend_train(a, image, T, bb.tile, bb.ckpt, s), "blend");
+    FGS_CUDA(fgs::launch_blend_train(a, image, T, s), "blend");
     return FGS_OK;
 }
 
@@ -526,7 +516,7 @@ int fgs_backward(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_setti
     fgs::PrimBuffers B = carve_prim(prim_ws, n, nullptr);
     const fgs::TileBuffers T = carve_tile(tile_ws, g, nullptr);
     InstBuffers I = carve_inst(inst_ws, static_cast<uint64_t>(frame->n_instances), g, nullptr);
-    BucketBuffers bb = carve_bucket(bucket_ws, static_cast<uint64_t>(frame->n_buckets), nullptr);
+    (void)bucket_ws;
     const fgs::View v = make_view(settings);
     const fgs::Params P = make_params(prims);
     if (nv > 0) {
@@ -542,8 +532,7 @@ int fgs_backward(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_setti
         a.grid_w = g.gw;
         a.grid_h = g.gh;
         ProfScope p_("blend_backward", s);
-        FGS_CUDA(fgs::launch_blend_backward(a, image, grad_image, T, bb.tile, bb.ckpt, static_cast<uint32_t>(frame->n_buckets), gb.rec,
-                                            v.proper_aa, densification_rows == 3 && densification_info ? 1 : 0, s),
+        FGS_CUDA(fgs::launch_blend_backward(a, image, grad_image, T, gb.rec, densification_rows == 3 && densification_info ? 1 : 0, s),
                  "blend backward");
     }
     if (n_mlp > 0) FGS_CUDA(cudaMemsetAsync(gb.mlp_scratch, 0, n_mlp * sizeof(float), s), "mlp gradient clear");

@@ -52,12 +52,10 @@ struct BlendArgs {
     const float* bg;
     int width, height, grid_w, grid_h;
 };
-cudaError_t launch_blend_train(const BlendArgs& a, float* image, const TileBuffers& T, uint32_t* bucket_tile, float4* ckpt,
-                               cudaStream_t s);
+cudaError_t launch_blend_train(const BlendArgs& a, float* image, const TileBuffers& T, cudaStream_t s);
 cudaError_t launch_blend_inference(const BlendArgs& a, float* image, int chw, int clamp, cudaStream_t s);
-cudaError_t launch_blend_backward(const BlendArgs& a, const float* image, const float* grad_image, const TileBuffers& T,
-                                  const uint32_t* bucket_tile, const float4* ckpt, uint32_t n_buckets_max, GradRecord* grads,
-                                  int proper_aa, int abs_grad, cudaStream_t s);
+cudaError_t launch_blend_backward(const BlendArgs& a, const float* image, const float* grad_image, const TileBuffers& T, GradRecord* grads,
+                                  int abs_grad, cudaStream_t s);
 
 // adam.cu
 struct AdamSegment {

@@ -124,6 +124,19 @@ __global__ void reorder_kernel(const uint32_t* __restrict__ sorted_idx, const Re
 
 
 
+// converts the blend backward's per-primitive sums into gradients w.r.t. mean2d, conic (off-diagonal halved as
+// in the reference's convention) and the opacity logit (sigmoid derivative folded in unless proper antialiasing)
+__device__ inline void blend_sums_to_grads(const GradRecord& g, const Record& q, int proper_aa, float& gmx, float& gmy, float& gca,
+                                           float& gcb, float& gcc, float& gop) {
+    const float ca = q.q1.x, cb = q.q1.y, cc = q.q1.z, o = q.q0.z;
+    gmx = ca * g.g0.x + cb * g.g0.y;
+    gmy = cb * g.g0.x + cc * g.g0.y;
+    gca = 0.5f * g.g0.z;
+    gcb = 0.5f * g.g0.w;
+    gcc = 0.5f * g.g1.x;
+    gop = proper_aa ? g.g2.x : (o - o * o) * g.g2.x;
+}
+
 __device__ inline void put(float* p, size_t k, float v, int acc) { if (acc) p[k] += v; else p[k] = v; }
 __device__ inline void put3(float* p, uint32_t i, f3 v, int acc) { put(p, 3ull * i, v.x, acc); put(p, 3ull * i + 1, v.y, acc); put(p, 3ull * i + 2, v.z, acc); }
 
@@ -261,14 +274,14 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(Params P, Appearanc
         return;
     }
     const GradRecord g = grads[r];
+    const Record rq = sorted_rec[r];
     const f3 g_color = mk3(g.g1.y, g.g1.z, g.g1.w);
     const f3 m = ld3(P.means, i);
     f3 gmean_color = mk3(0.0f, 0.0f, 0.0f);
     if (MODEL == kPrecomputed) {
         put3(O.precomputed, i, g_color, acc);
     } else {
-        const float4 q2 = sorted_rec[r].q2;
-        const f3 col = mk3(q2.x, q2.y, q2.z);
+        const f3 col = mk3(rq.q2.x, rq.q2.y, rq.q2.z);
         const f3 gpre = g_color * mk3(color_act_grad_from_y(A.color_act, col.x), color_act_grad_from_y(A.color_act, col.y),
                                       color_act_grad_from_y(A.color_act, col.z));
         const f3 base = ld3(P.base, i);
@@ -282,19 +295,27 @@ __global__ void __launch_bounds__(128) preprocess_bwd_kernel(Params P, Appearanc
         const f3 d = rn * dv;
         const int deg = min(v.degree, A.max_degree);
         const float* rp = P.residual + static_cast<size_t>(i) * stride;
-        float local[64];  // per-Gaussian residual gradients (max stride for the supported degrees)
-        f3 gd = mk3(0.0f, 0.0f, 0.0f);
-        if (MODEL == kSH) gd = sh_backward(rp, gpre, d, deg, A.res_act, local);
-        if (MODEL == kSV) gd = sv_backward(rp, gpre, d, deg, A.res_act, local);
-        if (MODEL == kNASG) gd = lobes_backward<false>(rp, gpre, d, deg, A.res_act, local);
-        if (MODEL == kNASGabor) gd = lobes_backward<true>(rp, gpre, d, deg, A.res_act, local);
-        const int active = residual_active(MODEL, deg, 0);
         float* gr = O.residual + static_cast<size_t>(i) * stride;
-        for (int k = 0; k < stride; k++) put(gr, k, k < active ? local[k] : 0.0f, acc);
+        // gradients go straight to the output row; only the accumulating mode stages them (the largest supported
+        // row is 10 NASGabor lobes, 90 floats)
+        float local[kMaxResidualStride];
+        float* out = acc ? local : gr;
+        f3 gd = mk3(0.0f, 0.0f, 0.0f);
+        if (MODEL == kSH) gd = sh_backward(rp, gpre, d, deg, A.res_act, out);
+        if (MODEL == kSV) gd = sv_backward(rp, gpre, d, deg, A.res_act, out);
+        if (MODEL == kNASG) gd = lobes_backward<false>(rp, gpre, d, deg, A.res_act, out);
+        if (MODEL == kNASGabor) gd = lobes_backward<true>(rp, gpre, d, deg, A.res_act, out);
+        const int active = residual_active(MODEL, deg, 0);
+        if (acc) {
+            for (int k = 0; k < active; k++) gr[k] += local[k];
+        } else {
+            for (int k = active; k < stride; k++) gr[k] = 0.0f;
+        }
         gmean_color = rn * (gd - dot3(gd, d) * d);
     }
-    float g_opacity = g.g2.x;
-    const f3 gmean = geometry_backward(P, v, i, m, g.g0.x, g.g0.y, g.g0.z, g.g0.w, g.g1.x, g_opacity, O);
+    float gmx, gmy, gca, gcb, gcc, g_opacity;
+    blend_sums_to_grads(g, rq, v.proper_aa, gmx, gmy, gca, gcb, gcc, g_opacity);
+    const f3 gmean = geometry_backward(P, v, i, m, gmx, gmy, gca, gcb, gcc, g_opacity, O);
     if (O.densification != nullptr && O.densification_rows == 3) {
         const float nx = 0.5f * (g.g2.y * static_cast<float>(v.width)), ny = 0.5f * (g.g2.z * static_cast<float>(v.height));
         O.densification[2ull * P.n + i] += sqrtf(nx * nx + ny * ny);
