@@ -83,6 +83,7 @@ PROTOTYPES = {
     'fgs_frame_buffers': (c_int, [_P(Frame), c_void_p, c_void_p, c_void_p, _P(FrameViews)]),
     'fgs_adam_step': (c_int, [_P(AdamSegment), c_int, c_void_p]),
     'fgs_profile_enable': (c_int, [c_int]),
+    'fgs_inference_noalloc': (c_int, [c_void_p, _P(Primitives), _P(Settings), c_void_p, c_int, c_int, c_void_p, _P(c_int64), _P(c_int64)]),
     'fgs_profile_collect': (c_int, [ctypes.c_char_p, c_size_t, _P(c_double), c_int, _P(c_int)]),
 }
 

@@ -642,4 +642,100 @@ int fgs_profile_collect(char* names, size_t names_bytes, double* ms, int max_ent
     return FGS_OK;
 }
 
+// ------------------------------------------------------------------------------------------------------
+// Render entry point that allocates nothing.
+//
+// Some callers cannot allocate device memory while they render: a viewer or engine plugin that runs inside a
+// host application owning a fixed device-memory budget, where a cudaMalloc in the middle of a frame may stall
+// the frame or fail outright. For them, fgs_inference_noalloc keeps every workspace of the inference path in
+// one file-scope device array of FGS_NOALLOC_SCRATCH_BYTES. The array is part of the library image, so every
+// GPU that loads the library holds it until the process exits. The caller still provides the inputs and the
+// output image.
+//
+// The device address of the array is looked up once per device, on that device's first call (with the device
+// current), so the first call on each device should happen before any stream capture. All calls share the
+// array and it keeps the previous call's contents; every buffer the kernels read is either fully rewritten by
+// the call or cleared by it (the tile ranges are set to zero before they are filled). Two calls whose work
+// overlaps on the GPU (different streams or threads without synchronisation) race on the array.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FGS_NOALLOC_SCRATCH_BYTES];
+static void* g_noalloc_ptr[64] = {nullptr};
+
+int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_settings* settings, float* image, int to_chw,
+                          int clamp_output, void* stream, int64_t* n_visible, int64_t* n_instances) {
+    if (!r || !image) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    int rc = check_settings(settings);
+    if (rc) return rc;
+    bool precomputed = false;
+    rc = check_prims(r, prims, &precomputed);
+    if (rc) return rc;
+    int dev = 0;
+    FGS_CUDA(cudaGetDevice(&dev), "noalloc device");
+    if (dev < 0 || dev >= 64) return fail(FGS_ERR_UNSUPPORTED, "device index beyond 63");
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        FGS_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "noalloc scratch address");
+        g_noalloc_ptr[dev] = p;
+    }
+    char* base = static_cast<char*>(g_noalloc_ptr[dev]);
+    const uint64_t n = static_cast<uint64_t>(prims->n_primitives);
+    const Grid g = grid_of(settings->width, settings->height);
+    size_t prim_bytes = 0, tile_bytes = 0;
+    carve_prim(nullptr, n, &prim_bytes);
+    carve_tile(nullptr, g, &tile_bytes);
+    prim_bytes = (prim_bytes + 255) & ~static_cast<size_t>(255);
+    tile_bytes = (tile_bytes + 255) & ~static_cast<size_t>(255);
+    if (prim_bytes + tile_bytes > FGS_NOALLOC_SCRATCH_BYTES)
+        return fail(FGS_ERR_WORKSPACE, "fgs_inference_noalloc: " + std::to_string(n) + " primitives at " + std::to_string(settings->width) + "x" +
+                                           std::to_string(settings->height) + " need " + std::to_string(prim_bytes + tile_bytes) +
+                                           " bytes of scratch before binning, more than the static maximum of " +
+                                           std::to_string(static_cast<size_t>(FGS_NOALLOC_SCRATCH_BYTES)));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    fgs::PrimBuffers B = carve_prim(base, n, nullptr);
+    const fgs::TileBuffers T = carve_tile(base + prim_bytes, g, nullptr);
+    const fgs::View v = make_view(settings);
+    const fgs::Params P = make_params(prims);
+    uint64_t nv = 0, ni = 0;
+    if (n > 0) {
+        FGS_CUDA(fgs::launch_preprocess_fwd(P, r->cfg, v, B, precomputed, s), "preprocess");
+        FGS_CUDA(fgs::launch_compaction(B, static_cast<uint32_t>(n), s), "compaction");
+        unsigned long long counts[2] = {0, 0};  // pageable host memory: no allocation
+        FGS_CUDA(cudaMemcpyAsync(counts, B.counters, sizeof(counts), cudaMemcpyDeviceToHost, s), "counter readback");
+        FGS_CUDA(cudaStreamSynchronize(s), "counter readback");
+        nv = counts[0];
+        ni = counts[1];
+    }
+    size_t inst_bytes = 0;
+    InstBuffers I = carve_inst(nullptr, ni, g, &inst_bytes);
+    if (prim_bytes + tile_bytes + inst_bytes > FGS_NOALLOC_SCRATCH_BYTES)
+        return fail(FGS_ERR_WORKSPACE, "fgs_inference_noalloc: " + std::to_string(ni) + " tile instances need " +
+                                           std::to_string(prim_bytes + tile_bytes + inst_bytes) + " bytes of scratch, more than the static maximum of " +
+                                           std::to_string(static_cast<size_t>(FGS_NOALLOC_SCRATCH_BYTES)));
+    I = carve_inst(base + prim_bytes + tile_bytes, ni, g, nullptr);
+    if (nv > 0) {
+        FGS_CUDA(fgs::depth_sort(B, static_cast<uint32_t>(nv), s), "depth sort");
+        FGS_CUDA(fgs::launch_reorder(B, static_cast<uint32_t>(nv), s), "reorder");
+        FGS_CUDA(fgs::exclusive_scan_u32(B.inst_off, static_cast<uint32_t>(nv), B.cub_temp, B.cub_temp_bytes, s), "offset scan");
+        FGS_CUDA(fgs::launch_emit(B.sorted_rec, B.inst_off, I.keys_a, I.vals_a, static_cast<uint32_t>(nv), g.gw, g.wide, s), "emit");
+    }
+    const void* keys = nullptr;
+    const uint32_t* vals = nullptr;
+    FGS_CUDA(fgs::tile_sort(I.keys_a, I.keys_b, I.vals_a, I.vals_b, ni, g.end_bit > 0 ? g.end_bit : 1, g.wide, I.temp, I.temp_bytes, &keys, &vals, s),
+             "tile sort");
+    FGS_CUDA(fgs::launch_ranges(keys, ni, g.wide, T, g.tiles, s), "ranges");
+    fgs::BlendArgs a;
+    a.ranges = T.ranges;
+    a.bucket_off = T.bucket_off;
+    a.vals = vals;
+    a.rec = B.sorted_rec;
+    a.bg = settings->bg_color;
+    a.width = settings->width;
+    a.height = settings->height;
+    a.grid_w = g.gw;
+    a.grid_h = g.gh;
+    FGS_CUDA(fgs::launch_blend_inference(a, image, to_chw, clamp_output, s), "blend");
+    if (n_visible) *n_visible = static_cast<int64_t>(nv);
+    if (n_instances) *n_instances = static_cast<int64_t>(ni);
+    return FGS_OK;
+}
+
 }  // extern "C"

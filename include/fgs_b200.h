@@ -187,6 +187,18 @@ int fgs_adam_step(const fgs_adam_segment* segments, int n_segments, void* stream
 int fgs_profile_enable(int enabled);
 int fgs_profile_collect(char* names, size_t names_bytes, double* ms, int max_entries, int* n_entries);
 
+/* Inference render that allocates nothing (no counterpart in the reference, which always allocates its buffers
+ * with torch). For callers that cannot allocate device memory while they render, such as a viewer or engine plugin
+ * running inside a host application that owns a fixed device-memory budget, where a cudaMalloc in the middle of a
+ * frame may stall it or fail. All workspaces live in one static device array of FGS_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading the library holds until exit; inputs and the output image stay caller-owned. The call rejects,
+ * with FGS_ERR_WORKSPACE and a message, any scene whose workspaces do not fit (roughly: 100k primitives at 720p
+ * with up to ~1M tile instances fit). Each device's first call looks up the array's address, so make it before any
+ * stream capture. Calls share the array: calls that overlap on the GPU race. Output as fgs_inference_render. */
+#define FGS_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_settings* settings, float* image, int to_chw,
+                          int clamp_output, void* stream, int64_t* n_visible, int64_t* n_instances);
+
 #ifdef __cplusplus
 }
 #endif
