@@ -98,8 +98,8 @@ def initialize_residual_mlp(
 ) -> None:
     """Configures the fused residual MLP from a tinycudann-style configuration (requires initialize_appearance('neural', ...) first).
 
-    Supported: Identity encoding; FullyFusedMLP / CutlassMLP networks with 16, 32, 64 or 128 neurons, ReLU or None hidden
-    activation, no output activation. Weights are a flat fp32 vector: the input layer [n_neurons, pad16(n_input_dims)],
+    Supported: Identity encoding; FullyFusedMLP / CutlassMLP networks with 16, 32 or 64 neurons, ReLU or None hidden
+    activation, no output activation; SH bands 0-3 of the view direction (every reference configuration). Weights are a flat fp32 vector: the input layer [n_neurons, pad16(n_input_dims)],
     n_hidden_layers - 1 hidden layers [n_neurons, n_neurons], the output layer [16, n_neurons] (rows beyond n_output_dims
     unused), each row-major; padded input dims carry the value 1.
     """
@@ -165,10 +165,31 @@ def _check_input(t: torch.Tensor | None, name: str) -> None:
         raise RuntimeError(f'{name} must be a contiguous CUDA float32 tensor')
 
 
+def _check_sizes(n: int, scales, rotations, opacities, precomputed, base, residual, mlp, rasterizer: 'Rasterizer | None') -> None:
+    """Rejects tensors whose sizes do not match N and the configured appearance (the kernels index them by N)."""
+    def need(t, count, name):
+        if t is not None and t.numel() > 0 and t.numel() != count:
+            raise ValueError(f'{name} has {t.numel()} elements, expected {count}')
+    need(scales, 3 * n, 'scales')
+    need(rotations, 4 * n, 'rotations')
+    need(opacities, n, 'opacities')
+    need(precomputed, 3 * n, 'precomputed_colors')
+    if precomputed is not None and precomputed.numel() > 0:
+        return
+    need(base, 3 * n, 'base_colors')
+    if rasterizer is not None and rasterizer.model is not None:
+        need(residual, rasterizer.residual_stride * n, 'residual_params')
+        if rasterizer.mlp is not None:
+            need(mlp, rasterizer.n_mlp_params, 'mlp_weights')
+
+
 def _c_primitives(means, scales, rotations, opacities, precomputed, base, residual, mlp) -> _lib.Primitives:
     for t, name in ((means, 'means'), (scales, 'scales'), (rotations, 'rotations'), (opacities, 'opacities'),
                     (precomputed, 'precomputed_colors'), (base, 'base_colors'), (residual, 'residual_params'), (mlp, 'mlp_weights')):
         _check_input(t, name)
+    if means.numel() % 3:
+        raise ValueError('means must have shape [N, 3]')
+    _check_sizes(means.numel() // 3, scales, rotations, opacities, precomputed, base, residual, mlp, _rasterizer)
     if rotations.numel() > 0 and rotations.data_ptr() % 16 != 0:
         raise RuntimeError('rotations must be 16-byte aligned')
     return _lib.Primitives(ptr(means), ptr(scales), ptr(rotations), ptr(opacities), ptr(precomputed), ptr(base), ptr(residual), ptr(mlp),

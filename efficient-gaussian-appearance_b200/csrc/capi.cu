@@ -278,12 +278,11 @@ int fgs_set_residual_mlp(fgs_rasterizer* r, int n_input, int n_output, int n_neu
     if (!r->appearance_set || r->cfg.model != fgs::kNeural)
         return fail(FGS_ERR_NOT_CONFIGURED, "FasterGSVDA: set_appearance must select the neural appearance model before set_residual_mlp");
     if (n_output != 3) return fail(FGS_ERR_UNSUPPORTED, "the residual mlp must have 3 outputs");
-    if (n_neurons != 16 && n_neurons != 32 && n_neurons != 64 && n_neurons != 128)
-        return fail(FGS_ERR_UNSUPPORTED, "n_neurons must be 16, 32, 64 or 128");
+    if (n_neurons != 16 && n_neurons != 32 && n_neurons != 64) return fail(FGS_ERR_UNSUPPORTED, "n_neurons must be 16, 32 or 64");
     if (n_hidden < 1 || n_hidden > 8) return fail(FGS_ERR_UNSUPPORTED, "n_hidden_layers must be in [1, 8]");
     if (hidden_act < 0 || hidden_act > 1) return fail(FGS_ERR_UNSUPPORTED, "hidden activation must be None or ReLU");
     if (n_freq < 0 || n_freq > 8) return fail(FGS_ERR_UNSUPPORTED, "n_frequencies must be in [0, 8]");
-    if (sh_mask < 0 || sh_mask >= (1 << 7)) return fail(FGS_ERR_UNSUPPORTED, "SH degrees must be in [0, 6]");
+    if (sh_mask < 0 || sh_mask >= (1 << 4)) return fail(FGS_ERR_UNSUPPORTED, "SH degrees of the direction encoding must be in [0, 3]");
     int n_sh = 0, bands = 0;
     for (int l = 0; l <= 6; l++)
         if (sh_mask & (1 << l)) { n_sh += 2 * l + 1; if (l > 0) bands++; }
@@ -307,6 +306,11 @@ int fgs_set_residual_mlp(fgs_rasterizer* r, int n_input, int n_output, int n_neu
     r->cfg.hidden_act = hidden_act;
     r->cfg.max_degree = bands;
     r->cfg.n_params = n_neurons * pad + (n_hidden - 1) * n_neurons * n_neurons + 16 * n_neurons;
+    if (fgs::neural_smem_bytes(r->cfg) > 227 * 1024) {
+        r->mlp_set = false;
+        return fail(FGS_ERR_UNSUPPORTED, "residual mlp too large for the fused kernels' shared memory (" + std::to_string(fgs::neural_smem_bytes(r->cfg)) +
+                                             " bytes > 227 KiB); reduce n_input_dims, n_neurons or n_hidden_layers");
+    }
     r->mlp_set = true;
     return FGS_OK;
 }

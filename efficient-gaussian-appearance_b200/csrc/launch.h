@@ -21,6 +21,7 @@ cudaError_t launch_preprocess_fwd_neural(const Params& P, const AppearanceConfig
 cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* rank_of,
                                          const Record* sorted_rec, const GradRecord* grads, const GradOut& O, cudaStream_t s);
 size_t neural_grad_scratch_floats(const AppearanceConfig& A);
+size_t neural_smem_bytes(const AppearanceConfig& A);  // largest dynamic shared memory of the neural kernels
 
 // sort.cu (depth sort, instance offsets, tile sort, scans)
 size_t depth_sort_temp_bytes(uint32_t n);

@@ -8,8 +8,8 @@ namespace fgs {
 
 __device__ inline float bits_of_bounds(uint32_t lo, uint32_t hi) { return __uint_as_float(lo | (hi << 16)); }
 
-// Stores primitive `idx`; must be reached by every thread of the CTA (kChunk threads).
-__device__ inline void store_primitive(const PrimBuffers& B, uint32_t idx, bool in_range, const Geometry& G, f3 color) {
+// Stores primitive `idx` of chunk `chunk`; must be reached by every thread of the CTA (kChunk threads).
+__device__ inline void store_primitive(const PrimBuffers& B, uint32_t idx, bool in_range, const Geometry& G, f3 color, uint32_t chunk) {
     const bool visible = in_range && G.n_touched > 0;
     if (in_range) {
         B.n_touched[idx] = G.n_touched;
@@ -33,7 +33,7 @@ __device__ inline void store_primitive(const PrimBuffers& B, uint32_t idx, bool 
     if (threadIdx.x == 0) {
         uint32_t s = 0;
         for (int w = 0; w < kChunk / 32; w++) s += warp_inst[w];
-        B.chunk_stats[blockIdx.x] = make_uint2(static_cast<uint32_t>(nvis), s);
+        B.chunk_stats[chunk] = make_uint2(static_cast<uint32_t>(nvis), s);
     }
 }
 

@@ -59,3 +59,19 @@ def test_settings_field_order_matches_reference():
     assert F.RasterizerSettings._fields == ('w2c', 'cam_position', 'bg_color', 'appearance_degree', 'width', 'height', 'focal_x', 'focal_y',
                                             'center_x', 'center_y', 'near_plane', 'far_plane', 'proper_antialiasing', 'render_base',
                                             'render_residual')
+
+
+def test_size_validation_rejects_mismatched_tensors():
+    import torch
+    import FasterGSVDACudaBackend as F
+    from FasterGSVDACudaBackend import rasterization as R
+    F.initialize_appearance('sh', 3, 'none', 'none', 'relu', True)
+    n = 10
+    with pytest.raises(ValueError, match='residual_params'):
+        R._check_sizes(n, torch.zeros(n, 3), torch.zeros(n, 4), torch.zeros(n, 1), None, torch.zeros(n, 3), torch.zeros(n, 14, 3), None,
+                       R._rasterizer)
+    with pytest.raises(ValueError, match='rotations'):
+        R._check_sizes(n, torch.zeros(n, 3), torch.zeros(n, 3), torch.zeros(n, 1), None, torch.zeros(n, 3), torch.zeros(n, 15, 3), None,
+                       R._rasterizer)
+    R._check_sizes(n, torch.zeros(n, 3), torch.zeros(n, 4), torch.zeros(n, 1), None, torch.zeros(n, 3), torch.zeros(n, 15, 3), None,
+                   R._rasterizer)

@@ -1,0 +1,97 @@
+"""GPU parity of the Neural appearance (latent features -> frequency encoding + SH bands of the view direction ->
+fp16 MLP on tensor cores) against the oracle's fp16-semantics restatement, for the reference's default
+configuration (8 features, 1 octave, bands 0-3, 2x16 hidden), the c2 configuration (32 features, 2x64 hidden,
+80 inputs), raw features with 1 and 3 hidden layers, and base colors as extra inputs.
+
+Binning is bit-exact (the MLP does not enter culling or bounds). Colors differ from the oracle only where an fp32
+sum lands on an fp16 rounding boundary in a different order (tensor-core accumulation), so images are compared at
+1e-3 max-abs and 1e-5 mean-abs. The backward rounds the loss-scaled output and hidden gradients to fp16 as the
+reference does, while the oracle differentiates in double: gradients are compared at 1e-2 relative L2 for the
+MLP weights and features and 1e-3 for the geometry."""
+import numpy as np
+import pytest
+import torch
+
+import synthetic as S
+from oracle import oracle as O
+from fgs_testutil import to_dev, settings_for, gpu_forward_stages, rel_err
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = [
+    # feature_dim, n_freq, neurons, hidden, base_input, res_act
+    (8, 1, 16, 2, False, 'tanh'),
+    (32, 1, 64, 2, False, 'tanh'),
+    (16, 0, 32, 1, False, 'none'),
+    (16, 0, 32, 3, False, 'softplus'),
+    (8, 1, 16, 2, True, 'tanh'),
+]
+
+
+def _setup(F, feat, nf, nn, nh, base_input, res_act):
+    n_enc = (feat + (3 if base_input else 0)) * (2 * nf if nf else 1)
+    n_in = n_enc + 16
+    F.initialize_appearance('neural', 0, 'none', res_act, 'relu', True)
+    F.initialize_residual_mlp(n_in, 3, {'otype': 'Identity'}, {'otype': 'FullyFusedMLP', 'activation': 'ReLU', 'output_activation': 'None',
+                                                                'n_neurons': nn, 'n_hidden_layers': nh}, base_input, nf, [0, 1, 2, 3])
+    pad = (n_in + 15) // 16 * 16
+    neural = dict(feature_dim=feat, base_input=int(base_input), n_freq=nf, sh_mask=15, n_input=n_in, n_input_pad=pad, n_neurons=nn,
+                  n_hidden=nh, hidden_act=1)
+    return neural, S.mlp_layer_shapes(pad, nn, nh)
+
+
+@pytest.mark.parametrize('cfg', CONFIGS, ids=[f'f{c[0]}x{c[1]}-n{c[2]}x{c[3]}{"-base" if c[4] else ""}-{c[5]}' for c in CONFIGS])
+def test_neural_parity(cuda, cfg):
+    import FasterGSVDACudaBackend as F
+    feat, nf, nn, nh, base_input, res_act = cfg
+    neural, shapes = _setup(F, feat, nf, nn, nh, base_input, res_act)
+    n, W, H = 12000, 192, 128
+    geo = S.geometry(n)
+    geo['scales'] = geo['scales'] + 1.0
+    app = S.neural_appearance(n, feature_dim=feat, layer_shapes=shapes)
+    prims = {**geo, **app}
+    cam = S.ring_cameras(3, W, H)[2]
+    settings = settings_for(F, cam, 3, cuda)
+    dev = to_dev(prims, cuda)
+    g = gpu_forward_stages(F, dev, settings)
+    a = O.make_appearance('neural', 0, 0, {'none': 0, 'tanh': 1, 'softplus': 2}[res_act], 1, True, neural=neural)
+    grad_image = torch.randn(3, H, W, generator=torch.Generator().manual_seed(2)) * 0.01
+    o = O.run(a, O.make_view(cam, 3), prims, grad_image=grad_image)
+    assert g['n_visible'] == o['n_visible'] and g['n_instances'] == o['n_instances']
+    for k in ('n_touched', 'sorted_idx', 'tile_keys', 'ranks', 'ranges'):
+        np.testing.assert_array_equal(g[k], o[k], err_msg=k)
+    img_err = np.abs(g['image'] - o['image'])
+    assert img_err.max() <= 1e-3 and img_err.mean() <= 1e-5, (img_err.max(), img_err.mean())
+
+    leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
+    img = F.diff_rasterize(leaves['means'], leaves['scales'], leaves['rotations'], leaves['opacities'], torch.empty(0, device=cuda), settings,
+                           base_colors=leaves['base_colors'], residual_params=leaves['residual_params'], mlp_weights=leaves['mlp_weights'])
+    img.backward(grad_image.to(cuda))
+    tol = {'means': 1e-3, 'scales': 1e-3, 'rotations': 1e-3, 'opacities': 1e-3, 'base_colors': 1e-2, 'residual_params': 1e-2,
+           'mlp_weights': 1e-2}
+    for k, t in leaves.items():
+        ref = o['grads'][k]
+        err = rel_err(t.grad.cpu().numpy().reshape(ref.shape), ref)
+        assert err <= tol[k], f'{k}: relative error {err:.2e}'
+
+
+def test_neural_degree_zero_and_inference(cuda):
+    import FasterGSVDACudaBackend as F
+    neural, shapes = _setup(F, 8, 1, 16, 2, False, 'tanh')
+    n, W, H = 8000, 160, 120
+    geo = S.geometry(n, seed=5)
+    geo['scales'] = geo['scales'] + 1.0
+    prims = {**geo, **S.neural_appearance(n, feature_dim=8, layer_shapes=shapes)}
+    cam = S.ring_cameras(2, W, H)[0]
+    dev = to_dev(prims, cuda)
+    a = O.make_appearance('neural', 0, 0, 1, 1, True, neural=neural)
+    for degree in (0, 2):
+        settings = settings_for(F, cam, degree, cuda)
+        img = F.rasterize(dev['means'], dev['scales'], dev['rotations'], dev['opacities'], settings, True, False,
+                          base_colors=dev['base_colors'], residual_params=dev['residual_params'], mlp_weights=dev['mlp_weights'])
+        o = O.run(a, O.make_view(cam, degree), prims)
+        err = np.abs(img.cpu().numpy() - o['image'])
+        if degree == 0:
+            np.testing.assert_array_equal(img.cpu().numpy(), o['image'])
+        else:
+            assert err.max() <= 1e-3 and err.mean() <= 1e-5
