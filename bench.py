@@ -1,23 +1,28 @@
 """Benchmark of the B200-native fused-appearance rasterizer (driver contract: one JSON line on rank 0).
 
-Default workload (c1 of the benchmark configurations): one full training step of the differentiable rasterizer with
-fused SH degree 3 -- forward (preprocess, binning, blend), backward (blend backward, preprocess backward) and the fused
-Adam update of every parameter group -- for N = 1,000,000 synthetic Gaussians and one 1280x720 view. With --gpus N
-(torchrun, one process per GPU) every rank trains its own replica on its own view (replicas only: the workload has no
-exchange step), so the aggregate value is the sum over ranks ("scaling": "weak").
+Default workload c4 (the headline "train steps/s @1080p"): one data-parallel training step of the Neural appearance
+model -- 6,000,000 Gaussians, 32 latent features per Gaussian, MLP 80 -> 64 -> 64 -> 3 (fp16 tensor cores) -- over a
+global batch of 8 views at 1920x1080. Every rank renders its share of the views (forward, loss 0.8 L1 + 0.2 (1 - SSIM)
+against a blurred random target, backward with gradients accumulated over its views); the flat gradient buffer is
+reduce-scattered, every rank runs the fused Adam on its slice, and the parameters are all-gathered (NCCL). The total
+work is fixed as N grows ("scaling": "strong").
 
-value: steps/s with all inputs resident in HBM; e2e: the same through the public API with the view's upstream
-gradient copied host->device from pinned memory and the rendered image copied back every step.
---impl reference times the CPU restatement of the reference path (oracle/, single thread) on a bounded sample.
+Workload c1 (--workload c1): one SH-3 training step (forward, backward, fused Adam through the public autograd API)
+of 1,000,000 Gaussians on one 1280x720 view with a fixed upstream image gradient; with N GPUs every rank trains its
+own replica (no exchange step, "scaling": "weak").
+
+value: steps/s with every input resident in HBM. e2e: the same step with the step's inputs (c4: the target images of
+the rank's views; c1: the upstream gradient) copied host->device from pinned memory and the step's result (c4: the
+loss; c1: the rendered image) copied back, every step. --impl reference times the CPU restatement of the reference
+path (oracle/, "port", one thread) on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
-import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -29,12 +34,19 @@ import numpy as np
 import torch
 
 WORKLOADS = {
-    'c1': dict(n=1_000_000, width=1280, height=720, model='sh', degree=3),
+    'c1': dict(n=1_000_000, width=1280, height=720, model='sh', degree=3, views=1),
+    'c4': dict(n=6_000_000, width=1920, height=1080, model='neural', degree=3, views=8, feature_dim=32, n_freq=1, neurons=64, hidden=2),
 }
-
-# kernels of this library launched per training step (preprocess, chunk scan, compaction, reorder, emit, ranges,
-# bucket scan, forward blend, backward blend, backward preprocess, adam); CUB sort / scan kernels are not counted
-OWN_KERNELS_PER_STEP = 11
+C1_LRS = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 'base_colors': 0.000705237, 'residual_params': 0.000125}
+C4_LRS = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 'base_colors': 0.00025, 'residual_params': 0.008,
+          'mlp_weights': 0.003}
+METRIC = {'c1': 'train steps/s (forward + backward + fused Adam), fused SH-3 appearance, 1M Gaussians @1280x720',
+          'c4': 'train steps/s (8 views @1920x1080, forward + loss + backward + gradient reduce-scatter + sharded fused Adam + '
+                'parameter all-gather), Neural appearance, 6M Gaussians'}
+# this library's kernels per rendered view (preprocess, chunk scan, compaction, reorder, emit, ranges, bucket scan,
+# forward blend, backward blend, backward preprocess) plus one fused Adam per step; CUB sort / scan kernels, torch's
+# loss kernels and NCCL are not counted
+OWN_KERNELS_PER_VIEW = 10
 
 
 def _peaks() -> tuple[float, str]:
@@ -46,237 +58,331 @@ def _peaks() -> tuple[float, str]:
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples SM clock and clock-event reasons through NVML every 20 ms while the timed region runs."""
 
-    def __init__(self, index: int) -> None:
-        self.index = index
-        self.proc = None
-        self.path = Path(f'/tmp/fgs_clocks_{os.getpid()}.csv')
+    REASONS = {0x4: 'sw_power_cap', 0x8: 'hw_slowdown', 0x20: 'sw_thermal_slowdown', 0x40: 'hw_thermal_slowdown', 0x80: 'hw_power_brake'}
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self.samples = []
+        self.reasons = set()
+        self.stop = threading.Event()
+        self.thread = None
+        self.handle = None
+        self.max_mhz = None
 
     def __enter__(self):
-        q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
-             'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
         try:
-            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={q}', '--format=csv,noheader,nounits', '-lms', '200'],
-                                         stdout=open(self.path, 'w'), stderr=subprocess.DEVNULL)
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith('GPU-') else 'GPU-' + uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.pynvml = pynvml
+
+            def run():
+                while not self.stop.is_set():
+                    try:
+                        self.samples.append(pynvml.nvmlDeviceGetClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+                        bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle) if hasattr(
+                            pynvml, 'nvmlDeviceGetCurrentClocksEventReasons') else pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+                        for b, name in self.REASONS.items():
+                            if bits & b:
+                                self.reasons.add(name)
+                    except Exception:
+                        pass
+                    self.stop.wait(0.02)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.handle = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            self.proc.wait(timeout=10)
+        self.stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
 
     def summary(self) -> dict:
-        if not self.path.exists():
-            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled']}
-        sm, smax, reasons = [], [], set()
-        for line in self.path.read_text().splitlines():
-            f = [x.strip() for x in line.split(',')]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for name, val in zip(('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap'), f[5:9]):
-                if val.lower() == 'active':
-                    reasons.add(name)
-        self.path.unlink(missing_ok=True)
-        if not sm:
-            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled']}
-        return {'sm_mhz': float(np.median(sm)), 'sm_max_mhz': float(max(smax)), 'reasons': sorted(reasons), 'samples': len(sm)}
+        if not self.samples:
+            return {'sm_mhz': None, 'sm_max_mhz': self.max_mhz, 'reasons': ['unsampled']}
+        return {'sm_mhz': float(np.median(self.samples)), 'sm_max_mhz': float(self.max_mhz), 'reasons': sorted(self.reasons),
+                'samples': len(self.samples)}
 
 
-def make_scene(wl: dict, seed_view: int):
+# ------------------------------------------------------------------------------------------------------------
+# scenes
+
+def scene(wl: dict) -> dict:
     import synthetic as S
     n = wl['n']
-    prims = {**S.geometry(n), **S.sh_appearance(n, wl['degree'])}
-    cams = S.ring_cameras(8, wl['width'], wl['height'])
-    cam = cams[seed_view % len(cams)]
-    grad = torch.randn(3, wl['height'], wl['width'], generator=torch.Generator().manual_seed(2)) * 0.01
-    return prims, cam, grad
+    geo = S.geometry(n)
+    if wl['model'] == 'sh':
+        return {**geo, **S.sh_appearance(n, wl['degree'])}
+    n_in = wl['feature_dim'] * 2 * wl['n_freq'] + 16
+    pad = (n_in + 15) // 16 * 16
+    return {**geo, **S.neural_appearance(n, wl['feature_dim'], layer_shapes=S.mlp_layer_shapes(pad, wl['neurons'], wl['hidden']))}
+
+
+def configure(wl: dict) -> None:
+    import FasterGSVDACudaBackend as F
+    if wl['model'] == 'sh':
+        F.initialize_appearance('sh', wl['degree'], 'none', 'none', 'relu', True)
+        return
+    F.initialize_appearance('neural', 0, 'none', 'tanh', 'relu', True)
+    F.initialize_residual_mlp(wl['feature_dim'] * 2 * wl['n_freq'] + 16, 3, {'otype': 'Identity'},
+                              {'otype': 'FullyFusedMLP', 'activation': 'ReLU', 'output_activation': 'None', 'n_neurons': wl['neurons'],
+                               'n_hidden_layers': wl['hidden']}, False, wl['n_freq'], [0, 1, 2, 3])
+
+
+def targets(wl: dict) -> list[torch.Tensor]:
+    """Per-view training targets: U(0,1) images smoothed by a 9x9 Gaussian blur (sigma 2), seed 2."""
+    from trainer import blur
+    g = torch.Generator().manual_seed(2)
+    return [blur(torch.rand(3, wl['height'], wl['width'], generator=g), 9, 2.0).contiguous() for _ in range(wl['views'])]
+
+
+def settings_of(cam, degree: int, dev):
+    import FasterGSVDACudaBackend as F
+    return F.RasterizerSettings(cam.w2c.to(dev), cam.position.to(dev), cam.bg.to(dev), degree, cam.width, cam.height, cam.focal_x,
+                                cam.focal_y, cam.center_x, cam.center_y, cam.near_plane, cam.far_plane, False, True, True)
 
 
 def stage_bytes(stage: str, s: dict) -> float:
-    """Algorithmic DRAM bytes of one launch of each stage (per-unit figures x units of the frame)."""
-    N, V, I, P = s['N'], s['V'], s['I'], s['pixels']
-    A = s['appearance_bytes']
-    B = s['buckets_used']
+    """Algorithmic DRAM bytes of one occurrence of each stage per view (per-unit figures x the frame's units)."""
+    N, V, I, P, A = s['N'], s['V'], s['I'], s['pixels'], s['appearance_bytes']
     if stage == 'preprocess':
-        return N * (44 + A) + N * 8 + V * (48 + 4)
+        return N * (44 + A) + N * 8 + V * 52
     if stage == 'blend_forward':
-        return I * (4 + 48) + P * (12 + 4 + 4) + B * 192 * 16
+        return I * 52 + P * 20
     if stage == 'blend_backward':
-        return I * (4 + 48) + B * 192 * (16 + 12 + 12 + 4 + 4) + V * 48
+        return I * 52 + P * 32 + V * 48
     if stage == 'preprocess_backward':
-        return N * (44 + A) * 2 + N * 4 + V * 96
+        return 2 * N * (44 + A) + N * 4 + V * 96
     if stage == 'adam':
         return 28 * s['params']
     return 0.0
 
 
-def run_b200(args, wl) -> dict:
-    import FasterGSVDACudaBackend as F
-    from FasterGSVDACudaBackend import _lib
+# ------------------------------------------------------------------------------------------------------------
+# B200 arm
 
+def run_b200(args, wl_name: str) -> dict | None:
+    from FasterGSVDACudaBackend import _lib, rasterization as R
+    import synthetic as S
+    wl = WORKLOADS[wl_name]
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
+    pg = None
     if world > 1:
         import datetime
-        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
-
-    F.initialize_appearance('sh', wl['degree'], 'none', 'none', 'relu', True)
-    prims, cam, grad_cpu = make_scene(wl, rank)
-    params = {k: torch.nn.Parameter(v.to(dev).contiguous()) for k, v in prims.items()}
-    settings = F.RasterizerSettings(cam.w2c.to(dev), cam.position.to(dev), cam.bg.to(dev), wl['degree'], wl['width'], wl['height'],
-                                    cam.focal_x, cam.focal_y, cam.center_x, cam.center_y, cam.near_plane, cam.far_plane, False, True, True)
-    lrs = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 'base_colors': 0.000705237, 'residual_params': 0.000125}
-    opt = F.FusedAdam([{'params': [params[k]], 'lr': lr} for k, lr in lrs.items()], lr=0.0, eps=1e-15)
-    grad_dev = grad_cpu.to(dev)
-    empty = torch.empty(0, device=dev)
-
-    def step(grad_image):
-        img = F.diff_rasterize(params['means'], params['scales'], params['rotations'], params['opacities'], empty, settings,
-                               base_colors=params['base_colors'], residual_params=params['residual_params'])
-        img.backward(grad_image)
-        opt.step()
-        for p in params.values():
-            p.grad = None
-        return img
+        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = torch.distributed.group.WORLD
+    configure(wl)
+    prims = scene(wl)
+    cams = S.ring_cameras(8, wl['width'], wl['height'])
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    if wl_name == 'c4':
+        from trainer import Trainer
+        assert wl['views'] % world == 0, 'the global batch of 8 views must split evenly over the GPUs'
+        per = wl['views'] // world
+        mine = list(range(rank * per, (rank + 1) * per))
+        trainer = Trainer({k: v.to(dev) for k, v in prims.items()}, C4_LRS, dev, group=pg)
+        del prims
+        settings = [settings_of(cams[v], wl['degree'], dev) for v in mine]
+        tg_host = [t.pin_memory() for t in [targets(wl)[v] for v in mine]]
+        tg_dev = [t.to(dev) for t in tg_host]
+        n_params = trainer.total
+
+        def step():
+            return trainer.step(settings, tg_dev)
+
+        def step_e2e():
+            for h, d in zip(tg_host, tg_dev):
+                d.copy_(h, non_blocking=True)
+            loss = trainer.step(settings, tg_dev)
+            return loss.to('cpu', non_blocking=True)
+
+        h2d = sum(t.numel() * 4 for t in tg_host)
+        d2h = 4
+        views_per_step = per
+        stat_settings = settings[0]
+        stat_prims = trainer._prims()
+    else:
+        import FasterGSVDACudaBackend as F
+        cam = cams[rank % len(cams)]
+        s0 = settings_of(cam, wl['degree'], dev)
+        params = {k: torch.nn.Parameter(v.to(dev).contiguous()) for k, v in prims.items()}
+        opt = F.FusedAdam([{'params': [params[k]], 'lr': lr} for k, lr in C1_LRS.items()], lr=0.0, eps=1e-15)
+        grad_host = (torch.randn(3, wl['height'], wl['width'], generator=torch.Generator().manual_seed(2)) * 0.01).pin_memory()
+        grad_dev = grad_host.to(dev)
+        img_host = torch.empty((3, wl['height'], wl['width']), pin_memory=True)
+        empty = torch.empty(0, device=dev)
+        n_params = sum(p.numel() for p in params.values())
+
+        def run(g):
+            img = F.diff_rasterize(params['means'], params['scales'], params['rotations'], params['opacities'], empty, s0,
+                                   base_colors=params['base_colors'], residual_params=params['residual_params'])
+            img.backward(g)
+            opt.step()
+            for p in params.values():
+                p.grad = None
+            return img
+
+        def step():
+            return run(grad_dev)
+
+        def step_e2e():
+            g = grad_host.to(dev, non_blocking=True)
+            img = run(g)
+            img_host.copy_(img.detach(), non_blocking=True)
+            return img_host
+
+        h2d = grad_host.numel() * 4
+        d2h = img_host.numel() * 4
+        views_per_step = 1
+        stat_settings = s0
+        stat_prims = R._c_primitives(params['means'].detach(), params['scales'].detach(), params['rotations'].detach(),
+                                     params['opacities'].detach(), None, params['base_colors'].detach(), params['residual_params'].detach(), None)
+
     for _ in range(args.warmup):
-        step(grad_dev)
+        step()
     barrier()
 
-    # device-resident timing
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev) as clk:
         barrier()
         e0.record(stream)
         for _ in range(args.steps):
-            step(grad_dev)
+            step()
         e1.record(stream)
         barrier()
     ms = e0.elapsed_time(e1) / args.steps
     clocks = clk.summary()
 
-    # end to end: upstream gradient H2D from pinned memory, rendered image D2H, every step
-    grad_pinned = grad_cpu.pin_memory()
-    img_host = torch.empty((3, wl['height'], wl['width']), pin_memory=True)
     barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(args.steps):
-        g = grad_pinned.to(dev, non_blocking=True)
-        img = step(g)
-        img_host.copy_(img.detach(), non_blocking=True)
+        step_e2e()
     e3.record(stream)
     barrier()
     ms_e2e = e2.elapsed_time(e3) / args.steps
 
-    # per-stage timing pass (CUDA events on the launching stream) for the roofline of the dominant kernel
+    # per-stage timing pass (CUDA events on the launching stream), averaged per step
     _lib.profile_enable(True)
-    n_prof = 3
-    stats = None
+    n_prof = 2
     for _ in range(n_prof):
-        img = F.diff_rasterize(params['means'], params['scales'], params['rotations'], params['opacities'], empty, settings,
-                               base_colors=params['base_colors'], residual_params=params['residual_params'])
-        img.backward(grad_dev)
-        opt.step()
-        for p in params.values():
-            p.grad = None
+        step()
     torch.cuda.synchronize()
     _lib.profile_enable(False)
     stage_ms = {k: v / n_prof for k, v in _lib.profile_collect().items()}
-    # frame statistics of this view (visible primitives, instances, buckets actually used)
-    from FasterGSVDACudaBackend import rasterization as R
-    cp = R._c_primitives(params['means'].detach(), params['scales'].detach(), params['rotations'].detach(), params['opacities'].detach(),
-                         None, params['base_colors'].detach(), params['residual_params'].detach(), None)
-    st = R.ForwardState(R._rasterizer, cp, settings, dev)
-    st.preprocess(cp)
-    im = torch.empty((3, wl['height'], wl['width']), device=dev)
-    st.render_train(im)
-    torch.cuda.synchronize()
+
+    # frame statistics of one view
+    st = R.ForwardState(R._rasterizer, stat_prims, stat_settings, dev)
+    st.preprocess(stat_prims)
     fr = st.frame
-    views = st.views()
-    T = fr.grid_w * fr.grid_h
-    off = views.bucket_offsets - st.tile_ws.data_ptr()
-    buckets_used = int(st.tile_ws[off + 4 * (T - 1): off + 4 * T].view(torch.int32).item())
-    n_params = sum(p.numel() for p in params.values())
-    s = dict(N=wl['n'], V=fr.n_visible, I=fr.n_instances, pixels=wl['width'] * wl['height'], appearance_bytes=12 + 4 * params['residual_params'][0].numel(),
-             buckets_used=buckets_used, params=n_params)
+    stats = dict(N=wl['n'], V=fr.n_visible, I=fr.n_instances, pixels=wl['width'] * wl['height'], params=n_params,
+                 appearance_bytes=12 + (4 * 45 if wl['model'] == 'sh' else 4 * wl['feature_dim']))
+    del st
+    per_view = {k: (v if k == 'adam' else v / views_per_step) for k, v in stage_ms.items()}
     dominant = max(stage_ms, key=stage_ms.get)
     peak, peak_kind = _peaks()
-    achieved = stage_bytes(dominant, s) / (stage_ms[dominant] * 1e-3) / 1e9 if stage_bytes(dominant, s) else 0.0
+    bytes_dom = stage_bytes(dominant, stats)
+    achieved = bytes_dom / (per_view[dominant] * 1e-3) / 1e9 if bytes_dom else 0.0
+    fracs = {k: round(stage_bytes(k, stats) / (per_view[k] * 1e-3) / 1e9 / peak, 4) for k in per_view if stage_bytes(k, stats) and per_view[k] > 0}
 
-    # max over ranks
     if world > 1:
         t = torch.tensor([ms, ms_e2e], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, ms_e2e = float(t[0]), float(t[1])
+    strong = wl_name == 'c4'
+    steps_per_s = 1000.0 / ms if strong else world * 1000.0 / ms
+    e2e_per_s = 1000.0 / ms_e2e if strong else world * 1000.0 / ms_e2e
     out = {
-        'metric': 'train steps/s (forward + backward + fused Adam), fused SH-3 appearance',
-        'value': world * 1000.0 / ms,
+        'metric': METRIC[wl_name],
+        'value': steps_per_s,
         'unit': 'steps/s',
         'n_gpus': world,
         'steps': args.steps,
         'warmup': args.warmup,
         'ms_per_step': ms,
         'higher_is_better': True,
-        'scaling': 'weak',
+        'scaling': 'strong' if strong else 'weak',
         'vs_baseline': None,
-        'dtype': 'f32',
-        'data': 'synthetic (seeded scene with the c1 shapes and distributions; no dataset available)',
-        'config': {'workload': 'c1: SH-3 differentiable rasterization fwd+bwd+Adam, 1,000,000 Gaussians, 1 view 1280x720 per GPU',
-                   'n_gaussians': wl['n'], 'width': wl['width'], 'height': wl['height'], 'n_visible': fr.n_visible,
-                   'n_instances': fr.n_instances, 'parallelism': f'replicas x{world}',
-                   'l2': 'inputs larger than L2 (236 MB of Gaussian parameters per step)'},
-        'e2e': {'value': world * 1000.0 / ms_e2e, 'unit': 'steps/s', 'h2d_bytes_per_step': int(grad_cpu.numel() * 4),
-                'd2h_bytes_per_step': int(img_host.numel() * 4)},
-        'gpu_launches': OWN_KERNELS_PER_STEP * args.steps,
+        'dtype': 'f32 (MLP fp16 operands, fp32 accumulation)' if wl['model'] == 'neural' else 'f32',
+        'data': 'synthetic (seeded scene with the configuration shapes and distributions; no dataset available)',
+        'config': {'workload': wl_name + (': Neural 6M Gaussians, 8 views 1920x1080 global batch, data-parallel' if strong else
+                                          ': SH-3 1M Gaussians, 1 view 1280x720 per GPU'),
+                   'n_gaussians': wl['n'], 'width': wl['width'], 'height': wl['height'], 'views_per_gpu': views_per_step,
+                   'n_visible_view0': fr.n_visible, 'n_instances_view0': fr.n_instances,
+                   'parallelism': (f'dp{world} (reduce-scatter / sharded Adam / all-gather)' if strong else f'replicas x{world}'),
+                   'l2': 'inputs larger than L2 (parameters alone exceed 126 MB)'},
+        'e2e': {'value': e2e_per_s, 'unit': 'steps/s', 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
+        'gpu_launches': (OWN_KERNELS_PER_VIEW * views_per_step + 1) * args.steps,
         'clocks': clocks,
-        'stage_ms': {k: round(v, 4) for k, v in stage_ms.items()},
+        'stage_ms_per_step': {k: round(v, 4) for k, v in stage_ms.items()},
         'roofline': {'kernel': dominant, 'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'peak_kind': peak_kind, 'unit': 'GB/s',
-                     'frac': achieved / peak, 'traffic': None, 'algorithmic_bytes': stage_bytes(dominant, s)},
+                     'frac': achieved / peak, 'traffic': None, 'algorithmic_bytes': bytes_dom, 'frac_by_stage': fracs},
     }
     if world > 1:
         torch.distributed.destroy_process_group()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out['cpu_baseline'] = cpu_step(wl, sample_tiles=args.cpu_sample)
+        out['cpu_baseline'] = cpu_step(wl_name, args.cpu_sample)
     return out if rank == 0 else None
 
 
-def cpu_step(wl: dict, sample_tiles: float = 0.05) -> dict:
-    """One training step of the CPU restatement (oracle/, one thread): preprocess, depth order and binning of all
-    Gaussians, forward and backward blend of a random `sample_tiles` fraction of the tiles (scaled to the full image),
-    backward preprocess of all Gaussians. Returns steps/s."""
+# ------------------------------------------------------------------------------------------------------------
+# CPU restatement (reference arm and cpu_baseline)
+
+def cpu_step(wl_name: str, tile_sample: float = 0.05) -> dict:
+    """Time of one step of the CPU restatement (oracle/, one thread), on a bounded sample:
+    c1: preprocess / depth order / binning / backward preprocess / Adam of all Gaussians, blends on a random
+        `tile_sample` fraction of the tiles (scaled to all tiles).
+    c4: one view of a scene with 1/64 of the Gaussians (same distributions) with blends on `tile_sample` of the tiles;
+        preprocess, binning and backward-preprocess times scaled x64, blend times x64 / tile_sample, times 8 views,
+        plus Adam over all 6M-Gaussian parameters (timed on 1/64 and scaled)."""
     import ctypes
+    import synthetic as S
     from oracle import oracle as O
-    prims, cam, grad = make_scene(wl, 0)
+    wl = dict(WORKLOADS[wl_name])
+    scale = 1
+    if wl_name == 'c4':
+        scale = 64
+        wl['n'] = wl['n'] // scale
+    prims = scene(wl)
+    cam = S.ring_cameras(8, wl['width'], wl['height'])[0]
     lib = O.load(False)
-    a = O.make_appearance('sh', wl['degree'], 0, 0, 1, True)
+    if wl['model'] == 'sh':
+        a = O.make_appearance('sh', wl['degree'], 0, 0, 1, True)
+    else:
+        n_in = wl['feature_dim'] * 2 * wl['n_freq'] + 16
+        neural = dict(feature_dim=wl['feature_dim'], base_input=0, n_freq=wl['n_freq'], sh_mask=15, n_input=n_in,
+                      n_input_pad=(n_in + 15) // 16 * 16, n_neurons=wl['neurons'], n_hidden=wl['hidden'], hidden_act=1)
+        a = O.make_appearance('neural', 0, 0, 1, 1, True, neural=neural)
     v = O.make_view(cam, wl['degree'])
     p = {k: O._f32(x) for k, x in prims.items()}
-    n = wl['n']
-    W, H = wl['width'], wl['height']
+    n, W, H = wl['n'], wl['width'], wl['height']
+    mlp = p.get('mlp_weights')
     t0 = time.perf_counter()
     n_touched = np.zeros(n, np.uint32)
     depth_key = np.zeros(n, np.uint32)
     rec = np.zeros((n, 14))
     lib.orc_preprocess(ctypes.byref(a), ctypes.byref(v), n, O._p(p['means']), O._p(p['scales']), O._p(p['rotations']), O._p(p['opacities']),
-                       None, O._p(p['base_colors']), O._p(p['residual_params']), None, O._p(n_touched), O._p(depth_key), O._p(rec))
+                       None, O._p(p['base_colors']), O._p(p['residual_params']), O._p(mlp), O._p(n_touched), O._p(depth_key), O._p(rec))
     sidx = np.zeros(n, np.uint32)
     V = lib.orc_depth_order(n, O._p(n_touched), O._p(depth_key), O._p(sidx))
     I = lib.orc_count_instances(V, O._p(sidx), O._p(n_touched))
@@ -286,34 +392,39 @@ def cpu_step(wl: dict, sample_tiles: float = 0.05) -> dict:
     ranges = np.zeros((T, 2), np.uint32)
     lib.orc_bin(V, O._p(sidx), O._p(rec), W, H, O._p(keys), O._p(ranks), O._p(ranges))
     t1 = time.perf_counter()
-    rng = np.random.default_rng(0)
-    keep = rng.random(T) < sample_tiles
-    frac = max(keep.mean(), 1.0 / T)
+    keep = np.random.default_rng(0).random(T) < tile_sample
+    frac = max(float(keep.mean()), 1.0 / T)
     ranges_s = ranges.copy()
     ranges_s[~keep] = 0
     image = np.zeros((3, H, W), np.float32)
     fT = np.zeros((H, W), np.float32)
     nc = np.zeros((H, W), np.uint32)
     lib.orc_blend(V, O._p(sidx), O._p(rec), O._p(ranks), O._p(ranges_s), ctypes.byref(v), O._p(image), O._p(fT), O._p(nc), 1, 0)
-    gimg = np.ascontiguousarray(grad.numpy())
+    gimg = np.ascontiguousarray((np.random.default_rng(2).standard_normal((3, H, W)) * 0.01).astype(np.float32))
     rg = np.zeros((max(V, 1), 12))
     lib.orc_blend_backward(V, O._p(sidx), O._p(rec), O._p(ranks), O._p(ranges_s), ctypes.byref(v), O._p(nc), O._p(gimg), O._p(rg))
     t2 = time.perf_counter()
     rank_of = np.full(n, 0xffffffff, np.uint32)
     rank_of[sidx[:V]] = np.arange(V, dtype=np.uint32)
     outs = [np.zeros((n, 3)), np.zeros((n, 3)), np.zeros((n, 4)), np.zeros(n), np.zeros((n, 3)), np.zeros(p['residual_params'].reshape(n, -1).shape)]
+    gm = np.zeros(mlp.shape[0]) if mlp is not None else None
     lib.orc_preprocess_backward(ctypes.byref(a), ctypes.byref(v), n, O._p(p['means']), O._p(p['scales']), O._p(p['rotations']),
-                                O._p(p['opacities']), None, O._p(p['base_colors']), O._p(p['residual_params']), None, O._p(rank_of), O._p(rec),
-                                O._p(rg), *[O._p(x) for x in outs[:4]], None, O._p(outs[4]), O._p(outs[5]), None, None, 0)
-    mom = [np.zeros_like(np.asarray(x, np.float32)) for x in p.values()]
-    for (k, x), m in zip(p.items(), mom):
-        xx = x.copy().reshape(-1)
-        O.adam(xx, np.ones_like(xx), m.reshape(-1), m.copy().reshape(-1), 1, 1e-3, (0.9, 0.999), 1e-15)
+                                O._p(p['opacities']), None, O._p(p['base_colors']), O._p(p['residual_params']), O._p(mlp), O._p(rank_of),
+                                O._p(rec), O._p(rg), *[O._p(x) for x in outs[:4]], None, O._p(outs[4]), O._p(outs[5]), O._p(gm), None, 0)
     t3 = time.perf_counter()
-    step_s = (t1 - t0) + (t2 - t1) / frac + (t3 - t2)
-    return {'value': 1.0 / step_s, 'unit': 'steps/s', 'cores': 1, 'kind': 'port',
-            'sample': f'c1 step: preprocess/binning/backward-preprocess/adam on all {n} Gaussians, blend fwd+bwd on {keep.sum()} of {T} tiles '
-                      f'scaled x{1 / frac:.1f}; single-threaded C restatement'}
+    for x in p.values():
+        xx = np.ascontiguousarray(x, np.float32).reshape(-1).copy()
+        O.adam(xx, np.ones_like(xx), np.zeros_like(xx), np.zeros_like(xx), 1, 1e-3, (0.9, 0.999), 1e-15)
+    t4 = time.perf_counter()
+    view_s = (t1 - t0) * scale + (t2 - t1) * scale / frac + (t3 - t2) * scale
+    step_s = view_s * wl['views'] + (t4 - t3) * scale
+    if wl_name == 'c4':
+        sample = (f'c4 step estimated from one view of a {n}-Gaussian scene (1/64 of 6M) at 1920x1080 with blends on {int(keep.sum())} of '
+                  f'{T} tiles, scaled x64 (x{64 / frac:.0f} for blends), x8 views, plus Adam; single-threaded C restatement')
+    else:
+        sample = (f'c1 step: preprocess/binning/backward-preprocess/Adam on all {n} Gaussians, blends on {int(keep.sum())} of {T} tiles scaled '
+                  f'x{1 / frac:.1f}; single-threaded C restatement')
+    return {'value': 1.0 / step_s, 'unit': 'steps/s', 'cores': 1, 'kind': 'port', 'sample': sample}
 
 
 def main() -> None:
@@ -322,26 +433,23 @@ def main() -> None:
     ap.add_argument('--steps', type=int, default=20)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--workload', default='c1', choices=sorted(WORKLOADS))
+    ap.add_argument('--workload', default='c4', choices=sorted(WORKLOADS))
     ap.add_argument('--cpu-sample', type=float, default=0.05)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     args = ap.parse_args()
-    wl = WORKLOADS[args.workload]
     if args.impl == 'reference':
-        rank = int(os.environ.get('RANK', '0'))
-        if rank != 0:
+        if int(os.environ.get('RANK', '0')) != 0:
             return
-        vals = [cpu_step(wl, args.cpu_sample) for _ in range(max(1, min(args.steps, 3)))]
-        v = float(np.median([x['value'] for x in vals]))
-        base = vals[0]
-        base['value'] = v
-        print(json.dumps({'impl': 'reference', 'metric': 'train steps/s (forward + backward + fused Adam), fused SH-3 appearance', 'value': v,
-                          'unit': 'steps/s', 'n_gpus': args.gpus, 'steps': len(vals), 'warmup': 0, 'ms_per_step': 1000.0 / v,
-                          'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-                          'config': {'workload': 'c1: SH-3 differentiable rasterization fwd+bwd+Adam, 1,000,000 Gaussians, 1 view 1280x720'},
-                          'cpu_baseline': base, 'e2e': {'value': v, 'unit': 'steps/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
+        runs = [cpu_step(args.workload, args.cpu_sample) for _ in range(max(1, min(args.steps, 2)))]
+        v = float(np.median([r['value'] for r in runs]))
+        base = dict(runs[0], value=v)
+        print(json.dumps({'impl': 'reference', 'metric': METRIC[args.workload], 'value': v, 'unit': 'steps/s', 'n_gpus': args.gpus,
+                          'steps': len(runs), 'warmup': 0, 'ms_per_step': 1000.0 / v, 'higher_is_better': True,
+                          'scaling': 'strong' if args.workload == 'c4' else 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+                          'config': {'workload': args.workload}, 'cpu_baseline': base,
+                          'e2e': {'value': v, 'unit': 'steps/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
         return
-    out = run_b200(args, wl)
+    out = run_b200(args, args.workload)
     if out is not None:
         print(json.dumps(out))
 

@@ -18,8 +18,8 @@ def _segment(param: torch.Tensor, grad: torch.Tensor, exp_avg: torch.Tensor, exp
     if not 1 <= len(lrs) <= 7:
         raise RuntimeError('between 1 and 7 learning rates are supported')
     for t, name in ((param, 'param'), (grad, 'grad'), (exp_avg, 'exp_avg'), (exp_avg_sq, 'exp_avg_sq')):
-        if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
-            raise RuntimeError(f'{name} must be a contiguous CUDA float32 tensor')
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.device != param.device or t.numel() != param.numel():
+            raise RuntimeError(f'{name} must be a contiguous float32 tensor on the device and of the size of param')
     seg = _lib.AdamSegment()
     seg.param, seg.grad, seg.exp_avg, seg.exp_avg_sq = param.data_ptr(), grad.data_ptr(), exp_avg.data_ptr(), exp_avg_sq.data_ptr()
     seg.n_elements = param.numel()
@@ -61,6 +61,8 @@ class FusedAdam(torch.optim.Adam):
                 state['exp_avg'] = torch.zeros_like(param)
                 state['exp_avg_sq'] = torch.zeros_like(param)
             state['step'] += 1
+            if not param.is_cuda:
+                raise RuntimeError('FusedAdam needs CUDA tensors')
             segments.append(_segment(param, param.grad, state['exp_avg'], state['exp_avg_sq'], state['step'], group['lr'],
                                      group['betas'], group['eps']))
         adam_step_segments(segments)

@@ -1,0 +1,169 @@
+"""Data-parallel training step over views for the fused-appearance rasterizer.
+
+The reference trains on one GPU (Renderer.py:62-65 warns and uses GPU 0). Here a global batch of views is split
+over the ranks of a torch.distributed group (one process per GPU); every rank holds a full replica of the Gaussians.
+Per step and rank:
+  1. render its views and backpropagate the loss, accumulating the gradients of all local views into one flat
+     fp32 gradient buffer (the backward kernels write the first view and add the following ones);
+  2. reduce-scatter (sum) the flat gradient buffer: rank r receives the summed gradients of the contiguous slice
+     [r*S, (r+1)*S) of the flat parameter vector;
+  3. fused Adam on that slice only (the optimizer moments exist only for the slice);
+  4. all-gather the updated slices back into every replica's flat parameter buffer.
+The flat buffer holds the parameter groups one after another (means, scales, rotations, opacities, base colors,
+residual parameters, MLP weights), each padded to a multiple of 64 floats, so a rank's slice can span several
+groups; the Adam segments carry each group's learning rate(s), betas and column offset.
+With one rank the collectives are skipped and the result equals the sequential accumulation over the same views.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as tf
+
+from FasterGSVDACudaBackend import rasterization as R, _lib
+from FasterGSVDACudaBackend.adam import _segment, adam_step_segments
+
+GROUP_ORDER = ('means', 'scales', 'rotations', 'opacities', 'base_colors', 'residual_params', 'mlp_weights')
+
+
+@dataclass
+class Group:
+    name: str
+    offset: int      # in floats, within the flat buffer
+    numel: int
+    shape: tuple
+    lr: float | list
+    betas: tuple = (0.9, 0.999)
+
+
+def gaussian_window(size: int, sigma: float, device) -> torch.Tensor:
+    x = torch.arange(size, dtype=torch.float32, device=device) - (size - 1) / 2.0
+    g = torch.exp(-x * x / (2.0 * sigma * sigma))
+    return g / g.sum()
+
+
+def blur(img: torch.Tensor, size: int, sigma: float) -> torch.Tensor:
+    """Separable Gaussian blur of a [C,H,W] image with zero padding."""
+    g = gaussian_window(size, sigma, img.device)
+    c = img.shape[0]
+    x = img[None]
+    x = tf.conv2d(x, g.view(1, 1, 1, size).expand(c, 1, 1, size), padding=(0, size // 2), groups=c)
+    x = tf.conv2d(x, g.view(1, 1, size, 1).expand(c, 1, size, 1), padding=(size // 2, 0), groups=c)
+    return x[0]
+
+
+def ssim(img: torch.Tensor, target: torch.Tensor, size: int = 11, sigma: float = 1.5) -> torch.Tensor:
+    """Mean SSIM with an 11x11 Gaussian window (sigma 1.5), C1 = 0.01^2, C2 = 0.03^2, zero padding."""
+    mu_x, mu_y = blur(img, size, sigma), blur(target, size, sigma)
+    sxx = blur(img * img, size, sigma) - mu_x * mu_x
+    syy = blur(target * target, size, sigma) - mu_y * mu_y
+    sxy = blur(img * target, size, sigma) - mu_x * mu_y
+    c1, c2 = 0.01 ** 2, 0.03 ** 2
+    m = ((2 * mu_x * mu_y + c1) * (2 * sxy + c2)) / ((mu_x * mu_x + mu_y * mu_y + c1) * (sxx + syy + c2))
+    return m.mean()
+
+
+def loss_and_grad(img: torch.Tensor, target: torch.Tensor, l1_weight: float = 0.8, dssim_weight: float = 0.2):
+    """0.8 * L1 + 0.2 * (1 - SSIM) (Loss.py:15-16 weights); returns (loss, dL/dimage)."""
+    x = img.detach().requires_grad_(True)
+    loss = l1_weight * (x - target).abs().mean() + dssim_weight * (1.0 - ssim(x, target))
+    loss.backward()
+    return loss.detach(), x.grad
+
+
+class Trainer:
+    """Holds the flat parameter / gradient buffers of one replica and runs data-parallel steps."""
+
+    def __init__(self, prims: dict[str, torch.Tensor], lrs: dict[str, float | list], device: torch.device, group=None,
+                 mlp_betas: tuple = (0.9, 0.99)) -> None:
+        self.device = device
+        self.pg = group
+        self.world = torch.distributed.get_world_size(group) if group is not None else 1
+        self.rank = torch.distributed.get_rank(group) if group is not None else 0
+        self.groups: list[Group] = []
+        off = 0
+        for name in GROUP_ORDER:
+            t = prims.get(name)
+            if t is None or t.numel() == 0:
+                continue
+            betas = mlp_betas if name == 'mlp_weights' else (0.9, 0.999)
+            self.groups.append(Group(name, off, t.numel(), tuple(t.shape), lrs[name], betas))
+            off += (t.numel() + 63) // 64 * 64
+        shard = (off + 64 * self.world - 1) // (64 * self.world) * 64
+        self.shard = shard
+        self.total = shard * self.world
+        self.params = torch.zeros(self.total, dtype=torch.float32, device=device)
+        self.grads = torch.zeros(self.total, dtype=torch.float32, device=device)
+        for g in self.groups:
+            self.params[g.offset:g.offset + g.numel].copy_(prims[g.name].reshape(-1))
+        self.exp_avg = torch.zeros(shard, dtype=torch.float32, device=device)
+        self.exp_avg_sq = torch.zeros(shard, dtype=torch.float32, device=device)
+        self.grad_shard = self.grads[self.rank * shard:(self.rank + 1) * shard] if self.world == 1 else torch.empty(shard, device=device)
+        self.step_count = 0
+        self.n = prims['means'].shape[0]
+
+    def view(self, buf: torch.Tensor, name: str) -> torch.Tensor | None:
+        for g in self.groups:
+            if g.name == name:
+                return buf[g.offset:g.offset + g.numel].view(g.shape)
+        return None
+
+    def _prims(self) -> tuple:
+        v = lambda k: self.view(self.params, k)
+        empty = torch.empty(0, device=self.device)
+        cp = R._c_primitives(v('means'), v('scales'), v('rotations'), v('opacities'), None, v('base_colors'), v('residual_params'),
+                             v('mlp_weights') if v('mlp_weights') is not None else None)
+        return cp
+
+    def _grads(self) -> _lib.Gradients:
+        v = lambda k: self.view(self.grads, k)
+        p = lambda t: t.data_ptr() if t is not None else None
+        return _lib.Gradients(p(v('means')), p(v('scales')), p(v('rotations')), p(v('opacities')), None, p(v('base_colors')),
+                              p(v('residual_params')), p(v('mlp_weights')))
+
+    def backward_views(self, settings_list: list, targets: list) -> torch.Tensor:
+        """Renders the local views and accumulates their gradients into the flat gradient buffer; returns the summed loss."""
+        cp = self._prims()
+        cg = self._grads()
+        total = torch.zeros((), device=self.device)
+        for k, (settings, target) in enumerate(zip(settings_list, targets)):
+            st = R.ForwardState(R._rasterizer, cp, settings, self.device)
+            st.preprocess(cp)
+            image = torch.empty((3, settings.height, settings.width), device=self.device)
+            st.render_train(image)
+            loss, grad_image = loss_and_grad(image, target)
+            total += loss
+            st.backward(cp, image, grad_image.contiguous(), cg, None, accumulate=k > 0)
+        return total
+
+    def adam_segments(self) -> list:
+        """Adam segments of this rank's slice [rank*S, (rank+1)*S), split at parameter-group boundaries."""
+        lo, hi = self.rank * self.shard, (self.rank + 1) * self.shard
+        segs = []
+        for g in self.groups:
+            a, b = max(lo, g.offset), min(hi, g.offset + g.numel)
+            if a >= b:
+                continue
+            s0 = a - lo
+            segs.append(_segment(self.params[a:b], self.grad_shard[s0:s0 + (b - a)], self.exp_avg[s0:s0 + (b - a)],
+                                 self.exp_avg_sq[s0:s0 + (b - a)], self.step_count, g.lr, g.betas, 1e-15, column_offset=a - g.offset))
+        return segs
+
+    def apply_gradients(self, adam_fn=None) -> None:
+        """Exchange step: reduce-scatter of the gradients, Adam on this rank's slice, all-gather of the parameters.
+        `adam_fn(segments)` replaces the fused GPU Adam (used by the CPU tests with the checker's Adam)."""
+        self.step_count += 1
+        if self.world > 1:
+            torch.distributed.reduce_scatter_tensor(self.grad_shard, self.grads, group=self.pg)
+        (adam_fn or adam_step_segments)(self.adam_segments())
+        if self.world > 1:
+            torch.distributed.all_gather_into_tensor(self.params, self.params[self.rank * self.shard:(self.rank + 1) * self.shard],
+                                                     group=self.pg)
+
+    def step(self, settings_list: list, targets: list) -> torch.Tensor:
+        loss = self.backward_views(settings_list, targets)
+        self.apply_gradients()
+        return loss
