@@ -325,8 +325,8 @@ def run_b200(args, wl_name: str) -> dict | None:
         'vs_baseline': None,
         'dtype': 'f32 (MLP fp16 operands, fp32 accumulation)' if wl['model'] == 'neural' else 'f32',
         'data': 'synthetic (seeded scene with the configuration shapes and distributions; no dataset available)',
-        'config': {'workload': wl_name + (': Neural 6M Gaussians, 8 views 1920x1080 global batch, data-parallel' if strong else
-                                          ': SH-3 1M Gaussians, 1 view 1280x720 per GPU'),
+        'config': {'workload': wl_name + (f": Neural {wl['n'] / 1e6:g}M Gaussians, {wl['views']} views 1920x1080 global batch, data-parallel"
+                                          if strong else f": SH-3 {wl['n'] / 1e6:g}M Gaussians, 1 view 1280x720 per GPU"),
                    'n_gaussians': wl['n'], 'width': wl['width'], 'height': wl['height'], 'views_per_gpu': views_per_step,
                    'n_visible_view0': fr.n_visible, 'n_instances_view0': fr.n_instances,
                    'parallelism': (f'dp{world} (reduce-scatter / sharded Adam / all-gather)' if strong else f'replicas x{world}'),
@@ -436,7 +436,13 @@ def main() -> None:
     ap.add_argument('--workload', default='c4', choices=sorted(WORKLOADS))
     ap.add_argument('--cpu-sample', type=float, default=0.05)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--gaussians', type=int, default=0, help='override the workload\'s Gaussian count (small profiling cases)')
+    ap.add_argument('--views', type=int, default=0, help='override the workload\'s global batch of views (c4)')
     args = ap.parse_args()
+    if args.gaussians:
+        WORKLOADS[args.workload]['n'] = args.gaussians
+    if args.views:
+        WORKLOADS[args.workload]['views'] = args.views
     if args.impl == 'reference':
         if int(os.environ.get('RANK', '0')) != 0:
             return

@@ -20,6 +20,9 @@ ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 # IEEE division / square root and denormals are nvcc's defaults without --use_fast_math.
 FLAGS = ['-O3', '-std=c++17', '-lineinfo', '-fmad=false', '-Xcompiler', '-fPIC', '--expt-relaxed-constexpr',
          '-Xptxas', '-warn-spills']
+# Sources whose outputs are checked against the CPU restatement within a tolerance rather than bit for bit (the fp16
+# tensor-core MLP of the neural appearance, whose backward also carries the geometry chain rule): contraction allowed.
+CONTRACTED = {'neural.cu'}
 
 
 def _digest(paths):
@@ -27,7 +30,7 @@ def _digest(paths):
     for p in sorted(paths):
         h.update(p.name.encode())
         h.update(p.read_bytes())
-    h.update(' '.join(FLAGS + ARCH).encode())
+    h.update(' '.join(FLAGS + ARCH + sorted(CONTRACTED)).encode())
     return h.hexdigest()
 
 
@@ -37,7 +40,8 @@ def _compile(src: Path, headers_digest: str) -> Path:
     key = headers_digest + hashlib.sha256(src.read_bytes()).hexdigest()
     if obj.exists() and stamp.exists() and stamp.read_text() == key:
         return obj
-    cmd = [NVCC, *ARCH, *FLAGS, '-c', str(src), '-o', str(obj)]
+    flags = [f if not (f == '-fmad=false' and src.name in CONTRACTED) else '-fmad=true' for f in FLAGS]
+    cmd = [NVCC, *ARCH, *flags, '-c', str(src), '-o', str(obj)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f'nvcc failed for {src.name}:\n{res.stdout}\n{res.stderr}')

@@ -85,6 +85,7 @@ fgs::PrimBuffers carve_prim(void* ws, uint64_t n, size_t* bytes) {
     B.keys_b = c.take<uint32_t>(n);
     B.idx_a = c.take<uint32_t>(n);
     B.idx_b = c.take<uint32_t>(n);
+    B.vis_idx = c.take<uint32_t>(n);
     B.sorted_rec = c.take<fgs::Record>(n);
     B.inst_off = c.take<uint32_t>(n);
     size_t tb = fgs::depth_sort_temp_bytes(static_cast<uint32_t>(n));
@@ -401,6 +402,10 @@ int fgs_forward_preprocess(fgs_rasterizer* r, const fgs_primitives* prims, const
     if (n_inst > 0x7fffff00ULL) return fail(FGS_ERR_UNSUPPORTED, "more than 2^31 instances");
     frame->n_visible = static_cast<int64_t>(n_visible);
     frame->n_instances = static_cast<int64_t>(n_inst);
+    if (n_visible > 0 && !precomputed && r->cfg.model == fgs::kNeural) {
+        ProfScope p_("appearance_mlp", s);
+        FGS_CUDA(fgs::launch_neural_color(P, r->cfg, v, B.vis_idx, static_cast<uint32_t>(n_visible), B.rec, s), "appearance mlp");
+    }
     if (n_visible > 0) {
         {
             ProfScope p_("depth_sort", s);
@@ -548,7 +553,8 @@ int fgs_backward(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_setti
     O.densification_rows = densification_rows;
     O.accumulate = accumulate ? 1 : 0;
     ProfScope p_("preprocess_backward", s);
-    FGS_CUDA(fgs::launch_preprocess_bwd(P, r->cfg, v, B.rank_of, B.sorted_rec, gb.rec, O, precomputed, s), "preprocess backward");
+    FGS_CUDA(fgs::launch_preprocess_bwd(P, r->cfg, v, B.rank_of, B.sorted_rec, gb.rec, O, precomputed, B.vis_idx, static_cast<uint32_t>(nv), s),
+             "preprocess backward");
     return FGS_OK;
 }
 
@@ -715,6 +721,8 @@ int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const 
                                            std::to_string(prim_bytes + tile_bytes + inst_bytes) + " bytes of scratch, more than the static maximum of " +
                                            std::to_string(static_cast<size_t>(FGS_NOALLOC_SCRATCH_BYTES)));
     I = carve_inst(base + prim_bytes + tile_bytes, ni, g, nullptr);
+    if (nv > 0 && !precomputed && r->cfg.model == fgs::kNeural)
+        FGS_CUDA(fgs::launch_neural_color(P, r->cfg, v, B.vis_idx, static_cast<uint32_t>(nv), B.rec, s), "appearance mlp");
     if (nv > 0) {
         FGS_CUDA(fgs::depth_sort(B, static_cast<uint32_t>(nv), s), "depth sort");
         FGS_CUDA(fgs::launch_reorder(B, static_cast<uint32_t>(nv), s), "reorder");

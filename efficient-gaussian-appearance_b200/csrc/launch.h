@@ -14,12 +14,15 @@ cudaError_t launch_compaction(const PrimBuffers& B, uint32_t n, cudaStream_t s);
 cudaError_t launch_reorder(const PrimBuffers& B, uint32_t n_visible, cudaStream_t s);
 cudaError_t launch_preprocess_bwd(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* rank_of,
                                   const Record* sorted_rec, const GradRecord* grads, const GradOut& O, bool precomputed,
-                                  cudaStream_t s);
+                                  const uint32_t* vis_idx, uint32_t n_visible, cudaStream_t s);
 
 // neural.cu
-cudaError_t launch_preprocess_fwd_neural(const Params& P, const AppearanceConfig& A, const View& v, const PrimBuffers& B, cudaStream_t s);
+// colour pass of the visible primitives (after the compaction): overwrites the colours the geometry pass wrote
+cudaError_t launch_neural_color(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis_idx, uint32_t n_visible,
+                                Record* rec, cudaStream_t s);
 cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* rank_of,
-                                         const Record* sorted_rec, const GradRecord* grads, const GradOut& O, cudaStream_t s);
+                                         const Record* sorted_rec, const GradRecord* grads, const GradOut& O, const uint32_t* vis_idx,
+                                         uint32_t n_visible, cudaStream_t s);
 size_t neural_grad_scratch_floats(const AppearanceConfig& A);
 size_t neural_smem_bytes(const AppearanceConfig& A);  // largest dynamic shared memory of the neural kernels
 

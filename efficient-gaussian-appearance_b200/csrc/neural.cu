@@ -8,13 +8,21 @@
 // the input layer [n_neurons, n_input_pad], the hidden layers [n_neurons, n_neurons] and the output layer
 // [16, n_neurons], each row-major.
 //
-// Design: persistent CTAs stage the weights once as fp16 in shared memory; each warp evaluates the MLP for its
-// own 32 primitives with mma.sync m16n8k16 (fp16 operands, fp32 accumulation), layer outputs rounded to fp16.
-// The backward recomputes the forward activations (no forward context is stored), scales the output gradient
-// by 128 before rounding it to fp16 (as the reference does), and accumulates the weight gradient in fp32 in
-// shared memory across all primitives a CTA processes, flushing it with one atomic add per weight and CTA.
+// Design (rows = visible primitives, taken from the order-preserving compaction list, so no MLP work is spent on
+// culled primitives):
+//  - forward: after the geometry pass, a colour pass evaluates the MLP for 32 rows per warp with mma.sync m16n8k16
+//    (fp16 operands, fp32 accumulation, layer outputs rounded to fp16) and writes the colour into the record;
+//    features are loaded and encoded one lane per feature (coalesced 128-byte rows), SH inputs one lane per row;
+//  - backward: 8 warps x 16 rows per CTA batch of 128 rows; the forward activations are recomputed, the output
+//    gradient is scaled by 128 before rounding to fp16 (as the reference does); the hidden-layer gradients
+//    overwrite their activations in place and the input gradient (fp32) reuses the dead buffers, so two CTAs fit
+//    on an SM; the weight gradient is accumulated in registers over every batch a CTA processes, each warp owning
+//    fixed 16x16 tiles, and flushed with one atomic add per weight and CTA at the end.
+//  Configurations whose weight-gradient tiles exceed the register budget (or degree-0 views) use a general
+//  backward over all primitives that keeps the weight gradient in shared memory.
 #include <cuda_fp16.h>
-#include "preprocess_store.cuh"
+
+#include <algorithm>
 #include "preprocess_bwd.cuh"
 #include "appearance.cuh"
 #include "launch.h"
@@ -23,10 +31,12 @@ namespace fgs {
 
 namespace {
 
-constexpr int kFwdRows = kChunk;  // 256 primitives per forward CTA iteration (the compaction granule)
-constexpr int kBwdRows = 128;     // 128 primitives per backward CTA iteration
+constexpr int kBwdRows = 128;  // rows per backward CTA batch
 constexpr float kLossScale = kMlpLossScale;
 constexpr float kShC0 = 0.28209479177387814f;
+
+// value * 2^f: the octave scaling of the frequency encoding (exact, so equal to scalbnf for every input)
+__device__ inline float octave(float value, int f) { return f == 0 ? value : value * static_cast<float>(1 << f); }
 
 __device__ inline uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -93,27 +103,27 @@ __device__ inline void load_weights(const MlpShape& s, const float* __restrict__
     }
 }
 
-// one layer for the warp's 32 rows: out[row][0..NOUT) = act(in[row][0..K) . W^T), rounded to fp16
-template <int NOUT>
+// one layer for the warp's 16 * MT rows: out[row][0..NOUT) = act(in[row][0..K) . W^T), rounded to fp16
+template <int NOUT, int MT>
 __device__ inline void layer_forward(const __half* in, int ld_in, int K, const __half* W, int ld_w, __half* out, int ld_out, int row0, bool relu) {
     const int lane = threadIdx.x & 31;
-    float acc[2][NOUT / 8][4];
+    float acc[MT][NOUT / 8][4];
 #pragma unroll
-    for (int m = 0; m < 2; m++)
+    for (int m = 0; m < MT; m++)
 #pragma unroll
         for (int n = 0; n < NOUT / 8; n++)
 #pragma unroll
             for (int q = 0; q < 4; q++) acc[m][n][q] = 0.0f;
     for (int k0 = 0; k0 < K; k0 += 16) {
-        uint32_t a[2][4];
+        uint32_t a[MT][4];
 #pragma unroll
-        for (int m = 0; m < 2; m++) ldsm_x4(a[m], in + (row0 + m * 16 + (lane & 15)) * ld_in + k0 + (lane >> 4) * 8);
+        for (int m = 0; m < MT; m++) ldsm_x4(a[m], in + (row0 + m * 16 + (lane & 15)) * ld_in + k0 + (lane >> 4) * 8);
 #pragma unroll
         for (int n = 0; n < NOUT / 8; n += 2) {
             uint32_t b[4];
             ldsm_x4(b, W + (n * 8 + (lane & 7) + (lane >> 4) * 8) * ld_w + k0 + ((lane >> 3) & 1) * 8);
 #pragma unroll
-            for (int m = 0; m < 2; m++) {
+            for (int m = 0; m < MT; m++) {
                 mma16816(acc[m][n], a[m], b[0], b[1]);
                 mma16816(acc[m][n + 1], a[m], b[2], b[3]);
             }
@@ -121,7 +131,7 @@ __device__ inline void layer_forward(const __half* in, int ld_in, int K, const _
     }
     const int g = lane >> 2, tq = lane & 3;
 #pragma unroll
-    for (int m = 0; m < 2; m++)
+    for (int m = 0; m < MT; m++)
 #pragma unroll
         for (int n = 0; n < NOUT / 8; n++) {
             float v0 = acc[m][n][0], v1 = acc[m][n][1], v2 = acc[m][n][2], v3 = acc[m][n][3];
@@ -133,35 +143,36 @@ __device__ inline void layer_forward(const __half* in, int ld_in, int K, const _
 }
 
 // SH band values of the MLP's direction input (bands 0..3 selected by mask; band l >= 1 is zero unless it is among
-// the first `deg` selected bands); returns the number written
-__device__ inline int sh_band_values(int mask, int deg, f3 d, float* out) {
+// the first `deg` selected bands), passed to out(k, value) in input order; returns the number written
+template <typename Out>
+__device__ inline int sh_band_values(int mask, int deg, f3 d, Out&& out) {
     const float x = d.x, y = d.y, z = d.z;
     const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z;
     int o = 0, rank = 0;
-    if (mask & 1) out[o++] = kShC0;
+    if (mask & 1) out(o++, kShC0);
     if (mask & 2) {
         const float m = rank++ < deg ? 1.0f : 0.0f;
-        out[o++] = m * (-kShC1 * y);
-        out[o++] = m * (kShC1 * z);
-        out[o++] = m * (-kShC1 * x);
+        out(o++, m * (-kShC1 * y));
+        out(o++, m * (kShC1 * z));
+        out(o++, m * (-kShC1 * x));
     }
     if (mask & 4) {
         const float m = rank++ < deg ? 1.0f : 0.0f;
-        out[o++] = m * (kShC2a * xy);
-        out[o++] = m * (-kShC2a * yz);
-        out[o++] = m * (kShC2b * zz - kShC2c);
-        out[o++] = m * (-kShC2a * xz);
-        out[o++] = m * (kShC2d * xx - kShC2d * yy);
+        out(o++, m * (kShC2a * xy));
+        out(o++, m * (-kShC2a * yz));
+        out(o++, m * (kShC2b * zz - kShC2c));
+        out(o++, m * (-kShC2a * xz));
+        out(o++, m * (kShC2d * xx - kShC2d * yy));
     }
     if (mask & 8) {
         const float m = rank++ < deg ? 1.0f : 0.0f;
-        out[o++] = m * (0.59004358992664352f * y * (-3.0f * xx + yy));
-        out[o++] = m * (2.8906114426405538f * xy * z);
-        out[o++] = m * (0.45704579946446572f * y * (1.0f - 5.0f * zz));
-        out[o++] = m * (0.3731763325901154f * z * (5.0f * zz - 3.0f));
-        out[o++] = m * (0.45704579946446572f * x * (1.0f - 5.0f * zz));
-        out[o++] = m * (1.4453057213202769f * z * (xx - yy));
-        out[o++] = m * (0.59004358992664352f * x * (-xx + 3.0f * yy));
+        out(o++, m * (0.59004358992664352f * y * (-3.0f * xx + yy)));
+        out(o++, m * (2.8906114426405538f * xy * z));
+        out(o++, m * (0.45704579946446572f * y * (1.0f - 5.0f * zz)));
+        out(o++, m * (0.3731763325901154f * z * (5.0f * zz - 3.0f)));
+        out(o++, m * (0.45704579946446572f * x * (1.0f - 5.0f * zz)));
+        out(o++, m * (1.4453057213202769f * z * (xx - yy)));
+        out(o++, m * (0.59004358992664352f * x * (-xx + 3.0f * yy)));
     }
     return o;
 }
@@ -210,6 +221,10 @@ __device__ inline f3 sh_band_grad(int mask, int deg, f3 d, const float* g) {
 
 // writes this thread's MLP input row (fp16): encoded features, SH band values, padding ones
 __device__ inline void assemble_inputs(const Params& P, const AppearanceConfig& A, uint32_t i, bool valid, f3 d, int deg, __half* row) {
+    if (!valid) {  // all-zero row: finite activations, no contribution to the weight gradient
+        for (int o = 0; o < A.n_input_pad; o++) row[o] = __float2half_rn(0.0f);
+        return;
+    }
     const int F = A.feature_dim, nraw = F + (A.base_input ? 3 : 0), nf = A.n_freq;
     int o = 0;
     for (int j = 0; j < nraw; j++) {
@@ -220,15 +235,14 @@ __device__ inline void assemble_inputs(const Params& P, const AppearanceConfig& 
         } else {
             for (int f = 0; f < nf; f++) {
                 float s, c;
-                sincosf(scalbnf(val, f), &s, &c);
+                sincosf(octave(val, f), &s, &c);
                 row[o++] = __float2half_rn(s);
                 row[o++] = __float2half_rn(c);
             }
         }
     }
-    float sh[16];
-    const int nsh = sh_band_values(A.sh_mask, deg, d, sh);
-    for (int k = 0; k < nsh; k++) row[o++] = __float2half_rn(sh[k]);
+    const int o0 = o;
+    o += sh_band_values(A.sh_mask, deg, d, [&](int k, float val) { row[o0 + k] = __float2half_rn(val); });
     for (; o < A.n_input_pad; o++) row[o] = __float2half_rn(1.0f);
 }
 
@@ -240,9 +254,9 @@ __device__ inline f3 view_dir(const View& v, f3 m, float* rn_out) {
     return rn * dv;
 }
 
-// runs the MLP for the warp's rows [row0, row0 + 32); buffers: bufA holds the input on entry; returns the buffer
-// (and its stride) that holds the 16 outputs
-template <int NN>
+// runs the MLP for the warp's rows [row0, row0 + 16 * MT); buffers: bufA holds the input on entry; returns the
+// buffer (and its stride) that holds the 16 outputs
+template <int NN, int MT>
 __device__ inline const __half* mlp_forward_warp(const MlpShape& s, const __half* sw, const int* soff, __half* bufA, int ldA, __half* bufB,
                                                  int ldB, int row0, int hidden_act, int* ld_out) {
     __half* in = bufA;
@@ -251,8 +265,8 @@ __device__ inline const __half* mlp_forward_warp(const MlpShape& s, const __half
     int ld_o = ldB;
     for (int l = 0; l < s.layers; l++) {
         const bool last = l == s.layers - 1;
-        if (last) layer_forward<16>(in, ld_in, s.w_cols[l], sw + soff[l], s.w_cols[l] + 8, out, ld_o, row0, false);
-        else layer_forward<NN>(in, ld_in, s.w_cols[l], sw + soff[l], s.w_cols[l] + 8, out, ld_o, row0, hidden_act == 1);
+        if (last) layer_forward<16, MT>(in, ld_in, s.w_cols[l], sw + soff[l], s.w_cols[l] + 8, out, ld_o, row0, false);
+        else layer_forward<NN, MT>(in, ld_in, s.w_cols[l], sw + soff[l], s.w_cols[l] + 8, out, ld_o, row0, hidden_act == 1);
         __syncwarp();
         __half* t = in; in = out; out = t;
         const int tl = ld_in; ld_in = ld_o; ld_o = tl;
@@ -262,88 +276,206 @@ __device__ inline const __half* mlp_forward_warp(const MlpShape& s, const __half
 }
 
 // ---------------------------------------------------------------------------------------------------
-// forward preprocess with the fused MLP
+// row helpers of the visible-row kernels. Row k of a warp's block belongs to lane k (lanes >= rows mirror it).
+
+// raw encoder input e of the rows k = 0..NR-1 (row k: primitive shfl(i, k), valid when bit k of vmask is set), one
+// lane per input, all loads issued before any is used
+template <int NR>
+__device__ inline void load_raw_rows(const Params& P, const AppearanceConfig& A, uint32_t i, uint32_t vmask, int e, float (&vals)[NR]) {
+    const int F = A.feature_dim, nraw = F + (A.base_input ? 3 : 0);
+#pragma unroll
+    for (int k = 0; k < NR; k++) {
+        const uint32_t ik = __shfl_sync(0xffffffffu, i, k);
+        vals[k] = 0.0f;
+        if (((vmask >> k) & 1u) && e < nraw) vals[k] = e < F ? P.residual[static_cast<size_t>(ik) * F + e] : P.base[3ull * ik + (e - F)];
+    }
+}
+
+// moves vals[k + 1] to vals[k] (the rolled row loops read row k from vals[0])
+template <int NR>
+__device__ inline void rotate(float (&vals)[NR]) {
+#pragma unroll
+    for (int k = 0; k + 1 < NR; k++) vals[k] = vals[k + 1];
+}
+
+// encoded features of the warp's NR rows into buf[k * ld + column], one lane per raw input so every row is one
+// coalesced load; invalid rows are skipped
+template <int NR>
+__device__ inline void encode_rows(const Params& P, const AppearanceConfig& A, uint32_t i, uint32_t vmask, __half* buf, int ld) {
+    const int nraw = A.feature_dim + (A.base_input ? 3 : 0), nf = A.n_freq, per = nf > 0 ? 2 * nf : 1;
+    const int lane = threadIdx.x & 31;
+    for (int e0 = 0; e0 < nraw; e0 += 32) {
+        const int e = e0 + lane;
+        float vals[NR];
+        load_raw_rows<NR>(P, A, i, vmask, e, vals);
+#pragma unroll 1
+        for (int k = 0; k < NR; k++) {
+            const float val = vals[0];
+            rotate<NR>(vals);
+            if (!((vmask >> k) & 1u) || e >= nraw) continue;
+            __half* row = buf + k * ld;
+            if (nf == 0) {
+                row[e] = __float2half_rn(val);
+            } else {
+                for (int f = 0; f < nf; f++) {
+                    float sn, cs;
+                    sincosf(octave(val, f), &sn, &cs);
+                    *reinterpret_cast<__half2*>(row + e * per + 2 * f) = __floats2half2_rn(sn, cs);
+                }
+            }
+        }
+    }
+}
+
+// SH band inputs and padding ones of one row (the calling lane's), or an all-zero row for an invalid row
+__device__ inline void direction_inputs(const AppearanceConfig& A, int deg, bool valid, f3 d, __half* row, int kin) {
+    const int nraw = A.feature_dim + (A.base_input ? 3 : 0), per = A.n_freq > 0 ? 2 * A.n_freq : 1;
+    if (!valid) {
+        for (int o = 0; o < kin; o++) row[o] = __float2half_rn(0.0f);
+        return;
+    }
+    const int o0 = nraw * per;
+    int o = o0 + sh_band_values(A.sh_mask, deg, d, [&](int k, float val) { row[o0 + k] = __float2half_rn(val); });
+    for (; o < kin; o++) row[o] = __float2half_rn(1.0f);
+}
+
+// feature (and base-input) gradients of the warp's NR rows from the loss-scaled fp32 input gradient rows gx;
+// feature gradients go to O.residual, base-input gradients to base_in[k * 3 + c]
+template <int NR>
+__device__ inline void feature_grads(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t i, uint32_t vmask, const float* gx,
+                                     int ldg, float* base_in, int acc) {
+    const int F = A.feature_dim, nraw = F + (A.base_input ? 3 : 0), nf = A.n_freq, per = nf > 0 ? 2 * nf : 1;
+    const int lane = threadIdx.x & 31;
+    const float inv = 1.0f / kLossScale;
+    for (int e0 = 0; e0 < nraw; e0 += 32) {
+        const int e = e0 + lane;
+        float vals[NR];
+        if (nf > 0) load_raw_rows<NR>(P, A, i, vmask, e, vals);
+#pragma unroll 1
+        for (int k = 0; k < NR; k++) {
+            const float val = vals[0];
+            if (nf > 0) rotate<NR>(vals);
+            const uint32_t ik = __shfl_sync(0xffffffffu, i, k);
+            if (!((vmask >> k) & 1u) || e >= nraw) continue;
+            const float* g = gx + k * ldg;
+            float gv = 0.0f;
+            if (nf == 0) gv = g[e];
+            else
+                for (int f = 0; f < nf; f++) {
+                    float sn, cs;
+                    sincosf(octave(val, f), &sn, &cs);
+                    gv += static_cast<float>(1 << f) * (cs * g[e * per + 2 * f] - sn * g[e * per + 2 * f + 1]);
+                }
+            gv *= inv;
+            if (e < F) {
+                float* dst = O.residual + static_cast<size_t>(ik) * F + e;
+                if (acc) *dst += gv; else *dst = gv;
+            } else {
+                base_in[k * 3 + (e - F)] = gv;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------
+// forward colour pass over the visible rows: the geometry pass already wrote the records (with the colour of a
+// zero residual); this overwrites the colour of every visible primitive with the MLP's
+__host__ __device__ inline int color_buf_halves(const MlpShape& s, int nn) {
+    const int ldA = (s.kin > nn ? s.kin : nn) + 8, ldB = nn + 8;
+    return 32 * (ldA + ldB);
+}
+
 template <int NN>
-__global__ void __launch_bounds__(kFwdRows) neural_fwd_kernel(Params P, AppearanceConfig A, View v, PrimBuffers B, uint32_t n_chunks) {
+__global__ void __launch_bounds__(256) neural_color_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
+                                                           Record* __restrict__ rec) {
     extern __shared__ __align__(16) unsigned char smem[];
-    const MlpShape s = mlp_shape(A);
-    int soff[10];
-    const int wh = smem_weights_halves(s, soff);
+    __shared__ MlpShape s_shape;
+    __shared__ int s_soff[10];
+    __shared__ int s_wh;
+    if (threadIdx.x == 0) {
+        s_shape = mlp_shape(A);
+        s_wh = smem_weights_halves(s_shape, s_soff);
+    }
+    __syncthreads();
+    const MlpShape& s = s_shape;  // uniform tables read from shared memory (no local-memory copies)
+    const int* soff = s_soff;
+    const int wh = s_wh;
     __half* sw = reinterpret_cast<__half*>(smem);
     const int ldA = (s.kin > NN ? s.kin : NN) + 8, ldB = NN + 8;
-    __half* bufA = sw + ((wh + 7) & ~7);
-    __half* bufB = bufA + kFwdRows * ldA;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    __half* bufA = sw + ((wh + 7) & ~7) + warp * color_buf_halves(s, NN);
+    __half* bufB = bufA + 32 * ldA;
     load_weights(s, P.mlp, sw, soff);
     __syncthreads();
     const int deg = min(v.degree, A.max_degree);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (uint32_t chunk = blockIdx.x; chunk < n_chunks; chunk += gridDim.x) {
-        const uint32_t i = chunk * kFwdRows + threadIdx.x;
-        const bool in_range = i < P.n;
-        const Geometry G = project_primitive(P.means, P.scales, P.rotations, P.opacities, in_range ? i : 0, in_range, v);
-        const bool visible = in_range && G.n_touched > 0;
-        f3 res = mk3(0.0f, 0.0f, 0.0f);
-        if (deg > 0 && __any_sync(0xffffffffu, visible)) {
-            const f3 d = view_dir(v, visible ? ld3(P.means, i) : mk3(0.0f, 0.0f, 1.0f), nullptr);
-            assemble_inputs(P, A, i, visible, d, deg, bufA + threadIdx.x * ldA);
-            __syncwarp();
-            int ldo;
-            const __half* y = mlp_forward_warp<NN>(s, sw, soff, bufA, ldA, bufB, ldB, warp * 32, A.hidden_act, &ldo);
-            const __half* yr = y + threadIdx.x * ldo;
-            res = residual_act3(A.res_act, mk3(__half2float(yr[0]), __half2float(yr[1]), __half2float(yr[2])));
-            __syncwarp();
-        }
-        (void)lane;
-        f3 color = mk3(0.0f, 0.0f, 0.0f);
-        if (visible) {
+    const uint32_t n_tiles = (n_rows + 31) / 32, stride = gridDim.x * nwarps;
+    for (uint32_t t = blockIdx.x * nwarps + warp; t < n_tiles; t += stride) {
+        const uint32_t gi = t * 32 + lane;
+        const bool valid = gi < n_rows;
+        const uint32_t i = valid ? vis[gi] : 0u;
+        const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
+        const f3 d = valid ? view_dir(v, ld3(P.means, i), nullptr) : mk3(0.0f, 0.0f, 1.0f);
+        direction_inputs(A, deg, valid, d, bufA + lane * ldA, s.kin);
+        encode_rows<32>(P, A, i, vmask, bufA, ldA);
+        __syncwarp();
+        int ldo;
+        const __half* y = mlp_forward_warp<NN, 2>(s, sw, soff, bufA, ldA, bufB, ldB, 0, A.hidden_act, &ldo);
+        if (valid) {
+            const __half* yr = y + lane * ldo;
+            const f3 res = residual_act3(A.res_act, mk3(__half2float(yr[0]), __half2float(yr[1]), __half2float(yr[2])));
             const f3 base = base_act3(A.base_act, ld3(P.base, i));
-            color = color_act3(A.color_act, base + res);
+            f3 color = color_act3(A.color_act, base + res);
             if (!v.render_base) {
                 const f3 bc = color_act3(A.color_act, base);
                 color = mk3(fabsf(color.x - bc.x), fabsf(color.y - bc.y), fabsf(color.z - bc.z));
             }
+            float* q2 = reinterpret_cast<float*>(rec + i) + 8;
+            q2[0] = color.x;
+            q2[1] = color.y;
+            q2[2] = color.z;
         }
-        store_primitive(B, i, in_range, G, color, chunk);
+        __syncwarp();
     }
 }
 
 // ---------------------------------------------------------------------------------------------------
 // backward
 
-// dIn[row][0..K) = dOut[row][0..NOUT) . W (W: [NOUT][K]) for the warp's rows, 32 output columns at a time;
-// masked by (act_in > 0) when relu, rounded to fp16 into `out` or stored as fp32 into `out32`
-template <int NOUT>
+// dIn[row][0..K) = dOut[row][0..NOUT) . W (W: [NOUT][K]) for the warp's 16 * MT rows, 32 output columns at a
+// time; masked by (act_in > 0) when relu, rounded to fp16 into `out` or stored as fp32 into `out32`. `out` may
+// alias `act_in` (each element is read and written by the same lane).
+template <int NOUT, int MT>
 __device__ inline void layer_backward_data(const __half* dout, int ld_dout, const __half* W, int ld_w, int K, const __half* act_in, int ld_act,
                                            bool relu, __half* out, int ld_out, float* out32, int ld_out32, int row0) {
     const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
     for (int c0 = 0; c0 < K; c0 += 32) {
         const int ncols = min(32, K - c0);
-        float acc[2][4][4];
+        float acc[MT][4][4];
 #pragma unroll
-        for (int m = 0; m < 2; m++)
+        for (int m = 0; m < MT; m++)
 #pragma unroll
             for (int n = 0; n < 4; n++)
 #pragma unroll
                 for (int q = 0; q < 4; q++) acc[m][n][q] = 0.0f;
 #pragma unroll
         for (int kk = 0; kk < NOUT; kk += 16) {
-            uint32_t a[2][4];
+            uint32_t a[MT][4];
 #pragma unroll
-            for (int m = 0; m < 2; m++) ldsm_x4(a[m], dout + (row0 + m * 16 + (lane & 15)) * ld_dout + kk + (lane >> 4) * 8);
+            for (int m = 0; m < MT; m++) ldsm_x4(a[m], dout + (row0 + m * 16 + (lane & 15)) * ld_dout + kk + (lane >> 4) * 8);
 #pragma unroll
             for (int n = 0; n < 4; n += 2) {
                 if (n * 8 >= ncols) break;
                 uint32_t b[4];
                 ldsm_x4_t(b, W + (kk + ((lane >> 3) & 1) * 8 + (lane & 7)) * ld_w + c0 + n * 8 + (lane >> 4) * 8);
 #pragma unroll
-                for (int m = 0; m < 2; m++) {
+                for (int m = 0; m < MT; m++) {
                     mma16816(acc[m][n], a[m], b[0], b[1]);
                     mma16816(acc[m][n + 1], a[m], b[2], b[3]);
                 }
             }
         }
 #pragma unroll
-        for (int m = 0; m < 2; m++)
+        for (int m = 0; m < MT; m++)
 #pragma unroll
             for (int n = 0; n < 4; n++) {
                 if (n * 8 >= ncols) break;
@@ -487,8 +619,8 @@ __global__ void __launch_bounds__(kBwdRows) neural_bwd_kernel(Params P, Appearan
             for (int l = 0; l < s.layers; l++) {
                 const __half* in = l == 0 ? X : H + (l - 1) * kBwdRows * L.ldH;
                 const int ldi = l == 0 ? L.ldX : L.ldH;
-                if (l == s.layers - 1) layer_forward<16>(in, ldi, s.w_cols[l], sw + L.soff[l], s.w_cols[l] + 8, Y, L.ldY, row0, false);
-                else layer_forward<NN>(in, ldi, s.w_cols[l], sw + L.soff[l], s.w_cols[l] + 8, H + l * kBwdRows * L.ldH, L.ldH, row0, A.hidden_act == 1);
+                if (l == s.layers - 1) layer_forward<16, 2>(in, ldi, s.w_cols[l], sw + L.soff[l], s.w_cols[l] + 8, Y, L.ldY, row0, false);
+                else layer_forward<NN, 2>(in, ldi, s.w_cols[l], sw + L.soff[l], s.w_cols[l] + 8, H + l * kBwdRows * L.ldH, L.ldH, row0, A.hidden_act == 1);
                 __syncwarp();
             }
             // scaled output gradient
@@ -517,14 +649,14 @@ __global__ void __launch_bounds__(kBwdRows) neural_bwd_kernel(Params P, Appearan
                 layer_backward_weights(dcur, ld_cur, s.w_rows[l], in, ldi, s.w_cols[l], dWl);
                 if (l > 0) {
                     __half* dnext = dbuf[pp];
-                    if (s.w_rows[l] == 16) layer_backward_data<16>(dcur, ld_cur, sw + L.soff[l], s.w_cols[l] + 8, s.w_cols[l], in, ldi, A.hidden_act == 1, dnext, L.ldD, nullptr, 0, row0);
-                    else layer_backward_data<NN>(dcur, ld_cur, sw + L.soff[l], s.w_cols[l] + 8, s.w_cols[l], in, ldi, A.hidden_act == 1, dnext, L.ldD, nullptr, 0, row0);
+                    if (s.w_rows[l] == 16) layer_backward_data<16, 2>(dcur, ld_cur, sw + L.soff[l], s.w_cols[l] + 8, s.w_cols[l], in, ldi, A.hidden_act == 1, dnext, L.ldD, nullptr, 0, row0);
+                    else layer_backward_data<NN, 2>(dcur, ld_cur, sw + L.soff[l], s.w_cols[l] + 8, s.w_cols[l], in, ldi, A.hidden_act == 1, dnext, L.ldD, nullptr, 0, row0);
                     dcur = dnext;
                     ld_cur = L.ldD;
                     pp ^= 1;
                 } else {
-                    if (s.w_rows[0] == 16) layer_backward_data<16>(dcur, ld_cur, sw + L.soff[0], s.w_cols[0] + 8, s.w_cols[0], nullptr, 0, false, nullptr, 0, GX, L.ldG, row0);
-                    else layer_backward_data<NN>(dcur, ld_cur, sw + L.soff[0], s.w_cols[0] + 8, s.w_cols[0], nullptr, 0, false, nullptr, 0, GX, L.ldG, row0);
+                    if (s.w_rows[0] == 16) layer_backward_data<16, 2>(dcur, ld_cur, sw + L.soff[0], s.w_cols[0] + 8, s.w_cols[0], nullptr, 0, false, nullptr, 0, GX, L.ldG, row0);
+                    else layer_backward_data<NN, 2>(dcur, ld_cur, sw + L.soff[0], s.w_cols[0] + 8, s.w_cols[0], nullptr, 0, false, nullptr, 0, GX, L.ldG, row0);
                 }
                 __syncthreads();
             }
@@ -540,7 +672,7 @@ __global__ void __launch_bounds__(kBwdRows) neural_bwd_kernel(Params P, Appearan
                     else
                         for (int f = 0; f < A.n_freq; f++) {
                             float sn, cs;
-                            sincosf(scalbnf(val, f), &sn, &cs);
+                            sincosf(octave(val, f), &sn, &cs);
                             gv += static_cast<float>(1 << f) * (cs * gx[j * per + 2 * f] - sn * gx[j * per + 2 * f + 1]);
                         }
                     gv *= inv;
@@ -589,6 +721,250 @@ __global__ void __launch_bounds__(kBwdRows) neural_bwd_kernel(Params P, Appearan
     for (int e = threadIdx.x; e < s.n_params; e += blockDim.x) atomicAdd(O.mlp + e, dW[e] * inv);
 }
 
+// ---------------------------------------------------------------------------------------------------
+// backward over the visible rows (8 warps x 16 rows per batch, weight gradient in registers)
+
+constexpr int kFastWarps = 8;
+constexpr int kMaxTilesPerWarp = 8;
+
+struct FastBwdLayout {
+    int soff[10];
+    int ldX, ldH, ldY, ldG;
+    int tb[11];  // first 16x16 weight-gradient tile of each layer; tb[layers] = number of tiles
+    size_t off_x, off_h, off_y, off_g, total;
+};
+
+__host__ __device__ inline FastBwdLayout fast_bwd_layout(const MlpShape& s) {
+    FastBwdLayout L;
+    const int wh = smem_weights_halves(s, L.soff);
+    L.ldX = s.kin + 8;
+    L.ldH = s.nn + 8;
+    L.ldY = 16 + 8;
+    L.ldG = s.kin + 4;
+    size_t off = (static_cast<size_t>(wh) * 2 + 15) & ~static_cast<size_t>(15);
+    L.off_x = off;
+    off += static_cast<size_t>(kBwdRows) * L.ldX * 2;
+    L.off_h = off;
+    const size_t hbuf = static_cast<size_t>(kBwdRows) * L.ldH * 2;
+    off += hbuf * (s.layers - 1);
+    L.off_y = off;
+    off += static_cast<size_t>(kBwdRows) * L.ldY * 2;
+    // the fp32 input gradient overwrites buffers that are dead once the second layer's gradients are done: the hidden
+    // buffers after the first and the output gradient (a network without hidden layers gets its own buffer)
+    L.off_g = s.layers >= 3 ? L.off_h + hbuf : (s.layers == 2 ? L.off_y : off);
+    const size_t g_end = L.off_g + static_cast<size_t>(kBwdRows) * L.ldG * 4;
+    L.total = g_end > off ? g_end : off;
+    L.tb[0] = 0;
+    for (int l = 0; l < s.layers; l++) L.tb[l + 1] = L.tb[l] + (s.w_rows[l] / 16) * (s.w_cols[l] / 16);
+    return L;
+}
+
+// dW tiles of layer l owned by this warp (tile t belongs to warp t % 8, register slot t / 8) += dOut^T . In over the
+// batch's rows
+template <int T>
+__device__ inline void wgrad_tiles(float (&dw)[T][2][4], int t_begin, int t_end, int tiles_k, int warp, const __half* dout, int ld_dout,
+                                   const __half* in, int ld_in) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < T; j++) {
+        const int t = warp + kFastWarps * j;
+        if (t < t_begin || t >= t_end) continue;
+        const int lt = t - t_begin;
+        const int m0 = (lt / tiles_k) * 16, n0 = (lt % tiles_k) * 16;
+#pragma unroll 2
+        for (int k0 = 0; k0 < kBwdRows; k0 += 16) {
+            uint32_t a[4], b[4];
+            ldsm_x4_t(a, dout + (k0 + (lane >> 4) * 8 + (lane & 7)) * ld_dout + m0 + ((lane >> 3) & 1) * 8);
+            ldsm_x4_t(b, in + (k0 + ((lane >> 3) & 1) * 8 + (lane & 7)) * ld_in + n0 + (lane >> 4) * 8);
+            mma16816(dw[j][0], a, b[0], b[1]);
+            mma16816(dw[j][1], a, b[2], b[3]);
+        }
+    }
+}
+
+template <int NN, int T>
+__global__ void __launch_bounds__(kFastWarps * 32, 2) neural_bwd_vis_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis,
+                                                                          uint32_t n_rows, const uint32_t* __restrict__ rank_of,
+                                                                          const Record* __restrict__ sorted_rec,
+                                                                          const GradRecord* __restrict__ grads, GradOut O) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ float s_base_in[kBwdRows * 3];
+    __shared__ MlpShape s_shape;
+    __shared__ FastBwdLayout s_layout;
+    if (threadIdx.x == 0) {
+        s_shape = mlp_shape(A);
+        s_layout = fast_bwd_layout(s_shape);
+    }
+    __syncthreads();
+    const MlpShape& s = s_shape;  // uniform tables read from shared memory (no local-memory copies)
+    const FastBwdLayout& L = s_layout;
+    __half* sw = reinterpret_cast<__half*>(smem);
+    __half* X = reinterpret_cast<__half*>(smem + L.off_x);
+    __half* H = reinterpret_cast<__half*>(smem + L.off_h);  // slot j: output of layer j (input of layer j + 1), later its gradient
+    __half* Y = reinterpret_cast<__half*>(smem + L.off_y);  // outputs, then the scaled output gradient
+    float* GX = reinterpret_cast<float*>(smem + L.off_g);   // loss-scaled input gradient
+    load_weights(s, P.mlp, sw, L.soff);
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int deg = min(v.degree, A.max_degree);
+    const int acc_mode = O.accumulate;
+    const int nraw = A.feature_dim + (A.base_input ? 3 : 0), per = A.n_freq > 0 ? 2 * A.n_freq : 1;
+    const int sh_col = nraw * per;
+    const int row = warp * 16 + (lane & 15);  // this lane's row in the batch (lanes 16..31 mirror 0..15)
+    const bool row_lane = lane < 16;
+    const size_t hslot = static_cast<size_t>(kBwdRows) * L.ldH;
+    float dw[T][2][4];
+#pragma unroll
+    for (int j = 0; j < T; j++)
+#pragma unroll
+        for (int n = 0; n < 2; n++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) dw[j][n][q] = 0.0f;
+    const uint32_t n_batches = (n_rows + kBwdRows - 1) / kBwdRows;
+    for (uint32_t b = blockIdx.x; b < n_batches; b += gridDim.x) {
+        const uint32_t gi = b * kBwdRows + row;
+        const bool valid = gi < n_rows;
+        const uint32_t i = valid ? vis[gi] : 0u;
+        const uint32_t r = valid ? rank_of[i] : 0u;
+        const uint32_t vmask = __ballot_sync(0xffffffffu, valid) & 0xffffu;
+        // inputs and recomputed forward of the warp's 16 rows
+        f3 gpre = mk3(0.0f, 0.0f, 0.0f);
+        if (row_lane) {
+            f3 d = mk3(0.0f, 0.0f, 1.0f);
+            if (valid) {
+                const float4 q2 = sorted_rec[r].q2, g1 = grads[r].g1;
+                gpre = mk3(g1.y, g1.z, g1.w) * mk3(color_act_grad_from_y(A.color_act, q2.x), color_act_grad_from_y(A.color_act, q2.y),
+                                                   color_act_grad_from_y(A.color_act, q2.z));
+                d = view_dir(v, ld3(P.means, i), nullptr);
+            }
+            direction_inputs(A, deg, valid, d, X + row * L.ldX, s.kin);
+        }
+        encode_rows<16>(P, A, i, vmask, X + warp * 16 * L.ldX, L.ldX);
+        __syncwarp();
+        for (int l = 0; l < s.layers; l++) {
+            const __half* in = l == 0 ? X : H + (l - 1) * hslot;
+            const int ldi = l == 0 ? L.ldX : L.ldH;
+            if (l == s.layers - 1) layer_forward<16, 1>(in, ldi, s.w_cols[l], sw + L.soff[l], s.w_cols[l] + 8, Y, L.ldY, warp * 16, false);
+            else layer_forward<NN, 1>(in, ldi, s.w_cols[l], sw + L.soff[l], s.w_cols[l] + 8, H + l * hslot, L.ldH, warp * 16, A.hidden_act == 1);
+            __syncwarp();
+        }
+        if (row_lane) {
+            __half* yr = Y + row * L.ldY;
+            float dy[3] = {0.0f, 0.0f, 0.0f};
+            if (valid) {
+                const float gv[3] = {gpre.x, gpre.y, gpre.z};
+                for (int c = 0; c < 3; c++) {
+                    const float y = __half2float(yr[c]);
+                    dy[c] = gv[c] * residual_act_grad_from_y(A.res_act, residual_act(A.res_act, y));
+                }
+            }
+            for (int c = 0; c < 16; c++) yr[c] = __float2half_rn(c < 3 ? kLossScale * dy[c] : 0.0f);
+        }
+        __syncthreads();
+        // layers last to first: weight gradient over all rows (shared), data gradient of the warp's rows
+        for (int l = s.layers - 1; l >= 0; l--) {
+            const __half* dout = l == s.layers - 1 ? Y : H + l * hslot;
+            const int ldd = l == s.layers - 1 ? L.ldY : L.ldH;
+            const __half* in = l == 0 ? X : H + (l - 1) * hslot;
+            const int ldi = l == 0 ? L.ldX : L.ldH;
+            wgrad_tiles<T>(dw, L.tb[l], L.tb[l + 1], s.w_cols[l] / 16, warp, dout, ldd, in, ldi);
+            if (l > 0) {
+                __syncthreads();  // every warp has read this layer's input before it is overwritten by its gradient
+                __half* hin = H + (l - 1) * hslot;
+                if (s.w_rows[l] == 16)
+                    layer_backward_data<16, 1>(dout, ldd, sw + L.soff[l], s.w_cols[l] + 8, s.w_cols[l], hin, L.ldH, A.hidden_act == 1, hin, L.ldH,
+                                               nullptr, 0, warp * 16);
+                else
+                    layer_backward_data<NN, 1>(dout, ldd, sw + L.soff[l], s.w_cols[l] + 8, s.w_cols[l], hin, L.ldH, A.hidden_act == 1, hin, L.ldH,
+                                               nullptr, 0, warp * 16);
+                __syncthreads();
+            } else {
+                if (s.w_rows[0] == 16)
+                    layer_backward_data<16, 1>(dout, ldd, sw + L.soff[0], s.w_cols[0] + 8, s.w_cols[0], nullptr, 0, false, nullptr, 0, GX, L.ldG, warp * 16);
+                else
+                    layer_backward_data<NN, 1>(dout, ldd, sw + L.soff[0], s.w_cols[0] + 8, s.w_cols[0], nullptr, 0, false, nullptr, 0, GX, L.ldG, warp * 16);
+                __syncwarp();
+            }
+        }
+        feature_grads<16>(P, A, O, i, vmask, GX + warp * 16 * L.ldG, L.ldG, s_base_in + warp * 16 * 3, acc_mode);
+        __syncwarp();
+        if (row_lane && valid) {
+            const GradRecord g = grads[r];
+            const Record rq = sorted_rec[r];
+            const f3 m = ld3(P.means, i);
+            float rn = 1.0f;
+            const f3 d = view_dir(v, m, &rn);
+            const f3 col = mk3(rq.q2.x, rq.q2.y, rq.q2.z);
+            const f3 gp = mk3(g.g1.y, g.g1.z, g.g1.w) * mk3(color_act_grad_from_y(A.color_act, col.x), color_act_grad_from_y(A.color_act, col.y),
+                                                             color_act_grad_from_y(A.color_act, col.z));
+            f3 gbase = mk3(0.0f, 0.0f, 0.0f);
+            if (v.render_base) {
+                const f3 bb = ld3(P.base, i);
+                gbase = mk3(base_act_grad(A.base_act, bb.x), base_act_grad(A.base_act, bb.y), base_act_grad(A.base_act, bb.z)) * gp;
+            }
+            if (A.base_input) {
+                const float* bi = s_base_in + row * 3;
+                gbase.x += bi[0];
+                gbase.y += bi[1];
+                gbase.z += bi[2];
+            }
+            put3n(O.base, i, gbase, acc_mode);
+            // direction gradient from the SH inputs' gradient, unscaled afterwards (scaling by 2^-7 is exact)
+            const f3 gd = (1.0f / kLossScale) * sh_band_grad(A.sh_mask, deg, d, GX + row * L.ldG + sh_col);
+            const f3 gmean_color = rn * (gd - dot3(gd, d) * d);
+            float gmx, gmy, gca, gcb, gcc, g_opacity;
+            blend_sums_to_grads(g, rq, v.proper_aa, gmx, gmy, gca, gcb, gcc, g_opacity);
+            const f3 gmean = geometry_backward(P, v, i, m, gmx, gmy, gca, gcb, gcc, g_opacity, O);
+            if (O.densification != nullptr && O.densification_rows == 3) {
+                const float nx = 0.5f * (g.g2.y * static_cast<float>(v.width)), ny = 0.5f * (g.g2.z * static_cast<float>(v.height));
+                O.densification[2ull * P.n + i] += sqrtf(nx * nx + ny * ny);
+            }
+            put1(O.opacities, i, g_opacity, acc_mode);
+            put3n(O.means, i, A.dir_grad ? gmean + gmean_color : gmean, acc_mode);
+        }
+        __syncthreads();  // the next batch overwrites buffers other warps may still read
+    }
+    // flush this warp's weight-gradient tiles (unscaled)
+    const float inv = 1.0f / kLossScale;
+    const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+    for (int j = 0; j < T; j++) {
+        const int t = warp + kFastWarps * j;
+        if (t >= L.tb[s.layers]) continue;
+        int l = 0;
+        while (t >= L.tb[l + 1]) l++;
+        const int lt = t - L.tb[l], tk = s.w_cols[l] / 16, cols = s.w_cols[l];
+        const int m0 = (lt / tk) * 16, n0 = (lt % tk) * 16;
+        float* base = O.mlp + s.w_off[l];
+#pragma unroll
+        for (int n = 0; n < 2; n++) {
+            const int rr = m0 + g, c = n0 + n * 8 + tq * 2;
+            atomicAdd(base + rr * cols + c, dw[j][n][0] * inv);
+            atomicAdd(base + rr * cols + c + 1, dw[j][n][1] * inv);
+            atomicAdd(base + (rr + 8) * cols + c, dw[j][n][2] * inv);
+            atomicAdd(base + (rr + 8) * cols + c + 1, dw[j][n][3] * inv);
+        }
+    }
+}
+
+// zero gradients of the primitives outside the view (overwrite mode of the visible-row backward)
+__global__ void zero_invisible_kernel(const uint32_t* __restrict__ rank_of, uint32_t n, int F, GradOut O) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        if (rank_of[i] != kInvalidRank) continue;
+        for (int k = 0; k < 3; k++) {
+            O.means[3 * i + k] = 0.0f;
+            O.scales[3 * i + k] = 0.0f;
+            O.base[3 * i + k] = 0.0f;
+        }
+        for (int k = 0; k < 4; k++) O.rotations[4 * i + k] = 0.0f;
+        O.opacities[i] = 0.0f;
+    }
+    const size_t ne = static_cast<size_t>(n) * F;
+    for (size_t e = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < ne; e += stride)
+        if (rank_of[e / F] == kInvalidRank) O.residual[e] = 0.0f;
+}
+
 int sm_count() {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -596,12 +972,13 @@ int sm_count() {
     return sms;
 }
 
-size_t fwd_smem_bytes(const AppearanceConfig& A) {
+size_t color_smem_bytes(const AppearanceConfig& A, int warps) {
     const MlpShape s = mlp_shape(A);
     const int wh = smem_weights_halves(s, nullptr);
-    const int ldA = (s.kin > s.nn ? s.kin : s.nn) + 8, ldB = s.nn + 8;
-    return static_cast<size_t>((wh + 7) & ~7) * 2 + static_cast<size_t>(kFwdRows) * (ldA + ldB) * 2;
+    return static_cast<size_t>((wh + 7) & ~7) * 2 + static_cast<size_t>(warps) * color_buf_halves(s, s.nn) * 2;
 }
+
+constexpr size_t kSmemLimit = 227 * 1024;
 
 template <typename K>
 cudaError_t launch_persistent(K kernel, size_t smem, int threads, uint32_t n_chunks, int* grid_out) {
@@ -618,31 +995,86 @@ cudaError_t launch_persistent(K kernel, size_t smem, int threads, uint32_t n_chu
 
 }  // namespace
 
-cudaError_t launch_preprocess_fwd_neural(const Params& P, const AppearanceConfig& A, const View& v, const PrimBuffers& B, cudaStream_t st) {
-    const uint32_t n_chunks = (P.n + kFwdRows - 1) / kFwdRows;
-    if (n_chunks == 0) return cudaSuccess;
-    const size_t smem = fwd_smem_bytes(A);
+cudaError_t launch_neural_color(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis, uint32_t n_visible, Record* rec,
+                                cudaStream_t st) {
+    if (n_visible == 0 || std::min(v.degree, A.max_degree) <= 0) return cudaSuccess;
+    int warps = 8;
+    while (warps > 1 && color_smem_bytes(A, warps) > kSmemLimit) warps >>= 1;
+    const size_t smem = color_smem_bytes(A, warps);
+    if (smem > kSmemLimit) return cudaErrorInvalidConfiguration;
+    const int threads = warps * 32;
+    const uint32_t n_tiles = (n_visible + 31) / 32, n_blocks = (n_tiles + warps - 1) / warps;
     int grid = 0;
     cudaError_t e = cudaSuccess;
     switch (A.n_neurons) {
-        case 16: e = launch_persistent(neural_fwd_kernel<16>, smem, kFwdRows, n_chunks, &grid); if (!e) neural_fwd_kernel<16><<<grid, kFwdRows, smem, st>>>(P, A, v, B, n_chunks); break;
-        case 32: e = launch_persistent(neural_fwd_kernel<32>, smem, kFwdRows, n_chunks, &grid); if (!e) neural_fwd_kernel<32><<<grid, kFwdRows, smem, st>>>(P, A, v, B, n_chunks); break;
-        case 64: e = launch_persistent(neural_fwd_kernel<64>, smem, kFwdRows, n_chunks, &grid); if (!e) neural_fwd_kernel<64><<<grid, kFwdRows, smem, st>>>(P, A, v, B, n_chunks); break;
+        case 16: e = launch_persistent(neural_color_kernel<16>, smem, threads, n_blocks, &grid); if (!e) neural_color_kernel<16><<<grid, threads, smem, st>>>(P, A, v, vis, n_visible, rec); break;
+        case 32: e = launch_persistent(neural_color_kernel<32>, smem, threads, n_blocks, &grid); if (!e) neural_color_kernel<32><<<grid, threads, smem, st>>>(P, A, v, vis, n_visible, rec); break;
+        case 64: e = launch_persistent(neural_color_kernel<64>, smem, threads, n_blocks, &grid); if (!e) neural_color_kernel<64><<<grid, threads, smem, st>>>(P, A, v, vis, n_visible, rec); break;
         default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
+namespace {
+
+template <int NN, int T>
+cudaError_t run_vis_bwd(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis, uint32_t n_visible, const uint32_t* rank_of,
+                        const Record* sorted_rec, const GradRecord* grads, const GradOut& O, size_t smem, cudaStream_t st) {
+    int grid = 0;
+    const uint32_t n_batches = (n_visible + kBwdRows - 1) / kBwdRows;
+    cudaError_t e = launch_persistent(neural_bwd_vis_kernel<NN, T>, smem, kFastWarps * 32, n_batches, &grid);
+    if (e != cudaSuccess) return e;
+    neural_bwd_vis_kernel<NN, T><<<grid, kFastWarps * 32, smem, st>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O);
+    return cudaGetLastError();
+}
+
+template <int NN>
+cudaError_t run_vis_bwd_t(int T, const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis, uint32_t n_visible,
+                          const uint32_t* rank_of, const Record* sorted_rec, const GradRecord* grads, const GradOut& O, size_t smem, cudaStream_t st) {
+    switch (T) {
+        case 2: return run_vis_bwd<NN, 2>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, smem, st);
+        case 3: return run_vis_bwd<NN, 3>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, smem, st);
+        case 5: return run_vis_bwd<NN, 5>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, smem, st);
+        default: return run_vis_bwd<NN, 8>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, smem, st);
+    }
+}
+
+}  // namespace
+
 cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* rank_of,
-                                         const Record* sorted_rec, const GradRecord* grads, const GradOut& O, cudaStream_t st) {
-    const uint32_t n_chunks = (P.n + kBwdRows - 1) / kBwdRows;
-    if (n_chunks == 0) return cudaSuccess;
+                                         const Record* sorted_rec, const GradRecord* grads, const GradOut& O, const uint32_t* vis,
+                                         uint32_t n_visible, cudaStream_t st) {
+    if (P.n == 0) return cudaSuccess;
     if (!O.accumulate) {
         cudaError_t e = cudaMemsetAsync(O.mlp, 0, static_cast<size_t>(A.n_params) * sizeof(float), st);
         if (e != cudaSuccess) return e;
     }
     const MlpShape s = mlp_shape(A);
+    const FastBwdLayout FL = fast_bwd_layout(s);
+    const int n_tiles = FL.tb[s.layers];
+    const size_t fast_smem = FL.total;
+    const bool fast = std::min(v.degree, A.max_degree) > 0 && n_tiles <= kFastWarps * kMaxTilesPerWarp &&
+                      fast_smem + kBwdRows * 3 * sizeof(float) <= kSmemLimit;
+    if (fast) {
+        if (!O.accumulate) {
+            const int blocks = std::max(1, std::min(static_cast<int>((P.n + 255) / 256), sm_count() * 8));
+            zero_invisible_kernel<<<blocks, 256, 0, st>>>(rank_of, P.n, A.feature_dim, O);
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return e;
+        }
+        if (n_visible == 0) return cudaSuccess;
+        const int per_warp = (n_tiles + kFastWarps - 1) / kFastWarps;
+        const int T = per_warp <= 2 ? 2 : (per_warp <= 3 ? 3 : (per_warp <= 5 ? 5 : 8));
+        switch (A.n_neurons) {
+            case 16: return run_vis_bwd_t<16>(T, P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, fast_smem, st);
+            case 32: return run_vis_bwd_t<32>(T, P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, fast_smem, st);
+            case 64: return run_vis_bwd_t<64>(T, P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, fast_smem, st);
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    // general path: every primitive, weight gradient in shared memory
+    const uint32_t n_chunks = (P.n + kBwdRows - 1) / kBwdRows;
     const size_t smem = neural_bwd_layout(s).total;
     int grid = 0;
     cudaError_t e = cudaSuccess;
@@ -659,7 +1091,7 @@ cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig
 size_t neural_grad_scratch_floats(const AppearanceConfig& A) { return static_cast<size_t>(A.n_params); }
 
 size_t neural_smem_bytes(const AppearanceConfig& A) {
-    const size_t b = neural_bwd_layout(mlp_shape(A)).total, f = fwd_smem_bytes(A);
+    const size_t b = neural_bwd_layout(mlp_shape(A)).total, f = color_smem_bytes(A, 1);
     return b > f ? b : f;
 }
 

@@ -28,6 +28,7 @@ __device__ inline f3 fused_color(const Params& P, const AppearanceConfig& A, con
     if (MODEL == kSV) res = sv_forward(rp, d, deg, A.res_act);
     if (MODEL == kNASG) res = lobes_forward<false>(rp, d, deg, A.res_act);
     if (MODEL == kNASGabor) res = lobes_forward<true>(rp, d, deg, A.res_act);
+    // kNeural: the residual comes from the colour pass over the visible primitives, which overwrites this colour
     const f3 base = base_act3(A.base_act, ld3(P.base, i));
     f3 col = color_act3(A.color_act, base + res);
     if (!v.render_base) {
@@ -91,7 +92,7 @@ __global__ void __launch_bounds__(1024) chunk_scan_kernel(const uint2* __restric
 // writes (depth key, primitive index) of visible primitives in primitive order
 __global__ void __launch_bounds__(kChunk) compact_kernel(const uint32_t* __restrict__ n_touched, const uint32_t* __restrict__ depth_key,
                                                          const uint32_t* __restrict__ chunk_off, uint32_t* __restrict__ keys,
-                                                         uint32_t* __restrict__ idx, uint32_t n) {
+                                                         uint32_t* __restrict__ idx, uint32_t* __restrict__ vis_idx, uint32_t n) {
     __shared__ uint32_t warp_counts[kChunk / 32];
     const uint32_t i = blockIdx.x * kChunk + threadIdx.x;
     const bool vis = i < n && n_touched[i] > 0;
@@ -105,6 +106,7 @@ __global__ void __launch_bounds__(kChunk) compact_kernel(const uint32_t* __restr
     if (vis) {
         keys[pos] = depth_key[i];
         idx[pos] = i;
+        vis_idx[pos] = i;
     }
 }
 
@@ -214,7 +216,7 @@ cudaError_t launch_preprocess_fwd(const Params& P, const AppearanceConfig& A, co
         case kSV: preprocess_fwd_kernel<kSV><<<grid, kChunk, 0, s>>>(P, A, v, B); break;
         case kNASG: preprocess_fwd_kernel<kNASG><<<grid, kChunk, 0, s>>>(P, A, v, B); break;
         case kNASGabor: preprocess_fwd_kernel<kNASGabor><<<grid, kChunk, 0, s>>>(P, A, v, B); break;
-        case kNeural: return launch_preprocess_fwd_neural(P, A, v, B, s);
+        case kNeural: preprocess_fwd_kernel<kNeural><<<grid, kChunk, 0, s>>>(P, A, v, B); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -224,7 +226,7 @@ cudaError_t launch_compaction(const PrimBuffers& B, uint32_t n, cudaStream_t s) 
     const int chunks = grid_of(n, kChunk);
     if (chunks == 0) return cudaMemsetAsync(B.counters, 0, 2 * sizeof(unsigned long long), s);
     chunk_scan_kernel<<<1, 1024, 0, s>>>(B.chunk_stats, B.chunk_off, B.counters, chunks);
-    compact_kernel<<<chunks, kChunk, 0, s>>>(B.n_touched, B.depth_key, B.chunk_off, B.keys_a, B.idx_a, n);
+    compact_kernel<<<chunks, kChunk, 0, s>>>(B.n_touched, B.depth_key, B.chunk_off, B.keys_a, B.idx_a, B.vis_idx, n);
     return cudaGetLastError();
 }
 
@@ -236,7 +238,7 @@ cudaError_t launch_reorder(const PrimBuffers& B, uint32_t n_visible, cudaStream_
 
 cudaError_t launch_preprocess_bwd(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* rank_of,
                                   const Record* sorted_rec, const GradRecord* grads, const GradOut& O, bool precomputed,
-                                  cudaStream_t s) {
+                                  const uint32_t* vis_idx, uint32_t n_visible, cudaStream_t s) {
     const int grid = grid_of(P.n, 128);
     if (grid == 0) return cudaSuccess;
     const int model = precomputed ? kPrecomputed : A.model;
@@ -246,7 +248,7 @@ cudaError_t launch_preprocess_bwd(const Params& P, const AppearanceConfig& A, co
         case kSV: preprocess_bwd_kernel<kSV><<<grid, 128, 0, s>>>(P, A, v, rank_of, sorted_rec, grads, O); break;
         case kNASG: preprocess_bwd_kernel<kNASG><<<grid, 128, 0, s>>>(P, A, v, rank_of, sorted_rec, grads, O); break;
         case kNASGabor: preprocess_bwd_kernel<kNASGabor><<<grid, 128, 0, s>>>(P, A, v, rank_of, sorted_rec, grads, O); break;
-        case kNeural: return launch_preprocess_bwd_neural(P, A, v, rank_of, sorted_rec, grads, O, s);
+        case kNeural: return launch_preprocess_bwd_neural(P, A, v, rank_of, sorted_rec, grads, O, vis_idx, n_visible, s);
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

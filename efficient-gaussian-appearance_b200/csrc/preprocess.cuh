@@ -50,6 +50,7 @@ struct PrimBuffers {
     unsigned long long* counters;  // [0] visible, [1] instances
     uint32_t* keys_a; uint32_t* keys_b;
     uint32_t* idx_a;  uint32_t* idx_b;
+    uint32_t* vis_idx;     // [V] visible primitives in primitive order (the compaction's list, kept past the depth sort)
     Record* sorted_rec;    // [V] records in depth order
     uint32_t* inst_off;    // [V] exclusive instance offsets in depth order
     void* cub_temp; size_t cub_temp_bytes;
