@@ -21,8 +21,9 @@ ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 FLAGS = ['-O3', '-std=c++17', '-lineinfo', '-fmad=false', '-Xcompiler', '-fPIC', '--expt-relaxed-constexpr',
          '-Xptxas', '-warn-spills']
 # Sources whose outputs are checked against the CPU restatement within a tolerance rather than bit for bit (the fp16
-# tensor-core MLP of the neural appearance, whose backward also carries the geometry chain rule): contraction allowed.
-CONTRACTED = {'neural.cu'}
+# tensor-core MLP of the neural appearance, whose backward also carries the geometry chain rule; the photometric loss,
+# checked against its fp32 PyTorch definition): contraction allowed.
+CONTRACTED = {'neural.cu', 'loss.cu'}
 
 
 def _digest(paths):

@@ -615,6 +615,23 @@ int fgs_adam_step(const fgs_adam_segment* segs, int n, void* stream) {
     return FGS_OK;
 }
 
+int fgs_loss_workspace_bytes(int channels, int height, int width, size_t* out) {
+    if (!out || channels <= 0 || height <= 0 || width <= 0) return fail(FGS_ERR_INVALID_ARGUMENT, "bad argument");
+    *out = fgs::loss_workspace_bytes(channels, height, width);
+    return FGS_OK;
+}
+
+int fgs_l1_dssim(const float* image, const float* target, int channels, int height, int width, float l1_weight, float dssim_weight,
+                 float* grad_image, float* loss, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!image || !target || !grad_image || !loss || !workspace) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (channels <= 0 || height <= 0 || width <= 0) return fail(FGS_ERR_INVALID_ARGUMENT, "bad image size");
+    if (workspace_bytes < fgs::loss_workspace_bytes(channels, height, width)) return fail(FGS_ERR_WORKSPACE, "loss workspace too small");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    ProfScope p_("loss", s);
+    FGS_CUDA(fgs::launch_l1_dssim(image, target, channels, height, width, l1_weight, dssim_weight, grad_image, loss, workspace, s), "loss");
+    return FGS_OK;
+}
+
 int fgs_profile_enable(int enabled) {
     g_prof.enabled = enabled != 0;
     return FGS_OK;

@@ -61,6 +61,11 @@ cudaError_t launch_blend_inference(const BlendArgs& a, float* image, int chw, in
 cudaError_t launch_blend_backward(const BlendArgs& a, const float* image, const float* grad_image, const TileBuffers& T, GradRecord* grads,
                                   int abs_grad, cudaStream_t s);
 
+// loss.cu
+size_t loss_workspace_bytes(int C, int H, int W);
+cudaError_t launch_l1_dssim(const float* image, const float* target, int C, int H, int W, float l1_weight, float dssim_weight, float* grad,
+                            float* loss, void* ws, cudaStream_t s);
+
 // adam.cu
 struct AdamSegment {
     float* param; const float* grad; float* m; float* v;

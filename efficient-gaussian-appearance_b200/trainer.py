@@ -39,15 +39,15 @@ class Group:
     betas: tuple = (0.9, 0.999)
 
 
-def gaussian_window(size: int, sigma: float, device) -> torch.Tensor:
-    x = torch.arange(size, dtype=torch.float32, device=device) - (size - 1) / 2.0
+def gaussian_window(size: int, sigma: float, device, dtype=torch.float32) -> torch.Tensor:
+    x = torch.arange(size, dtype=dtype, device=device) - (size - 1) / 2.0
     g = torch.exp(-x * x / (2.0 * sigma * sigma))
     return g / g.sum()
 
 
 def blur(img: torch.Tensor, size: int, sigma: float) -> torch.Tensor:
     """Separable Gaussian blur of a [C,H,W] image with zero padding."""
-    g = gaussian_window(size, sigma, img.device)
+    g = gaussian_window(size, sigma, img.device, img.dtype)
     c = img.shape[0]
     x = img[None]
     x = tf.conv2d(x, g.view(1, 1, 1, size).expand(c, 1, 1, size), padding=(0, size // 2), groups=c)
@@ -66,12 +66,39 @@ def ssim(img: torch.Tensor, target: torch.Tensor, size: int = 11, sigma: float =
     return m.mean()
 
 
-def loss_and_grad(img: torch.Tensor, target: torch.Tensor, l1_weight: float = 0.8, dssim_weight: float = 0.2):
-    """0.8 * L1 + 0.2 * (1 - SSIM) (Loss.py:15-16 weights); returns (loss, dL/dimage)."""
+def loss_and_grad_reference(img: torch.Tensor, target: torch.Tensor, l1_weight: float = 0.8, dssim_weight: float = 0.2):
+    """The loss definition in PyTorch fp32 (the check for the fused kernel): 0.8 * L1 + 0.2 * (1 - SSIM)
+    (Loss.py:14-15 weights); returns (loss, dL/dimage)."""
     x = img.detach().requires_grad_(True)
     loss = l1_weight * (x - target).abs().mean() + dssim_weight * (1.0 - ssim(x, target))
     loss.backward()
     return loss.detach(), x.grad
+
+
+class FusedLoss:
+    """The same loss through the library's fused CUDA kernels (fgs_l1_dssim): loss value and image gradient stay on
+    the device; the workspace is kept between calls of the same image size."""
+
+    def __init__(self, l1_weight: float = 0.8, dssim_weight: float = 0.2) -> None:
+        self.l1_weight, self.dssim_weight = l1_weight, dssim_weight
+        self.ws = None
+
+    def __call__(self, img: torch.Tensor, target: torch.Tensor, grad_out: torch.Tensor | None = None,
+                 loss_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        if not img.is_cuda:
+            raise RuntimeError('FusedLoss needs CUDA tensors (the fused loss has no CPU path)')
+        c, h, w = img.shape
+        for t in (img, target):
+            if t.dtype != torch.float32 or not t.is_contiguous() or t.shape != img.shape or t.device != img.device:
+                raise ValueError('image and target must be contiguous float32 [C,H,W] tensors of the same shape on one device')
+        need = _lib.size_out(_lib.lib.fgs_loss_workspace_bytes, c, h, w)
+        if self.ws is None or self.ws.numel() < need or self.ws.device != img.device:
+            self.ws = torch.empty(need, dtype=torch.uint8, device=img.device)
+        grad = grad_out if grad_out is not None else torch.empty_like(img)
+        loss = loss_out if loss_out is not None else torch.empty((), dtype=torch.float32, device=img.device)
+        _lib.check(_lib.lib.fgs_l1_dssim(img.data_ptr(), target.data_ptr(), c, h, w, self.l1_weight, self.dssim_weight, grad.data_ptr(),
+                                         loss.data_ptr(), self.ws.data_ptr(), self.ws.numel(), torch.cuda.current_stream(img.device).cuda_stream))
+        return loss, grad
 
 
 class Trainer:
@@ -104,6 +131,9 @@ class Trainer:
         self.grad_shard = self.grads[self.rank * shard:(self.rank + 1) * shard] if self.world == 1 else torch.empty(shard, device=device)
         self.step_count = 0
         self.n = prims['means'].shape[0]
+        self.loss_fn = FusedLoss()
+        self._image = None
+        self._grad_image = None
 
     def view(self, buf: torch.Tensor, name: str) -> torch.Tensor | None:
         for g in self.groups:
@@ -132,11 +162,14 @@ class Trainer:
         for k, (settings, target) in enumerate(zip(settings_list, targets)):
             st = R.ForwardState(R._rasterizer, cp, settings, self.device)
             st.preprocess(cp)
-            image = torch.empty((3, settings.height, settings.width), device=self.device)
-            st.render_train(image)
-            loss, grad_image = loss_and_grad(image, target)
+            shape = (3, settings.height, settings.width)
+            if self._image is None or tuple(self._image.shape) != shape:
+                self._image = torch.empty(shape, device=self.device)
+                self._grad_image = torch.empty(shape, device=self.device)
+            st.render_train(self._image)
+            loss, _ = self.loss_fn(self._image, target, grad_out=self._grad_image)
             total += loss
-            st.backward(cp, image, grad_image.contiguous(), cg, None, accumulate=k > 0)
+            st.backward(cp, self._image, self._grad_image, cg, None, accumulate=k > 0)
         return total
 
     def adam_segments(self) -> list:

@@ -180,6 +180,15 @@ int fgs_frame_buffers(const fgs_frame* frame, void* prim_ws, void* tile_ws, void
 /* fused Adam over up to 12 segments in one launch (adam/src/adam.cu:18-42 per element) */
 int fgs_adam_step(const fgs_adam_segment* segments, int n_segments, void* stream);
 
+/* Fused photometric loss of the training step and its image gradient: for planar [C,H,W] fp32 images,
+ * loss = l1_weight * mean|image - target| + dssim_weight * (1 - mean SSIM(image, target)) with an 11x11 Gaussian
+ * window (sigma 1.5, zero padding, C1 = 0.01^2, C2 = 0.03^2). Replaces the caller-side loss of the reference
+ * trainer (FasterGSVDA/Loss.py:14-15: L1 plus NeRFICG's fused_dssim, weights LAMBDA_L1 / LAMBDA_DSSIM) so the
+ * whole step stays on the device; `loss` is one device float, written deterministically. */
+int fgs_loss_workspace_bytes(int channels, int height, int width, size_t* out);
+int fgs_l1_dssim(const float* image, const float* target, int channels, int height, int width, float l1_weight, float dssim_weight,
+                 float* grad_image, float* loss, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Optional per-stage timing: while enabled, every stage above records a CUDA event pair on its stream;
  * fgs_profile_collect waits for them, returns the summed milliseconds per stage since the last collect
  * (names comma-separated in `names`) and resets the totals. No counterpart in the reference, which has
