@@ -349,12 +349,20 @@ __device__ inline void feature_grads(const Params& P, const AppearanceConfig& A,
     const float inv = 1.0f / kLossScale;
     for (int e0 = 0; e0 < nraw; e0 += 32) {
         const int e = e0 + lane;
-        float vals[NR];
+        float vals[NR], olds[NR];
         if (nf > 0) load_raw_rows<NR>(P, A, i, vmask, e, vals);
+        if (acc) {  // the accumulated gradients, loaded up front so the row loop never waits on memory
+#pragma unroll
+            for (int k = 0; k < NR; k++) {
+                const uint32_t ik = __shfl_sync(0xffffffffu, i, k);
+                olds[k] = (((vmask >> k) & 1u) && e < F) ? O.residual[static_cast<size_t>(ik) * F + e] : 0.0f;
+            }
+        }
 #pragma unroll 1
         for (int k = 0; k < NR; k++) {
-            const float val = vals[0];
+            const float val = vals[0], old = olds[0];
             if (nf > 0) rotate<NR>(vals);
+            if (acc) rotate<NR>(olds);
             const uint32_t ik = __shfl_sync(0xffffffffu, i, k);
             if (!((vmask >> k) & 1u) || e >= nraw) continue;
             const float* g = gx + k * ldg;
@@ -368,8 +376,7 @@ __device__ inline void feature_grads(const Params& P, const AppearanceConfig& A,
                 }
             gv *= inv;
             if (e < F) {
-                float* dst = O.residual + static_cast<size_t>(ik) * F + e;
-                if (acc) *dst += gv; else *dst = gv;
+                O.residual[static_cast<size_t>(ik) * F + e] = acc ? old + gv : gv;
             } else {
                 base_in[k * 3 + (e - F)] = gv;
             }
@@ -760,22 +767,28 @@ __host__ __device__ inline FastBwdLayout fast_bwd_layout(const MlpShape& s) {
 }
 
 // dW tiles of layer l owned by this warp (tile t belongs to warp t % 8, register slot t / 8) += dOut^T . In over the
-// batch's rows
+// batch's rows; the row loop is outside the tile loop so the tiles' mma chains interleave
 template <int T>
 __device__ inline void wgrad_tiles(float (&dw)[T][2][4], int t_begin, int t_end, int tiles_k, int warp, const __half* dout, int ld_dout,
                                    const __half* in, int ld_in) {
     const int lane = threadIdx.x & 31;
+    int m0[T], n0[T];
+    bool own[T];
 #pragma unroll
     for (int j = 0; j < T; j++) {
         const int t = warp + kFastWarps * j;
-        if (t < t_begin || t >= t_end) continue;
-        const int lt = t - t_begin;
-        const int m0 = (lt / tiles_k) * 16, n0 = (lt % tiles_k) * 16;
-#pragma unroll 2
-        for (int k0 = 0; k0 < kBwdRows; k0 += 16) {
+        own[j] = t >= t_begin && t < t_end;
+        const int lt = own[j] ? t - t_begin : 0;
+        m0[j] = (lt / tiles_k) * 16;
+        n0[j] = (lt % tiles_k) * 16;
+    }
+    for (int k0 = 0; k0 < kBwdRows; k0 += 16) {
+#pragma unroll
+        for (int j = 0; j < T; j++) {
+            if (!own[j]) continue;
             uint32_t a[4], b[4];
-            ldsm_x4_t(a, dout + (k0 + (lane >> 4) * 8 + (lane & 7)) * ld_dout + m0 + ((lane >> 3) & 1) * 8);
-            ldsm_x4_t(b, in + (k0 + ((lane >> 3) & 1) * 8 + (lane & 7)) * ld_in + n0 + (lane >> 4) * 8);
+            ldsm_x4_t(a, dout + (k0 + (lane >> 4) * 8 + (lane & 7)) * ld_dout + m0[j] + ((lane >> 3) & 1) * 8);
+            ldsm_x4_t(b, in + (k0 + ((lane >> 3) & 1) * 8 + (lane & 7)) * ld_in + n0[j] + (lane >> 4) * 8);
             mma16816(dw[j][0], a, b[0], b[1]);
             mma16816(dw[j][1], a, b[2], b[3]);
         }
@@ -889,14 +902,11 @@ __global__ void __launch_bounds__(kFastWarps * 32, 2) neural_bwd_vis_kernel(Para
         feature_grads<16>(P, A, O, i, vmask, GX + warp * 16 * L.ldG, L.ldG, s_base_in + warp * 16 * 3, acc_mode);
         __syncwarp();
         if (row_lane && valid) {
-            const GradRecord g = grads[r];
-            const Record rq = sorted_rec[r];
-            const f3 m = ld3(P.means, i);
-            float rn = 1.0f;
-            const f3 d = view_dir(v, m, &rn);
-            const f3 col = mk3(rq.q2.x, rq.q2.y, rq.q2.z);
-            const f3 gp = mk3(g.g1.y, g.g1.z, g.g1.w) * mk3(color_act_grad_from_y(A.color_act, col.x), color_act_grad_from_y(A.color_act, col.y),
-                                                             color_act_grad_from_y(A.color_act, col.z));
+            // base colours (through the colour and, with base input, the MLP) and the view-direction part of the
+            // mean gradient; the geometry chain rule follows in neural_geometry_bwd_kernel
+            const float4 q2 = sorted_rec[r].q2, g1 = grads[r].g1;
+            const f3 gp = mk3(g1.y, g1.z, g1.w) * mk3(color_act_grad_from_y(A.color_act, q2.x), color_act_grad_from_y(A.color_act, q2.y),
+                                                       color_act_grad_from_y(A.color_act, q2.z));
             f3 gbase = mk3(0.0f, 0.0f, 0.0f);
             if (v.render_base) {
                 const f3 bb = ld3(P.base, i);
@@ -909,18 +919,15 @@ __global__ void __launch_bounds__(kFastWarps * 32, 2) neural_bwd_vis_kernel(Para
                 gbase.z += bi[2];
             }
             put3n(O.base, i, gbase, acc_mode);
-            // direction gradient from the SH inputs' gradient, unscaled afterwards (scaling by 2^-7 is exact)
-            const f3 gd = (1.0f / kLossScale) * sh_band_grad(A.sh_mask, deg, d, GX + row * L.ldG + sh_col);
-            const f3 gmean_color = rn * (gd - dot3(gd, d) * d);
-            float gmx, gmy, gca, gcb, gcc, g_opacity;
-            blend_sums_to_grads(g, rq, v.proper_aa, gmx, gmy, gca, gcb, gcc, g_opacity);
-            const f3 gmean = geometry_backward(P, v, i, m, gmx, gmy, gca, gcb, gcc, g_opacity, O);
-            if (O.densification != nullptr && O.densification_rows == 3) {
-                const float nx = 0.5f * (g.g2.y * static_cast<float>(v.width)), ny = 0.5f * (g.g2.z * static_cast<float>(v.height));
-                O.densification[2ull * P.n + i] += sqrtf(nx * nx + ny * ny);
+            f3 gmean_color = mk3(0.0f, 0.0f, 0.0f);
+            if (A.dir_grad) {
+                float rn = 1.0f;
+                const f3 d = view_dir(v, ld3(P.means, i), &rn);
+                // direction gradient from the SH inputs' gradient, unscaled afterwards (scaling by 2^-7 is exact)
+                const f3 gd = (1.0f / kLossScale) * sh_band_grad(A.sh_mask, deg, d, GX + row * L.ldG + sh_col);
+                gmean_color = rn * (gd - dot3(gd, d) * d);
             }
-            put1(O.opacities, i, g_opacity, acc_mode);
-            put3n(O.means, i, A.dir_grad ? gmean + gmean_color : gmean, acc_mode);
+            put3n(O.means, i, gmean_color, acc_mode);
         }
         __syncthreads();  // the next batch overwrites buffers other warps may still read
     }
@@ -947,8 +954,32 @@ __global__ void __launch_bounds__(kFastWarps * 32, 2) neural_bwd_vis_kernel(Para
     }
 }
 
-// zero gradients of the primitives outside the view (overwrite mode of the visible-row backward)
-__global__ void zero_invisible_kernel(const uint32_t* __restrict__ rank_of, uint32_t n, int F, GradOut O) {
+// geometry chain rule of the visible primitives (one thread per row, rows in primitive order): mean (added to the
+// view-direction part written by the MLP backward), log-scale, rotation and opacity gradients, densification
+__global__ void __launch_bounds__(256) neural_geometry_bwd_kernel(Params P, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
+                                                                  const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec,
+                                                                  const GradRecord* __restrict__ grads, GradOut O) {
+    const uint32_t gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= n_rows) return;
+    const uint32_t i = vis[gi];
+    const uint32_t r = rank_of[i];
+    const GradRecord g = grads[r];
+    const Record rq = sorted_rec[r];
+    const f3 m = ld3(P.means, i);
+    float gmx, gmy, gca, gcb, gcc, g_opacity;
+    blend_sums_to_grads(g, rq, v.proper_aa, gmx, gmy, gca, gcb, gcc, g_opacity);
+    const f3 gmean = geometry_backward(P, v, i, m, gmx, gmy, gca, gcb, gcc, g_opacity, O);
+    if (O.densification != nullptr && O.densification_rows == 3) {
+        const float nx = 0.5f * (g.g2.y * static_cast<float>(v.width)), ny = 0.5f * (g.g2.z * static_cast<float>(v.height));
+        O.densification[2ull * P.n + i] += sqrtf(nx * nx + ny * ny);
+    }
+    put1(O.opacities, i, g_opacity, O.accumulate);
+    put3n(O.means, i, gmean, 1);
+}
+
+// zero gradients of the primitives outside the view (overwrite mode of the visible-row backward); one thread per
+// primitive; vec4 bit 0: feature rows 16-byte aligned, bit 1: rotation rows 16-byte aligned (16-byte stores)
+__global__ void zero_invisible_kernel(const uint32_t* __restrict__ rank_of, uint32_t n, int F, int vec4, GradOut O) {
     const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
         if (rank_of[i] != kInvalidRank) continue;
@@ -957,12 +988,16 @@ __global__ void zero_invisible_kernel(const uint32_t* __restrict__ rank_of, uint
             O.scales[3 * i + k] = 0.0f;
             O.base[3 * i + k] = 0.0f;
         }
-        for (int k = 0; k < 4; k++) O.rotations[4 * i + k] = 0.0f;
+        if (vec4 & 2) reinterpret_cast<float4*>(O.rotations)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        else
+            for (int k = 0; k < 4; k++) O.rotations[4 * i + k] = 0.0f;
         O.opacities[i] = 0.0f;
+        float* row = O.residual + i * F;
+        if (vec4 & 1)
+            for (int k = 0; k < F; k += 4) *reinterpret_cast<float4*>(row + k) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        else
+            for (int k = 0; k < F; k++) row[k] = 0.0f;
     }
-    const size_t ne = static_cast<size_t>(n) * F;
-    for (size_t e = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < ne; e += stride)
-        if (rank_of[e / F] == kInvalidRank) O.residual[e] = 0.0f;
 }
 
 int sm_count() {
@@ -1026,6 +1061,9 @@ cudaError_t run_vis_bwd(const Params& P, const AppearanceConfig& A, const View& 
     cudaError_t e = launch_persistent(neural_bwd_vis_kernel<NN, T>, smem, kFastWarps * 32, n_batches, &grid);
     if (e != cudaSuccess) return e;
     neural_bwd_vis_kernel<NN, T><<<grid, kFastWarps * 32, smem, st>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    neural_geometry_bwd_kernel<<<(n_visible + 255) / 256, 256, 0, st>>>(P, v, vis, n_visible, rank_of, sorted_rec, grads, O);
     return cudaGetLastError();
 }
 
@@ -1059,7 +1097,9 @@ cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig
     if (fast) {
         if (!O.accumulate) {
             const int blocks = std::max(1, std::min(static_cast<int>((P.n + 255) / 256), sm_count() * 8));
-            zero_invisible_kernel<<<blocks, 256, 0, st>>>(rank_of, P.n, A.feature_dim, O);
+            const int vec4 = ((A.feature_dim % 4 == 0 && reinterpret_cast<uintptr_t>(O.residual) % 16 == 0) ? 1 : 0) |
+                             (reinterpret_cast<uintptr_t>(O.rotations) % 16 == 0 ? 2 : 0);
+            zero_invisible_kernel<<<blocks, 256, 0, st>>>(rank_of, P.n, A.feature_dim, vec4, O);
             cudaError_t e = cudaGetLastError();
             if (e != cudaSuccess) return e;
         }
