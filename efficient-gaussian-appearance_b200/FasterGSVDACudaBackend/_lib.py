@@ -86,6 +86,7 @@ PROTOTYPES = {
     'fgs_inference_noalloc': (c_int, [c_void_p, _P(Primitives), _P(Settings), c_void_p, c_int, c_int, c_void_p, _P(c_int64), _P(c_int64)]),
     'fgs_profile_collect': (c_int, [ctypes.c_char_p, c_size_t, _P(c_double), c_int, _P(c_int)]),
     'fgs_loss_workspace_bytes': (c_int, [c_int, c_int, c_int, _P(c_size_t)]),
+    'fgs_tc_selftest': (c_int, [c_void_p, _P(c_int), c_void_p]),
     'fgs_l1_dssim': (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, ctypes.c_float, ctypes.c_float, c_void_p, c_void_p, c_void_p, c_size_t,
                              c_void_p]),
 }

@@ -632,6 +632,13 @@ int fgs_l1_dssim(const float* image, const float* target, int channels, int heig
     return FGS_OK;
 }
 
+int fgs_tc_selftest(float* scratch, int* mismatches, void* stream) {
+    if (!scratch || !mismatches) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    static_assert(FGS_TC_SELFTEST_FLOATS == fgs::kTcSelftestFloats, "self-test buffer size");
+    FGS_CUDA(fgs::tc_selftest(scratch, mismatches, static_cast<cudaStream_t>(stream)), "tensor-core self-test");
+    return FGS_OK;
+}
+
 int fgs_profile_enable(int enabled) {
     g_prof.enabled = enabled != 0;
     return FGS_OK;

@@ -66,6 +66,11 @@ size_t loss_workspace_bytes(int C, int H, int W);
 cudaError_t launch_l1_dssim(const float* image, const float* target, int C, int H, int W, float l1_weight, float dssim_weight, float* grad,
                             float* loss, void* ws, cudaStream_t s);
 
+// neural_tc.cu
+constexpr int kTcSelftestFloats = 14400;
+constexpr int kTcSelftestStatus = 14336;
+cudaError_t tc_selftest(float* scratch, int* mismatches, cudaStream_t s);
+
 // adam.cu
 struct AdamSegment {
     float* param; const float* grad; float* m; float* v;

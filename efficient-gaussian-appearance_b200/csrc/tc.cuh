@@ -1,0 +1,108 @@
+// Thin wrappers over the sm_100a tensor-core instructions (tcgen05) used by the neural appearance MLP:
+// shared-memory matrix descriptors, the kind::f16 MMA with fp32 accumulation in tensor memory (TMEM),
+// completion tracking through an mbarrier, TMEM allocation and TMEM -> register loads.
+//
+// Operand layouts are the no-swizzle canonical layouts of 16-bit elements: a "core matrix" is 8 rows of 16 bytes
+// (8 elements) stored contiguously (128 bytes).
+//   K-major (rows r, reduction index k):  byte(r, k) = (r / 8) * SBO + (k / 8) * LBO + (r % 8) * 16 + (k % 8) * 2
+//   MN-major (index m along M or N, k):   byte(m, k) = (m / 8) * SBO + (k / 8) * LBO + (k % 8) * 16 + (m % 8) * 2
+// so one buffer written K-major with LBO = 128 and SBO = 16 * K is also the MN-major view of its transpose with
+// SBO' = 128 and LBO' = 16 * K: weights serve the forward (B K-major) and the data gradient (B MN-major), and
+// activations serve the forward (A K-major) and the weight gradient (A / B MN-major, reduction over rows).
+#pragma once
+
+#include <cstdint>
+
+namespace fgs {
+namespace tc {
+
+__device__ inline uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// byte offset of element (r, k) in a K-major buffer with K columns (LBO = 128, SBO = 16 * K)
+__host__ __device__ constexpr uint32_t kmajor_offset(uint32_t r, uint32_t k, uint32_t K) {
+    return (r >> 3) * (16u * K) + (k >> 3) * 128u + (r & 7u) * 16u + (k & 7u) * 2u;
+}
+
+// shared-memory matrix descriptor (no swizzle): start address, leading and stride byte offsets, version 1
+__device__ inline uint64_t desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator, operand majors (0 = K, 1 = MN), M x N
+__host__ __device__ constexpr uint32_t idesc(uint32_t M, uint32_t N, uint32_t a_mn, uint32_t b_mn) {
+    return (1u << 4) | (a_mn << 15) | (b_mn << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[desc] * B[desc]; issued by a single thread
+__device__ inline void mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(id), "r"(accumulate)
+        : "memory");
+}
+
+// arrive once on the mbarrier when every MMA this thread issued before has completed
+__device__ inline void commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ inline void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait for the phase with the given parity to complete; false when the bound ran out
+__device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t it = 0; it < (1u << 20); it++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// TMEM allocation (whole warp): the base address is written to *dst
+__device__ inline void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ inline void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ inline void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ inline void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// generic-proxy shared-memory writes become visible to the tensor core's operand reads
+__device__ inline void fence_smem_to_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes (lane = thread), completed before returning
+__device__ inline void ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+          "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// TMEM address of (lane, column)
+__device__ inline uint32_t taddr(uint32_t base, uint32_t lane, uint32_t col) { return base + (lane << 16) + col; }
+
+}  // namespace tc
+}  // namespace fgs

@@ -189,6 +189,13 @@ int fgs_loss_workspace_bytes(int channels, int height, int width, size_t* out);
 int fgs_l1_dssim(const float* image, const float* target, int channels, int height, int width, float l1_weight, float dssim_weight,
                  float* grad_image, float* loss, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Diagnostics (no reference counterpart): runs three small tensor-core (tcgen05) GEMMs on the current device, one
+ * per operand orientation the neural MLP kernels use, and compares them exactly with host results; *mismatches
+ * receives the number of differing elements (0 = pass). `scratch` is a device buffer of FGS_TC_SELFTEST_FLOATS
+ * floats. Synchronises the stream. */
+#define FGS_TC_SELFTEST_FLOATS 14400
+int fgs_tc_selftest(float* scratch, int* mismatches, void* stream);
+
 /* Optional per-stage timing: while enabled, every stage above records a CUDA event pair on its stream;
  * fgs_profile_collect waits for them, returns the summed milliseconds per stage since the last collect
  * (names comma-separated in `names`) and resets the totals. No counterpart in the reference, which has

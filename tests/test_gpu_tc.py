@@ -1,0 +1,16 @@
+"""Tensor-core (tcgen05) building blocks of the neural MLP kernels: descriptors, operand majors, M = 64 / 128
+accumulator layouts and accumulation, checked exactly against host results (fgs_tc_selftest)."""
+import ctypes
+
+import pytest
+import torch
+
+from FasterGSVDACudaBackend import _lib
+
+
+@pytest.mark.gpu
+def test_tcgen05_selftest(cuda):
+    scratch = torch.zeros(14400, dtype=torch.float32, device=cuda)
+    bad = ctypes.c_int(-1)
+    _lib.check(_lib.lib.fgs_tc_selftest(scratch.data_ptr(), ctypes.byref(bad), torch.cuda.current_stream().cuda_stream))
+    assert bad.value == 0
