@@ -67,6 +67,12 @@ cudaError_t launch_l1_dssim(const float* image, const float* target, int C, int 
                             float* loss, void* ws, cudaStream_t s);
 
 // neural_tc.cu
+bool tc_mlp_supported(const AppearanceConfig& A);  // 64-wide MLP with hidden layers: the tcgen05 kernels apply
+size_t tc_mlp_smem_bytes(const AppearanceConfig& A);  // their largest dynamic shared memory (0 when unsupported)
+cudaError_t launch_tc_color(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis_idx, uint32_t n_visible,
+                            Record* rec, cudaStream_t s);
+cudaError_t launch_tc_backward(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis_idx, uint32_t n_visible,
+                               const uint32_t* rank_of, const Record* sorted_rec, const GradRecord* grads, const GradOut& O, cudaStream_t s);
 constexpr int kTcSelftestFloats = 14400;
 constexpr int kTcSelftestStatus = 14336;
 cudaError_t tc_selftest(float* scratch, int* mismatches, cudaStream_t s);

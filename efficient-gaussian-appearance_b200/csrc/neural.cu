@@ -24,7 +24,7 @@
 
 #include <algorithm>
 #include "preprocess_bwd.cuh"
-#include "appearance.cuh"
+#include "neural_common.cuh"
 #include "launch.h"
 
 namespace fgs {
@@ -32,11 +32,6 @@ namespace fgs {
 namespace {
 
 constexpr int kBwdRows = 128;  // rows per backward CTA batch
-constexpr float kLossScale = kMlpLossScale;
-constexpr float kShC0 = 0.28209479177387814f;
-
-// value * 2^f: the octave scaling of the frequency encoding (exact, so equal to scalbnf for every input)
-__device__ inline float octave(float value, int f) { return f == 0 ? value : value * static_cast<float>(1 << f); }
 
 __device__ inline uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -54,33 +49,6 @@ __device__ inline void mma16816(float c[4], const uint32_t a[4], uint32_t b0, ui
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};\n"
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// MLP geometry of one configuration (all widths multiples of 16)
-struct MlpShape {
-    int kin;        // padded input width
-    int nn;         // hidden width
-    int layers;     // n_hidden + 1 matmuls
-    int w_off[10];  // offset of each layer in the flat weight vector
-    int w_rows[10]; // output rows of each layer (nn, ..., 16)
-    int w_cols[10]; // input columns of each layer (kin, nn, ...)
-    int n_params;
-};
-
-__host__ __device__ inline MlpShape mlp_shape(const AppearanceConfig& A) {
-    MlpShape s;
-    s.kin = A.n_input_pad;
-    s.nn = A.n_neurons;
-    s.layers = A.n_hidden + 1;
-    int off = 0;
-    for (int l = 0; l < s.layers; l++) {
-        s.w_off[l] = off;
-        s.w_cols[l] = l == 0 ? s.kin : s.nn;
-        s.w_rows[l] = l == s.layers - 1 ? 16 : s.nn;
-        off += s.w_rows[l] * s.w_cols[l];
-    }
-    s.n_params = off;
-    return s;
 }
 
 // half-precision weight matrices in shared memory: layer l at offset sw_off[l] (halves), row stride cols + 8
@@ -142,83 +110,6 @@ __device__ inline void layer_forward(const __half* in, int ld_in, int K, const _
         }
 }
 
-// SH band values of the MLP's direction input (bands 0..3 selected by mask; band l >= 1 is zero unless it is among
-// the first `deg` selected bands), passed to out(k, value) in input order; returns the number written
-template <typename Out>
-__device__ inline int sh_band_values(int mask, int deg, f3 d, Out&& out) {
-    const float x = d.x, y = d.y, z = d.z;
-    const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z;
-    int o = 0, rank = 0;
-    if (mask & 1) out(o++, kShC0);
-    if (mask & 2) {
-        const float m = rank++ < deg ? 1.0f : 0.0f;
-        out(o++, m * (-kShC1 * y));
-        out(o++, m * (kShC1 * z));
-        out(o++, m * (-kShC1 * x));
-    }
-    if (mask & 4) {
-        const float m = rank++ < deg ? 1.0f : 0.0f;
-        out(o++, m * (kShC2a * xy));
-        out(o++, m * (-kShC2a * yz));
-        out(o++, m * (kShC2b * zz - kShC2c));
-        out(o++, m * (-kShC2a * xz));
-        out(o++, m * (kShC2d * xx - kShC2d * yy));
-    }
-    if (mask & 8) {
-        const float m = rank++ < deg ? 1.0f : 0.0f;
-        out(o++, m * (0.59004358992664352f * y * (-3.0f * xx + yy)));
-        out(o++, m * (2.8906114426405538f * xy * z));
-        out(o++, m * (0.45704579946446572f * y * (1.0f - 5.0f * zz)));
-        out(o++, m * (0.3731763325901154f * z * (5.0f * zz - 3.0f)));
-        out(o++, m * (0.45704579946446572f * x * (1.0f - 5.0f * zz)));
-        out(o++, m * (1.4453057213202769f * z * (xx - yy)));
-        out(o++, m * (0.59004358992664352f * x * (-xx + 3.0f * yy)));
-    }
-    return o;
-}
-
-// gradient of sum_k g[k] * band_k(d) with respect to the unit direction
-__device__ inline f3 sh_band_grad(int mask, int deg, f3 d, const float* g) {
-    const float x = d.x, y = d.y, z = d.z;
-    const float xx = x * x, yy = y * y, zz = z * z;
-    f3 r = mk3(0.0f, 0.0f, 0.0f);
-    int o = 0, rank = 0;
-    if (mask & 1) o++;
-    if (mask & 2) {
-        if (rank++ < deg) {
-            r.y += -kShC1 * g[o];
-            r.z += kShC1 * g[o + 1];
-            r.x += -kShC1 * g[o + 2];
-        }
-        o += 3;
-    }
-    if (mask & 4) {
-        if (rank++ < deg) {
-            r = r + g[o] * mk3(kShC2a * y, kShC2a * x, 0.0f);
-            r = r + g[o + 1] * mk3(0.0f, -kShC2a * z, -kShC2a * y);
-            r = r + g[o + 2] * mk3(0.0f, 0.0f, 2.0f * kShC2b * z);
-            r = r + g[o + 3] * mk3(-kShC2a * z, 0.0f, -kShC2a * x);
-            r = r + g[o + 4] * mk3(2.0f * kShC2d * x, -2.0f * kShC2d * y, 0.0f);
-        }
-        o += 5;
-    }
-    if (mask & 8) {
-        if (rank++ < deg) {
-            const float A = 0.59004358992664352f, B = 2.8906114426405538f, C = 0.45704579946446572f;
-            const float D = 0.3731763325901154f, E = 1.4453057213202769f;
-            r = r + g[o] * mk3(-6.0f * A * x * y, A * (3.0f * yy - 3.0f * xx), 0.0f);
-            r = r + g[o + 1] * mk3(B * y * z, B * x * z, B * x * y);
-            r = r + g[o + 2] * mk3(0.0f, C * (1.0f - 5.0f * zz), -10.0f * C * y * z);
-            r = r + g[o + 3] * mk3(0.0f, 0.0f, D * (15.0f * zz - 3.0f));
-            r = r + g[o + 4] * mk3(C * (1.0f - 5.0f * zz), 0.0f, -10.0f * C * x * z);
-            r = r + g[o + 5] * mk3(2.0f * E * x * z, -2.0f * E * y * z, E * (xx - yy));
-            r = r + g[o + 6] * mk3(A * (3.0f * yy - 3.0f * xx), 6.0f * A * x * y, 0.0f);
-        }
-        o += 7;
-    }
-    return r;
-}
-
 // writes this thread's MLP input row (fp16): encoded features, SH band values, padding ones
 __device__ inline void assemble_inputs(const Params& P, const AppearanceConfig& A, uint32_t i, bool valid, f3 d, int deg, __half* row) {
     if (!valid) {  // all-zero row: finite activations, no contribution to the weight gradient
@@ -246,13 +137,6 @@ __device__ inline void assemble_inputs(const Params& P, const AppearanceConfig& 
     for (; o < A.n_input_pad; o++) row[o] = __float2half_rn(1.0f);
 }
 
-__device__ inline f3 view_dir(const View& v, f3 m, float* rn_out) {
-    const f3 cam = mk3(v.cam_pos[0], v.cam_pos[1], v.cam_pos[2]);
-    const f3 dv = m - cam;
-    const float rn = rnorm3(dv);
-    if (rn_out) *rn_out = rn;
-    return rn * dv;
-}
 
 // runs the MLP for the warp's rows [row0, row0 + 16 * MT); buffers: bufA holds the input on entry; returns the
 // buffer (and its stride) that holds the 16 outputs
@@ -535,8 +419,6 @@ __device__ inline void layer_backward_weights(const __half* dout, int ld_dout, i
     }
 }
 
-__device__ inline void put1(float* p, size_t k, float v, int acc) { if (acc) p[k] += v; else p[k] = v; }
-__device__ inline void put3n(float* p, uint32_t i, f3 v, int acc) { put1(p, 3ull * i, v.x, acc); put1(p, 3ull * i + 1, v.y, acc); put1(p, 3ull * i + 2, v.z, acc); }
 
 struct NeuralBwdSmem {
     int soff[10];
@@ -977,6 +859,30 @@ __global__ void __launch_bounds__(256) neural_geometry_bwd_kernel(Params P, View
     put3n(O.means, i, gmean, 1);
 }
 
+// backward of a view rendered at appearance degree 0 (the MLP is not evaluated, the residual is zero): base-colour
+// gradients of the visible rows; features and the view-direction part of the mean gradient are zero
+__global__ void __launch_bounds__(256) neural_base_bwd_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
+                                                              const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec,
+                                                              const GradRecord* __restrict__ grads, GradOut O) {
+    const uint32_t gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= n_rows) return;
+    const uint32_t i = vis[gi];
+    const uint32_t r = rank_of[i];
+    const float4 q2 = sorted_rec[r].q2, g1 = grads[r].g1;
+    const f3 gp = mk3(g1.y, g1.z, g1.w) * mk3(color_act_grad_from_y(A.color_act, q2.x), color_act_grad_from_y(A.color_act, q2.y),
+                                               color_act_grad_from_y(A.color_act, q2.z));
+    f3 gbase = mk3(0.0f, 0.0f, 0.0f);
+    if (v.render_base) {
+        const f3 bb = ld3(P.base, i);
+        gbase = mk3(base_act_grad(A.base_act, bb.x), base_act_grad(A.base_act, bb.y), base_act_grad(A.base_act, bb.z)) * gp;
+    }
+    put3n(O.base, i, gbase, O.accumulate);
+    if (!O.accumulate) {
+        put3n(O.means, i, mk3(0.0f, 0.0f, 0.0f), 0);
+        for (int j = 0; j < A.feature_dim; j++) O.residual[static_cast<size_t>(i) * A.feature_dim + j] = 0.0f;
+    }
+}
+
 // zero gradients of the primitives outside the view (overwrite mode of the visible-row backward); one thread per
 // primitive; vec4 bit 0: feature rows 16-byte aligned, bit 1: rotation rows 16-byte aligned (16-byte stores)
 __global__ void zero_invisible_kernel(const uint32_t* __restrict__ rank_of, uint32_t n, int F, int vec4, GradOut O) {
@@ -1033,6 +939,7 @@ cudaError_t launch_persistent(K kernel, size_t smem, int threads, uint32_t n_chu
 cudaError_t launch_neural_color(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis, uint32_t n_visible, Record* rec,
                                 cudaStream_t st) {
     if (n_visible == 0 || std::min(v.degree, A.max_degree) <= 0) return cudaSuccess;
+    if (tc_mlp_supported(A)) return launch_tc_color(P, A, v, vis, n_visible, rec, st);
     int warps = 8;
     while (warps > 1 && color_smem_bytes(A, warps) > kSmemLimit) warps >>= 1;
     const size_t smem = color_smem_bytes(A, warps);
@@ -1088,12 +995,25 @@ cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig
         cudaError_t e = cudaMemsetAsync(O.mlp, 0, static_cast<size_t>(A.n_params) * sizeof(float), st);
         if (e != cudaSuccess) return e;
     }
+    if (std::min(v.degree, A.max_degree) <= 0) {
+        if (!O.accumulate) {
+            const int blocks = std::max(1, std::min(static_cast<int>((P.n + 255) / 256), sm_count() * 8));
+            const int vec4 = ((A.feature_dim % 4 == 0 && reinterpret_cast<uintptr_t>(O.residual) % 16 == 0) ? 1 : 0) |
+                             (reinterpret_cast<uintptr_t>(O.rotations) % 16 == 0 ? 2 : 0);
+            zero_invisible_kernel<<<blocks, 256, 0, st>>>(rank_of, P.n, A.feature_dim, vec4, O);
+        }
+        if (n_visible > 0) {
+            neural_base_bwd_kernel<<<(n_visible + 255) / 256, 256, 0, st>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O);
+            neural_geometry_bwd_kernel<<<(n_visible + 255) / 256, 256, 0, st>>>(P, v, vis, n_visible, rank_of, sorted_rec, grads, O);
+        }
+        return cudaGetLastError();
+    }
     const MlpShape s = mlp_shape(A);
     const FastBwdLayout FL = fast_bwd_layout(s);
     const int n_tiles = FL.tb[s.layers];
     const size_t fast_smem = FL.total;
-    const bool fast = std::min(v.degree, A.max_degree) > 0 && n_tiles <= kFastWarps * kMaxTilesPerWarp &&
-                      fast_smem + kBwdRows * 3 * sizeof(float) <= kSmemLimit;
+    const bool fast = tc_mlp_supported(A) ||
+                      (n_tiles <= kFastWarps * kMaxTilesPerWarp && fast_smem + kBwdRows * 3 * sizeof(float) <= kSmemLimit);
     if (fast) {
         if (!O.accumulate) {
             const int blocks = std::max(1, std::min(static_cast<int>((P.n + 255) / 256), sm_count() * 8));
@@ -1104,6 +1024,12 @@ cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig
             if (e != cudaSuccess) return e;
         }
         if (n_visible == 0) return cudaSuccess;
+        if (tc_mlp_supported(A)) {
+            cudaError_t e = launch_tc_backward(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, st);
+            if (e != cudaSuccess) return e;
+            neural_geometry_bwd_kernel<<<(n_visible + 255) / 256, 256, 0, st>>>(P, v, vis, n_visible, rank_of, sorted_rec, grads, O);
+            return cudaGetLastError();
+        }
         const int per_warp = (n_tiles + kFastWarps - 1) / kFastWarps;
         const int T = per_warp <= 2 ? 2 : (per_warp <= 3 ? 3 : (per_warp <= 5 ? 5 : 8));
         switch (A.n_neurons) {
@@ -1131,6 +1057,7 @@ cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig
 size_t neural_grad_scratch_floats(const AppearanceConfig& A) { return static_cast<size_t>(A.n_params); }
 
 size_t neural_smem_bytes(const AppearanceConfig& A) {
+    if (tc_mlp_supported(A)) return tc_mlp_smem_bytes(A);
     const size_t b = neural_bwd_layout(mlp_shape(A)).total, f = color_smem_bytes(A, 1);
     return b > f ? b : f;
 }

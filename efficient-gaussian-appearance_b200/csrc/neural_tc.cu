@@ -1,5 +1,16 @@
 // Neural appearance MLP on the sm_100a tensor cores (tcgen05 + TMEM); see tc.cuh for the operand layouts.
 //
+// Semantics as in neural.cu (appearance_neural.cuh:10-407 of the reference: encoding, SH inputs, fp16 network
+// without biases, loss scale 128 in the backward). Design: one CTA of 128 threads handles tiles of 128 visible
+// rows, thread t owning row t of the tile (the 32x32b TMEM load gives each thread its row). Per layer one thread
+// issues the K/16 MMAs (M = 128 rows, N = layer width, fp16 operands from shared memory in the canonical layouts,
+// fp32 accumulator in TMEM) and commits them to an mbarrier; the threads read their row from TMEM, apply the
+// activation, round to fp16 and store the next layer's operand. The backward issues, per layer, the data-gradient
+// MMAs (into the layer accumulator) and the weight-gradient MMAs (M = 64, reduction over the tile's rows) into
+// TMEM accumulators that persist over every tile the CTA processes; they are read out and added to the weight
+// gradient once per CTA. Hidden gradients overwrite their activations in place after the MMAs that read them
+// completed. Used for 64-wide networks with at least one hidden layer (neural.cu keeps the other shapes).
+//
 // This file also holds the tensor-core self-test behind fgs_tc_selftest: three small GEMMs covering every operand
 // orientation the MLP kernels use (forward: A and B K-major; data gradient: B MN-major; weight gradient: M = 64,
 // A and B MN-major, accumulated over two passes), checked exactly on the host.
@@ -9,6 +20,7 @@
 #include <vector>
 
 #include "launch.h"
+#include "neural_common.cuh"
 #include "tc.cuh"
 
 namespace fgs {
@@ -115,6 +127,596 @@ cudaError_t tc_selftest(float* scratch, int* mismatches, cudaStream_t s) {
         }
     *mismatches = bad;
     return cudaSuccess;
+}
+
+
+// ---------------------------------------------------------------------------------------------------
+// MLP on tcgen05
+
+namespace {
+
+constexpr int kTcRows = 128;
+constexpr int kTcWidth = 64;
+constexpr int kTcMaxLayers = 8;
+
+// one MLP configuration laid out for the tensor-core kernels
+struct TcPlan {
+    int layers, kin, backward;
+    int rows[kTcMaxLayers], cols[kTcMaxLayers];  // W_l is rows x cols (out x in)
+    uint32_t w_off[kTcMaxLayers];                // flat fp32 weight offsets
+    uint32_t w_smem[kTcMaxLayers];               // fp16 K-major copies (bytes into dynamic shared memory)
+    uint32_t x_smem, h_smem, y_smem, smem_bytes;
+    int h_slots;                                 // activation buffers: 1 (forward, rewritten in place) or layers - 1
+    uint32_t wg_col[kTcMaxLayers];               // TMEM column of each layer's weight-gradient accumulator
+    uint32_t tmem_cols;                          // allocated TMEM columns (power of two)
+};
+
+__device__ __forceinline__ uint32_t h_slot(const TcPlan& p, int j) { return p.h_smem + static_cast<uint32_t>(j % p.h_slots) * (kTcRows * kTcWidth * 2); }
+
+__device__ inline void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ inline uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+__device__ inline uint32_t pack2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ inline float2 unpack2(uint32_t w) {
+    const __half2 h = *reinterpret_cast<const __half2*>(&w);
+    return __half22float2(h);
+}
+
+// fp32 master weights -> fp16 K-major copies in shared memory
+__device__ inline void stage_weights_tc(const TcPlan& p, const float* __restrict__ w, unsigned char* smem) {
+    for (int l = 0; l < p.layers; l++) {
+        const int rows = p.rows[l], cols = p.cols[l];
+        __half* dst = reinterpret_cast<__half*>(smem + p.w_smem[l]);
+        for (int e = threadIdx.x; e < rows * cols; e += blockDim.x) {
+            const int r = e / cols, c = e - r * cols;
+            dst[tc::kmajor_offset(r, c, cols) / 2] = __float2half_rn(w[p.w_off[l] + e]);
+        }
+    }
+}
+
+// collects fp16 values in input order and stores them 8 at a time (16 bytes) into a K-major row
+struct RowWriter {
+    uint32_t base;  // shared address of element (row, 0)
+    int K, chunk = 0, fill = 0;
+    uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+    __device__ void push(float v) {
+        const uint32_t h = __half_as_ushort(__float2half_rn(v));
+        w0 = (w0 >> 16) | (w1 << 16);
+        w1 = (w1 >> 16) | (w2 << 16);
+        w2 = (w2 >> 16) | (w3 << 16);
+        w3 = (w3 >> 16) | (h << 16);
+        if (++fill == 8) {
+            st_shared_v4(base + chunk * 128, w0, w1, w2, w3);
+            chunk++;
+            fill = 0;
+        }
+    }
+    __device__ void push8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {  // at a chunk boundary
+        st_shared_v4(base + chunk * 128, a, b, c, d);
+        chunk++;
+    }
+};
+
+__device__ inline bool fast_features(const Params& P, const AppearanceConfig& A) {
+    return A.n_freq == 1 && A.feature_dim % 8 == 0 && (reinterpret_cast<uintptr_t>(P.residual) & 15u) == 0;
+}
+
+// the MLP input row of primitive i (thread t's row of the tile): encoded features, SH inputs, padding ones
+__device__ inline void write_input_row(const Params& P, const AppearanceConfig& A, const View& v, int deg, uint32_t i, bool valid,
+                                       uint32_t row_base, int kin) {
+    RowWriter w{row_base, kin};
+    if (!valid) {
+        for (int c = 0; c < kin; c += 8) w.push8(0u, 0u, 0u, 0u);
+        return;
+    }
+    const int F = A.feature_dim, nf = A.n_freq;
+    const float* feat = P.residual + static_cast<size_t>(i) * F;
+    int j0 = 0;
+    if (fast_features(P, A)) {  // 4 features = 8 encoded columns per 16-byte load and store
+        for (; j0 < F; j0 += 4) {
+            const float4 q = *reinterpret_cast<const float4*>(feat + j0);
+            float s0, c0, s1, c1, s2, c2, s3, c3;
+            sincosf(q.x, &s0, &c0);
+            sincosf(q.y, &s1, &c1);
+            sincosf(q.z, &s2, &c2);
+            sincosf(q.w, &s3, &c3);
+            w.push8(pack2(s0, c0), pack2(s1, c1), pack2(s2, c2), pack2(s3, c3));
+        }
+    }
+    const int nraw = F + (A.base_input ? 3 : 0);
+    for (int j = j0; j < nraw; j++) {
+        const float val = j < F ? feat[j] : P.base[3ull * i + (j - F)];
+        if (nf == 0) {
+            w.push(val);
+        } else {
+            for (int f = 0; f < nf; f++) {
+                float sn, cs;
+                sincosf(octave(val, f), &sn, &cs);
+                w.push(sn);
+                w.push(cs);
+            }
+        }
+    }
+    const f3 d = view_dir(v, ld3(P.means, i), nullptr);
+    const int nsh = sh_band_values(A.sh_mask, deg, d, [&](int, float val) { w.push(val); });
+    for (int c = nraw * (nf > 0 ? 2 * nf : 1) + nsh; c < kin; c++) w.push(1.0f);
+}
+
+// forward MMAs of layer l for the whole tile into the layer accumulator (TMEM columns 0..)
+__device__ inline void issue_forward(const TcPlan& p, uint32_t sbase, uint32_t tb, int l) {
+    const uint32_t in = sbase + (l == 0 ? p.x_smem : h_slot(p, l - 1));
+    const uint32_t K = p.cols[l], sbo = 16u * K, w = sbase + p.w_smem[l];
+    const uint32_t id = tc::idesc(128, p.rows[l], 0, 0);
+    for (uint32_t ks = 0; ks < K / 16; ks++) tc::mma(tb, tc::desc(in + ks * 256, 128, sbo), tc::desc(w + ks * 256, 128, sbo), id, ks > 0);
+}
+
+// hidden-layer epilogue: row t of the accumulator -> activation -> fp16 K-major row of the slot
+__device__ inline void hidden_epilogue(uint32_t t_addr, uint32_t row_base, bool relu) {
+    float a[16];
+#pragma unroll 1
+    for (int c0 = 0; c0 < kTcWidth; c0 += 16) {
+        tc::ld16(t_addr + c0, a);
+        if (relu)
+#pragma unroll
+            for (int k = 0; k < 16; k++) a[k] = fmaxf(a[k], 0.0f);
+        st_shared_v4(row_base + (c0 / 8) * 128, pack2(a[0], a[1]), pack2(a[2], a[3]), pack2(a[4], a[5]), pack2(a[6], a[7]));
+        st_shared_v4(row_base + (c0 / 8 + 1) * 128, pack2(a[8], a[9]), pack2(a[10], a[11]), pack2(a[12], a[13]), pack2(a[14], a[15]));
+    }
+}
+
+// bounded wait on the tile's mbarrier; flips the parity
+__device__ inline bool wait_mma(uint64_t* bar, uint32_t& phase) {
+    const bool ok = tc::mbar_wait(bar, phase);
+    phase ^= 1u;
+    return ok;
+}
+
+// every thread waits for the committed MMAs; the CTA agrees on the outcome (true: completed) and orders the
+// following TMEM reads after the wait
+__device__ inline bool wait_all(uint64_t* bar, uint32_t& phase) {
+    const bool ok = wait_mma(bar, phase);
+    const bool any_failed = __syncthreads_or(!ok) != 0;
+    tc::fence_after_sync();
+    return !any_failed;
+}
+
+__device__ inline void sync_tile() {
+    tc::fence_smem_to_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+}
+
+__device__ int g_tc_timeout;  // set when an mbarrier wait ran out (the kernel then stops issuing work)
+
+__global__ void __launch_bounds__(kTcRows) tc_color_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
+                                                           Record* __restrict__ rec, const __grid_constant__ TcPlan plan) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    __shared__ uint32_t tbase;
+    const int t = threadIdx.x, warp = t >> 5;
+    stage_weights_tc(plan, P.mlp, smem);
+    if (warp == 0) tc::tmem_alloc(&tbase, plan.tmem_cols);
+    if (t == 0) tc::mbar_init(&bar, 1);
+    sync_tile();
+    bool alive = true;
+    const uint32_t tb = tbase, sbase = tc::smem_addr(smem);
+    const uint32_t t_row = tb + (static_cast<uint32_t>(warp * 32) << 16);
+    const int deg = min(v.degree, A.max_degree);
+    uint32_t phase = 0;
+    const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const uint32_t gi = tile * kTcRows + t;
+        const bool valid = gi < n_rows;
+        const uint32_t i = valid ? vis[gi] : 0u;
+        write_input_row(P, A, v, deg, i, valid, sbase + plan.x_smem + tc::kmajor_offset(t, 0, plan.kin), plan.kin);
+        sync_tile();
+        for (int l = 0; l < plan.layers; l++) {
+            if (t == 0) {
+                issue_forward(plan, sbase, tb, l);
+                tc::commit(&bar);
+            }
+            __syncwarp();
+            alive = wait_all(&bar, phase);
+            if (!alive) break;
+            if (l < plan.layers - 1) {
+                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(t, 0, kTcWidth), A.hidden_act == 1);
+            } else {
+                float y[16];
+                tc::ld16(t_row, y);  // every lane: the TMEM load is warp-collective
+                if (valid) {
+                const f3 res = residual_act3(A.res_act, mk3(__half2float(__float2half_rn(y[0])), __half2float(__float2half_rn(y[1])),
+                                                             __half2float(__float2half_rn(y[2]))));
+                const f3 base = base_act3(A.base_act, ld3(P.base, i));
+                f3 color = color_act3(A.color_act, base + res);
+                if (!v.render_base) {
+                    const f3 bc = color_act3(A.color_act, base);
+                    color = mk3(fabsf(color.x - bc.x), fabsf(color.y - bc.y), fabsf(color.z - bc.z));
+                }
+                float* q2 = reinterpret_cast<float*>(rec + i) + 8;
+                q2[0] = color.x;
+                q2[1] = color.y;
+                q2[2] = color.z;
+                }
+            }
+            sync_tile();
+        }
+        if (!alive) break;
+    }
+    if (!alive) {
+        tc::mbar_wait(&bar, phase ^ 1u);  // the timed-out MMAs must not be in flight when the columns are freed
+        if (t == 0) atomicExch(&g_tc_timeout, 1);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tb, plan.tmem_cols);
+}
+
+// feature / base-input / direction gradients of one row from the loss-scaled input gradient in TMEM (columns 0..kin)
+__device__ inline void input_grad_row(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t t_row, uint32_t i, bool valid,
+                                      int kin, int deg, f3 d, f3& gbase_in, f3& gdir) {
+    const float inv = 1.0f / kLossScale;
+    const int F = A.feature_dim, nf = A.n_freq, per = nf > 0 ? 2 * nf : 1, nraw = F + (A.base_input ? 3 : 0);
+    const int enc = nraw * per;
+    int nsh = 0;
+    for (int l = 0; l <= 3; l++)
+        if (A.sh_mask & (1 << l)) nsh += 2 * l + 1;
+    const float* feat = P.residual + static_cast<size_t>(i) * F;
+    float* gout = O.residual + static_cast<size_t>(i) * F;
+    const int acc = O.accumulate;
+    float g[16];
+    int c = 0;
+    if (fast_features(P, A)) {  // 16 columns = 8 features per TMEM load; 16-byte loads and stores
+        for (; c < 2 * F; c += 16) {
+            tc::ld16(t_row + c, g);
+            if (!valid) continue;
+            const int j = c / 2;
+            const float4 v0 = *reinterpret_cast<const float4*>(feat + j), v1 = *reinterpret_cast<const float4*>(feat + j + 4);
+            const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+            float gv[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                float sn, cs;
+                sincosf(vv[k], &sn, &cs);
+                gv[k] = (cs * g[2 * k] - sn * g[2 * k + 1]) * inv;
+            }
+            float4 o0 = make_float4(gv[0], gv[1], gv[2], gv[3]), o1 = make_float4(gv[4], gv[5], gv[6], gv[7]);
+            if (acc) {
+                const float4 a0 = *reinterpret_cast<const float4*>(gout + j), a1 = *reinterpret_cast<const float4*>(gout + j + 4);
+                o0 = make_float4(a0.x + o0.x, a0.y + o0.y, a0.z + o0.z, a0.w + o0.w);
+                o1 = make_float4(a1.x + o1.x, a1.y + o1.y, a1.z + o1.z, a1.w + o1.w);
+            }
+            *reinterpret_cast<float4*>(gout + j) = o0;
+            *reinterpret_cast<float4*>(gout + j + 4) = o1;
+        }
+    }
+    // remaining columns in order: encoded inputs (feature j, octave f, sin then cos), SH inputs, padding
+    int j = c / per, q = c - j * per;
+    float val = 0.0f, gacc = 0.0f, sn = 0.0f, cs = 0.0f, g_even = 0.0f;
+    float gsh[16];
+    float gb[3] = {0.0f, 0.0f, 0.0f};
+    for (int c0 = c & ~15; c0 < kin; c0 += 16) {
+        tc::ld16(t_row + c0, g);
+        if (!valid) continue;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const int col = c0 + k;
+            if (col < c) continue;
+            if (col < enc) {
+                if (q == 0) {
+                    val = j < F ? feat[j] : P.base[3ull * i + (j - F)];
+                    gacc = 0.0f;
+                }
+                if (nf == 0) {
+                    gacc = g[k];
+                } else {
+                    const int f = q >> 1;
+                    if ((q & 1) == 0) {
+                        sincosf(octave(val, f), &sn, &cs);
+                        g_even = g[k];
+                    } else {
+                        gacc += static_cast<float>(1 << f) * (cs * g_even - sn * g[k]);
+                    }
+                }
+                if (++q == per) {
+                    const float gv = gacc * inv;
+                    if (j < F) gout[j] = acc ? gout[j] + gv : gv;
+                    else gb[j - F] = gv;
+                    j++;
+                    q = 0;
+                }
+            } else if (col < enc + nsh) {
+                gsh[col - enc] = g[k];
+            }
+        }
+    }
+    gbase_in = mk3(gb[0], gb[1], gb[2]);
+    // direction gradient from the SH inputs' gradient, unscaled afterwards (scaling by 2^-7 is exact)
+    gdir = inv * sh_band_grad(A.sh_mask, deg, d, gsh);
+}
+
+// data-gradient epilogue of a hidden layer: dL/d(activation) of row t, masked by the ReLU of the stored activation,
+// written over that activation (fp16, in place)
+__device__ inline void hidden_grad_epilogue(uint32_t t_addr, uint32_t row_base, bool relu) {
+    float a[16];
+#pragma unroll 1
+    for (int c0 = 0; c0 < kTcWidth; c0 += 16) {
+        tc::ld16(t_addr + c0, a);
+        if (relu) {
+            const uint4 h0 = ld_shared_v4(row_base + (c0 / 8) * 128), h1 = ld_shared_v4(row_base + (c0 / 8 + 1) * 128);
+            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const float2 hv = unpack2(hw[k]);
+                if (!(hv.x > 0.0f)) a[2 * k] = 0.0f;
+                if (!(hv.y > 0.0f)) a[2 * k + 1] = 0.0f;
+            }
+        }
+        st_shared_v4(row_base + (c0 / 8) * 128, pack2(a[0], a[1]), pack2(a[2], a[3]), pack2(a[4], a[5]), pack2(a[6], a[7]));
+        st_shared_v4(row_base + (c0 / 8 + 1) * 128, pack2(a[8], a[9]), pack2(a[10], a[11]), pack2(a[12], a[13]), pack2(a[14], a[15]));
+    }
+}
+
+// backward MMAs of layer l: weight gradient (M = 64, accumulated in TMEM) and data gradient (layer accumulator)
+__device__ inline void issue_backward(const TcPlan& p, uint32_t sbase, uint32_t tb, int l, bool wg_accumulate) {
+    const int last = p.layers - 1;
+    const uint32_t in = sbase + (l == 0 ? p.x_smem : h_slot(p, l - 1));
+    const uint32_t K = p.cols[l], in_row_group = 16u * K;  // bytes per 8 rows of the layer input
+    const uint32_t dout = sbase + (l == last ? p.y_smem : h_slot(p, l));
+    const uint32_t R = p.rows[l], dout_row_group = 16u * R;
+    const uint32_t w = sbase + p.w_smem[l];
+    const uint32_t dw = tb + p.wg_col[l];
+    if (l == last) {  // dW^T [in x out] += In^T . dOut (M = input width 64, N = 16)
+        const uint32_t id = tc::idesc(64, R, 1, 1);
+        for (uint32_t ks = 0; ks < kTcRows / 16; ks++)
+            tc::mma(dw, tc::desc(in + ks * 2 * in_row_group, in_row_group, 128), tc::desc(dout + ks * 2 * dout_row_group, dout_row_group, 128), id,
+                    (wg_accumulate || ks > 0) ? 1u : 0u);
+    } else {  // dW [out x in] += dOut^T . In (M = 64 outputs, N = input width)
+        const uint32_t id = tc::idesc(64, K, 1, 1);
+        for (uint32_t ks = 0; ks < kTcRows / 16; ks++)
+            tc::mma(dw, tc::desc(dout + ks * 2 * dout_row_group, dout_row_group, 128), tc::desc(in + ks * 2 * in_row_group, in_row_group, 128), id,
+                    (wg_accumulate || ks > 0) ? 1u : 0u);
+    }
+    // dIn [rows x in] = dOut . W (B = W read MN-major: N = inputs, K = outputs)
+    const uint32_t id = tc::idesc(128, K, 0, 1);
+    for (uint32_t ks = 0; ks < R / 16; ks++)
+        tc::mma(tb, tc::desc(dout + ks * 256, 128, dout_row_group), tc::desc(w + ks * 2 * in_row_group, in_row_group, 128), id, ks > 0);
+}
+
+__global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
+                                                         const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec,
+                                                         const GradRecord* __restrict__ grads, GradOut O, const __grid_constant__ TcPlan plan) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    __shared__ uint32_t tbase;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    stage_weights_tc(plan, P.mlp, smem);
+    if (warp == 0) tc::tmem_alloc(&tbase, plan.tmem_cols);
+    if (t == 0) tc::mbar_init(&bar, 1);
+    sync_tile();
+    bool alive = true;
+    const uint32_t tb = tbase, sbase = tc::smem_addr(smem);
+    const uint32_t t_row = tb + (static_cast<uint32_t>(warp * 32) << 16);
+    const int deg = min(v.degree, A.max_degree);
+    const int last = plan.layers - 1;
+    const bool relu = A.hidden_act == 1;
+    uint32_t phase = 0;
+    bool wg_started = false;
+    const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles && alive; tile += gridDim.x) {
+        const uint32_t gi = tile * kTcRows + t;
+        const bool valid = gi < n_rows;
+        const uint32_t i = valid ? vis[gi] : 0u;
+        const uint32_t r = valid ? rank_of[i] : 0u;
+        f3 gpre = mk3(0.0f, 0.0f, 0.0f);
+        if (valid) {
+            const float4 q2 = sorted_rec[r].q2, g1 = grads[r].g1;
+            gpre = mk3(g1.y, g1.z, g1.w) * mk3(color_act_grad_from_y(A.color_act, q2.x), color_act_grad_from_y(A.color_act, q2.y),
+                                               color_act_grad_from_y(A.color_act, q2.z));
+        }
+        write_input_row(P, A, v, deg, i, valid, sbase + plan.x_smem + tc::kmajor_offset(t, 0, plan.kin), plan.kin);
+        sync_tile();
+        // recomputed forward; the last layer's outputs become the scaled output gradient
+        for (int l = 0; l < plan.layers && alive; l++) {
+            if (t == 0) {
+                issue_forward(plan, sbase, tb, l);
+                tc::commit(&bar);
+            }
+            __syncwarp();
+            alive = wait_all(&bar, phase);
+            if (!alive) break;
+            if (l < last) {
+                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(t, 0, kTcWidth), relu);
+            } else {
+                float y[16];
+                tc::ld16(t_row, y);
+                float dy[3] = {0.0f, 0.0f, 0.0f};
+                if (valid) {
+                    const float gv[3] = {gpre.x, gpre.y, gpre.z};
+                    for (int c = 0; c < 3; c++) {
+                        const float yh = __half2float(__float2half_rn(y[c]));
+                        dy[c] = gv[c] * residual_act_grad_from_y(A.res_act, residual_act(A.res_act, yh));
+                    }
+                }
+                const uint32_t yrow = sbase + plan.y_smem + tc::kmajor_offset(t, 0, 16);
+                st_shared_v4(yrow, pack2(kLossScale * dy[0], kLossScale * dy[1]), pack2(kLossScale * dy[2], 0.0f), 0u, 0u);
+                st_shared_v4(yrow + 128, 0u, 0u, 0u, 0u);
+            }
+            sync_tile();
+        }
+        // layers last to first
+        for (int l = last; l >= 0 && alive; l--) {
+            if (t == 0) {
+                issue_backward(plan, sbase, tb, l, wg_started);
+                tc::commit(&bar);
+            }
+            __syncwarp();
+            alive = wait_all(&bar, phase);
+            if (!alive) break;
+            if (l > 0) {
+                hidden_grad_epilogue(t_row, sbase + h_slot(plan, l - 1) + tc::kmajor_offset(t, 0, kTcWidth), relu);
+                sync_tile();
+            }
+        }
+        if (!alive) break;
+        wg_started = true;
+        // input gradient (layer-0 data gradient, TMEM columns 0..kin) -> feature, base and direction gradients;
+        // every lane runs the TMEM loads, invalid rows skip the memory accesses
+        float rn = 1.0f;
+        const f3 d = valid ? view_dir(v, ld3(P.means, i), &rn) : mk3(0.0f, 0.0f, 1.0f);
+        f3 gbase_in, gd;
+        input_grad_row(P, A, O, t_row, i, valid, plan.kin, deg, d, gbase_in, gd);
+        if (valid) {
+            f3 gbase = mk3(0.0f, 0.0f, 0.0f);
+            if (v.render_base) {
+                const f3 bb = ld3(P.base, i);
+                gbase = mk3(base_act_grad(A.base_act, bb.x), base_act_grad(A.base_act, bb.y), base_act_grad(A.base_act, bb.z)) * gpre;
+            }
+            if (A.base_input) gbase = gbase + gbase_in;
+            put3n(O.base, i, gbase, O.accumulate);
+            const f3 gmean_color = A.dir_grad ? rn * (gd - dot3(gd, d) * d) : mk3(0.0f, 0.0f, 0.0f);
+            put3n(O.means, i, gmean_color, O.accumulate);
+        }
+        sync_tile();
+    }
+    // weight gradients: M = 64 accumulators (row m in lane (m % 16) + 32 (m / 16)), unscaled and added once per CTA
+    if (wg_started && alive) {
+        const float inv = 1.0f / kLossScale;
+        const int m = warp * 16 + lane;
+        for (int l = 0; l < plan.layers; l++) {
+            const int ncol = l == last ? plan.rows[l] : plan.cols[l];
+            for (int c0 = 0; c0 < ncol; c0 += 16) {
+                float a[16];
+                tc::ld16(t_row + plan.wg_col[l] + c0, a);
+                if (lane < 16)
+                    for (int k = 0; k < 16; k++) {
+                        const int c = c0 + k;
+                        float* dst = l == last ? O.mlp + plan.w_off[l] + c * kTcWidth + m : O.mlp + plan.w_off[l] + m * plan.cols[l] + c;
+                        atomicAdd(dst, a[k] * inv);
+                    }
+            }
+        }
+    }
+    if (!alive) {
+        tc::mbar_wait(&bar, phase ^ 1u);  // the timed-out MMAs must not be in flight when the columns are freed
+        if (t == 0) atomicExch(&g_tc_timeout, 1);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tb, plan.tmem_cols);
+}
+
+bool make_plan(const AppearanceConfig& A, bool backward, TcPlan& p) {
+    if (A.n_neurons != kTcWidth || A.n_hidden < 1 || A.n_hidden + 1 > kTcMaxLayers) return false;
+    p = TcPlan{};
+    p.layers = A.n_hidden + 1;
+    p.kin = A.n_input_pad;
+    p.backward = backward ? 1 : 0;
+    if (p.kin % 16 != 0 || p.kin > 256) return false;
+    uint32_t off = 0, w = 0;
+    for (int l = 0; l < p.layers; l++) {
+        p.cols[l] = l == 0 ? p.kin : kTcWidth;
+        p.rows[l] = l == p.layers - 1 ? 16 : kTcWidth;
+        p.w_off[l] = w;
+        w += static_cast<uint32_t>(p.rows[l] * p.cols[l]);
+        p.w_smem[l] = off;
+        off += static_cast<uint32_t>(p.rows[l] * p.cols[l]) * 2;
+    }
+    off = (off + 127) & ~127u;
+    p.x_smem = off;
+    off += kTcRows * static_cast<uint32_t>(p.kin) * 2;
+    p.h_slots = backward ? (p.layers - 1) : 1;
+    p.h_smem = off;
+    off += static_cast<uint32_t>(p.h_slots) * kTcRows * kTcWidth * 2;
+    p.y_smem = off;
+    if (backward) off += kTcRows * 16 * 2;
+    p.smem_bytes = off;
+    uint32_t cols = static_cast<uint32_t>(p.kin > kTcWidth ? p.kin : kTcWidth);
+    if (backward)
+        for (int l = 0; l < p.layers; l++) {
+            p.wg_col[l] = cols;
+            cols += static_cast<uint32_t>(l == p.layers - 1 ? p.rows[l] : p.cols[l]);
+        }
+    uint32_t alloc = 32;
+    while (alloc < cols) alloc <<= 1;
+    if (alloc > 512) return false;
+    p.tmem_cols = alloc;
+    return p.smem_bytes + 64 <= 227u * 1024u;
+}
+
+int tc_sm_count() {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+template <typename K>
+cudaError_t tc_grid(K kernel, const TcPlan& p, uint32_t n_tiles, int* grid) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem_bytes));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    // resident CTAs per SM: shared memory (228 KiB per SM, 1 KiB reserved per CTA), TMEM (512 columns per SM), threads
+    int dev = 0, smem_sm = 0;
+    cudaGetDevice(&dev);
+    e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    if (e != cudaSuccess) return e;
+    int per_sm = smem_sm / static_cast<int>(p.smem_bytes + 1024 + 256);
+    const int tmem_cap = static_cast<int>(512 / p.tmem_cols);
+    if (per_sm > tmem_cap) per_sm = tmem_cap;
+    if (per_sm > 2048 / kTcRows) per_sm = 2048 / kTcRows;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const uint32_t cap = static_cast<uint32_t>(per_sm) * static_cast<uint32_t>(tc_sm_count());
+    *grid = static_cast<int>(n_tiles < cap ? n_tiles : cap);
+    return cudaSuccess;
+}
+
+}  // namespace
+
+bool tc_mlp_supported(const AppearanceConfig& A) {
+    TcPlan p;
+    return make_plan(A, true, p) && make_plan(A, false, p);
+}
+
+size_t tc_mlp_smem_bytes(const AppearanceConfig& A) {
+    TcPlan f, b;
+    if (!make_plan(A, false, f) || !make_plan(A, true, b)) return 0;
+    return f.smem_bytes > b.smem_bytes ? f.smem_bytes : b.smem_bytes;
+}
+
+cudaError_t launch_tc_color(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis, uint32_t n_visible, Record* rec,
+                            cudaStream_t s) {
+    TcPlan p;
+    if (!make_plan(A, false, p)) return cudaErrorInvalidConfiguration;
+    if (n_visible == 0) return cudaSuccess;
+    int grid = 0;
+    cudaError_t e = tc_grid(tc_color_kernel, p, (n_visible + kTcRows - 1) / kTcRows, &grid);
+    if (e != cudaSuccess) return e;
+    tc_color_kernel<<<grid, kTcRows, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rec, p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tc_backward(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis, uint32_t n_visible,
+                               const uint32_t* rank_of, const Record* sorted_rec, const GradRecord* grads, const GradOut& O, cudaStream_t s) {
+    TcPlan p;
+    if (!make_plan(A, true, p)) return cudaErrorInvalidConfiguration;
+    if (n_visible == 0) return cudaSuccess;
+    int grid = 0;
+    cudaError_t e = tc_grid(tc_bwd_kernel, p, (n_visible + kTcRows - 1) / kTcRows, &grid);
+    if (e != cudaSuccess) return e;
+    tc_bwd_kernel<<<grid, kTcRows, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, p);
+    return cudaGetLastError();
 }
 
 }  // namespace fgs

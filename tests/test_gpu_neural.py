@@ -25,6 +25,11 @@ CONFIGS = [
     (16, 0, 32, 1, False, 'none'),
     (16, 0, 32, 3, False, 'softplus'),
     (8, 1, 16, 2, True, 'tanh'),
+    # 64-wide networks run on the tcgen05 kernels: one hidden layer and raw features, two octaves with base inputs and
+    # three hidden layers, and a feature count that is not a multiple of 8 (generic encoding path)
+    (16, 0, 64, 1, False, 'none'),
+    (8, 2, 64, 3, True, 'softplus'),
+    (12, 1, 64, 2, False, 'tanh'),
 ]
 
 
@@ -73,6 +78,93 @@ def test_neural_parity(cuda, cfg):
         ref = o['grads'][k]
         err = rel_err(t.grad.cpu().numpy().reshape(ref.shape), ref)
         assert err <= tol[k], f'{k}: relative error {err:.2e}'
+
+
+def test_neural_tensor_core_many_tiles(cuda):
+    """Enough visible rows that CTAs process several 128-row tiles and carry the weight gradient across them."""
+    import FasterGSVDACudaBackend as F
+    neural, shapes = _setup(F, 32, 1, 64, 2, False, 'tanh')
+    n, W, H = 160000, 256, 192
+    geo = S.geometry(n, seed=3)
+    prims = {**geo, **S.neural_appearance(n, feature_dim=32, layer_shapes=shapes, seed=4)}
+    cam = S.ring_cameras(4, W, H)[1]
+    settings = settings_for(F, cam, 3, cuda)
+    dev = to_dev(prims, cuda)
+    a = O.make_appearance('neural', 0, 0, 1, 1, True, neural=neural)
+    grad_image = torch.randn(3, H, W, generator=torch.Generator().manual_seed(6)) * 0.01
+    o = O.run(a, O.make_view(cam, 3), prims, grad_image=grad_image)
+    assert o['n_visible'] > 2 * 148 * 128, o['n_visible']
+    leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
+    img = F.diff_rasterize(leaves['means'], leaves['scales'], leaves['rotations'], leaves['opacities'], torch.empty(0, device=cuda), settings,
+                           base_colors=leaves['base_colors'], residual_params=leaves['residual_params'], mlp_weights=leaves['mlp_weights'])
+    img_err = np.abs(img.detach().cpu().numpy() - o['image'])
+    assert img_err.max() <= 1e-3 and img_err.mean() <= 1e-5, (img_err.max(), img_err.mean())
+    img.backward(grad_image.to(cuda))
+    for k, t in (('means', 1e-3), ('opacities', 1e-3), ('base_colors', 1e-2), ('residual_params', 1e-2), ('mlp_weights', 1e-2)):
+        ref = o['grads'][k]
+        err = rel_err(leaves[k].grad.cpu().numpy().reshape(ref.shape), ref)
+        assert err <= t, f'{k}: relative error {err:.2e}'
+
+
+def test_neural_accumulate_two_views(cuda):
+    """accumulate=True adds a second view's gradients to the first's (the data-parallel trainer's mode)."""
+    import FasterGSVDACudaBackend as F
+    from FasterGSVDACudaBackend import rasterization as R, _lib
+    neural, shapes = _setup(F, 32, 1, 64, 2, False, 'tanh')
+    n, W, H = 30000, 192, 128
+    prims = {**S.geometry(n, seed=8), **S.neural_appearance(n, feature_dim=32, layer_shapes=shapes, seed=9)}
+    dev = to_dev(prims, cuda)
+    cams = S.ring_cameras(4, W, H)
+    gimgs = [torch.randn(3, H, W, generator=torch.Generator().manual_seed(10 + k)).to(cuda) * 0.01 for k in range(2)]
+    cp = R._c_primitives(dev['means'], dev['scales'], dev['rotations'], dev['opacities'], None, dev['base_colors'], dev['residual_params'],
+                         dev['mlp_weights'])
+
+    def grads_of(views, accumulate_second):
+        out = {k: torch.zeros_like(v) for k, v in dev.items()}
+        cg = _lib.Gradients(*[out[k].data_ptr() if k in out else None for k in
+                              ('means', 'scales', 'rotations', 'opacities', 'precomputed_colors', 'base_colors', 'residual_params', 'mlp_weights')])
+        for j, (cam, gi) in enumerate(views):
+            st = R.ForwardState(R._rasterizer, cp, settings_for(F, cam, 3, cuda), cuda)
+            st.preprocess(cp)
+            image = torch.empty(3, H, W, device=cuda)
+            st.render_train(image)
+            st.backward(cp, image, gi, cg, None, accumulate=accumulate_second and j > 0)
+        torch.cuda.synchronize()
+        return out
+
+    both = grads_of([(cams[0], gimgs[0]), (cams[1], gimgs[1])], True)
+    g0 = grads_of([(cams[0], gimgs[0])], False)
+    g1 = grads_of([(cams[1], gimgs[1])], False)
+    for k in both:
+        ref = (g0[k] + g1[k]).cpu().numpy()
+        err = rel_err(both[k].cpu().numpy(), ref)
+        assert err <= 1e-5, f'{k}: relative error {err:.2e}'
+
+
+def test_neural_degree_zero_backward(cuda):
+    """A view rendered at degree 0 skips the MLP: only base colours and geometry receive gradients."""
+    import FasterGSVDACudaBackend as F
+    neural, shapes = _setup(F, 32, 1, 64, 2, False, 'tanh')
+    n, W, H = 10000, 160, 120
+    geo = S.geometry(n, seed=11)
+    geo['scales'] = geo['scales'] + 1.0
+    prims = {**geo, **S.neural_appearance(n, feature_dim=32, layer_shapes=shapes, seed=12)}
+    cam = S.ring_cameras(2, W, H)[1]
+    dev = to_dev(prims, cuda)
+    a = O.make_appearance('neural', 0, 0, 1, 1, True, neural=neural)
+    grad_image = torch.randn(3, H, W, generator=torch.Generator().manual_seed(13)) * 0.01
+    o = O.run(a, O.make_view(cam, 0), prims, grad_image=grad_image)
+    leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
+    img = F.diff_rasterize(leaves['means'], leaves['scales'], leaves['rotations'], leaves['opacities'], torch.empty(0, device=cuda),
+                           settings_for(F, cam, 0, cuda), base_colors=leaves['base_colors'], residual_params=leaves['residual_params'],
+                           mlp_weights=leaves['mlp_weights'])
+    np.testing.assert_array_equal(img.detach().cpu().numpy(), o['image'])
+    img.backward(grad_image.to(cuda))
+    for k in ('means', 'opacities', 'base_colors'):
+        ref = o['grads'][k]
+        assert rel_err(leaves[k].grad.cpu().numpy().reshape(ref.shape), ref) <= 1e-3, k
+    assert float(leaves['residual_params'].grad.abs().max()) == 0.0
+    assert leaves['mlp_weights'].grad is None or float(leaves['mlp_weights'].grad.abs().max()) == 0.0
 
 
 def test_neural_degree_zero_and_inference(cuda):
