@@ -145,7 +145,7 @@ struct TcPlan {
     int rows[kTcMaxLayers], cols[kTcMaxLayers];  // W_l is rows x cols (out x in)
     uint32_t w_off[kTcMaxLayers];                // flat fp32 weight offsets
     uint32_t w_smem[kTcMaxLayers];               // fp16 K-major copies (bytes into dynamic shared memory)
-    uint32_t x_smem, h_smem, y_smem, smem_bytes;
+    uint32_t x_smem, h_smem, y_smem, trig_smem, smem_bytes;
     int h_slots;                                 // activation buffers: 1 (forward, rewritten in place) or layers - 1
     uint32_t wg_col[kTcMaxLayers];               // TMEM column of each layer's weight-gradient accumulator
     uint32_t tmem_cols;                          // allocated TMEM columns (power of two)
@@ -209,26 +209,87 @@ __device__ inline bool fast_features(const Params& P, const AppearanceConfig& A)
     return A.n_freq == 1 && A.feature_dim % 8 == 0 && (reinterpret_cast<uintptr_t>(P.residual) & 15u) == 0;
 }
 
-// the MLP input row of primitive i (thread t's row of the tile): encoded features, SH inputs, padding ones
-__device__ inline void write_input_row(const Params& P, const AppearanceConfig& A, const View& v, int deg, uint32_t i, bool valid,
-                                       uint32_t row_base, int kin) {
+constexpr int kPrefetchFeatures = 32;  // rows of up to 32 latent floats are prefetched into registers
+
+// per-row inputs of a tile, loaded one tile ahead so their latency hides behind the previous tile's MMAs
+struct RowData {
+    uint32_t i, r;
+    bool valid;
+    f3 mean;
+    float4 f[kPrefetchFeatures / 4];  // latent features (fast encoding path)
+    float4 q2, g1;                    // colour of the record and its blend gradient sums (backward)
+};
+
+__device__ inline bool prefetch_features(const Params& P, const AppearanceConfig& A) {
+    return fast_features(P, A) && A.feature_dim <= kPrefetchFeatures;
+}
+
+// (backward data with rank_of non-null)
+__device__ inline void load_row(const Params& P, const AppearanceConfig& A, bool pf, const uint32_t* __restrict__ vis, uint32_t n_rows, uint32_t gi,
+                                const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec, const GradRecord* __restrict__ grads,
+                                RowData& d) {
+    d.valid = gi < n_rows;
+    d.i = d.valid ? vis[gi] : 0u;
+    if (!d.valid) return;
+    d.mean = ld3(P.means, d.i);
+    const int F = A.feature_dim;
+    if (pf) {
+        const float4* src = reinterpret_cast<const float4*>(P.residual + static_cast<size_t>(d.i) * F);
+#pragma unroll
+        for (int q = 0; q < kPrefetchFeatures / 4; q++)
+            if (4 * q < F) d.f[q] = src[q];
+    }
+    if (rank_of) {
+        d.r = rank_of[d.i];
+        d.q2 = sorted_rec[d.r].q2;
+        d.g1 = grads[d.r].g1;
+    }
+}
+
+// the MLP input row of a tile row (thread t's): encoded features, SH inputs, padding ones. With `trig` (fast path of
+// the backward) the fp32 sine and cosine of every feature are kept at trig[column * 128 + t] for the input gradient.
+__device__ inline void write_input_row(const Params& P, const AppearanceConfig& A, const View& v, int deg, const RowData& d, bool pf, uint32_t row_base,
+                                       int kin, float* trig, int t) {
     RowWriter w{row_base, kin};
-    if (!valid) {
+    if (!d.valid) {
         for (int c = 0; c < kin; c += 8) w.push8(0u, 0u, 0u, 0u);
         return;
     }
+    const uint32_t i = d.i;
     const int F = A.feature_dim, nf = A.n_freq;
     const float* feat = P.residual + static_cast<size_t>(i) * F;
     int j0 = 0;
     if (fast_features(P, A)) {  // 4 features = 8 encoded columns per 16-byte load and store
-        for (; j0 < F; j0 += 4) {
-            const float4 q = *reinterpret_cast<const float4*>(feat + j0);
+#pragma unroll
+        for (int q = 0; q < kPrefetchFeatures / 4; q++) {
+            if (4 * q >= F) break;
+            const float4 x = pf ? d.f[q] : *reinterpret_cast<const float4*>(feat + 4 * q);
             float s0, c0, s1, c1, s2, c2, s3, c3;
-            sincosf(q.x, &s0, &c0);
-            sincosf(q.y, &s1, &c1);
-            sincosf(q.z, &s2, &c2);
-            sincosf(q.w, &s3, &c3);
+            det_sincos(x.x, &s0, &c0);
+            det_sincos(x.y, &s1, &c1);
+            det_sincos(x.z, &s2, &c2);
+            det_sincos(x.w, &s3, &c3);
             w.push8(pack2(s0, c0), pack2(s1, c1), pack2(s2, c2), pack2(s3, c3));
+            if (trig) {
+                float* tq = trig + (8 * q) * kTcRows + t;
+                tq[0] = s0; tq[kTcRows] = c0; tq[2 * kTcRows] = s1; tq[3 * kTcRows] = c1;
+                tq[4 * kTcRows] = s2; tq[5 * kTcRows] = c2; tq[6 * kTcRows] = s3; tq[7 * kTcRows] = c3;
+            }
+        }
+        j0 = F;
+        for (int jq = kPrefetchFeatures; jq < F; jq += 4) {  // rows longer than the prefetch (no trig cache then)
+            const float4 x = *reinterpret_cast<const float4*>(feat + jq);
+            float s0, c0, s1, c1, s2, c2, s3, c3;
+            det_sincos(x.x, &s0, &c0);
+            det_sincos(x.y, &s1, &c1);
+            det_sincos(x.z, &s2, &c2);
+            det_sincos(x.w, &s3, &c3);
+            w.push8(pack2(s0, c0), pack2(s1, c1), pack2(s2, c2), pack2(s3, c3));
+            if (trig) {
+                float* tq = trig + (2 * jq) * kTcRows + t;
+                tq[0] = s0; tq[kTcRows] = c0; tq[2 * kTcRows] = s1; tq[3 * kTcRows] = c1;
+                tq[4 * kTcRows] = s2; tq[5 * kTcRows] = c2; tq[6 * kTcRows] = s3; tq[7 * kTcRows] = c3;
+            }
         }
     }
     const int nraw = F + (A.base_input ? 3 : 0);
@@ -239,14 +300,14 @@ __device__ inline void write_input_row(const Params& P, const AppearanceConfig& 
         } else {
             for (int f = 0; f < nf; f++) {
                 float sn, cs;
-                sincosf(octave(val, f), &sn, &cs);
+                det_sincos(octave(val, f), &sn, &cs);
                 w.push(sn);
                 w.push(cs);
             }
         }
     }
-    const f3 d = view_dir(v, ld3(P.means, i), nullptr);
-    const int nsh = sh_band_values(A.sh_mask, deg, d, [&](int, float val) { w.push(val); });
+    const f3 dir = view_dir(v, d.mean, nullptr);
+    const int nsh = sh_band_values(A.sh_mask, deg, dir, [&](int, float val) { w.push(val); });
     for (int c = nraw * (nf > 0 ? 2 * nf : 1) + nsh; c < kin; c++) w.push(1.0f);
 }
 
@@ -255,20 +316,21 @@ __device__ inline void issue_forward(const TcPlan& p, uint32_t sbase, uint32_t t
     const uint32_t in = sbase + (l == 0 ? p.x_smem : h_slot(p, l - 1));
     const uint32_t K = p.cols[l], sbo = 16u * K, w = sbase + p.w_smem[l];
     const uint32_t id = tc::idesc(128, p.rows[l], 0, 0);
-    for (uint32_t ks = 0; ks < K / 16; ks++) tc::mma(tb, tc::desc(in + ks * 256, 128, sbo), tc::desc(w + ks * 256, 128, sbo), id, ks > 0);
+    const uint64_t a = tc::desc(in, 128, sbo), b = tc::desc(w, 128, sbo);
+    for (uint32_t ks = 0; ks < K / 16; ks++) tc::mma(tb, tc::desc_advance(a, ks * 256), tc::desc_advance(b, ks * 256), id, ks > 0);
 }
 
 // hidden-layer epilogue: row t of the accumulator -> activation -> fp16 K-major row of the slot
 __device__ inline void hidden_epilogue(uint32_t t_addr, uint32_t row_base, bool relu) {
-    float a[16];
-#pragma unroll 1
-    for (int c0 = 0; c0 < kTcWidth; c0 += 16) {
-        tc::ld16(t_addr + c0, a);
+    float a[64];
+    tc::ld64(t_addr, a);
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        float* x = a + 8 * q;
         if (relu)
 #pragma unroll
-            for (int k = 0; k < 16; k++) a[k] = fmaxf(a[k], 0.0f);
-        st_shared_v4(row_base + (c0 / 8) * 128, pack2(a[0], a[1]), pack2(a[2], a[3]), pack2(a[4], a[5]), pack2(a[6], a[7]));
-        st_shared_v4(row_base + (c0 / 8 + 1) * 128, pack2(a[8], a[9]), pack2(a[10], a[11]), pack2(a[12], a[13]), pack2(a[14], a[15]));
+            for (int k = 0; k < 8; k++) x[k] = fmaxf(x[k], 0.0f);
+        st_shared_v4(row_base + q * 128, pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
     }
 }
 
@@ -313,12 +375,16 @@ __global__ void __launch_bounds__(kTcRows) tc_color_kernel(Params P, AppearanceC
     const int deg = min(v.degree, A.max_degree);
     uint32_t phase = 0;
     const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows;
+    const bool pf = prefetch_features(P, A);
+    RowData cur, nxt;
+    if (blockIdx.x < n_tiles) load_row(P, A, pf, vis, n_rows, blockIdx.x * kTcRows + t, nullptr, nullptr, nullptr, cur);
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const uint32_t gi = tile * kTcRows + t;
-        const bool valid = gi < n_rows;
-        const uint32_t i = valid ? vis[gi] : 0u;
-        write_input_row(P, A, v, deg, i, valid, sbase + plan.x_smem + tc::kmajor_offset(t, 0, plan.kin), plan.kin);
+        const bool valid = cur.valid;
+        const uint32_t i = cur.i;
+        write_input_row(P, A, v, deg, cur, pf, sbase + plan.x_smem + tc::kmajor_offset(t, 0, plan.kin), plan.kin, nullptr, t);
         sync_tile();
+        const uint32_t next = tile + gridDim.x;
+        if (next < n_tiles) load_row(P, A, pf, vis, n_rows, next * kTcRows + t, nullptr, nullptr, nullptr, nxt);
         for (int l = 0; l < plan.layers; l++) {
             if (t == 0) {
                 issue_forward(plan, sbase, tb, l);
@@ -350,6 +416,7 @@ __global__ void __launch_bounds__(kTcRows) tc_color_kernel(Params P, AppearanceC
             sync_tile();
         }
         if (!alive) break;
+        cur = nxt;
     }
     if (!alive) {
         tc::mbar_wait(&bar, phase ^ 1u);  // the timed-out MMAs must not be in flight when the columns are freed
@@ -361,12 +428,15 @@ __global__ void __launch_bounds__(kTcRows) tc_color_kernel(Params P, AppearanceC
     if (warp == 0) tc::tmem_dealloc(tb, plan.tmem_cols);
 }
 
-// feature / base-input / direction gradients of one row from the loss-scaled input gradient in TMEM (columns 0..kin)
-__device__ inline void input_grad_row(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t t_row, uint32_t i, bool valid,
-                                      int kin, int deg, f3 d, f3& gbase_in, f3& gdir) {
+// feature / base-input / direction gradients of one row from the loss-scaled input gradient in TMEM (columns 0..kin);
+// with `trig` the fast path takes the sine and cosine the encoding kept instead of evaluating them again
+__device__ inline void input_grad_row(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t t_row, const RowData& d, bool pf,
+                                      const float* trig, int t, int kin, int deg, f3 dir, f3& gbase_in, f3& gdir) {
     const float inv = 1.0f / kLossScale;
     const int F = A.feature_dim, nf = A.n_freq, per = nf > 0 ? 2 * nf : 1, nraw = F + (A.base_input ? 3 : 0);
     const int enc = nraw * per;
+    const bool valid = d.valid;
+    const uint32_t i = d.i;
     int nsh = 0;
     for (int l = 0; l <= 3; l++)
         if (A.sh_mask & (1 << l)) nsh += 2 * l + 1;
@@ -375,29 +445,58 @@ __device__ inline void input_grad_row(const Params& P, const AppearanceConfig& A
     const int acc = O.accumulate;
     float g[16];
     int c = 0;
-    if (fast_features(P, A)) {  // 16 columns = 8 features per TMEM load; 16-byte loads and stores
-        for (; c < 2 * F; c += 16) {
-            tc::ld16(t_row + c, g);
-            if (!valid) continue;
-            const int j = c / 2;
+    // 16 columns = 8 features per TMEM load; 16-byte loads and stores (every lane runs the TMEM load)
+    auto chunk = [&](int c0, float4 a0, float4 a1) {
+        tc::ld16(t_row + c0, g);
+        if (!valid) return;
+        const int j = c0 / 2;
+        float gv[8];
+        if (trig) {
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const float sn = trig[(c0 + 2 * k) * kTcRows + t], cs = trig[(c0 + 2 * k + 1) * kTcRows + t];
+                gv[k] = (cs * g[2 * k] - sn * g[2 * k + 1]) * inv;
+            }
+        } else {
             const float4 v0 = *reinterpret_cast<const float4*>(feat + j), v1 = *reinterpret_cast<const float4*>(feat + j + 4);
             const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-            float gv[8];
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 float sn, cs;
-                sincosf(vv[k], &sn, &cs);
+                det_sincos(vv[k], &sn, &cs);
                 gv[k] = (cs * g[2 * k] - sn * g[2 * k + 1]) * inv;
             }
-            float4 o0 = make_float4(gv[0], gv[1], gv[2], gv[3]), o1 = make_float4(gv[4], gv[5], gv[6], gv[7]);
-            if (acc) {
-                const float4 a0 = *reinterpret_cast<const float4*>(gout + j), a1 = *reinterpret_cast<const float4*>(gout + j + 4);
-                o0 = make_float4(a0.x + o0.x, a0.y + o0.y, a0.z + o0.z, a0.w + o0.w);
-                o1 = make_float4(a1.x + o1.x, a1.y + o1.y, a1.z + o1.z, a1.w + o1.w);
-            }
-            *reinterpret_cast<float4*>(gout + j) = o0;
-            *reinterpret_cast<float4*>(gout + j + 4) = o1;
         }
+        float4 o0 = make_float4(gv[0], gv[1], gv[2], gv[3]), o1 = make_float4(gv[4], gv[5], gv[6], gv[7]);
+        if (acc) {
+            o0 = make_float4(a0.x + o0.x, a0.y + o0.y, a0.z + o0.z, a0.w + o0.w);
+            o1 = make_float4(a1.x + o1.x, a1.y + o1.y, a1.z + o1.z, a1.w + o1.w);
+        }
+        *reinterpret_cast<float4*>(gout + j) = o0;
+        *reinterpret_cast<float4*>(gout + j + 4) = o1;
+    };
+    if (fast_features(P, A)) {
+        if (pf) {  // accumulated values loaded up front, their latency overlapping the TMEM loads
+            float4 old[kPrefetchFeatures / 4];
+#pragma unroll
+            for (int q = 0; q < kPrefetchFeatures / 4; q++)
+                old[q] = (acc && valid && 4 * q < F) ? reinterpret_cast<const float4*>(gout)[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int q = 0; q < kPrefetchFeatures / 8; q++) {
+                if (16 * q >= 2 * F) break;
+                chunk(16 * q, old[2 * q], old[2 * q + 1]);
+            }
+        } else {
+            for (int c0 = 0; c0 < 2 * F; c0 += 16) {
+                float4 a0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), a1 = a0;
+                if (acc && valid) {
+                    a0 = *reinterpret_cast<const float4*>(gout + c0 / 2);
+                    a1 = *reinterpret_cast<const float4*>(gout + c0 / 2 + 4);
+                }
+                chunk(c0, a0, a1);
+            }
+        }
+        c = 2 * F;
     }
     // remaining columns in order: encoded inputs (feature j, octave f, sin then cos), SH inputs, padding
     int j = c / per, q = c - j * per;
@@ -421,7 +520,7 @@ __device__ inline void input_grad_row(const Params& P, const AppearanceConfig& A
                 } else {
                     const int f = q >> 1;
                     if ((q & 1) == 0) {
-                        sincosf(octave(val, f), &sn, &cs);
+                        det_sincos(octave(val, f), &sn, &cs);
                         g_even = g[k];
                     } else {
                         gacc += static_cast<float>(1 << f) * (cs * g_even - sn * g[k]);
@@ -441,28 +540,28 @@ __device__ inline void input_grad_row(const Params& P, const AppearanceConfig& A
     }
     gbase_in = mk3(gb[0], gb[1], gb[2]);
     // direction gradient from the SH inputs' gradient, unscaled afterwards (scaling by 2^-7 is exact)
-    gdir = inv * sh_band_grad(A.sh_mask, deg, d, gsh);
+    gdir = inv * sh_band_grad(A.sh_mask, deg, dir, gsh);
 }
 
 // data-gradient epilogue of a hidden layer: dL/d(activation) of row t, masked by the ReLU of the stored activation,
 // written over that activation (fp16, in place)
 __device__ inline void hidden_grad_epilogue(uint32_t t_addr, uint32_t row_base, bool relu) {
-    float a[16];
-#pragma unroll 1
-    for (int c0 = 0; c0 < kTcWidth; c0 += 16) {
-        tc::ld16(t_addr + c0, a);
-        if (relu) {
-            const uint4 h0 = ld_shared_v4(row_base + (c0 / 8) * 128), h1 = ld_shared_v4(row_base + (c0 / 8 + 1) * 128);
-            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    float a[64];
+    tc::ld64(t_addr, a);
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
+    for (int q = 0; q < 8; q++) {
+        float* x = a + 8 * q;
+        if (relu) {
+            const uint4 h = ld_shared_v4(row_base + q * 128);
+            const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
                 const float2 hv = unpack2(hw[k]);
-                if (!(hv.x > 0.0f)) a[2 * k] = 0.0f;
-                if (!(hv.y > 0.0f)) a[2 * k + 1] = 0.0f;
+                if (!(hv.x > 0.0f)) x[2 * k] = 0.0f;
+                if (!(hv.y > 0.0f)) x[2 * k + 1] = 0.0f;
             }
         }
-        st_shared_v4(row_base + (c0 / 8) * 128, pack2(a[0], a[1]), pack2(a[2], a[3]), pack2(a[4], a[5]), pack2(a[6], a[7]));
-        st_shared_v4(row_base + (c0 / 8 + 1) * 128, pack2(a[8], a[9]), pack2(a[10], a[11]), pack2(a[12], a[13]), pack2(a[14], a[15]));
+        st_shared_v4(row_base + q * 128, pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
     }
 }
 
@@ -475,21 +574,23 @@ __device__ inline void issue_backward(const TcPlan& p, uint32_t sbase, uint32_t 
     const uint32_t R = p.rows[l], dout_row_group = 16u * R;
     const uint32_t w = sbase + p.w_smem[l];
     const uint32_t dw = tb + p.wg_col[l];
+    const uint64_t in_mn = tc::desc(in, in_row_group, 128), dout_mn = tc::desc(dout, dout_row_group, 128);
     if (l == last) {  // dW^T [in x out] += In^T . dOut (M = input width 64, N = 16)
         const uint32_t id = tc::idesc(64, R, 1, 1);
         for (uint32_t ks = 0; ks < kTcRows / 16; ks++)
-            tc::mma(dw, tc::desc(in + ks * 2 * in_row_group, in_row_group, 128), tc::desc(dout + ks * 2 * dout_row_group, dout_row_group, 128), id,
+            tc::mma(dw, tc::desc_advance(in_mn, ks * 2 * in_row_group), tc::desc_advance(dout_mn, ks * 2 * dout_row_group), id,
                     (wg_accumulate || ks > 0) ? 1u : 0u);
     } else {  // dW [out x in] += dOut^T . In (M = 64 outputs, N = input width)
         const uint32_t id = tc::idesc(64, K, 1, 1);
         for (uint32_t ks = 0; ks < kTcRows / 16; ks++)
-            tc::mma(dw, tc::desc(dout + ks * 2 * dout_row_group, dout_row_group, 128), tc::desc(in + ks * 2 * in_row_group, in_row_group, 128), id,
+            tc::mma(dw, tc::desc_advance(dout_mn, ks * 2 * dout_row_group), tc::desc_advance(in_mn, ks * 2 * in_row_group), id,
                     (wg_accumulate || ks > 0) ? 1u : 0u);
     }
     // dIn [rows x in] = dOut . W (B = W read MN-major: N = inputs, K = outputs)
     const uint32_t id = tc::idesc(128, K, 0, 1);
+    const uint64_t dk = tc::desc(dout, 128, dout_row_group), wmn = tc::desc(w, in_row_group, 128);
     for (uint32_t ks = 0; ks < R / 16; ks++)
-        tc::mma(tb, tc::desc(dout + ks * 256, 128, dout_row_group), tc::desc(w + ks * 2 * in_row_group, in_row_group, 128), id, ks > 0);
+        tc::mma(tb, tc::desc_advance(dk, ks * 256), tc::desc_advance(wmn, ks * 2 * in_row_group), id, ks > 0);
 }
 
 __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
@@ -512,19 +613,21 @@ __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceCon
     uint32_t phase = 0;
     bool wg_started = false;
     const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows;
+    const bool pf = prefetch_features(P, A);
+    float* trig = pf && plan.trig_smem ? reinterpret_cast<float*>(smem + plan.trig_smem) : nullptr;
+    RowData cur, nxt;
+    if (blockIdx.x < n_tiles) load_row(P, A, pf, vis, n_rows, blockIdx.x * kTcRows + t, rank_of, sorted_rec, grads, cur);
     for (uint32_t tile = blockIdx.x; tile < n_tiles && alive; tile += gridDim.x) {
-        const uint32_t gi = tile * kTcRows + t;
-        const bool valid = gi < n_rows;
-        const uint32_t i = valid ? vis[gi] : 0u;
-        const uint32_t r = valid ? rank_of[i] : 0u;
+        const bool valid = cur.valid;
+        const uint32_t i = cur.i;
         f3 gpre = mk3(0.0f, 0.0f, 0.0f);
-        if (valid) {
-            const float4 q2 = sorted_rec[r].q2, g1 = grads[r].g1;
-            gpre = mk3(g1.y, g1.z, g1.w) * mk3(color_act_grad_from_y(A.color_act, q2.x), color_act_grad_from_y(A.color_act, q2.y),
-                                               color_act_grad_from_y(A.color_act, q2.z));
-        }
-        write_input_row(P, A, v, deg, i, valid, sbase + plan.x_smem + tc::kmajor_offset(t, 0, plan.kin), plan.kin);
+        if (valid)
+            gpre = mk3(cur.g1.y, cur.g1.z, cur.g1.w) * mk3(color_act_grad_from_y(A.color_act, cur.q2.x), color_act_grad_from_y(A.color_act, cur.q2.y),
+                                                           color_act_grad_from_y(A.color_act, cur.q2.z));
+        write_input_row(P, A, v, deg, cur, pf, sbase + plan.x_smem + tc::kmajor_offset(t, 0, plan.kin), plan.kin, trig, t);
         sync_tile();
+        const uint32_t next = tile + gridDim.x;
+        if (next < n_tiles) load_row(P, A, pf, vis, n_rows, next * kTcRows + t, rank_of, sorted_rec, grads, nxt);
         // recomputed forward; the last layer's outputs become the scaled output gradient
         for (int l = 0; l < plan.layers && alive; l++) {
             if (t == 0) {
@@ -572,9 +675,9 @@ __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceCon
         // input gradient (layer-0 data gradient, TMEM columns 0..kin) -> feature, base and direction gradients;
         // every lane runs the TMEM loads, invalid rows skip the memory accesses
         float rn = 1.0f;
-        const f3 d = valid ? view_dir(v, ld3(P.means, i), &rn) : mk3(0.0f, 0.0f, 1.0f);
+        const f3 d = valid ? view_dir(v, cur.mean, &rn) : mk3(0.0f, 0.0f, 1.0f);
         f3 gbase_in, gd;
-        input_grad_row(P, A, O, t_row, i, valid, plan.kin, deg, d, gbase_in, gd);
+        input_grad_row(P, A, O, t_row, cur, pf, trig, t, plan.kin, deg, d, gbase_in, gd);
         if (valid) {
             f3 gbase = mk3(0.0f, 0.0f, 0.0f);
             if (v.render_base) {
@@ -587,6 +690,7 @@ __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceCon
             put3n(O.means, i, gmean_color, O.accumulate);
         }
         sync_tile();
+        cur = nxt;
     }
     // weight gradients: M = 64 accumulators (row m in lane (m % 16) + 32 (m / 16)), unscaled and added once per CTA
     if (wg_started && alive) {
@@ -636,10 +740,22 @@ bool make_plan(const AppearanceConfig& A, bool backward, TcPlan& p) {
     p.x_smem = off;
     off += kTcRows * static_cast<uint32_t>(p.kin) * 2;
     p.h_slots = backward ? (p.layers - 1) : 1;
-    p.h_smem = off;
-    off += static_cast<uint32_t>(p.h_slots) * kTcRows * kTcWidth * 2;
-    p.y_smem = off;
-    if (backward) off += kTcRows * 16 * 2;
+    if (backward) {
+        p.h_smem = off;
+        off += static_cast<uint32_t>(p.h_slots) * kTcRows * kTcWidth * 2;
+        p.y_smem = off;
+        off += kTcRows * 16 * 2;
+        // fp32 sine / cosine of the encoding (fast path, up to 32 features) for the input gradient
+        if (A.n_freq == 1 && A.feature_dim % 8 == 0 && A.feature_dim <= kPrefetchFeatures) {
+            p.trig_smem = off;
+            off += static_cast<uint32_t>(2 * A.feature_dim) * kTcRows * 4;
+        }
+    } else {
+        // the forward's activations overwrite its input (each layer's MMAs completed before its epilogue writes)
+        p.h_smem = p.x_smem;
+        const uint32_t h_bytes = kTcRows * kTcWidth * 2;
+        if (h_bytes > static_cast<uint32_t>(kTcRows * p.kin * 2)) off = p.x_smem + h_bytes;
+    }
     p.smem_bytes = off;
     uint32_t cols = static_cast<uint32_t>(p.kin > kTcWidth ? p.kin : kTcWidth);
     if (backward)

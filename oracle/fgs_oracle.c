@@ -66,6 +66,38 @@ static float det_exp_f(float x) {
     return p * f_from_bits((uint32_t)((int)n + 127) << 23);
 }
 
+/* sine and cosine as the kernels' det_sincos (fgs_common.cuh): Cody-Waite reduction modulo pi/2 in three parts,
+ * Taylor series of sin through r^9 and cos through r^10, quadrant rotation; libm beyond |x| = 8192 */
+static void det_sincos_f(float x, float* sp, float* cp) {
+    if (!(fabsf(x) <= 8192.0f)) {
+        *sp = sinf(x);
+        *cp = cosf(x);
+        return;
+    }
+    const float k = rintf(x * 0.636619746685028076171875f);
+    float r = fmaf(-k, 1.57079637050628662109375f, x);
+    r = fmaf(-k, -4.371138828673792886547744274139404296875e-08f, r);
+    r = fmaf(-k, -1.7151245100058819e-15f, r);
+    const float r2 = r * r;
+    float ps = 1.0f / 362880.0f;
+    ps = fmaf(ps, r2, -1.0f / 5040.0f);
+    ps = fmaf(ps, r2, 1.0f / 120.0f);
+    ps = fmaf(ps, r2, -1.0f / 6.0f);
+    const float s = fmaf(ps, r2 * r, r);
+    float pc = -1.0f / 3628800.0f;
+    pc = fmaf(pc, r2, 1.0f / 40320.0f);
+    pc = fmaf(pc, r2, -1.0f / 720.0f);
+    pc = fmaf(pc, r2, 1.0f / 24.0f);
+    pc = fmaf(pc, r2, -0.5f);
+    const float c = fmaf(pc, r2, 1.0f);
+    switch (((int)k) & 3) {
+        case 0: *sp = s; *cp = c; break;
+        case 1: *sp = c; *cp = -s; break;
+        case 2: *sp = -s; *cp = -c; break;
+        default: *sp = -c; *cp = s; break;
+    }
+}
+
 static float det_exp_blend_f(float x) {
     const float n = rintf(x * 1.44269504088896341f);
     float r = fmaf(-n, 0.693145751953125f, x);
@@ -799,6 +831,7 @@ void orc_adam(int64_t n, float* param, const float* grad, float* m, float* v, in
 float orc_det_exp(float x) { return det_exp_f(x); }
 float orc_det_exp_blend(float x) { return det_exp_blend_f(x); }
 float orc_det_log(float x) { return det_log_f(x); }
+void orc_det_sincos(float x, float* s, float* c) { det_sincos_f(x, s, c); }
 int orc_is_double(void) {
 #ifdef ORC_DOUBLE
     return 1;

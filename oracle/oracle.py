@@ -66,6 +66,8 @@ def load(double: bool = False) -> ctypes.CDLL:
         getattr(lib, f).argtypes = [ctypes.c_float]
         getattr(lib, f).restype = ctypes.c_float
     lib.orc_residual_stride.argtypes = [P]
+    lib.orc_det_sincos.argtypes = [ctypes.c_float, P, P]
+    lib.orc_det_sincos.restype = None
     _LIBS[double] = lib
     return lib
 

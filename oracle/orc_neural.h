@@ -88,9 +88,10 @@ static int neural_inputs(const orc_appearance* A, const inreal* feat, const inre
         for (int f = 0; f < A->n_freq; f++) {
             const double s = ldexp(val, f);
 #ifndef ORC_DOUBLE
-            const float sf = (float)s;
-            x[o++] = sinf(sf);
-            x[o++] = cosf(sf);
+            float sn, cs;
+            det_sincos_f((float)s, &sn, &cs);
+            x[o++] = sn;
+            x[o++] = cs;
 #else
             x[o++] = sin(s);
             x[o++] = cos(s);
