@@ -204,7 +204,7 @@ def run_b200(args, wl_name: str) -> dict | None:
         settings = [settings_of(cams[v], wl['degree'], dev) for v in mine]
         tg_host = [t.pin_memory() for t in [targets(wl)[v] for v in mine]]
         tg_dev = [t.to(dev) for t in tg_host]
-        n_params = trainer.total
+        n_params = trainer.shard  # parameters this rank's Adam updates
 
         def step():
             return trainer.step(settings, tg_dev)

@@ -131,13 +131,16 @@ cudaError_t tc_selftest(float* scratch, int* mismatches, cudaStream_t s) {
 
 
 // ---------------------------------------------------------------------------------------------------
-// MLP on tcgen05
+// MLP on tcgen05: 256 threads per CTA, two threads per tile row (warps w and w + 4 read the same TMEM lane quarter);
+// each half of a row's columns belongs to one of the two threads
 
 namespace {
 
 constexpr int kTcRows = 128;
+constexpr int kTcThreads = 256;
 constexpr int kTcWidth = 64;
 constexpr int kTcMaxLayers = 8;
+constexpr int kPrefetchFeatures = 32;  // rows of up to 32 latent floats are prefetched into registers (16 per thread)
 
 // one MLP configuration laid out for the tensor-core kernels
 struct TcPlan {
@@ -182,10 +185,10 @@ __device__ inline void stage_weights_tc(const TcPlan& p, const float* __restrict
     }
 }
 
-// collects fp16 values in input order and stores them 8 at a time (16 bytes) into a K-major row
+// collects fp16 values in input order and stores them 8 at a time (16 bytes) into a K-major row from `chunk` on
 struct RowWriter {
     uint32_t base;  // shared address of element (row, 0)
-    int K, chunk = 0, fill = 0;
+    int chunk = 0, fill = 0;
     uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
     __device__ void push(float v) {
         const uint32_t h = __half_as_ushort(__float2half_rn(v));
@@ -205,39 +208,35 @@ struct RowWriter {
     }
 };
 
+// the fast encoding path: one octave, features in groups of 8, 16-byte aligned rows, at most 32 features (split in
+// halves of groups of 4 between a row's two threads)
 __device__ inline bool fast_features(const Params& P, const AppearanceConfig& A) {
-    return A.n_freq == 1 && A.feature_dim % 8 == 0 && (reinterpret_cast<uintptr_t>(P.residual) & 15u) == 0;
+    return A.n_freq == 1 && A.feature_dim % 8 == 0 && A.feature_dim <= kPrefetchFeatures && (reinterpret_cast<uintptr_t>(P.residual) & 15u) == 0;
 }
-
-constexpr int kPrefetchFeatures = 32;  // rows of up to 32 latent floats are prefetched into registers
 
 // per-row inputs of a tile, loaded one tile ahead so their latency hides behind the previous tile's MMAs
 struct RowData {
     uint32_t i, r;
     bool valid;
     f3 mean;
-    float4 f[kPrefetchFeatures / 4];  // latent features (fast encoding path)
+    float4 f[kPrefetchFeatures / 8];  // this thread's half of the latent features (fast path)
     float4 q2, g1;                    // colour of the record and its blend gradient sums (backward)
 };
 
-__device__ inline bool prefetch_features(const Params& P, const AppearanceConfig& A) {
-    return fast_features(P, A) && A.feature_dim <= kPrefetchFeatures;
-}
-
 // (backward data with rank_of non-null)
-__device__ inline void load_row(const Params& P, const AppearanceConfig& A, bool pf, const uint32_t* __restrict__ vis, uint32_t n_rows, uint32_t gi,
-                                const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec, const GradRecord* __restrict__ grads,
-                                RowData& d) {
+__device__ inline void load_row(const Params& P, const AppearanceConfig& A, bool fast, int half, const uint32_t* __restrict__ vis, uint32_t n_rows,
+                                uint32_t gi, const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec,
+                                const GradRecord* __restrict__ grads, RowData& d) {
     d.valid = gi < n_rows;
     d.i = d.valid ? vis[gi] : 0u;
     if (!d.valid) return;
     d.mean = ld3(P.means, d.i);
     const int F = A.feature_dim;
-    if (pf) {
-        const float4* src = reinterpret_cast<const float4*>(P.residual + static_cast<size_t>(d.i) * F);
+    if (fast) {
+        const float4* src = reinterpret_cast<const float4*>(P.residual + static_cast<size_t>(d.i) * F + half * (F / 2));
 #pragma unroll
-        for (int q = 0; q < kPrefetchFeatures / 4; q++)
-            if (4 * q < F) d.f[q] = src[q];
+        for (int q = 0; q < kPrefetchFeatures / 8; q++)
+            if (8 * q < F) d.f[q] = src[q];
     }
     if (rank_of) {
         d.r = rank_of[d.i];
@@ -246,24 +245,30 @@ __device__ inline void load_row(const Params& P, const AppearanceConfig& A, bool
     }
 }
 
-// the MLP input row of a tile row (thread t's): encoded features, SH inputs, padding ones. With `trig` (fast path of
-// the backward) the fp32 sine and cosine of every feature are kept at trig[column * 128 + t] for the input gradient.
-__device__ inline void write_input_row(const Params& P, const AppearanceConfig& A, const View& v, int deg, const RowData& d, bool pf, uint32_t row_base,
-                                       int kin, float* trig, int t) {
-    RowWriter w{row_base, kin};
+// this thread's part of the MLP input row: with the fast path each thread encodes its half of the features
+// (sin, cos per feature), the second also the base inputs, SH inputs and padding; otherwise the first thread writes
+// the whole row. With `trig` the fp32 sine and cosine of every feature are kept at trig[column * 128 + row].
+__device__ inline void write_input_row(const Params& P, const AppearanceConfig& A, const View& v, int deg, const RowData& d, bool fast, int half,
+                                       uint32_t row_base, int kin, float* trig, int row) {
+    const int F = A.feature_dim, nf = A.n_freq;
     if (!d.valid) {
-        for (int c = 0; c < kin; c += 8) w.push8(0u, 0u, 0u, 0u);
+        if (half == 0)
+            for (int c = 0; c < kin; c += 8) st_shared_v4(row_base + (c / 8) * 128, 0u, 0u, 0u, 0u);
         return;
     }
+    if (!fast && half == 1) return;
+    RowWriter w{row_base};
     const uint32_t i = d.i;
-    const int F = A.feature_dim, nf = A.n_freq;
     const float* feat = P.residual + static_cast<size_t>(i) * F;
     int j0 = 0;
-    if (fast_features(P, A)) {  // 4 features = 8 encoded columns per 16-byte load and store
+    if (fast) {  // 4 features = 8 encoded columns per store
+        const int jb = half * (F / 2);
+        w.chunk = jb / 4;
+        // the prefetch holds this half's F/2 floats as F/8 float4 values
 #pragma unroll
-        for (int q = 0; q < kPrefetchFeatures / 4; q++) {
-            if (4 * q >= F) break;
-            const float4 x = pf ? d.f[q] : *reinterpret_cast<const float4*>(feat + 4 * q);
+        for (int q = 0; q < kPrefetchFeatures / 8; q++) {
+            if (4 * q >= F / 2) break;
+            const float4 x = d.f[q];
             float s0, c0, s1, c1, s2, c2, s3, c3;
             det_sincos(x.x, &s0, &c0);
             det_sincos(x.y, &s1, &c1);
@@ -271,26 +276,14 @@ __device__ inline void write_input_row(const Params& P, const AppearanceConfig& 
             det_sincos(x.w, &s3, &c3);
             w.push8(pack2(s0, c0), pack2(s1, c1), pack2(s2, c2), pack2(s3, c3));
             if (trig) {
-                float* tq = trig + (8 * q) * kTcRows + t;
+                float* tq = trig + (2 * (jb + 4 * q)) * kTcRows + row;
                 tq[0] = s0; tq[kTcRows] = c0; tq[2 * kTcRows] = s1; tq[3 * kTcRows] = c1;
                 tq[4 * kTcRows] = s2; tq[5 * kTcRows] = c2; tq[6 * kTcRows] = s3; tq[7 * kTcRows] = c3;
             }
         }
+        if (half == 0) return;
         j0 = F;
-        for (int jq = kPrefetchFeatures; jq < F; jq += 4) {  // rows longer than the prefetch (no trig cache then)
-            const float4 x = *reinterpret_cast<const float4*>(feat + jq);
-            float s0, c0, s1, c1, s2, c2, s3, c3;
-            det_sincos(x.x, &s0, &c0);
-            det_sincos(x.y, &s1, &c1);
-            det_sincos(x.z, &s2, &c2);
-            det_sincos(x.w, &s3, &c3);
-            w.push8(pack2(s0, c0), pack2(s1, c1), pack2(s2, c2), pack2(s3, c3));
-            if (trig) {
-                float* tq = trig + (2 * jq) * kTcRows + t;
-                tq[0] = s0; tq[kTcRows] = c0; tq[2 * kTcRows] = s1; tq[3 * kTcRows] = c1;
-                tq[4 * kTcRows] = s2; tq[5 * kTcRows] = c2; tq[6 * kTcRows] = s3; tq[7 * kTcRows] = c3;
-            }
-        }
+        w.chunk = F / 4;
     }
     const int nraw = F + (A.base_input ? 3 : 0);
     for (int j = j0; j < nraw; j++) {
@@ -320,17 +313,40 @@ __device__ inline void issue_forward(const TcPlan& p, uint32_t sbase, uint32_t t
     for (uint32_t ks = 0; ks < K / 16; ks++) tc::mma(tb, tc::desc_advance(a, ks * 256), tc::desc_advance(b, ks * 256), id, ks > 0);
 }
 
-// hidden-layer epilogue: row t of the accumulator -> activation -> fp16 K-major row of the slot
-__device__ inline void hidden_epilogue(uint32_t t_addr, uint32_t row_base, bool relu) {
-    float a[64];
-    tc::ld64(t_addr, a);
+// hidden-layer epilogue, this thread's 32 columns: accumulator -> activation -> fp16 K-major row of the slot
+__device__ inline void hidden_epilogue(uint32_t t_addr, uint32_t row_base, int half, bool relu) {
+    float a[32];
+    tc::ld32(t_addr + 32 * half, a);
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
+    for (int q = 0; q < 4; q++) {
         float* x = a + 8 * q;
         if (relu)
 #pragma unroll
             for (int k = 0; k < 8; k++) x[k] = fmaxf(x[k], 0.0f);
-        st_shared_v4(row_base + q * 128, pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+        st_shared_v4(row_base + (4 * half + q) * 128, pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+    }
+}
+
+// data-gradient epilogue of a hidden layer, this thread's 32 columns: dL/d(activation), masked by the ReLU of the
+// stored activation, written over that activation (fp16, in place)
+__device__ inline void hidden_grad_epilogue(uint32_t t_addr, uint32_t row_base, int half, bool relu) {
+    float a[32];
+    tc::ld32(t_addr + 32 * half, a);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        float* x = a + 8 * q;
+        const uint32_t addr = row_base + (4 * half + q) * 128;
+        if (relu) {
+            const uint4 h = ld_shared_v4(addr);
+            const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float2 hv = unpack2(hw[k]);
+                if (!(hv.x > 0.0f)) x[2 * k] = 0.0f;
+                if (!(hv.y > 0.0f)) x[2 * k + 1] = 0.0f;
+            }
+        }
+        st_shared_v4(addr, pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
     }
 }
 
@@ -359,32 +375,31 @@ __device__ inline void sync_tile() {
 
 __device__ int g_tc_timeout;  // set when an mbarrier wait ran out (the kernel then stops issuing work)
 
-__global__ void __launch_bounds__(kTcRows) tc_color_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
-                                                           Record* __restrict__ rec, const __grid_constant__ TcPlan plan) {
+__global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis,
+                                                                 uint32_t n_rows, Record* __restrict__ rec, const __grid_constant__ TcPlan plan) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar;
     __shared__ uint32_t tbase;
-    const int t = threadIdx.x, warp = t >> 5;
+    const int t = threadIdx.x, warp = t >> 5, half = t >> 7, row = t & (kTcRows - 1);
     stage_weights_tc(plan, P.mlp, smem);
     if (warp == 0) tc::tmem_alloc(&tbase, plan.tmem_cols);
     if (t == 0) tc::mbar_init(&bar, 1);
     sync_tile();
     bool alive = true;
     const uint32_t tb = tbase, sbase = tc::smem_addr(smem);
-    const uint32_t t_row = tb + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t t_row = tb + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int deg = min(v.degree, A.max_degree);
     uint32_t phase = 0;
     const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows;
-    const bool pf = prefetch_features(P, A);
+    const bool fast = fast_features(P, A);
+    const uint32_t x_row = sbase + plan.x_smem + tc::kmajor_offset(row, 0, plan.kin);
     RowData cur, nxt;
-    if (blockIdx.x < n_tiles) load_row(P, A, pf, vis, n_rows, blockIdx.x * kTcRows + t, nullptr, nullptr, nullptr, cur);
+    if (blockIdx.x < n_tiles) load_row(P, A, fast, half, vis, n_rows, blockIdx.x * kTcRows + row, nullptr, nullptr, nullptr, cur);
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const bool valid = cur.valid;
-        const uint32_t i = cur.i;
-        write_input_row(P, A, v, deg, cur, pf, sbase + plan.x_smem + tc::kmajor_offset(t, 0, plan.kin), plan.kin, nullptr, t);
+        write_input_row(P, A, v, deg, cur, fast, half, x_row, plan.kin, nullptr, row);
         sync_tile();
         const uint32_t next = tile + gridDim.x;
-        if (next < n_tiles) load_row(P, A, pf, vis, n_rows, next * kTcRows + t, nullptr, nullptr, nullptr, nxt);
+        if (next < n_tiles) load_row(P, A, fast, half, vis, n_rows, next * kTcRows + row, nullptr, nullptr, nullptr, nxt);
         for (int l = 0; l < plan.layers; l++) {
             if (t == 0) {
                 issue_forward(plan, sbase, tb, l);
@@ -394,23 +409,23 @@ __global__ void __launch_bounds__(kTcRows) tc_color_kernel(Params P, AppearanceC
             alive = wait_all(&bar, phase);
             if (!alive) break;
             if (l < plan.layers - 1) {
-                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(t, 0, kTcWidth), A.hidden_act == 1);
-            } else {
+                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(row, 0, kTcWidth), half, A.hidden_act == 1);
+            } else if (half == 0) {  // whole warps: the TMEM load is warp-collective
                 float y[16];
-                tc::ld16(t_row, y);  // every lane: the TMEM load is warp-collective
-                if (valid) {
-                const f3 res = residual_act3(A.res_act, mk3(__half2float(__float2half_rn(y[0])), __half2float(__float2half_rn(y[1])),
-                                                             __half2float(__float2half_rn(y[2]))));
-                const f3 base = base_act3(A.base_act, ld3(P.base, i));
-                f3 color = color_act3(A.color_act, base + res);
-                if (!v.render_base) {
-                    const f3 bc = color_act3(A.color_act, base);
-                    color = mk3(fabsf(color.x - bc.x), fabsf(color.y - bc.y), fabsf(color.z - bc.z));
-                }
-                float* q2 = reinterpret_cast<float*>(rec + i) + 8;
-                q2[0] = color.x;
-                q2[1] = color.y;
-                q2[2] = color.z;
+                tc::ld16(t_row, y);
+                if (cur.valid) {
+                    const f3 res = residual_act3(A.res_act, mk3(__half2float(__float2half_rn(y[0])), __half2float(__float2half_rn(y[1])),
+                                                                 __half2float(__float2half_rn(y[2]))));
+                    const f3 base = base_act3(A.base_act, ld3(P.base, cur.i));
+                    f3 color = color_act3(A.color_act, base + res);
+                    if (!v.render_base) {
+                        const f3 bc = color_act3(A.color_act, base);
+                        color = mk3(fabsf(color.x - bc.x), fabsf(color.y - bc.y), fabsf(color.z - bc.z));
+                    }
+                    float* q2 = reinterpret_cast<float*>(rec + cur.i) + 8;
+                    q2[0] = color.x;
+                    q2[1] = color.y;
+                    q2[2] = color.z;
                 }
             }
             sync_tile();
@@ -428,86 +443,74 @@ __global__ void __launch_bounds__(kTcRows) tc_color_kernel(Params P, AppearanceC
     if (warp == 0) tc::tmem_dealloc(tb, plan.tmem_cols);
 }
 
-// feature / base-input / direction gradients of one row from the loss-scaled input gradient in TMEM (columns 0..kin);
-// with `trig` the fast path takes the sine and cosine the encoding kept instead of evaluating them again
-__device__ inline void input_grad_row(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t t_row, const RowData& d, bool pf,
-                                      const float* trig, int t, int kin, int deg, f3 dir, f3& gbase_in, f3& gdir) {
+// Input gradient of a row (loss-scaled dL/dinput in TMEM columns 0..kin) -> feature, base-input and direction
+// gradients. Fast path: each thread handles its half of the features (groups of 4 = 8 columns per TMEM load, sine
+// and cosine from `trig` when kept, else recomputed), the second thread also the base-input and SH columns.
+// Otherwise the first thread walks every column. Returns true for the thread that holds gbase_in / gdir.
+__device__ inline bool input_grad_row(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t t_row, const RowData& d, bool fast,
+                                      int half, const float* trig, int row, int kin, int deg, f3 dir, f3& gbase_in, f3& gdir) {
     const float inv = 1.0f / kLossScale;
     const int F = A.feature_dim, nf = A.n_freq, per = nf > 0 ? 2 * nf : 1, nraw = F + (A.base_input ? 3 : 0);
     const int enc = nraw * per;
     const bool valid = d.valid;
     const uint32_t i = d.i;
+    const int acc = O.accumulate;
+    const float* feat = P.residual + static_cast<size_t>(i) * F;
+    float* gout = O.residual + static_cast<size_t>(i) * F;
+    int c = 0;
+    if (fast) {
+        const int jb = half * (F / 2);
+        float4 old[kPrefetchFeatures / 8];  // accumulated values, loaded before the TMEM reads
+#pragma unroll
+        for (int q = 0; q < kPrefetchFeatures / 8; q++)
+            old[q] = (acc && valid && 4 * q < F / 2) ? reinterpret_cast<const float4*>(gout + jb)[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int q = 0; q < kPrefetchFeatures / 8; q++) {
+            if (4 * q >= F / 2) break;
+            const int j = jb + 4 * q;  // features j .. j + 3, columns 2j .. 2j + 7
+            float g[8];
+            tc::ld8(t_row + 2 * j, g);
+            if (!valid) continue;
+            float sn[4], cs[4];
+            if (trig) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    sn[k] = trig[(2 * j + 2 * k) * kTcRows + row];
+                    cs[k] = trig[(2 * j + 2 * k + 1) * kTcRows + row];
+                }
+            } else {
+                const float4 x = *reinterpret_cast<const float4*>(feat + j);
+                det_sincos(x.x, &sn[0], &cs[0]);
+                det_sincos(x.y, &sn[1], &cs[1]);
+                det_sincos(x.z, &sn[2], &cs[2]);
+                det_sincos(x.w, &sn[3], &cs[3]);
+            }
+            float gv[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) gv[k] = (cs[k] * g[2 * k] - sn[k] * g[2 * k + 1]) * inv;
+            float4 o = make_float4(gv[0], gv[1], gv[2], gv[3]);
+            if (acc) o = make_float4(old[q].x + o.x, old[q].y + o.y, old[q].z + o.z, old[q].w + o.w);
+            *reinterpret_cast<float4*>(gout + j) = o;
+        }
+        if (half == 0) return false;
+        c = 2 * F;
+    } else if (half == 1) {
+        return false;
+    }
+    // remaining columns in order: encoded inputs (feature j, octave f, sin then cos), SH inputs, padding
     int nsh = 0;
     for (int l = 0; l <= 3; l++)
         if (A.sh_mask & (1 << l)) nsh += 2 * l + 1;
-    const float* feat = P.residual + static_cast<size_t>(i) * F;
-    float* gout = O.residual + static_cast<size_t>(i) * F;
-    const int acc = O.accumulate;
-    float g[16];
-    int c = 0;
-    // 16 columns = 8 features per TMEM load; 16-byte loads and stores (every lane runs the TMEM load)
-    auto chunk = [&](int c0, float4 a0, float4 a1) {
-        tc::ld16(t_row + c0, g);
-        if (!valid) return;
-        const int j = c0 / 2;
-        float gv[8];
-        if (trig) {
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const float sn = trig[(c0 + 2 * k) * kTcRows + t], cs = trig[(c0 + 2 * k + 1) * kTcRows + t];
-                gv[k] = (cs * g[2 * k] - sn * g[2 * k + 1]) * inv;
-            }
-        } else {
-            const float4 v0 = *reinterpret_cast<const float4*>(feat + j), v1 = *reinterpret_cast<const float4*>(feat + j + 4);
-            const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                float sn, cs;
-                det_sincos(vv[k], &sn, &cs);
-                gv[k] = (cs * g[2 * k] - sn * g[2 * k + 1]) * inv;
-            }
-        }
-        float4 o0 = make_float4(gv[0], gv[1], gv[2], gv[3]), o1 = make_float4(gv[4], gv[5], gv[6], gv[7]);
-        if (acc) {
-            o0 = make_float4(a0.x + o0.x, a0.y + o0.y, a0.z + o0.z, a0.w + o0.w);
-            o1 = make_float4(a1.x + o1.x, a1.y + o1.y, a1.z + o1.z, a1.w + o1.w);
-        }
-        *reinterpret_cast<float4*>(gout + j) = o0;
-        *reinterpret_cast<float4*>(gout + j + 4) = o1;
-    };
-    if (fast_features(P, A)) {
-        if (pf) {  // accumulated values loaded up front, their latency overlapping the TMEM loads
-            float4 old[kPrefetchFeatures / 4];
-#pragma unroll
-            for (int q = 0; q < kPrefetchFeatures / 4; q++)
-                old[q] = (acc && valid && 4 * q < F) ? reinterpret_cast<const float4*>(gout)[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-            for (int q = 0; q < kPrefetchFeatures / 8; q++) {
-                if (16 * q >= 2 * F) break;
-                chunk(16 * q, old[2 * q], old[2 * q + 1]);
-            }
-        } else {
-            for (int c0 = 0; c0 < 2 * F; c0 += 16) {
-                float4 a0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), a1 = a0;
-                if (acc && valid) {
-                    a0 = *reinterpret_cast<const float4*>(gout + c0 / 2);
-                    a1 = *reinterpret_cast<const float4*>(gout + c0 / 2 + 4);
-                }
-                chunk(c0, a0, a1);
-            }
-        }
-        c = 2 * F;
-    }
-    // remaining columns in order: encoded inputs (feature j, octave f, sin then cos), SH inputs, padding
     int j = c / per, q = c - j * per;
     float val = 0.0f, gacc = 0.0f, sn = 0.0f, cs = 0.0f, g_even = 0.0f;
     float gsh[16];
     float gb[3] = {0.0f, 0.0f, 0.0f};
-    for (int c0 = c & ~15; c0 < kin; c0 += 16) {
-        tc::ld16(t_row + c0, g);
+    float g[8];
+    for (int c0 = c & ~7; c0 < kin; c0 += 8) {
+        tc::ld8(t_row + c0, g);
         if (!valid) continue;
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
+        for (int k = 0; k < 8; k++) {
             const int col = c0 + k;
             if (col < c) continue;
             if (col < enc) {
@@ -541,28 +544,7 @@ __device__ inline void input_grad_row(const Params& P, const AppearanceConfig& A
     gbase_in = mk3(gb[0], gb[1], gb[2]);
     // direction gradient from the SH inputs' gradient, unscaled afterwards (scaling by 2^-7 is exact)
     gdir = inv * sh_band_grad(A.sh_mask, deg, dir, gsh);
-}
-
-// data-gradient epilogue of a hidden layer: dL/d(activation) of row t, masked by the ReLU of the stored activation,
-// written over that activation (fp16, in place)
-__device__ inline void hidden_grad_epilogue(uint32_t t_addr, uint32_t row_base, bool relu) {
-    float a[64];
-    tc::ld64(t_addr, a);
-#pragma unroll
-    for (int q = 0; q < 8; q++) {
-        float* x = a + 8 * q;
-        if (relu) {
-            const uint4 h = ld_shared_v4(row_base + q * 128);
-            const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float2 hv = unpack2(hw[k]);
-                if (!(hv.x > 0.0f)) x[2 * k] = 0.0f;
-                if (!(hv.y > 0.0f)) x[2 * k + 1] = 0.0f;
-            }
-        }
-        st_shared_v4(row_base + q * 128, pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
-    }
+    return true;
 }
 
 // backward MMAs of layer l: weight gradient (M = 64, accumulated in TMEM) and data gradient (layer accumulator)
@@ -593,30 +575,32 @@ __device__ inline void issue_backward(const TcPlan& p, uint32_t sbase, uint32_t 
         tc::mma(tb, tc::desc_advance(dk, ks * 256), tc::desc_advance(wmn, ks * 2 * in_row_group), id, ks > 0);
 }
 
-__global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
-                                                         const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec,
-                                                         const GradRecord* __restrict__ grads, GradOut O, const __grid_constant__ TcPlan plan) {
+__global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis,
+                                                               uint32_t n_rows, const uint32_t* __restrict__ rank_of,
+                                                               const Record* __restrict__ sorted_rec, const GradRecord* __restrict__ grads, GradOut O,
+                                                               const __grid_constant__ TcPlan plan) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar;
     __shared__ uint32_t tbase;
-    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31, half = t >> 7, row = t & (kTcRows - 1);
     stage_weights_tc(plan, P.mlp, smem);
     if (warp == 0) tc::tmem_alloc(&tbase, plan.tmem_cols);
     if (t == 0) tc::mbar_init(&bar, 1);
     sync_tile();
     bool alive = true;
     const uint32_t tb = tbase, sbase = tc::smem_addr(smem);
-    const uint32_t t_row = tb + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t t_row = tb + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int deg = min(v.degree, A.max_degree);
     const int last = plan.layers - 1;
     const bool relu = A.hidden_act == 1;
     uint32_t phase = 0;
     bool wg_started = false;
     const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows;
-    const bool pf = prefetch_features(P, A);
-    float* trig = pf && plan.trig_smem ? reinterpret_cast<float*>(smem + plan.trig_smem) : nullptr;
+    const bool fast = fast_features(P, A);
+    float* trig = fast && plan.trig_smem ? reinterpret_cast<float*>(smem + plan.trig_smem) : nullptr;
+    const uint32_t x_row = sbase + plan.x_smem + tc::kmajor_offset(row, 0, plan.kin);
     RowData cur, nxt;
-    if (blockIdx.x < n_tiles) load_row(P, A, pf, vis, n_rows, blockIdx.x * kTcRows + t, rank_of, sorted_rec, grads, cur);
+    if (blockIdx.x < n_tiles) load_row(P, A, fast, half, vis, n_rows, blockIdx.x * kTcRows + row, rank_of, sorted_rec, grads, cur);
     for (uint32_t tile = blockIdx.x; tile < n_tiles && alive; tile += gridDim.x) {
         const bool valid = cur.valid;
         const uint32_t i = cur.i;
@@ -624,10 +608,10 @@ __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceCon
         if (valid)
             gpre = mk3(cur.g1.y, cur.g1.z, cur.g1.w) * mk3(color_act_grad_from_y(A.color_act, cur.q2.x), color_act_grad_from_y(A.color_act, cur.q2.y),
                                                            color_act_grad_from_y(A.color_act, cur.q2.z));
-        write_input_row(P, A, v, deg, cur, pf, sbase + plan.x_smem + tc::kmajor_offset(t, 0, plan.kin), plan.kin, trig, t);
+        write_input_row(P, A, v, deg, cur, fast, half, x_row, plan.kin, trig, row);
         sync_tile();
         const uint32_t next = tile + gridDim.x;
-        if (next < n_tiles) load_row(P, A, pf, vis, n_rows, next * kTcRows + t, rank_of, sorted_rec, grads, nxt);
+        if (next < n_tiles) load_row(P, A, fast, half, vis, n_rows, next * kTcRows + row, rank_of, sorted_rec, grads, nxt);
         // recomputed forward; the last layer's outputs become the scaled output gradient
         for (int l = 0; l < plan.layers && alive; l++) {
             if (t == 0) {
@@ -638,8 +622,8 @@ __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceCon
             alive = wait_all(&bar, phase);
             if (!alive) break;
             if (l < last) {
-                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(t, 0, kTcWidth), relu);
-            } else {
+                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(row, 0, kTcWidth), half, relu);
+            } else if (half == 0) {
                 float y[16];
                 tc::ld16(t_row, y);
                 float dy[3] = {0.0f, 0.0f, 0.0f};
@@ -650,7 +634,7 @@ __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceCon
                         dy[c] = gv[c] * residual_act_grad_from_y(A.res_act, residual_act(A.res_act, yh));
                     }
                 }
-                const uint32_t yrow = sbase + plan.y_smem + tc::kmajor_offset(t, 0, 16);
+                const uint32_t yrow = sbase + plan.y_smem + tc::kmajor_offset(row, 0, 16);
                 st_shared_v4(yrow, pack2(kLossScale * dy[0], kLossScale * dy[1]), pack2(kLossScale * dy[2], 0.0f), 0u, 0u);
                 st_shared_v4(yrow + 128, 0u, 0u, 0u, 0u);
             }
@@ -666,19 +650,18 @@ __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceCon
             alive = wait_all(&bar, phase);
             if (!alive) break;
             if (l > 0) {
-                hidden_grad_epilogue(t_row, sbase + h_slot(plan, l - 1) + tc::kmajor_offset(t, 0, kTcWidth), relu);
+                hidden_grad_epilogue(t_row, sbase + h_slot(plan, l - 1) + tc::kmajor_offset(row, 0, kTcWidth), half, relu);
                 sync_tile();
             }
         }
         if (!alive) break;
         wg_started = true;
-        // input gradient (layer-0 data gradient, TMEM columns 0..kin) -> feature, base and direction gradients;
-        // every lane runs the TMEM loads, invalid rows skip the memory accesses
+        // input gradient (layer-0 data gradient) -> feature, base and direction gradients
         float rn = 1.0f;
         const f3 d = valid ? view_dir(v, cur.mean, &rn) : mk3(0.0f, 0.0f, 1.0f);
-        f3 gbase_in, gd;
-        input_grad_row(P, A, O, t_row, cur, pf, trig, t, plan.kin, deg, d, gbase_in, gd);
-        if (valid) {
+        f3 gbase_in = mk3(0.0f, 0.0f, 0.0f), gd = mk3(0.0f, 0.0f, 0.0f);
+        const bool owner = input_grad_row(P, A, O, t_row, cur, fast, half, trig, row, plan.kin, deg, d, gbase_in, gd);
+        if (owner && valid) {
             f3 gbase = mk3(0.0f, 0.0f, 0.0f);
             if (v.render_base) {
                 const f3 bb = ld3(P.base, i);
@@ -692,13 +675,14 @@ __global__ void __launch_bounds__(kTcRows) tc_bwd_kernel(Params P, AppearanceCon
         sync_tile();
         cur = nxt;
     }
-    // weight gradients: M = 64 accumulators (row m in lane (m % 16) + 32 (m / 16)), unscaled and added once per CTA
+    // weight gradients: M = 64 accumulators (row m in lane (m % 16) + 32 (m / 16)), unscaled and added once per CTA;
+    // 16-column chunks alternate between the two halves
     if (wg_started && alive) {
         const float inv = 1.0f / kLossScale;
-        const int m = warp * 16 + lane;
+        const int m = (warp & 3) * 16 + lane;
         for (int l = 0; l < plan.layers; l++) {
             const int ncol = l == last ? plan.rows[l] : plan.cols[l];
-            for (int c0 = 0; c0 < ncol; c0 += 16) {
+            for (int c0 = 16 * half; c0 < ncol; c0 += 32) {
                 float a[16];
                 tc::ld16(t_row + plan.wg_col[l] + c0, a);
                 if (lane < 16)
@@ -745,7 +729,7 @@ bool make_plan(const AppearanceConfig& A, bool backward, TcPlan& p) {
         off += static_cast<uint32_t>(p.h_slots) * kTcRows * kTcWidth * 2;
         p.y_smem = off;
         off += kTcRows * 16 * 2;
-        // fp32 sine / cosine of the encoding (fast path, up to 32 features) for the input gradient
+        // fp32 sine / cosine of the encoding (fast path) for the input gradient
         if (A.n_freq == 1 && A.feature_dim % 8 == 0 && A.feature_dim <= kPrefetchFeatures) {
             p.trig_smem = off;
             off += static_cast<uint32_t>(2 * A.feature_dim) * kTcRows * 4;
@@ -778,12 +762,12 @@ int tc_sm_count() {
 }
 
 template <typename K>
-cudaError_t tc_grid(K kernel, const TcPlan& p, uint32_t n_tiles, int* grid) {
+cudaError_t tc_grid(K kernel, const TcPlan& p, uint32_t n_tiles, int max_per_sm, int* grid) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem_bytes));
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
-    // resident CTAs per SM: shared memory (228 KiB per SM, 1 KiB reserved per CTA), TMEM (512 columns per SM), threads
+    // resident CTAs per SM: shared memory (1 KiB reserved per CTA), TMEM (512 columns per SM), registers (launch bounds)
     int dev = 0, smem_sm = 0;
     cudaGetDevice(&dev);
     e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
@@ -791,7 +775,7 @@ cudaError_t tc_grid(K kernel, const TcPlan& p, uint32_t n_tiles, int* grid) {
     int per_sm = smem_sm / static_cast<int>(p.smem_bytes + 1024 + 256);
     const int tmem_cap = static_cast<int>(512 / p.tmem_cols);
     if (per_sm > tmem_cap) per_sm = tmem_cap;
-    if (per_sm > 2048 / kTcRows) per_sm = 2048 / kTcRows;
+    if (per_sm > max_per_sm) per_sm = max_per_sm;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const uint32_t cap = static_cast<uint32_t>(per_sm) * static_cast<uint32_t>(tc_sm_count());
     *grid = static_cast<int>(n_tiles < cap ? n_tiles : cap);
@@ -817,9 +801,9 @@ cudaError_t launch_tc_color(const Params& P, const AppearanceConfig& A, const Vi
     if (!make_plan(A, false, p)) return cudaErrorInvalidConfiguration;
     if (n_visible == 0) return cudaSuccess;
     int grid = 0;
-    cudaError_t e = tc_grid(tc_color_kernel, p, (n_visible + kTcRows - 1) / kTcRows, &grid);
+    cudaError_t e = tc_grid(tc_color_kernel, p, (n_visible + kTcRows - 1) / kTcRows, 3, &grid);
     if (e != cudaSuccess) return e;
-    tc_color_kernel<<<grid, kTcRows, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rec, p);
+    tc_color_kernel<<<grid, kTcThreads, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rec, p);
     return cudaGetLastError();
 }
 
@@ -829,9 +813,9 @@ cudaError_t launch_tc_backward(const Params& P, const AppearanceConfig& A, const
     if (!make_plan(A, true, p)) return cudaErrorInvalidConfiguration;
     if (n_visible == 0) return cudaSuccess;
     int grid = 0;
-    cudaError_t e = tc_grid(tc_bwd_kernel, p, (n_visible + kTcRows - 1) / kTcRows, &grid);
+    cudaError_t e = tc_grid(tc_bwd_kernel, p, (n_visible + kTcRows - 1) / kTcRows, 2, &grid);
     if (e != cudaSuccess) return e;
-    tc_bwd_kernel<<<grid, kTcRows, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, p);
+    tc_bwd_kernel<<<grid, kTcThreads, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, p);
     return cudaGetLastError();
 }
 
