@@ -1,0 +1,130 @@
+// Backward of the tile blend: for every pixel, the fragments of its tile are walked front to back again (the same
+// acceptance and termination decisions as the forward: the exponent, alpha, 1 - alpha and the transmittance are
+// evaluated with the forward's single-rounding operations), and the gradient terms of each accepted fragment are
+// summed over the warp and added to the primitive's gradient record.
+//
+// Semantics: FasterGSVDACudaBackend/.../rasterization/include/kernels_backward.cuh:12-231 (the reference processes
+// buckets of 32 instances with the pixels pipelined through the lanes, which for small footprints spends most issue
+// slots on pairs that do not overlap); here each warp walks its subtile's fragments front to back like the forward.
+// This translation unit is compiled with contraction (its outputs are checked within a tolerance); the decisions
+// above use explicit intrinsics so they do not depend on it.
+#include "blend_common.cuh"
+#include "launch.h"
+
+namespace fgs {
+
+template <bool kAbs>
+__global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A, const float* __restrict__ image, const float* __restrict__ grad_image,
+                                                                     TileBuffers T, GradRecord* __restrict__ grads) {
+    __shared__ StagedB st[kTilePixels];
+    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const uint32_t tile = blockIdx.y * A.grid_w + blockIdx.x;
+    const uint32_t sx0 = blockIdx.x * kTileW + (warp % 2) * kSubtileW;
+    const uint32_t sy0 = blockIdx.y * kTileH + (warp / 2) * kSubtileH;
+    const uint32_t px = sx0 + lane % kSubtileW, py = sy0 + lane / kSubtileW;
+    const uint32_t local = (py - blockIdx.y * kTileH) * kTileW + (px - blockIdx.x * kTileW);
+    const bool inside = px < static_cast<uint32_t>(A.width) && py < static_cast<uint32_t>(A.height);
+    const float pxf = static_cast<float>(px) + 0.5f, pyf = static_cast<float>(py) + 0.5f;
+    const uint2 range = A.ranges[tile];
+    const uint32_t n = range.y - range.x;
+    uint32_t last = 0;
+    float cfr = 0.0f, cfg = 0.0f, cfb = 0.0f, gr = 0.0f, gg = 0.0f, gb = 0.0f, gac = 0.0f;
+    if (inside) {
+        const size_t pix = static_cast<size_t>(py) * A.width + px;
+        const size_t np = static_cast<size_t>(A.width) * A.height;
+        last = T.n_contrib[static_cast<size_t>(tile) * kTilePixels + local];
+        const float tf = T.final_T[static_cast<size_t>(tile) * kTilePixels + local];
+        const float bgr = A.bg[0], bgg = A.bg[1], bgb = A.bg[2];
+        cfr = image[pix] - tf * bgr;
+        cfg = image[np + pix] - tf * bgg;
+        cfb = image[2 * np + pix] - tf * bgb;
+        gr = grad_image[pix];
+        gg = grad_image[np + pix];
+        gb = grad_image[2 * np + pix];
+        gac = tf * -(gr * bgr + gg * bgg + gb * bgb);
+    }
+    float tr = 1.0f, accr = 0.0f, accg = 0.0f, accb = 0.0f;
+    bool done = last == 0;
+    for (uint32_t start = 0; start < n; start += kTilePixels) {
+        if (__syncthreads_and(done)) break;
+        if (start + t < n) {
+            const uint32_t r = A.vals[range.x + start + t];
+            const Record q = A.rec[r];
+            StagedB& s = st[t];
+            s.a = make_float4(q.q0.x, q.q0.y, -q.q0.w, q.q0.z);
+            s.h = make_float4(-0.5f * q.q1.x, -q.q1.y, -0.5f * q.q1.z, __uint_as_float(r));
+            s.c = make_float4(q.q2.x, q.q2.y, q.q2.z, 0.0f);
+            s.bnd = make_uint2(__float_as_uint(q.q1.w), __float_as_uint(q.q2.w));
+        }
+        __syncthreads();
+        const uint32_t bs = min(static_cast<uint32_t>(kTilePixels), n - start);
+        for (uint32_t g = 0; g < bs; g += 32) {
+            const bool ov = g + lane < bs && overlaps_subtile(st[g + lane].bnd, sx0, sy0);
+            uint32_t pending = __ballot_sync(0xffffffffu, ov);
+            while (pending) {
+                if (__all_sync(0xffffffffu, done)) break;
+                const uint32_t k = g + __ffs(pending) - 1;
+                pending &= pending - 1;
+                const float4 a = st[k].a;
+                const float4 h = st[k].h;
+                const float dx = a.x - pxf, dy = a.y - pyf;
+                bool acc = !done && start + k < last;
+                float e = 0.0f;
+                if (acc) {
+                    e = gauss_exponent(dx, dy, h);
+                    acc = e >= a.z;
+                }
+                if (!__any_sync(0xffffffffu, acc)) continue;
+                float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+                float v8 = 0.0f, ax = 0.0f, ay = 0.0f;
+                if (acc) {
+                    const float G = det_exp_blend(fminf(e, 0.0f));
+                    const float alpha = __fmul_rn(a.w, G);
+                    const float4 c = st[k].c;
+                    const float w = tr * alpha;
+                    accr = fmaf(w, c.x, accr);
+                    accg = fmaf(w, c.y, accg);
+                    accb = fmaf(w, c.z, accb);
+                    const float oma = __fsub_rn(1.0f, alpha);
+                    const float rcp = __frcp_rn(fmaxf(oma, kOneMinusAlphaEps));  // = 1 / x, correctly rounded
+                    const float afr = cfr - accr, afg = cfg - accg, afb = cfb - accb;
+                    const float dl_da = (tr * c.x - afr * rcp) * gr + (tr * c.y - afg * rcp) * gg + (tr * c.z - afb * rcp) * gb + gac * rcp;
+                    const float hl = -alpha * dl_da;
+                    const float hx = hl * dx, hy = hl * dy;
+                    v[0] = hx; v[1] = hy; v[2] = hx * dx; v[3] = hx * dy;
+                    v[4] = hy * dy; v[5] = w * gr; v[6] = w * gg; v[7] = w * gb;
+                    v8 = G * dl_da;
+                    if (kAbs) {
+                        // |dL/dmean2d| of this fragment, with the raw conic recovered exactly from the staged halves
+                        const float ca = -2.0f * h.x, cb = -h.y, cc = -2.0f * h.z;
+                        ax = fabsf(ca * hx + cb * hy);
+                        ay = fabsf(cb * hx + cc * hy);
+                    }
+                    tr = __fmul_rn(tr, oma);
+                    if (tr < kTransmittanceThreshold) done = true;
+                }
+                const float s = butterfly8(v, lane);
+                const float s8 = warp_sum(v8);
+                float sax = 0.0f, say = 0.0f;
+                if (kAbs) { sax = warp_sum(ax); say = warp_sum(ay); }
+                const uint32_t r = __float_as_uint(h.w);
+                float* gp = reinterpret_cast<float*>(grads + r);
+                if ((lane & 3) == 0) atomicAdd(gp + (lane >> 2), s);
+                if (lane == 0) {
+                    atomicAdd(gp + 8, s8);
+                    if (kAbs) { atomicAdd(gp + 9, sax); atomicAdd(gp + 10, say); }
+                }
+            }
+        }
+    }
+}
+
+cudaError_t launch_blend_backward(const BlendArgs& a, const float* image, const float* grad_image, const TileBuffers& T, GradRecord* grads,
+                                  int abs_grad, cudaStream_t s) {
+    const dim3 grid(a.grid_w, a.grid_h);
+    if (abs_grad) blend_backward_kernel<true><<<grid, kTilePixels, 0, s>>>(a, image, grad_image, T, grads);
+    else blend_backward_kernel<false><<<grid, kTilePixels, 0, s>>>(a, image, grad_image, T, grads);
+    return cudaGetLastError();
+}
+
+}  // namespace fgs
