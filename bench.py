@@ -36,11 +36,15 @@ import torch
 WORKLOADS = {
     'c1': dict(n=1_000_000, width=1280, height=720, model='sh', degree=3, views=1),
     'c4': dict(n=6_000_000, width=1920, height=1080, model='neural', degree=3, views=8, feature_dim=32, n_freq=1, neurons=64, hidden=2),
+    'c3': dict(n=3_000_000, width=1920, height=1080, model='nasg', degree=8, views=64),
+    'c3sv': dict(n=3_000_000, width=1920, height=1080, model='sv', degree=8, views=64),
 }
 C1_LRS = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 'base_colors': 0.000705237, 'residual_params': 0.000125}
 C4_LRS = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 'base_colors': 0.00025, 'residual_params': 0.008,
           'mlp_weights': 0.003}
-METRIC = {'c1': 'train steps/s (forward + backward + fused Adam), fused SH-3 appearance, 1M Gaussians @1280x720',
+RENDER = ('c3', 'c3sv')
+METRIC = {'c3': 'render FPS (inference, NASG 8 lobes, 3M Gaussians, 64 ring views @1920x1080, views sharded over the GPUs)',
+          'c3sv': 'render FPS (inference, Spherical Voronoi 8 sites, 3M Gaussians, 64 ring views @1920x1080, views sharded over the GPUs)','c1': 'train steps/s (forward + backward + fused Adam), fused SH-3 appearance, 1M Gaussians @1280x720',
           'c4': 'train steps/s (8 views @1920x1080, forward + loss + backward + gradient reduce-scatter + sharded fused Adam + '
                 'parameter all-gather), Neural appearance, 6M Gaussians'}
 # this library's kernels per rendered view (preprocess, chunk scan, compaction, reorder, emit, ranges, bucket scan,
@@ -123,6 +127,10 @@ def scene(wl: dict) -> dict:
     geo = S.geometry(n)
     if wl['model'] == 'sh':
         return {**geo, **S.sh_appearance(n, wl['degree'])}
+    if wl['model'] == 'nasg':
+        return {**geo, **S.nasg_appearance(n, wl['degree'])}
+    if wl['model'] == 'sv':
+        return {**geo, **S.sv_appearance(n, wl['degree'])}
     n_in = wl['feature_dim'] * 2 * wl['n_freq'] + 16
     pad = (n_in + 15) // 16 * 16
     return {**geo, **S.neural_appearance(n, wl['feature_dim'], layer_shapes=S.mlp_layer_shapes(pad, wl['neurons'], wl['hidden']))}
@@ -130,8 +138,8 @@ def scene(wl: dict) -> dict:
 
 def configure(wl: dict) -> None:
     import FasterGSVDACudaBackend as F
-    if wl['model'] == 'sh':
-        F.initialize_appearance('sh', wl['degree'], 'none', 'none', 'relu', True)
+    if wl['model'] in ('sh', 'nasg', 'sv'):
+        F.initialize_appearance(wl['model'], wl['degree'], 'none', 'none', 'relu', True)
         return
     F.initialize_appearance('neural', 0, 'none', 'tanh', 'relu', True)
     F.initialize_residual_mlp(wl['feature_dim'] * 2 * wl['n_freq'] + 16, 3, {'otype': 'Identity'},
@@ -159,6 +167,8 @@ def stage_bytes(stage: str, s: dict) -> float:
         return N * (44 + A) + N * 8 + V * 52
     if stage == 'blend_forward':
         return I * 52 + P * 20
+    if stage == 'blend_inference':
+        return I * 52 + P * 12
     if stage == 'blend_backward':
         return I * 52 + P * 32 + V * 48
     if stage == 'preprocess_backward':
@@ -187,14 +197,41 @@ def run_b200(args, wl_name: str) -> dict | None:
         pg = torch.distributed.group.WORLD
     configure(wl)
     prims = scene(wl)
-    cams = S.ring_cameras(8, wl['width'], wl['height'])
+    cams = S.ring_cameras(wl['views'] if wl_name in RENDER else 8, wl['width'], wl['height'])
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    if wl_name == 'c4':
+    if wl_name in RENDER:
+        import FasterGSVDACudaBackend as F
+        per = (wl['views'] + world - 1) // world
+        mine = [v for v in range(rank * per, min((rank + 1) * per, wl['views']))]
+        dp = {k: v.to(dev).contiguous() for k, v in prims.items()}
+        del prims
+        settings = [settings_of(cams[v], wl['degree'], dev) for v in mine]
+        imgs_host = [torch.empty((wl['height'], wl['width'], 3), pin_memory=True) for _ in range(2)]
+
+        def render(s0):
+            return F.rasterize(dp['means'], dp['scales'], dp['rotations'], dp['opacities'], s0, False, True,
+                               base_colors=dp['base_colors'], residual_params=dp['residual_params'])
+
+        def step():
+            for s0 in settings:
+                render(s0)
+
+        def step_e2e():
+            for k, s0 in enumerate(settings):
+                imgs_host[k % 2].copy_(render(s0), non_blocking=True)
+
+        h2d = 0
+        d2h = len(mine) * wl['height'] * wl['width'] * 3 * 4
+        views_per_step = len(mine)
+        n_params = sum(v.numel() for v in dp.values())
+        stat_settings = settings[0]
+        stat_prims = R._c_primitives(dp['means'], dp['scales'], dp['rotations'], dp['opacities'], None, dp['base_colors'], dp['residual_params'], None)
+    elif wl_name == 'c4':
         from trainer import Trainer
         assert wl['views'] % world == 0, 'the global batch of 8 views must split evenly over the GPUs'
         per = wl['views'] // world
@@ -295,8 +332,8 @@ def run_b200(args, wl_name: str) -> dict | None:
     st = R.ForwardState(R._rasterizer, stat_prims, stat_settings, dev)
     st.preprocess(stat_prims)
     fr = st.frame
-    stats = dict(N=wl['n'], V=fr.n_visible, I=fr.n_instances, pixels=wl['width'] * wl['height'], params=n_params,
-                 appearance_bytes=12 + (4 * 45 if wl['model'] == 'sh' else 4 * wl['feature_dim']))
+    stride = {'sh': 45, 'neural': wl.get('feature_dim', 0), 'nasg': 8 * wl['degree'], 'sv': 7 * wl['degree']}[wl['model']]
+    stats = dict(N=wl['n'], V=fr.n_visible, I=fr.n_instances, pixels=wl['width'] * wl['height'], params=n_params, appearance_bytes=12 + 4 * stride)
     del st
     per_view = {k: (v if k == 'adam' else v / views_per_step) for k, v in stage_ms.items()}
     dominant = max(stage_ms, key=stage_ms.get)
@@ -309,13 +346,15 @@ def run_b200(args, wl_name: str) -> dict | None:
         t = torch.tensor([ms, ms_e2e], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, ms_e2e = float(t[0]), float(t[1])
-    strong = wl_name == 'c4'
-    steps_per_s = 1000.0 / ms if strong else world * 1000.0 / ms
-    e2e_per_s = 1000.0 / ms_e2e if strong else world * 1000.0 / ms_e2e
+    strong = wl_name == 'c4' or wl_name in RENDER
+    render = wl_name in RENDER
+    units_per_step = wl['views'] if render else 1  # frames (render) or training steps per timed step, all ranks together
+    steps_per_s = units_per_step * 1000.0 / ms if strong else world * 1000.0 / ms
+    e2e_per_s = units_per_step * 1000.0 / ms_e2e if strong else world * 1000.0 / ms_e2e
     out = {
         'metric': METRIC[wl_name],
         'value': steps_per_s,
-        'unit': 'steps/s',
+        'unit': 'frames/s' if render else 'steps/s',
         'n_gpus': world,
         'steps': args.steps,
         'warmup': args.warmup,
@@ -325,14 +364,18 @@ def run_b200(args, wl_name: str) -> dict | None:
         'vs_baseline': None,
         'dtype': 'f32 (MLP fp16 operands, fp32 accumulation)' if wl['model'] == 'neural' else 'f32',
         'data': 'synthetic (seeded scene with the configuration shapes and distributions; no dataset available)',
-        'config': {'workload': wl_name + (f": Neural {wl['n'] / 1e6:g}M Gaussians, {wl['views']} views 1920x1080 global batch, data-parallel"
+        'config': {'workload': wl_name + (f": {wl['model']}-{wl['degree']} {wl['n'] / 1e6:g}M Gaussians, {wl['views']} views 1920x1080, inference, "
+                                          f"views sharded" if render else
+                                          f": Neural {wl['n'] / 1e6:g}M Gaussians, {wl['views']} views 1920x1080 global batch, data-parallel"
                                           if strong else f": SH-3 {wl['n'] / 1e6:g}M Gaussians, 1 view 1280x720 per GPU"),
+                   'mpix_per_s': steps_per_s * wl['width'] * wl['height'] / 1e6 if render else None,
                    'n_gaussians': wl['n'], 'width': wl['width'], 'height': wl['height'], 'views_per_gpu': views_per_step,
                    'n_visible_view0': fr.n_visible, 'n_instances_view0': fr.n_instances,
-                   'parallelism': (f'dp{world} (reduce-scatter / sharded Adam / all-gather)' if strong else f'replicas x{world}'),
+                   'parallelism': (f'{world} GPU(s), views split, no collective' if render else
+                                   f'dp{world} (reduce-scatter / sharded Adam / all-gather)' if strong else f'replicas x{world}'),
                    'l2': 'inputs larger than L2 (parameters alone exceed 126 MB)'},
-        'e2e': {'value': e2e_per_s, 'unit': 'steps/s', 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
-        'gpu_launches': (OWN_KERNELS_PER_VIEW * views_per_step + 1) * args.steps,
+        'e2e': {'value': e2e_per_s, 'unit': 'frames/s' if render else 'steps/s', 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
+        'gpu_launches': ((8 * views_per_step) if render else (OWN_KERNELS_PER_VIEW * views_per_step + 1)) * args.steps,
         'clocks': clocks,
         'stage_ms_per_step': {k: round(v, 4) for k, v in stage_ms.items()},
         'roofline': {'kernel': dominant, 'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'peak_kind': peak_kind, 'unit': 'GB/s',
@@ -360,14 +403,14 @@ def cpu_step(wl_name: str, tile_sample: float = 0.05) -> dict:
     from oracle import oracle as O
     wl = dict(WORKLOADS[wl_name])
     scale = 1
-    if wl_name == 'c4':
-        scale = 64
+    if wl_name == 'c4' or wl_name in RENDER:
+        scale = 64 if wl_name == 'c4' else 32
         wl['n'] = wl['n'] // scale
     prims = scene(wl)
     cam = S.ring_cameras(8, wl['width'], wl['height'])[0]
     lib = O.load(False)
-    if wl['model'] == 'sh':
-        a = O.make_appearance('sh', wl['degree'], 0, 0, 1, True)
+    if wl['model'] in ('sh', 'nasg', 'sv'):
+        a = O.make_appearance(wl['model'], wl['degree'], 0, 0, 1, True)
     else:
         n_in = wl['feature_dim'] * 2 * wl['n_freq'] + 16
         neural = dict(feature_dim=wl['feature_dim'], base_input=0, n_freq=wl['n_freq'], sh_mask=15, n_input=n_in,
@@ -400,6 +443,12 @@ def cpu_step(wl_name: str, tile_sample: float = 0.05) -> dict:
     fT = np.zeros((H, W), np.float32)
     nc = np.zeros((H, W), np.uint32)
     lib.orc_blend(V, O._p(sidx), O._p(rec), O._p(ranks), O._p(ranges_s), ctypes.byref(v), O._p(image), O._p(fT), O._p(nc), 1, 0)
+    if wl_name in RENDER:  # inference: one frame = preprocess + binning + blend
+        t2 = time.perf_counter()
+        frame_s = (t1 - t0) * scale + (t2 - t1) * scale / frac
+        sample = (f'{wl_name} frame estimated from one view of a {n}-Gaussian scene (1/32 of 3M) at 1920x1080 with the blend on '
+                  f'{int(keep.sum())} of {T} tiles, scaled x32 (x{32 / frac:.0f} for the blend); single-threaded C restatement')
+        return {'value': 1.0 / frame_s, 'unit': 'frames/s', 'cores': 1, 'kind': 'port', 'sample': sample}
     gimg = np.ascontiguousarray((np.random.default_rng(2).standard_normal((3, H, W)) * 0.01).astype(np.float32))
     rg = np.zeros((max(V, 1), 12))
     lib.orc_blend_backward(V, O._p(sidx), O._p(rec), O._p(ranks), O._p(ranges_s), ctypes.byref(v), O._p(nc), O._p(gimg), O._p(rg))
@@ -449,11 +498,12 @@ def main() -> None:
         runs = [cpu_step(args.workload, args.cpu_sample) for _ in range(max(1, min(args.steps, 2)))]
         v = float(np.median([r['value'] for r in runs]))
         base = dict(runs[0], value=v)
-        print(json.dumps({'impl': 'reference', 'metric': METRIC[args.workload], 'value': v, 'unit': 'steps/s', 'n_gpus': args.gpus,
+        unit = 'frames/s' if args.workload in RENDER else 'steps/s'
+        print(json.dumps({'impl': 'reference', 'metric': METRIC[args.workload], 'value': v, 'unit': unit, 'n_gpus': args.gpus,
                           'steps': len(runs), 'warmup': 0, 'ms_per_step': 1000.0 / v, 'higher_is_better': True,
-                          'scaling': 'strong' if args.workload == 'c4' else 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+                          'scaling': 'strong' if args.workload in ('c4',) + RENDER else 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
                           'config': {'workload': args.workload}, 'cpu_baseline': base,
-                          'e2e': {'value': v, 'unit': 'steps/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
+                          'e2e': {'value': v, 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
         return
     out = run_b200(args, args.workload)
     if out is not None:
