@@ -236,7 +236,7 @@ def run_b200(args, wl_name: str) -> dict | None:
         assert wl['views'] % world == 0, 'the global batch of 8 views must split evenly over the GPUs'
         per = wl['views'] // world
         mine = list(range(rank * per, (rank + 1) * per))
-        trainer = Trainer({k: v.to(dev) for k, v in prims.items()}, C4_LRS, dev, group=pg)
+        trainer = Trainer({k: v.to(dev) for k, v in prims.items()}, C4_LRS, dev, group=pg, exchange=args.exchange, multicast=args.multicast)
         del prims
         settings = [settings_of(cams[v], wl['degree'], dev) for v in mine]
         tg_host = [t.pin_memory() for t in [targets(wl)[v] for v in mine]]
@@ -294,6 +294,10 @@ def run_b200(args, wl_name: str) -> dict | None:
         stat_prims = R._c_primitives(params['means'].detach(), params['scales'].detach(), params['rotations'].detach(),
                                      params['opacities'].detach(), None, params['base_colors'].detach(), params['residual_params'].detach(), None)
 
+    exchange_desc = 'none'
+    if wl_name == 'c4' and world > 1:
+        exchange_desc = ('one fused kernel over NVLink ' + ('multicast (multimem)' if trainer.multicast else 'peer loads/stores')
+                         if trainer.exchange == 'peer' else 'NCCL + fused Adam')
     for _ in range(args.warmup):
         step()
     barrier()
@@ -372,7 +376,7 @@ def run_b200(args, wl_name: str) -> dict | None:
                    'n_gaussians': wl['n'], 'width': wl['width'], 'height': wl['height'], 'views_per_gpu': views_per_step,
                    'n_visible_view0': fr.n_visible, 'n_instances_view0': fr.n_instances,
                    'parallelism': (f'{world} GPU(s), views split, no collective' if render else
-                                   f'dp{world} (reduce-scatter / sharded Adam / all-gather)' if strong else f'replicas x{world}'),
+                                   f'dp{world} (reduce-scatter / sharded Adam / all-gather: {exchange_desc})' if strong else f'replicas x{world}'),
                    'l2': 'inputs larger than L2 (parameters alone exceed 126 MB)'},
         'e2e': {'value': e2e_per_s, 'unit': 'frames/s' if render else 'steps/s', 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
         'gpu_launches': ((8 * views_per_step) if render else (OWN_KERNELS_PER_VIEW * views_per_step + 1)) * args.steps,
@@ -485,6 +489,8 @@ def main() -> None:
     ap.add_argument('--workload', default='c4', choices=sorted(WORKLOADS))
     ap.add_argument('--cpu-sample', type=float, default=0.05)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--exchange', default='auto', choices=['auto', 'peer', 'nccl'], help='c4 data-parallel exchange (N > 1)')
+    ap.add_argument('--multicast', action='store_true', help='peer exchange through NVSwitch multicast (multimem)')
     ap.add_argument('--gaussians', type=int, default=0, help='override the workload\'s Gaussian count (small profiling cases)')
     ap.add_argument('--views', type=int, default=0, help='override the workload\'s global batch of views (c4)')
     args = ap.parse_args()

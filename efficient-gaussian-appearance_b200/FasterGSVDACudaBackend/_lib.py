@@ -58,6 +58,11 @@ class AdamSegment(ctypes.Structure):
                 ('n_learning_rates', c_int32), ('beta1', c_double), ('beta2', c_double), ('eps', c_double)]
 
 
+class PeerBuffers(ctypes.Structure):
+    _fields_ = [('n_ranks', c_int), ('grads', c_void_p * 8), ('params', c_void_p * 8), ('local_params', c_void_p),
+                ('multicast_grads', c_void_p), ('multicast_params', c_void_p)]
+
+
 _P = ctypes.POINTER
 PROTOTYPES = {
     'fgs_last_error': (ctypes.c_char_p, []),
@@ -87,6 +92,7 @@ PROTOTYPES = {
     'fgs_profile_collect': (c_int, [ctypes.c_char_p, c_size_t, _P(c_double), c_int, _P(c_int)]),
     'fgs_loss_workspace_bytes': (c_int, [c_int, c_int, c_int, _P(c_size_t)]),
     'fgs_tc_selftest': (c_int, [c_void_p, _P(c_int), c_void_p]),
+    'fgs_dp_shard_adam': (c_int, [_P(AdamSegment), c_int, _P(PeerBuffers), c_void_p]),
     'fgs_l1_dssim': (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, ctypes.c_float, ctypes.c_float, c_void_p, c_void_p, c_void_p, c_size_t,
                              c_void_p]),
 }

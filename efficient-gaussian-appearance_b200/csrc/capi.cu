@@ -587,16 +587,16 @@ int fgs_frame_buffers(const fgs_frame* frame, void* prim_ws, void* tile_ws, void
     return FGS_OK;
 }
 
-int fgs_adam_step(const fgs_adam_segment* segs, int n, void* stream) {
-    if (n < 0 || n > fgs::kMaxAdamSegments || (n > 0 && !segs)) return fail(FGS_ERR_INVALID_ARGUMENT, "between 0 and 12 segments");
-    fgs::AdamSegment S[fgs::kMaxAdamSegments];
+// converts and checks the C-ABI segments; returns the number kept (empty segments are dropped) or -1
+static int convert_segments(const fgs_adam_segment* segs, int n, fgs::AdamSegment* S) {
+    if (n < 0 || n > fgs::kMaxAdamSegments || (n > 0 && !segs)) return fail(FGS_ERR_INVALID_ARGUMENT, "between 0 and 12 segments"), -1;
     int k = 0;
     for (int i = 0; i < n; i++) {
         const fgs_adam_segment& a = segs[i];
         if (a.n_elements <= 0) continue;
-        if (!a.param || !a.grad || !a.exp_avg || !a.exp_avg_sq) return fail(FGS_ERR_INVALID_ARGUMENT, "segment pointer is NULL");
-        if (a.n_learning_rates < 1 || a.n_learning_rates > 7) return fail(FGS_ERR_INVALID_ARGUMENT, "between 1 and 7 learning rates are supported");
-        if (a.step < 1) return fail(FGS_ERR_INVALID_ARGUMENT, "step must be >= 1");
+        if (!a.param || !a.grad || !a.exp_avg || !a.exp_avg_sq) return fail(FGS_ERR_INVALID_ARGUMENT, "segment pointer is NULL"), -1;
+        if (a.n_learning_rates < 1 || a.n_learning_rates > 7) return fail(FGS_ERR_INVALID_ARGUMENT, "between 1 and 7 learning rates are supported"), -1;
+        if (a.step < 1) return fail(FGS_ERR_INVALID_ARGUMENT, "step must be >= 1"), -1;
         const double bc1 = 1.0 / (1.0 - std::pow(a.beta1, static_cast<double>(a.step)));
         const double bc2 = 1.0 / std::sqrt(1.0 - std::pow(a.beta2, static_cast<double>(a.step)));
         fgs::AdamSegment& s = S[k++];
@@ -610,8 +610,37 @@ int fgs_adam_step(const fgs_adam_segment* segs, int n, void* stream) {
         s.eps = static_cast<float>(a.eps);
         s.bc2_sqrt_rcp = static_cast<float>(bc2);
     }
+    return k;
+}
+
+int fgs_adam_step(const fgs_adam_segment* segs, int n, void* stream) {
+    fgs::AdamSegment S[fgs::kMaxAdamSegments];
+    const int k = convert_segments(segs, n, S);
+    if (k < 0) return FGS_ERR_INVALID_ARGUMENT;
     ProfScope p_("adam", static_cast<cudaStream_t>(stream));
     FGS_CUDA(fgs::launch_adam(S, k, static_cast<cudaStream_t>(stream)), "adam");
+    return FGS_OK;
+}
+
+int fgs_dp_shard_adam(const fgs_adam_segment* segs, int n, const fgs_peer_buffers* peers, void* stream) {
+    if (!peers) return fail(FGS_ERR_INVALID_ARGUMENT, "peers is NULL");
+    if (peers->n_ranks < 1 || peers->n_ranks > FGS_MAX_PEERS) return fail(FGS_ERR_INVALID_ARGUMENT, "n_ranks must be in [1, 8]");
+    if (!peers->local_params) return fail(FGS_ERR_INVALID_ARGUMENT, "local_params is NULL");
+    if ((peers->multicast_grads == nullptr) != (peers->multicast_params == nullptr))
+        return fail(FGS_ERR_INVALID_ARGUMENT, "give both multicast addresses or neither");
+    if (!peers->multicast_grads)
+        for (int r = 0; r < peers->n_ranks; r++)
+            if (!peers->grads[r] || !peers->params[r]) return fail(FGS_ERR_INVALID_ARGUMENT, "peer buffer pointer is NULL");
+    fgs::AdamSegment S[fgs::kMaxAdamSegments];
+    const int k = convert_segments(segs, n, S);
+    if (k < 0) return FGS_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < k; i++)
+        if (S[i].param < peers->local_params) return fail(FGS_ERR_INVALID_ARGUMENT, "segment parameters must lie in the local flat buffer");
+    static_assert(FGS_MAX_PEERS == fgs::kMaxPeers, "peer table size");
+    ProfScope p_("exchange_adam", static_cast<cudaStream_t>(stream));
+    FGS_CUDA(fgs::launch_dp_shard_adam(S, k, peers->grads, peers->params, peers->n_ranks, peers->local_params, peers->multicast_grads,
+                                       peers->multicast_params, static_cast<cudaStream_t>(stream)),
+             "exchange adam");
     return FGS_OK;
 }
 

@@ -86,6 +86,10 @@ struct AdamSegment {
     float beta1, beta2, eps, bc2_sqrt_rcp;
 };
 constexpr int kMaxAdamSegments = 12;
+constexpr int kMaxPeers = 8;
 cudaError_t launch_adam(const AdamSegment* segs, int n_segs, cudaStream_t s);
+// sharded Adam fused with the gradient sum over all ranks and the parameter broadcast (peer memory / multicast)
+cudaError_t launch_dp_shard_adam(const AdamSegment* segs, int n_segs, const float* const* grads, float* const* params, int n_ranks,
+                                 const float* local_params, const float* mc_grads, float* mc_params, cudaStream_t s);
 
 }  // namespace fgs

@@ -13,6 +13,13 @@ The flat buffer holds the parameter groups one after another (means, scales, rot
 residual parameters, MLP weights), each padded to a multiple of 64 floats, so a rank's slice can span several
 groups; the Adam segments carry each group's learning rate(s), betas and column offset.
 With one rank the collectives are skipped and the result equals the sequential accumulation over the same views.
+
+Exchange modes: 'nccl' runs steps 2-4 as NCCL reduce-scatter, the fused Adam kernel and NCCL all-gather; 'peer'
+keeps the flat buffers in symmetric memory (mapped into every rank) and runs steps 2-4 as one kernel
+(fgs_dp_shard_adam) that sums the slice's gradients over NVLink (or through the switch with multicast), applies Adam
+and writes the new parameters into every rank's buffer, between two device-side barriers. 'auto' picks 'peer' when
+symmetric memory can be set up on the group and falls back to 'nccl' otherwise. The switch-multicast variant
+(multimem) is opt-in (multicast=True).
 """
 from __future__ import annotations
 
@@ -105,7 +112,7 @@ class Trainer:
     """Holds the flat parameter / gradient buffers of one replica and runs data-parallel steps."""
 
     def __init__(self, prims: dict[str, torch.Tensor], lrs: dict[str, float | list], device: torch.device, group=None,
-                 mlp_betas: tuple = (0.9, 0.99)) -> None:
+                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool = False) -> None:
         self.device = device
         self.pg = group
         self.world = torch.distributed.get_world_size(group) if group is not None else 1
@@ -122,8 +129,20 @@ class Trainer:
         shard = (off + 64 * self.world - 1) // (64 * self.world) * 64
         self.shard = shard
         self.total = shard * self.world
-        self.params = torch.zeros(self.total, dtype=torch.float32, device=device)
-        self.grads = torch.zeros(self.total, dtype=torch.float32, device=device)
+        self.exchange = 'nccl'
+        self.peers = None
+        self.use_multicast = multicast
+        if self.world > 1 and exchange in ('peer', 'auto'):
+            try:
+                self._setup_peer_buffers()
+                self.exchange = 'peer'
+            except Exception as err:  # symmetric memory unavailable on this group / driver
+                if exchange == 'peer':
+                    raise
+                self.exchange_error = str(err)
+        if self.exchange != 'peer':
+            self.params = torch.zeros(self.total, dtype=torch.float32, device=device)
+            self.grads = torch.zeros(self.total, dtype=torch.float32, device=device)
         for g in self.groups:
             self.params[g.offset:g.offset + g.numel].copy_(prims[g.name].reshape(-1))
         self.exp_avg = torch.zeros(shard, dtype=torch.float32, device=device)
@@ -134,6 +153,31 @@ class Trainer:
         self.loss_fn = FusedLoss()
         self._image = None
         self._grad_image = None
+
+    def _setup_peer_buffers(self) -> None:
+        """Flat buffers in symmetric memory: every rank's buffers mapped on every device (peer pointers), plus the
+        NVLink multicast mappings when the switch provides them."""
+        import torch.distributed._symmetric_memory as symm
+        name = self.pg.group_name
+        if hasattr(symm, 'enable_symm_mem_for_group') and not symm.is_symm_mem_enabled_for_group(name):
+            symm.enable_symm_mem_for_group(name)
+        self.params = symm.empty(self.total, dtype=torch.float32, device=self.device)
+        self.grads = symm.empty(self.total, dtype=torch.float32, device=self.device)
+        self.params.zero_()
+        self.grads.zero_()
+        self.h_params = symm.rendezvous(self.params, name)
+        self.h_grads = symm.rendezvous(self.grads, name)
+        pb = _lib.PeerBuffers()
+        pb.n_ranks = self.world
+        for r in range(self.world):
+            pb.grads[r] = self.h_grads.buffer_ptrs[r]
+            pb.params[r] = self.h_params.buffer_ptrs[r]
+        pb.local_params = self.params.data_ptr()
+        mg, mp = int(getattr(self.h_grads, 'multicast_ptr', 0) or 0), int(getattr(self.h_params, 'multicast_ptr', 0) or 0)
+        self.multicast = bool(mg and mp) and self.use_multicast
+        pb.multicast_grads = mg if self.multicast else None
+        pb.multicast_params = mp if self.multicast else None
+        self.peers = pb
 
     def view(self, buf: torch.Tensor, name: str) -> torch.Tensor | None:
         for g in self.groups:
@@ -172,8 +216,10 @@ class Trainer:
             st.backward(cp, self._image, self._grad_image, cg, None, accumulate=k > 0)
         return total
 
-    def adam_segments(self) -> list:
-        """Adam segments of this rank's slice [rank*S, (rank+1)*S), split at parameter-group boundaries."""
+    def adam_segments(self, grad_slice: torch.Tensor | None = None) -> list:
+        """Adam segments of this rank's slice [rank*S, (rank+1)*S), split at parameter-group boundaries (gradients from
+        grad_slice, by default the reduce-scattered shard)."""
+        grad_shard = self.grad_shard if grad_slice is None else grad_slice
         lo, hi = self.rank * self.shard, (self.rank + 1) * self.shard
         segs = []
         for g in self.groups:
@@ -181,7 +227,7 @@ class Trainer:
             if a >= b:
                 continue
             s0 = a - lo
-            segs.append(_segment(self.params[a:b], self.grad_shard[s0:s0 + (b - a)], self.exp_avg[s0:s0 + (b - a)],
+            segs.append(_segment(self.params[a:b], grad_shard[s0:s0 + (b - a)], self.exp_avg[s0:s0 + (b - a)],
                                  self.exp_avg_sq[s0:s0 + (b - a)], self.step_count, g.lr, g.betas, 1e-15, column_offset=a - g.offset))
         return segs
 
@@ -189,6 +235,13 @@ class Trainer:
         """Exchange step: reduce-scatter of the gradients, Adam on this rank's slice, all-gather of the parameters.
         `adam_fn(segments)` replaces the fused GPU Adam (used by the CPU tests with the checker's Adam)."""
         self.step_count += 1
+        if self.exchange == 'peer':
+            self.h_grads.barrier(channel=0)  # every rank's gradients are final
+            segs = self.adam_segments(self.grads[self.rank * self.shard:(self.rank + 1) * self.shard])
+            arr = (_lib.AdamSegment * len(segs))(*segs)
+            _lib.check(_lib.lib.fgs_dp_shard_adam(arr, len(segs), ctypes.byref(self.peers), torch.cuda.current_stream(self.device).cuda_stream))
+            self.h_params.barrier(channel=1)  # every rank's parameters are written
+            return
         if self.world > 1:
             torch.distributed.reduce_scatter_tensor(self.grad_shard, self.grads, group=self.pg)
         (adam_fn or adam_step_segments)(self.adam_segments())

@@ -180,6 +180,25 @@ int fgs_frame_buffers(const fgs_frame* frame, void* prim_ws, void* tile_ws, void
 /* fused Adam over up to 12 segments in one launch (adam/src/adam.cu:18-42 per element) */
 int fgs_adam_step(const fgs_adam_segment* segments, int n_segments, void* stream);
 
+/* Data-parallel training (no reference counterpart: the reference trains on one GPU, Renderer.py:62-65): the
+ * gradient reduce-scatter, the sharded Adam and the parameter all-gather of one step in one kernel over NVLink.
+ * Every rank holds identically laid-out flat fp32 parameter and gradient buffers mapped into all ranks (symmetric
+ * memory); `segments` describe this rank's slice (param / grad pointers inside the local buffers, moments local).
+ * Each slice element sums the gradients of all ranks (rank order, peer loads; or multimem.ld_reduce through the
+ * switch when multicast addresses are given), takes the Adam step and writes the parameter into every rank's
+ * buffer (peer stores, or multimem.st). The caller places a cross-rank barrier before (all gradients final) and
+ * after (all parameters written). */
+#define FGS_MAX_PEERS 8
+typedef struct fgs_peer_buffers {
+    int n_ranks;                   /* 1..8 */
+    const float* grads[FGS_MAX_PEERS];   /* every rank's flat gradient buffer as mapped on this device */
+    float* params[FGS_MAX_PEERS];        /* every rank's flat parameter buffer as mapped on this device */
+    const float* local_params;     /* this rank's parameter buffer (the segments' parameter pointers lie in it) */
+    const float* multicast_grads;  /* multicast addresses of the two buffers, or both NULL */
+    float* multicast_params;
+} fgs_peer_buffers;
+int fgs_dp_shard_adam(const fgs_adam_segment* segments, int n_segments, const fgs_peer_buffers* peers, void* stream);
+
 /* Fused photometric loss of the training step and its image gradient: for planar [C,H,W] fp32 images,
  * loss = l1_weight * mean|image - target| + dssim_weight * (1 - mean SSIM(image, target)) with an 11x11 Gaussian
  * window (sigma 1.5, zero padding, C1 = 0.01^2, C2 = 0.03^2). Replaces the caller-side loss of the reference
