@@ -80,6 +80,8 @@ fgs::PrimBuffers carve_prim(void* ws, uint64_t n, size_t* bytes) {
     B.rank_of = c.take<uint32_t>(n);
     B.chunk_stats = c.take<uint2>(chunks);
     B.chunk_off = c.take<uint32_t>(chunks);
+    B.group_vis = c.take<uint32_t>((chunks + 1023) / 1024);
+    B.group_inst = c.take<unsigned long long>((chunks + 1023) / 1024);
     B.counters = c.take<unsigned long long>(2);
     B.keys_a = c.take<uint32_t>(n);
     B.keys_b = c.take<uint32_t>(n);

@@ -48,45 +48,84 @@ __global__ void __launch_bounds__(kChunk) preprocess_fwd_kernel(Params P, Appear
     store_primitive(B, i, in_range, G, color, blockIdx.x);
 }
 
-// exclusive scan of the per-chunk visible counts (one CTA); also totals visible primitives and instances
-__global__ void __launch_bounds__(1024) chunk_scan_kernel(const uint2* __restrict__ stats, uint32_t* __restrict__ off,
-                                                          unsigned long long* __restrict__ counters, uint32_t n_chunks) {
-    __shared__ uint32_t warp_sums[32];
-    __shared__ uint32_t carry;
-    __shared__ unsigned long long inst_total;
-    if (threadIdx.x == 0) { carry = 0; inst_total = 0; }
-    __syncthreads();
+// Compaction offsets in three parallel phases: per group of 1024 chunks the visible and instance sums; one CTA scans
+// the group sums (and writes the totals); per group the exclusive scan of the chunks' visible counts.
+constexpr int kScanGroup = 1024;
+
+__device__ inline uint32_t block1024_exclusive_scan(uint32_t x, uint32_t* warp_sums, uint32_t* total) {
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    unsigned long long my_inst = 0;
-    for (uint32_t base = 0; base < n_chunks; base += 1024) {
-        const uint32_t c = base + threadIdx.x;
-        const uint2 s = c < n_chunks ? stats[c] : make_uint2(0, 0);
-        my_inst += s.y;
-        uint32_t x = s.x;
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
-            if (lane >= static_cast<uint32_t>(o)) x += y;
-        }
-        if (lane == 31) warp_sums[warp] = x;
-        __syncthreads();
-        if (warp == 0) {
-            uint32_t w = warp_sums[lane];
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
-                if (lane >= static_cast<uint32_t>(o)) w += y;
-            }
-            warp_sums[lane] = w;
-        }
-        __syncthreads();
-        const uint32_t incl = x + (warp > 0 ? warp_sums[warp - 1] : 0u) + carry;
-        if (c < n_chunks) off[c] = incl - s.x;
-        __syncthreads();
-        if (threadIdx.x == 1023) carry = incl;
-        __syncthreads();
+    uint32_t incl = x;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= static_cast<uint32_t>(o)) incl += y;
     }
-    atomicAdd(&inst_total, my_inst);
+    if (lane == 31) warp_sums[warp] = incl;
     __syncthreads();
-    if (threadIdx.x == 0) { counters[0] = carry; counters[1] = inst_total; }
+    if (warp == 0) {
+        uint32_t w = warp_sums[lane];
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= static_cast<uint32_t>(o)) w += y;
+        }
+        warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const uint32_t r = incl - x + (warp > 0 ? warp_sums[warp - 1] : 0u);
+    if (total) *total = warp_sums[31];
+    __syncthreads();
+    return r;
+}
+
+__global__ void __launch_bounds__(kScanGroup) chunk_group_sums(const uint2* __restrict__ stats, uint32_t n_chunks, uint32_t* __restrict__ g_vis,
+                                                              unsigned long long* __restrict__ g_inst) {
+    __shared__ uint32_t warp_sums[32];
+    __shared__ unsigned long long inst;
+    if (threadIdx.x == 0) inst = 0;
+    const uint32_t c = blockIdx.x * kScanGroup + threadIdx.x;
+    const uint2 st = c < n_chunks ? stats[c] : make_uint2(0, 0);
+    uint32_t tot = 0;
+    block1024_exclusive_scan(st.x, warp_sums, &tot);
+    unsigned long long y = st.y;
+    for (int o = 16; o > 0; o >>= 1) y += __shfl_down_sync(0xffffffffu, y, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&inst, y);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        g_vis[blockIdx.x] = tot;
+        g_inst[blockIdx.x] = inst;
+    }
+}
+
+__global__ void __launch_bounds__(kScanGroup) chunk_group_scan(uint32_t* __restrict__ g_vis, const unsigned long long* __restrict__ g_inst,
+                                                              uint32_t n_groups, unsigned long long* __restrict__ counters) {
+    __shared__ uint32_t warp_sums[32];
+    __shared__ unsigned long long inst;
+    if (threadIdx.x == 0) inst = 0;
+    uint32_t carry = 0;
+    unsigned long long my_inst = 0;
+    for (uint32_t base = 0; base < n_groups; base += kScanGroup) {
+        const uint32_t g = base + threadIdx.x;
+        const uint32_t x = g < n_groups ? g_vis[g] : 0u;
+        if (g < n_groups) my_inst += g_inst[g];
+        uint32_t tot = 0;
+        const uint32_t ex = block1024_exclusive_scan(x, warp_sums, &tot);
+        if (g < n_groups) g_vis[g] = carry + ex;
+        carry += tot;
+    }
+    atomicAdd(&inst, my_inst);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        counters[0] = carry;
+        counters[1] = inst;
+    }
+}
+
+__global__ void __launch_bounds__(kScanGroup) chunk_offsets(const uint2* __restrict__ stats, uint32_t n_chunks, const uint32_t* __restrict__ g_vis,
+                                                           uint32_t* __restrict__ off) {
+    __shared__ uint32_t warp_sums[32];
+    const uint32_t c = blockIdx.x * kScanGroup + threadIdx.x;
+    const uint32_t x = c < n_chunks ? stats[c].x : 0u;
+    const uint32_t ex = block1024_exclusive_scan(x, warp_sums, nullptr);
+    if (c < n_chunks) off[c] = g_vis[blockIdx.x] + ex;
 }
 
 // writes (depth key, primitive index) of visible primitives in primitive order
@@ -225,7 +264,10 @@ cudaError_t launch_preprocess_fwd(const Params& P, const AppearanceConfig& A, co
 cudaError_t launch_compaction(const PrimBuffers& B, uint32_t n, cudaStream_t s) {
     const int chunks = grid_of(n, kChunk);
     if (chunks == 0) return cudaMemsetAsync(B.counters, 0, 2 * sizeof(unsigned long long), s);
-    chunk_scan_kernel<<<1, 1024, 0, s>>>(B.chunk_stats, B.chunk_off, B.counters, chunks);
+    const int groups = (chunks + kScanGroup - 1) / kScanGroup;
+    chunk_group_sums<<<groups, kScanGroup, 0, s>>>(B.chunk_stats, chunks, B.group_vis, B.group_inst);
+    chunk_group_scan<<<1, kScanGroup, 0, s>>>(B.group_vis, B.group_inst, groups, B.counters);
+    chunk_offsets<<<groups, kScanGroup, 0, s>>>(B.chunk_stats, chunks, B.group_vis, B.chunk_off);
     compact_kernel<<<chunks, kChunk, 0, s>>>(B.n_touched, B.depth_key, B.chunk_off, B.keys_a, B.idx_a, B.vis_idx, n);
     return cudaGetLastError();
 }

@@ -47,6 +47,8 @@ struct PrimBuffers {
     uint32_t* rank_of;     // [N] depth rank or kInvalidRank
     uint2* chunk_stats;    // [chunks] (visible, instances)
     uint32_t* chunk_off;   // [chunks] exclusive visible offsets
+    uint32_t* group_vis;   // [chunks / 1024] visible sums, then their exclusive offsets
+    unsigned long long* group_inst;  // [chunks / 1024] instance sums
     unsigned long long* counters;  // [0] visible, [1] instances
     uint32_t* keys_a; uint32_t* keys_b;
     uint32_t* idx_a;  uint32_t* idx_b;
