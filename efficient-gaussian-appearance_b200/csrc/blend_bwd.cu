@@ -13,6 +13,14 @@
 
 namespace fgs {
 
+// reciprocal of x in [kOneMinusAlphaEps, 1] by the hardware approximation (only gradients use it; the acceptance and
+// termination decisions that must match the forward do not)
+__device__ inline float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 template <bool kAbs>
 __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A, const float* __restrict__ image, const float* __restrict__ grad_image,
                                                                      TileBuffers T, GradRecord* __restrict__ grads) {
@@ -28,22 +36,24 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
     const uint2 range = A.ranges[tile];
     const uint32_t n = range.y - range.x;
     uint32_t last = 0;
-    float cfr = 0.0f, cfg = 0.0f, cfb = 0.0f, gr = 0.0f, gg = 0.0f, gb = 0.0f, gac = 0.0f;
+    float gcf = 0.0f, gr = 0.0f, gg = 0.0f, gb = 0.0f, gac = 0.0f;
     if (inside) {
         const size_t pix = static_cast<size_t>(py) * A.width + px;
         const size_t np = static_cast<size_t>(A.width) * A.height;
         last = T.n_contrib[static_cast<size_t>(tile) * kTilePixels + local];
         const float tf = T.final_T[static_cast<size_t>(tile) * kTilePixels + local];
         const float bgr = A.bg[0], bgg = A.bg[1], bgb = A.bg[2];
-        cfr = image[pix] - tf * bgr;
-        cfg = image[np + pix] - tf * bgg;
-        cfb = image[2 * np + pix] - tf * bgb;
+        const float cfr = image[pix] - tf * bgr;
+        const float cfg = image[np + pix] - tf * bgg;
+        const float cfb = image[2 * np + pix] - tf * bgb;
         gr = grad_image[pix];
         gg = grad_image[np + pix];
         gb = grad_image[2 * np + pix];
         gac = tf * -(gr * bgr + gg * bgg + gb * bgb);
+        gcf = cfr * gr + cfg * gg + cfb * gb;  // (final colour without background) . dL/dcolour
     }
-    float tr = 1.0f, accr = 0.0f, accg = 0.0f, accb = 0.0f;
+    // accd = (colour accumulated so far) . dL/dcolour, so that (final - accumulated) . dL/dcolour = gcf - accd
+    float tr = 1.0f, accd = 0.0f;
     bool done = last == 0;
     for (uint32_t start = 0; start < n; start += kTilePixels) {
         if (__syncthreads_and(done)) break;
@@ -82,13 +92,12 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
                     const float alpha = __fmul_rn(a.w, G);
                     const float4 c = st[k].c;
                     const float w = tr * alpha;
-                    accr = fmaf(w, c.x, accr);
-                    accg = fmaf(w, c.y, accg);
-                    accb = fmaf(w, c.z, accb);
+                    const float cg = c.x * gr + c.y * gg + c.z * gb;
+                    accd = fmaf(w, cg, accd);
                     const float oma = __fsub_rn(1.0f, alpha);
-                    const float rcp = __frcp_rn(fmaxf(oma, kOneMinusAlphaEps));  // = 1 / x, correctly rounded
-                    const float afr = cfr - accr, afg = cfg - accg, afb = cfb - accb;
-                    const float dl_da = (tr * c.x - afr * rcp) * gr + (tr * c.y - afg * rcp) * gg + (tr * c.z - afb * rcp) * gb + gac * rcp;
+                    const float rcp = rcp_approx(fmaxf(oma, kOneMinusAlphaEps));
+                    // sum_c (tr c_c - (final_c - accumulated_c) / (1 - alpha)) g_c + gac / (1 - alpha)
+                    const float dl_da = fmaf(tr, cg, rcp * (gac - (gcf - accd)));
                     const float hl = -alpha * dl_da;
                     const float hx = hl * dx, hy = hl * dy;
                     v[0] = hx; v[1] = hy; v[2] = hx * dx; v[3] = hx * dy;

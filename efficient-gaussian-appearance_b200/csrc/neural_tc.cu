@@ -221,16 +221,23 @@ struct RowData {
     f3 mean;
     float4 f[kPrefetchFeatures / 8];  // this thread's half of the latent features (fast path)
     float4 q2, g1;                    // colour of the record and its blend gradient sums (backward)
+    f3 base;                          // base colour parameters
 };
 
-// (backward data with rank_of non-null)
-__device__ inline void load_row(const Params& P, const AppearanceConfig& A, bool fast, int half, const uint32_t* __restrict__ vis, uint32_t n_rows,
-                                uint32_t gi, const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec,
-                                const GradRecord* __restrict__ grads, RowData& d) {
+// The prefetch of a row runs in three stages placed in different phases of the current tile, because each stage's
+// addresses come from the loads of the one before: a thread that issued a stage's loads never waits on them inside
+// the same phase (in particular not before issuing the MMAs).
+// stage 1: primitive index of tile row gi
+__device__ inline void load_row_index(const uint32_t* __restrict__ vis, uint32_t n_rows, uint32_t gi, RowData& d) {
     d.valid = gi < n_rows;
     d.i = d.valid ? vis[gi] : 0u;
+}
+// stage 2: the primitive's parameters (and, backward, its depth rank)
+__device__ inline void load_row_params(const Params& P, const AppearanceConfig& A, bool fast, int half, const uint32_t* __restrict__ rank_of,
+                                       RowData& d) {
     if (!d.valid) return;
     d.mean = ld3(P.means, d.i);
+    d.base = ld3(P.base, d.i);
     const int F = A.feature_dim;
     if (fast) {
         const float4* src = reinterpret_cast<const float4*>(P.residual + static_cast<size_t>(d.i) * F + half * (F / 2));
@@ -238,11 +245,13 @@ __device__ inline void load_row(const Params& P, const AppearanceConfig& A, bool
         for (int q = 0; q < kPrefetchFeatures / 8; q++)
             if (8 * q < F) d.f[q] = src[q];
     }
-    if (rank_of) {
-        d.r = rank_of[d.i];
-        d.q2 = sorted_rec[d.r].q2;
-        d.g1 = grads[d.r].g1;
-    }
+    if (rank_of) d.r = rank_of[d.i];
+}
+// stage 3 (backward): the record colour and blend gradient sums at the depth rank
+__device__ inline void load_row_rank(const Record* __restrict__ sorted_rec, const GradRecord* __restrict__ grads, RowData& d) {
+    if (!d.valid) return;
+    d.q2 = sorted_rec[d.r].q2;
+    d.g1 = grads[d.r].g1;
 }
 
 // this thread's part of the MLP input row: with the fast path each thread encodes its half of the features
@@ -394,18 +403,23 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
     const bool fast = fast_features(P, A);
     const uint32_t x_row = sbase + plan.x_smem + tc::kmajor_offset(row, 0, plan.kin);
     RowData cur, nxt;
-    if (blockIdx.x < n_tiles) load_row(P, A, fast, half, vis, n_rows, blockIdx.x * kTcRows + row, nullptr, nullptr, nullptr, cur);
+    if (blockIdx.x < n_tiles) {
+        load_row_index(vis, n_rows, blockIdx.x * kTcRows + row, cur);
+        load_row_params(P, A, fast, half, nullptr, cur);
+    }
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const uint32_t next = tile + gridDim.x;
+        const bool more = next < n_tiles;
+        if (more) load_row_index(vis, n_rows, next * kTcRows + row, nxt);
         write_input_row(P, A, v, deg, cur, fast, half, x_row, plan.kin, nullptr, row);
         sync_tile();
-        const uint32_t next = tile + gridDim.x;
-        if (next < n_tiles) load_row(P, A, fast, half, vis, n_rows, next * kTcRows + row, nullptr, nullptr, nullptr, nxt);
         for (int l = 0; l < plan.layers; l++) {
             if (t == 0) {
                 issue_forward(plan, sbase, tb, l);
                 tc::commit(&bar);
             }
             __syncwarp();
+            if (l == 0 && more) load_row_params(P, A, fast, half, nullptr, nxt);
             alive = wait_all(&bar, phase);
             if (!alive) break;
             if (l < plan.layers - 1) {
@@ -416,7 +430,7 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
                 if (cur.valid) {
                     const f3 res = residual_act3(A.res_act, mk3(__half2float(__float2half_rn(y[0])), __half2float(__float2half_rn(y[1])),
                                                                  __half2float(__float2half_rn(y[2]))));
-                    const f3 base = base_act3(A.base_act, ld3(P.base, cur.i));
+                    const f3 base = base_act3(A.base_act, cur.base);
                     f3 color = color_act3(A.color_act, base + res);
                     if (!v.render_base) {
                         const f3 bc = color_act3(A.color_act, base);
@@ -444,11 +458,16 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
 }
 
 // Input gradient of a row (loss-scaled dL/dinput in TMEM columns 0..kin) -> feature, base-input and direction
-// gradients. Fast path: each thread handles its half of the features (groups of 4 = 8 columns per TMEM load, sine
-// and cosine from `trig` when kept, else recomputed), the second thread also the base-input and SH columns.
-// Otherwise the first thread walks every column. Returns true for the thread that holds gbase_in / gdir.
-__device__ inline bool input_grad_row(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t t_row, const RowData& d, bool fast,
-                                      int half, const float* trig, int row, int kin, int deg, f3 dir, f3& gbase_in, f3& gdir) {
+// gradients. Fast path: each thread handles its half of the features (sine and cosine from `trig` when kept, else
+// recomputed); with 32 features one TMEM load brings a thread's 32 columns. The remaining columns (base inputs, SH
+// inputs, padding): with the full SH input (all four bands) and no base input, the first thread takes the SH columns
+// (direction gradient) and the second the base colour; otherwise the second thread walks them. Without the fast
+// path the first thread walks every column. Returns which of the row's remaining gradients this thread holds:
+// kOwnDir (gdir, means) and / or kOwnBase (gbase_in, base colour).
+constexpr int kOwnDir = 1, kOwnBase = 2;
+
+__device__ inline int input_grad_row(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t t_row, const RowData& d, bool fast,
+                                     int half, const float* trig, int row, int kin, int deg, f3 dir, f3& gbase_in, f3& gdir) {
     const float inv = 1.0f / kLossScale;
     const int F = A.feature_dim, nf = A.n_freq, per = nf > 0 ? 2 * nf : 1, nraw = F + (A.base_input ? 3 : 0);
     const int enc = nraw * per;
@@ -460,17 +479,8 @@ __device__ inline bool input_grad_row(const Params& P, const AppearanceConfig& A
     int c = 0;
     if (fast) {
         const int jb = half * (F / 2);
-        float4 old[kPrefetchFeatures / 8];  // accumulated values, loaded before the TMEM reads
-#pragma unroll
-        for (int q = 0; q < kPrefetchFeatures / 8; q++)
-            old[q] = (acc && valid && 4 * q < F / 2) ? reinterpret_cast<const float4*>(gout + jb)[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-        for (int q = 0; q < kPrefetchFeatures / 8; q++) {
-            if (4 * q >= F / 2) break;
-            const int j = jb + 4 * q;  // features j .. j + 3, columns 2j .. 2j + 7
-            float g[8];
-            tc::ld8(t_row + 2 * j, g);
-            if (!valid) continue;
+        // features j .. j + 3 from their 8 columns g[0..7]
+        auto group = [&](int j, const float* g) {
             float sn[4], cs[4];
             if (trig) {
 #pragma unroll
@@ -488,14 +498,38 @@ __device__ inline bool input_grad_row(const Params& P, const AppearanceConfig& A
             float gv[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) gv[k] = (cs[k] * g[2 * k] - sn[k] * g[2 * k + 1]) * inv;
-            float4 o = make_float4(gv[0], gv[1], gv[2], gv[3]);
-            if (acc) o = make_float4(old[q].x + o.x, old[q].y + o.y, old[q].z + o.z, old[q].w + o.w);
-            *reinterpret_cast<float4*>(gout + j) = o;
+            const float4 o = make_float4(gv[0], gv[1], gv[2], gv[3]);
+            float4* dst = reinterpret_cast<float4*>(gout + j);
+            if (acc) atomicAdd(dst, o);  // one addition per element and launch: the same value as load, add, store
+            else *dst = o;
+        };
+        if (F == 32) {
+            float g[32];
+            tc::ld32(t_row + 2 * jb, g);
+            if (valid)
+#pragma unroll
+                for (int q = 0; q < 4; q++) group(jb + 4 * q, g + 8 * q);
+        } else {
+#pragma unroll
+            for (int q = 0; q < kPrefetchFeatures / 8; q++) {
+                if (4 * q >= F / 2) break;
+                float g[8];
+                tc::ld8(t_row + 2 * (jb + 4 * q), g);
+                if (valid) group(jb + 4 * q, g);
+            }
         }
-        if (half == 0) return false;
+        if (!A.base_input && A.sh_mask == 15) {  // SH columns 2F .. 2F + 15 (2F is a multiple of 16)
+            gbase_in = mk3(0.0f, 0.0f, 0.0f);
+            if (half == 1) return kOwnBase;
+            float g[16];
+            tc::ld16(t_row + 2 * F, g);
+            gdir = inv * sh_band_grad(15, deg, dir, g);
+            return kOwnDir;
+        }
+        if (half == 0) return 0;
         c = 2 * F;
     } else if (half == 1) {
-        return false;
+        return 0;
     }
     // remaining columns in order: encoded inputs (feature j, octave f, sin then cos), SH inputs, padding
     int nsh = 0;
@@ -531,7 +565,10 @@ __device__ inline bool input_grad_row(const Params& P, const AppearanceConfig& A
                 }
                 if (++q == per) {
                     const float gv = gacc * inv;
-                    if (j < F) gout[j] = acc ? gout[j] + gv : gv;
+                    if (j < F) {
+                        if (acc) atomicAdd(gout + j, gv);
+                        else gout[j] = gv;
+                    }
                     else gb[j - F] = gv;
                     j++;
                     q = 0;
@@ -544,7 +581,7 @@ __device__ inline bool input_grad_row(const Params& P, const AppearanceConfig& A
     gbase_in = mk3(gb[0], gb[1], gb[2]);
     // direction gradient from the SH inputs' gradient, unscaled afterwards (scaling by 2^-7 is exact)
     gdir = inv * sh_band_grad(A.sh_mask, deg, dir, gsh);
-    return true;
+    return kOwnDir | kOwnBase;
 }
 
 // backward MMAs of layer l: weight gradient (M = 64, accumulated in TMEM) and data gradient (layer accumulator)
@@ -596,12 +633,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
     uint32_t phase = 0;
     bool wg_started = false;
     const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows;
-    const bool fast = fast_features(P, A);
+    const bool fast = fast_features(P, A) && (reinterpret_cast<uintptr_t>(O.residual) & 15u) == 0;  // 16-byte gradient stores
     float* trig = fast && plan.trig_smem ? reinterpret_cast<float*>(smem + plan.trig_smem) : nullptr;
     const uint32_t x_row = sbase + plan.x_smem + tc::kmajor_offset(row, 0, plan.kin);
     RowData cur, nxt;
-    if (blockIdx.x < n_tiles) load_row(P, A, fast, half, vis, n_rows, blockIdx.x * kTcRows + row, rank_of, sorted_rec, grads, cur);
+    if (blockIdx.x < n_tiles) {
+        load_row_index(vis, n_rows, blockIdx.x * kTcRows + row, cur);
+        load_row_params(P, A, fast, half, rank_of, cur);
+        load_row_rank(sorted_rec, grads, cur);
+    }
     for (uint32_t tile = blockIdx.x; tile < n_tiles && alive; tile += gridDim.x) {
+        const uint32_t next = tile + gridDim.x;
+        const bool more = next < n_tiles;
+        if (more) load_row_index(vis, n_rows, next * kTcRows + row, nxt);
         const bool valid = cur.valid;
         const uint32_t i = cur.i;
         f3 gpre = mk3(0.0f, 0.0f, 0.0f);
@@ -610,8 +654,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
                                                            color_act_grad_from_y(A.color_act, cur.q2.z));
         write_input_row(P, A, v, deg, cur, fast, half, x_row, plan.kin, trig, row);
         sync_tile();
-        const uint32_t next = tile + gridDim.x;
-        if (next < n_tiles) load_row(P, A, fast, half, vis, n_rows, next * kTcRows + row, rank_of, sorted_rec, grads, nxt);
         // recomputed forward; the last layer's outputs become the scaled output gradient
         for (int l = 0; l < plan.layers && alive; l++) {
             if (t == 0) {
@@ -619,6 +661,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
                 tc::commit(&bar);
             }
             __syncwarp();
+            if (l == 0 && more) load_row_params(P, A, fast, half, rank_of, nxt);
             alive = wait_all(&bar, phase);
             if (!alive) break;
             if (l < last) {
@@ -647,6 +690,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
                 tc::commit(&bar);
             }
             __syncwarp();
+            if (l == last && more) load_row_rank(sorted_rec, grads, nxt);
             alive = wait_all(&bar, phase);
             if (!alive) break;
             if (l > 0) {
@@ -660,17 +704,19 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
         float rn = 1.0f;
         const f3 d = valid ? view_dir(v, cur.mean, &rn) : mk3(0.0f, 0.0f, 1.0f);
         f3 gbase_in = mk3(0.0f, 0.0f, 0.0f), gd = mk3(0.0f, 0.0f, 0.0f);
-        const bool owner = input_grad_row(P, A, O, t_row, cur, fast, half, trig, row, plan.kin, deg, d, gbase_in, gd);
-        if (owner && valid) {
+        const int own = input_grad_row(P, A, O, t_row, cur, fast, half, trig, row, plan.kin, deg, d, gbase_in, gd);
+        if ((own & kOwnBase) && valid) {
             f3 gbase = mk3(0.0f, 0.0f, 0.0f);
             if (v.render_base) {
-                const f3 bb = ld3(P.base, i);
+                const f3 bb = cur.base;
                 gbase = mk3(base_act_grad(A.base_act, bb.x), base_act_grad(A.base_act, bb.y), base_act_grad(A.base_act, bb.z)) * gpre;
             }
             if (A.base_input) gbase = gbase + gbase_in;
-            put3n(O.base, i, gbase, O.accumulate);
+            add3n(O.base, i, gbase, O.accumulate);
+        }
+        if ((own & kOwnDir) && valid) {
             const f3 gmean_color = A.dir_grad ? rn * (gd - dot3(gd, d) * d) : mk3(0.0f, 0.0f, 0.0f);
-            put3n(O.means, i, gmean_color, O.accumulate);
+            add3n(O.means, i, gmean_color, O.accumulate);
         }
         sync_tile();
         cur = nxt;
