@@ -250,6 +250,10 @@ class ForwardState:
                                grad_ws.data_ptr(), grad_ws.numel(), image.data_ptr(), grad_image.data_ptr(), ctypes.byref(grads), dens,
                                rows, int(bool(accumulate)), _stream()))
 
+    def pruning_scores(self, image: torch.Tensor, scores: torch.Tensor) -> None:
+        check(lib.fgs_pruning_scores(ctypes.byref(self.c_settings), ctypes.byref(self.frame), self.prim_ws.data_ptr(), self.tile_ws.data_ptr(),
+                                     self.inst_ws.data_ptr(), image.data_ptr(), scores.data_ptr(), _stream()))
+
     def views(self) -> _lib.FrameViews:
         out = _lib.FrameViews()
         check(lib.fgs_frame_buffers(ctypes.byref(self.frame), self.prim_ws.data_ptr(), self.tile_ws.data_ptr(),
@@ -372,6 +376,33 @@ def rasterize(
     return image
 
 
-def update_pruning_scores(*args, **kwargs) -> torch.Tensor:
-    """Speedy-Splat pruning scores (rasterization.py:227-251) are not part of this build."""
-    raise NotImplementedError('update_pruning_scores is not implemented by the B200 backend')
+@torch.no_grad()
+def update_pruning_scores(
+    scores: torch.Tensor,
+    means: torch.Tensor,
+    scales: torch.Tensor,
+    rotations: torch.Tensor,
+    opacities: torch.Tensor,
+    rasterizer_settings: RasterizerSettings,
+    precomputed_colors: torch.Tensor | None = None,
+    base_colors: torch.Tensor | None = None,
+    residual_params: torch.Tensor | None = None,
+    mlp_weights: torch.Tensor | None = None,
+) -> None:
+    """Adds the view's Speedy-Splat pruning scores to `scores` [N] (contiguous CUDA float32, updated in place):
+    per primitive, the sum over its accepted fragments of (opacity * dL/dalpha)^2 for an all-ones image gradient.
+    Mirrors torch_bindings/rasterization.py:227-251 (returns None like the reference's binding)."""
+    device = means.device
+    n = means.shape[0]
+    if not scores.is_cuda or scores.dtype != torch.float32 or not scores.is_contiguous() or scores.numel() != n:
+        raise RuntimeError('scores must be a contiguous CUDA float32 tensor with one element per Gaussian')
+    mlp = mlp_weights.detach() if mlp_weights is not None else None
+    prims = _c_primitives(means.detach(), scales.detach(), rotations.detach(), opacities.detach(),
+                          precomputed_colors.detach() if precomputed_colors is not None else None,
+                          base_colors.detach() if base_colors is not None else None,
+                          residual_params.detach() if residual_params is not None else None, mlp)
+    state = ForwardState(_rasterizer, prims, rasterizer_settings, device)
+    state.preprocess(prims)
+    image = torch.empty((3, int(rasterizer_settings.height), int(rasterizer_settings.width)), dtype=torch.float32, device=device)
+    state.render_train(image)
+    state.pruning_scores(image, scores)

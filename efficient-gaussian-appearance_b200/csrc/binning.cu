@@ -6,6 +6,11 @@
 
 namespace fgs {
 
+// One warp emits the instances of its 32 primitives together: their candidate tiles (the bounds rectangles,
+// row-major) are laid end to end and every lane tests one candidate per round, so a warp spends
+// ceil(sum of candidates / 32) rounds whatever the mix of footprint sizes. A hit of primitive L goes to
+// inst_off[L] + (hits of L before it), which keeps depth order across primitives and row-major tile order within one;
+// consecutive hits of one primitive are consecutive lanes and consecutive addresses.
 template <typename K>
 __global__ void __launch_bounds__(256) emit_kernel(const Record* __restrict__ rec, const uint32_t* __restrict__ inst_off,
                                                    K* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t n_visible,
@@ -29,38 +34,51 @@ __global__ void __launch_bounds__(256) emit_kernel(const Record* __restrict__ re
         w = inst_off[r];
     }
     const uint32_t bw = tb.y - tb.x;
-    if (active && n_max <= kSequentialTiles) {
-        for (uint32_t t = 0; t < n_max; t++) {
-            const uint32_t tx = tb.x + t % bw, ty = tb.z + t / bw;
-            if (tile_overlaps(sx, sy, ca, cb, cc, tx, ty, thr)) {
-                keys[w] = static_cast<K>(ty * grid_w + tx);
-                vals[w] = r;
-                w++;
-            }
-        }
+    // candidate ranges [excl, incl) of the lanes' primitives in the warp's flattened list
+    uint32_t incl = n_max;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= static_cast<uint32_t>(o)) incl += y;
     }
-    uint32_t big = __ballot_sync(0xffffffffu, active && n_max > kSequentialTiles);
-    while (big) {
-        const uint32_t src = __ffs(big) - 1;
-        big &= big - 1;
-        const float qx = __shfl_sync(0xffffffffu, sx, src), qy = __shfl_sync(0xffffffffu, sy, src);
-        const float qa = __shfl_sync(0xffffffffu, ca, src), qb = __shfl_sync(0xffffffffu, cb, src);
-        const float qc = __shfl_sync(0xffffffffu, cc, src), qt = __shfl_sync(0xffffffffu, thr, src);
-        const uint32_t qx0 = __shfl_sync(0xffffffffu, tb.x, src), qy0 = __shfl_sync(0xffffffffu, tb.z, src);
-        const uint32_t qw = __shfl_sync(0xffffffffu, bw, src), qn = __shfl_sync(0xffffffffu, n_max, src);
-        const uint32_t qr = __shfl_sync(0xffffffffu, r, src);
-        uint32_t pos = __shfl_sync(0xffffffffu, w, src);
-        for (uint32_t base = 0; base < qn; base += 32) {
-            const uint32_t t = base + lane;
-            const uint32_t tx = qx0 + t % qw, ty = qy0 + t / qw;
-            const bool hit = t < qn && tile_overlaps(qx, qy, qa, qb, qc, tx, ty, qt);
-            const uint32_t ballot = __ballot_sync(0xffffffffu, hit);
-            if (hit) {
-                const uint32_t o = pos + __popc(ballot & ((1u << lane) - 1u));
-                keys[o] = static_cast<K>(ty * grid_w + tx);
-                vals[o] = qr;
-            }
-            pos += __popc(ballot);
+    const uint32_t excl = incl - n_max;
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    uint32_t emitted = 0;  // hits of this lane's primitive in earlier rounds
+    for (uint32_t base = 0; base < total; base += 32) {
+        const uint32_t c = base + lane;
+        // owner: the lane whose range holds candidate c (the last lane with excl <= c; empty ranges are skipped
+        // because a later lane with the same excl exists only when the earlier range is empty)
+        uint32_t owner = 0;
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const uint32_t probe = owner + step;
+            if (__shfl_sync(0xffffffffu, excl, probe) <= c) owner = probe;
+        }
+        const uint32_t o_excl = __shfl_sync(0xffffffffu, excl, owner);
+        const float qx = __shfl_sync(0xffffffffu, sx, owner), qy = __shfl_sync(0xffffffffu, sy, owner);
+        const float qa = __shfl_sync(0xffffffffu, ca, owner), qb = __shfl_sync(0xffffffffu, cb, owner);
+        const float qc = __shfl_sync(0xffffffffu, cc, owner), qt = __shfl_sync(0xffffffffu, thr, owner);
+        const uint32_t qx0 = __shfl_sync(0xffffffffu, tb.x, owner), qy0 = __shfl_sync(0xffffffffu, tb.z, owner);
+        const uint32_t qw = __shfl_sync(0xffffffffu, bw, owner);
+        const uint32_t qpos = __shfl_sync(0xffffffffu, w, owner) + __shfl_sync(0xffffffffu, emitted, owner);
+        const bool valid = c < total;  // then the owner has candidates and qw >= 1
+        const uint32_t t = c - o_excl, qw1 = valid ? qw : 1u;
+        const uint32_t tx = qx0 + t % qw1, ty = qy0 + t / qw1;
+        const bool hit = valid && tile_overlaps(qx, qy, qa, qb, qc, tx, ty, qt);
+        const uint32_t hits = __ballot_sync(0xffffffffu, hit);
+        // lanes of this round that belong to the owner: from the owner's first candidate in the round up to this lane
+        const uint32_t first = o_excl > base ? o_excl - base : 0u;
+        const uint32_t before = hits & ((1u << lane) - 1u) & ~((1u << first) - 1u);
+        if (hit) {
+            const uint32_t o = qpos + __popc(before);
+            keys[o] = static_cast<K>(ty * grid_w + tx);
+            vals[o] = (r & ~31u) + owner;  // the owner's depth rank
+        }
+        // this lane's primitive: its candidates in this round are lanes [excl - base, incl - base) clipped to the round
+        const uint32_t lo = excl > base ? excl - base : 0u, hi = incl > base ? incl - base : 0u;
+        if (lo < 32 && hi > lo) {
+            const uint32_t top = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
+            emitted += __popc(hits & top & ~((1u << lo) - 1u));
         }
     }
 }

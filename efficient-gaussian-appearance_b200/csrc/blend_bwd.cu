@@ -128,6 +128,96 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
     }
 }
 
+// Pruning scores (Speedy-Splat): the blend backward of an all-ones image gradient; every accepted fragment adds
+// (opacity * dL/dalpha)^2 of its pixel to the score of its primitive. Semantics:
+// FasterGSVDACudaBackend/.../rasterization/include/kernels_pruning_scores.cuh:11-173 (which re-runs the forward
+// blend inside the kernel; here the training forward's final transmittance and contributor counts are reused, so
+// the accepted fragments are exactly the forward's). The per-pixel terms are summed over the warp before the single
+// addition per (fragment, warp).
+__global__ void __launch_bounds__(kTilePixels) pruning_scores_kernel(BlendArgs A, const float* __restrict__ image, TileBuffers T,
+                                                                     const uint32_t* __restrict__ rank_to_prim, float* __restrict__ scores) {
+    __shared__ float4 sa[kTilePixels], sh[kTilePixels];
+    __shared__ float sc[kTilePixels];  // colour sum c.r + c.g + c.b (the colour gradient is all ones)
+    __shared__ uint2 sbnd[kTilePixels];
+    __shared__ uint32_t sprim[kTilePixels];
+    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const uint32_t tile = blockIdx.y * A.grid_w + blockIdx.x;
+    const uint32_t sx0 = blockIdx.x * kTileW + (warp % 2) * kSubtileW;
+    const uint32_t sy0 = blockIdx.y * kTileH + (warp / 2) * kSubtileH;
+    const uint32_t px = sx0 + lane % kSubtileW, py = sy0 + lane / kSubtileW;
+    const uint32_t local = (py - blockIdx.y * kTileH) * kTileW + (px - blockIdx.x * kTileW);
+    const bool inside = px < static_cast<uint32_t>(A.width) && py < static_cast<uint32_t>(A.height);
+    const float pxf = static_cast<float>(px) + 0.5f, pyf = static_cast<float>(py) + 0.5f;
+    const uint2 range = A.ranges[tile];
+    const uint32_t n = range.y - range.x;
+    uint32_t last = 0;
+    float gcf = 0.0f, gac = 0.0f;
+    if (inside) {
+        const size_t pix = static_cast<size_t>(py) * A.width + px;
+        const size_t np = static_cast<size_t>(A.width) * A.height;
+        last = T.n_contrib[static_cast<size_t>(tile) * kTilePixels + local];
+        const float tf = T.final_T[static_cast<size_t>(tile) * kTilePixels + local];
+        const float bgr = A.bg[0], bgg = A.bg[1], bgb = A.bg[2];
+        gcf = (image[pix] - tf * bgr) + (image[np + pix] - tf * bgg) + (image[2 * np + pix] - tf * bgb);
+        gac = tf * -(bgr + bgg + bgb);
+    }
+    float tr = 1.0f, accd = 0.0f;
+    bool done = last == 0;
+    for (uint32_t start = 0; start < n; start += kTilePixels) {
+        if (__syncthreads_and(done)) break;
+        if (start + t < n) {
+            const uint32_t r = A.vals[range.x + start + t];
+            const Record q = A.rec[r];
+            sa[t] = make_float4(q.q0.x, q.q0.y, -q.q0.w, q.q0.z);
+            sh[t] = make_float4(-0.5f * q.q1.x, -q.q1.y, -0.5f * q.q1.z, 0.0f);
+            sc[t] = q.q2.x + q.q2.y + q.q2.z;
+            sbnd[t] = make_uint2(__float_as_uint(q.q1.w), __float_as_uint(q.q2.w));
+            sprim[t] = rank_to_prim[r];
+        }
+        __syncthreads();
+        const uint32_t bs = min(static_cast<uint32_t>(kTilePixels), n - start);
+        for (uint32_t g = 0; g < bs; g += 32) {
+            const bool ov = g + lane < bs && overlaps_subtile(sbnd[g + lane], sx0, sy0);
+            uint32_t pending = __ballot_sync(0xffffffffu, ov);
+            while (pending) {
+                if (__all_sync(0xffffffffu, done)) break;
+                const uint32_t k = g + __ffs(pending) - 1;
+                pending &= pending - 1;
+                const float4 a = sa[k];
+                const float dx = a.x - pxf, dy = a.y - pyf;
+                bool acc = !done && start + k < last;
+                float e = 0.0f;
+                if (acc) {
+                    e = gauss_exponent(dx, dy, sh[k]);
+                    acc = e >= a.z;
+                }
+                if (!__any_sync(0xffffffffu, acc)) continue;
+                float score = 0.0f;
+                if (acc) {
+                    const float alpha = __fmul_rn(a.w, det_exp_blend(fminf(e, 0.0f)));
+                    const float cg = sc[k];
+                    accd = fmaf(tr * alpha, cg, accd);
+                    const float oma = __fsub_rn(1.0f, alpha);
+                    const float rcp = 1.0f / fmaxf(oma, kOneMinusAlphaEps);
+                    const float dl_da = fmaf(tr, cg, rcp * (gac - (gcf - accd)));
+                    const float dl_dg = a.w * dl_da;
+                    score = dl_dg * dl_dg;
+                    tr = __fmul_rn(tr, oma);
+                    if (tr < kTransmittanceThreshold) done = true;
+                }
+                const float total = warp_sum(score);
+                if (lane == 0) atomicAdd(scores + sprim[k], total);
+            }
+        }
+    }
+}
+
+cudaError_t launch_pruning_scores(const BlendArgs& a, const float* image, const TileBuffers& T, const uint32_t* rank_to_prim, float* scores,
+                                  cudaStream_t s) {
+    pruning_scores_kernel<<<dim3(a.grid_w, a.grid_h), kTilePixels, 0, s>>>(a, image, T, rank_to_prim, scores);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_blend_backward(const BlendArgs& a, const float* image, const float* grad_image, const TileBuffers& T, GradRecord* grads,
                                   int abs_grad, cudaStream_t s) {
     const dim3 grid(a.grid_w, a.grid_h);

@@ -560,6 +560,35 @@ int fgs_backward(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_setti
     return FGS_OK;
 }
 
+int fgs_pruning_scores(const fgs_settings* settings, const fgs_frame* frame, void* prim_ws, void* tile_ws, void* inst_ws, const float* image,
+                       float* scores, void* stream) {
+    if (!frame || !image || !scores) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    int rc = check_settings(settings);
+    if (rc) return rc;
+    if (settings->width != frame->width || settings->height != frame->height) return fail(FGS_ERR_INVALID_ARGUMENT, "settings do not match the frame");
+    const uint64_t nv = static_cast<uint64_t>(frame->n_visible);
+    if (nv == 0) return FGS_OK;
+    if (!prim_ws || !tile_ws || !inst_ws) return fail(FGS_ERR_INVALID_ARGUMENT, "the forward pass workspaces are required");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const Grid g = grid_of(frame->width, frame->height);
+    fgs::PrimBuffers B = carve_prim(prim_ws, static_cast<uint64_t>(frame->n_primitives), nullptr);
+    const fgs::TileBuffers T = carve_tile(tile_ws, g, nullptr);
+    InstBuffers I = carve_inst(inst_ws, static_cast<uint64_t>(frame->n_instances), g, nullptr);
+    fgs::BlendArgs a;
+    a.ranges = T.ranges;
+    a.bucket_off = T.bucket_off;
+    a.vals = frame->tile_selector ? I.vals_b : I.vals_a;
+    a.rec = B.sorted_rec;
+    a.bg = settings->bg_color;
+    a.width = frame->width;
+    a.height = frame->height;
+    a.grid_w = g.gw;
+    a.grid_h = g.gh;
+    ProfScope p_("pruning_scores", s);
+    FGS_CUDA(fgs::launch_pruning_scores(a, image, T, frame->depth_selector ? B.idx_b : B.idx_a, scores, s), "pruning scores");
+    return FGS_OK;
+}
+
 int fgs_frame_buffers(const fgs_frame* frame, void* prim_ws, void* tile_ws, void* inst_ws, fgs_frame_views* out) {
     if (!frame || !out) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
     std::memset(out, 0, sizeof(fgs_frame_views));

@@ -60,6 +60,8 @@ cudaError_t launch_blend_train(const BlendArgs& a, float* image, const TileBuffe
 cudaError_t launch_blend_inference(const BlendArgs& a, float* image, int chw, int clamp, cudaStream_t s);
 cudaError_t launch_blend_backward(const BlendArgs& a, const float* image, const float* grad_image, const TileBuffers& T, GradRecord* grads,
                                   int abs_grad, cudaStream_t s);
+cudaError_t launch_pruning_scores(const BlendArgs& a, const float* image, const TileBuffers& T, const uint32_t* rank_to_prim, float* scores,
+                                  cudaStream_t s);
 
 // loss.cu
 size_t loss_workspace_bytes(int C, int H, int W);

@@ -12,6 +12,8 @@
  *   _C.forward   (rasterization/src/rasterization_api.cu:16-123)  -> fgs_forward_preprocess + fgs_forward_render
  *   _C.backward  (rasterization/src/rasterization_api.cu:125-247) -> fgs_backward
  *   _C.inference (rasterization/src/rasterization_api.cu:249-335) -> fgs_forward_preprocess + fgs_inference_render
+ *   _C.pruning_scores (rasterization/src/rasterization_api.cu:337-416, src/pruning_scores.cu:11-204)
+ *                     -> fgs_forward_preprocess + fgs_forward_render + fgs_pruning_scores
  *   _C.adam_step (adam/src/adam.cu:44-87)                          -> fgs_adam_step (several tensors per launch)
  * The reference's forward reads the visible-primitive and instance counts back to the host in the middle
  * of the call (rasterization/src/forward.cu:82-85) to size its buffers; here that point is the boundary
@@ -176,6 +178,11 @@ int fgs_backward(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_setti
                  const float* image, const float* grad_image, const fgs_gradients* grads, float* densification_info,
                  int densification_rows, int accumulate, void* stream);
 int fgs_frame_buffers(const fgs_frame* frame, void* prim_ws, void* tile_ws, void* inst_ws, fgs_frame_views* out);
+/* pruning scores of a training forward (image = its [3,H,W] output): scores[N] += sum over the accepted fragments
+ * of each primitive of (opacity * dL/dalpha)^2 for an all-ones image gradient
+ * (rasterization/include/kernels_pruning_scores.cuh:11-173) */
+int fgs_pruning_scores(const fgs_settings* settings, const fgs_frame* frame, void* prim_ws, void* tile_ws, void* inst_ws,
+                       const float* image, float* scores, void* stream);
 
 /* fused Adam over up to 12 segments in one launch (adam/src/adam.cu:18-42 per element) */
 int fgs_adam_step(const fgs_adam_segment* segments, int n_segments, void* stream);

@@ -644,6 +644,74 @@ int orc_blend_backward(int64_t n_visible, const uint32_t* sorted_idx, const doub
 }
 /* layout note: grads[r] = {mx, my, ca, cb, cc, col r, col g, col b, opacity, |mx|, |my|, 0} */
 
+/* Pruning scores in double (rasterization/include/kernels_pruning_scores.cuh:11-173): the accepted fragments of a
+ * pixel are found as in orc_blend_backward (working-precision acceptance, truncated at n_contrib); with an all-ones
+ * colour gradient, scores[primitive] += (opacity * dL/dalpha)^2 for every accepted fragment. scores has one entry
+ * per primitive (primitive order) and is accumulated into. */
+int orc_pruning_scores(int64_t n_visible, const uint32_t* sorted_idx, const double* rec, const uint32_t* ranks, const uint32_t* ranges,
+                       const orc_view* v, const uint32_t* n_contrib, double* scores) {
+    (void)n_visible;
+    const int W = v->width, H = v->height, gw = (W + TILE_W - 1) / TILE_W;
+    uint32_t* prim = (uint32_t*)malloc(sizeof(uint32_t) * 1);
+    double* alpha = (double*)malloc(sizeof(double) * 1);
+    size_t cap = 1;
+    const double bgsum = (double)v->bg[0] + (double)v->bg[1] + (double)v->bg[2];
+    for (int py = 0; py < H; py++) {
+        for (int px = 0; px < W; px++) {
+            const int tx = px / TILE_W, ty = py / TILE_H, tile = ty * gw + tx;
+            const uint32_t lx = (uint32_t)(px - tx * TILE_W), ly = (uint32_t)(py - ty * TILE_H);
+            const uint32_t sx0 = (uint32_t)(tx * TILE_W) + (lx / SUB_W) * SUB_W, sy0 = (uint32_t)(ty * TILE_H) + (ly / SUB_H) * SUB_H;
+            const size_t pix = (size_t)py * W + px;
+            const uint32_t s = ranges[2 * tile], last = n_contrib[pix];
+            size_t nf = 0;
+            for (uint32_t j = s; j < s + last; j++) {
+                orc_rec q;
+                const uint32_t pi = sorted_idx[ranks[j]];
+                rec_of(rec, pi, &q);
+                if (!overlaps_subtile(&q, sx0, sy0)) continue;
+                const real pxf = (real)px + R(0.5), pyf = (real)py + R(0.5);
+                const real dxr = q.mx - pxf, dyr = q.my - pyf;
+                const real ex = RFMA(dxr, RFMA(R(-0.5) * q.ca, dxr, -q.cb * dyr), (R(-0.5) * q.cc * dyr) * dyr);
+                if (ex < -q.thr) continue;
+                const double* o = rec + 14 * (size_t)pi;
+                const double dx = o[0] - ((double)px + 0.5), dy = o[1] - ((double)py + 0.5);
+                const double e = -0.5 * (o[4] * dx * dx + o[6] * dy * dy) - o[5] * dx * dy;
+                if (nf == cap) {
+                    cap *= 2;
+                    prim = (uint32_t*)realloc(prim, sizeof(uint32_t) * cap);
+                    alpha = (double*)realloc(alpha, sizeof(double) * cap);
+                }
+                prim[nf] = pi;
+                alpha[nf] = o[2] * exp(fmin(e, 0.0));
+                nf++;
+            }
+            /* colour sum (all-ones gradient) of the blended colour without background, and the final transmittance */
+            double T = 1.0, C = 0.0;
+            for (size_t k = 0; k < nf; k++) {
+                const double* o = rec + 14 * (size_t)prim[k];
+                C += T * alpha[k] * (o[7] + o[8] + o[9]);
+                T *= 1.0 - alpha[k];
+            }
+            const double gbg = -T * bgsum;
+            double after = C;
+            T = 1.0;
+            for (size_t k = 0; k < nf; k++) {
+                const double* o = rec + 14 * (size_t)prim[k];
+                const double a = alpha[k], cs = o[7] + o[8] + o[9];
+                after -= T * a * cs;
+                const double rcp = 1.0 / fmax(1.0 - a, 1e-6);
+                const double dl_da = T * cs - after * rcp + gbg * rcp;
+                const double dl_dg = o[2] * dl_da;
+                scores[prim[k]] += dl_dg * dl_dg;
+                T *= 1.0 - a;
+            }
+        }
+    }
+    free(prim);
+    free(alpha);
+    return 0;
+}
+
 /* ------------------------------------------------------------------------------------------------ */
 /* backward preprocess (double)                                                                      */
 

@@ -59,6 +59,7 @@ def load(double: bool = False) -> ctypes.CDLL:
     lib.orc_count_instances.restype = i64
     lib.orc_blend.argtypes = [i64, P, P, P, P, P, P, P, P, ctypes.c_int, ctypes.c_int]
     lib.orc_blend_backward.argtypes = [i64, P, P, P, P, P, P, P, P]
+    lib.orc_pruning_scores.argtypes = [i64, P, P, P, P, P, P, P]
     lib.orc_preprocess_backward.argtypes = [P, P, i64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, ctypes.c_int]
     lib.orc_adam.argtypes = [i64, P, P, P, P, i64, P, ctypes.c_int, i64, ctypes.c_double, ctypes.c_double, ctypes.c_double]
     lib.orc_adam.restype = None
@@ -122,9 +123,11 @@ def make_appearance(model: str, max_degree: int = 0, base_act: int = 0, res_act:
     return a
 
 
-def run(app: Appearance, view: View, prims: dict, grad_image=None, double: bool = False, densification_rows: int = 0) -> dict:
+def run(app: Appearance, view: View, prims: dict, grad_image=None, double: bool = False, densification_rows: int = 0,
+        pruning: bool = False) -> dict:
     """Runs the restated pipeline; prims holds numpy/torch arrays (means, scales, rotations, opacities and the
-    appearance inputs). Returns intermediates, the image [3,H,W] and, with grad_image, all gradients."""
+    appearance inputs). Returns intermediates, the image [3,H,W], with pruning the per-primitive pruning scores and,
+    with grad_image, all gradients."""
     lib = load(double)
     means, scales, rots, opac = (_in(prims[k], double) for k in ('means', 'scales', 'rotations', 'opacities'))
     pre = _in(prims.get('precomputed_colors'), double)
@@ -165,6 +168,10 @@ def run(app: Appearance, view: View, prims: dict, grad_image=None, double: bool 
         offsets = (np.cumsum(counts) - counts).astype(np.uint32)
     out = dict(n_visible=int(V), n_instances=int(I), n_touched=n_touched, depth_key=depth_key, records=rec, sorted_idx=sorted_idx,
                instance_offsets=offsets, tile_keys=tile_keys, ranks=ranks, ranges=ranges, image=image, final_T=final_T, n_contrib=n_contrib)
+    if pruning:
+        scores = np.zeros(max(n, 1), np.float64)
+        lib.orc_pruning_scores(V, _p(sorted_idx), _p(rec), _p(ranks), _p(ranges), ctypes.byref(view), _p(n_contrib), _p(scores))
+        out['pruning_scores'] = scores[:n]
     if grad_image is None:
         return out
     gimg = _f32(grad_image)
