@@ -129,8 +129,9 @@ __device__ inline f3 view_dir(const View& v, f3 m, float* rn_out) {
 
 __device__ inline void put1(float* p, size_t k, float v, int acc) { if (acc) p[k] += v; else p[k] = v; }
 __device__ inline void put3n(float* p, uint32_t i, f3 v, int acc) { put1(p, 3ull * i, v.x, acc); put1(p, 3ull * i + 1, v.y, acc); put1(p, 3ull * i + 2, v.z, acc); }
-// as put3n, accumulating with reductions: each element receives one addition per launch, so the result equals the
-// load-add-store of put3n, without the load on the thread's critical path
+// as put3n, accumulating with reductions: each element receives one addition per launch, so the result is the
+// load-add-store value of put3n (a float atomic may flush a subnormal sum to zero), without the load on the thread's
+// critical path
 __device__ inline void add3n(float* p, uint32_t i, f3 v, int acc) {
     float* q = p + 3ull * i;
     if (acc) {

@@ -500,7 +500,7 @@ __device__ inline int input_grad_row(const Params& P, const AppearanceConfig& A,
             for (int k = 0; k < 4; k++) gv[k] = (cs[k] * g[2 * k] - sn[k] * g[2 * k + 1]) * inv;
             const float4 o = make_float4(gv[0], gv[1], gv[2], gv[3]);
             float4* dst = reinterpret_cast<float4*>(gout + j);
-            if (acc) atomicAdd(dst, o);  // one addition per element and launch: the same value as load, add, store
+            if (acc) atomicAdd(dst, o);  // one addition per element and launch (deterministic)
             else *dst = o;
         };
         if (F == 32) {
