@@ -30,7 +30,6 @@ constexpr int kTileH = 12;
 constexpr int kTilePixels = kTileW * kTileH;  // 192
 constexpr int kSubtileW = 8;
 constexpr int kSubtileH = 4;
-constexpr int kSequentialTiles = 4;           // tiles tested by the owning thread before the warp helps
 constexpr uint32_t kInvalidRank = 0xffffffffu;
 
 enum Model : int { kPrecomputed = 0, kSH = 1, kSV = 2, kNASG = 3, kNASGabor = 4, kNeural = 5 };

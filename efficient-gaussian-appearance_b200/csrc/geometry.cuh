@@ -170,31 +170,44 @@ __device__ inline Geometry project_primitive(const float* __restrict__ means, co
         if (n_max == 0) active = false;
     }
     G.mx = mx; G.my = my; G.ca = ca; G.cb = cb; G.cc = cc; G.opacity = opacity; G.power_thr = thr;
-    // exact tile count: small footprints by the owning lane, large ones by the whole warp
+    // exact tile count: the warp lays its primitives' candidate tiles (bounds rectangles, row-major) end to end and
+    // every lane tests one candidate per round (the same test and operands as the instance emission)
     const float sx = mx - 0.5f, sy = my - 0.5f;
     const uint32_t bw = tb.y - tb.x;
-    uint32_t count = 0;
-    if (active && n_max <= kSequentialTiles) {
-        for (uint32_t t = 0; t < n_max; t++)
-            if (tile_overlaps(sx, sy, ca, cb, cc, tb.x + t % bw, tb.z + t / bw, thr)) count++;
-    }
     const uint32_t lane = threadIdx.x & 31u;
-    uint32_t big = __ballot_sync(0xffffffffu, active && n_max > kSequentialTiles);
-    while (big) {
-        const uint32_t src = __ffs(big) - 1;
-        big &= big - 1;
-        const float qx = __shfl_sync(0xffffffffu, sx, src), qy = __shfl_sync(0xffffffffu, sy, src);
-        const float qa = __shfl_sync(0xffffffffu, ca, src), qb = __shfl_sync(0xffffffffu, cb, src);
-        const float qc = __shfl_sync(0xffffffffu, cc, src), qt = __shfl_sync(0xffffffffu, thr, src);
-        const uint32_t qx0 = __shfl_sync(0xffffffffu, tb.x, src), qy0 = __shfl_sync(0xffffffffu, tb.z, src);
-        const uint32_t qw = __shfl_sync(0xffffffffu, bw, src), qn = __shfl_sync(0xffffffffu, n_max, src);
-        uint32_t total = 0;
-        for (uint32_t base = 0; base < qn; base += 32) {
-            const uint32_t t = base + lane;
-            const bool hit = t < qn && tile_overlaps(qx, qy, qa, qb, qc, qx0 + t % qw, qy0 + t / qw, qt);
-            total += __popc(__ballot_sync(0xffffffffu, hit));
+    const uint32_t n_cand = active ? n_max : 0u;
+    uint32_t incl = n_cand;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= static_cast<uint32_t>(o)) incl += y;
+    }
+    const uint32_t excl = incl - n_cand;
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    uint32_t count = 0;
+    for (uint32_t base = 0; base < total; base += 32) {
+        const uint32_t c = base + lane;
+        uint32_t owner = 0;  // last lane whose range starts at or before c
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const uint32_t probe = owner + step;
+            if (__shfl_sync(0xffffffffu, excl, probe) <= c) owner = probe;
         }
-        if (lane == src) count = total;
+        const uint32_t o_excl = __shfl_sync(0xffffffffu, excl, owner);
+        const float qx = __shfl_sync(0xffffffffu, sx, owner), qy = __shfl_sync(0xffffffffu, sy, owner);
+        const float qa = __shfl_sync(0xffffffffu, ca, owner), qb = __shfl_sync(0xffffffffu, cb, owner);
+        const float qc = __shfl_sync(0xffffffffu, cc, owner), qt = __shfl_sync(0xffffffffu, thr, owner);
+        const uint32_t qx0 = __shfl_sync(0xffffffffu, tb.x, owner), qy0 = __shfl_sync(0xffffffffu, tb.z, owner);
+        const uint32_t qw = __shfl_sync(0xffffffffu, bw, owner);
+        const bool valid = c < total;  // then the owner has candidates and qw >= 1
+        const uint32_t t = c - o_excl, qw1 = valid ? qw : 1u;
+        const bool hit = valid && tile_overlaps(qx, qy, qa, qb, qc, qx0 + t % qw1, qy0 + t / qw1, qt);
+        const uint32_t hits = __ballot_sync(0xffffffffu, hit);
+        const uint32_t lo = excl > base ? excl - base : 0u, hi = incl > base ? incl - base : 0u;
+        if (lo < 32 && hi > lo) {
+            const uint32_t top = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
+            count += __popc(hits & top & ~((1u << lo) - 1u));
+        }
     }
     G.n_touched = active ? count : 0;
     return G;

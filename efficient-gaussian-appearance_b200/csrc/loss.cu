@@ -44,7 +44,7 @@ __global__ void __launch_bounds__(kThreads) ssim_stats_kernel(const float* __res
                                                               float* __restrict__ A, float* __restrict__ B, float* __restrict__ Cm,
                                                               float2* __restrict__ partial) {
     __shared__ float xs[kE * (kE + 1)], ts[kE * (kE + 1)];
-    __shared__ float hs[5][kE * kT];
+    __shared__ __align__(16) float hs[5][kE * kT];  // 16-byte aligned rows: float4 stores
     __shared__ float red[2][kThreads / 32];
     const int x0 = blockIdx.x * kT, y0 = blockIdx.y * kT, ch = blockIdx.z;
     const size_t plane = static_cast<size_t>(H) * W;
@@ -53,56 +53,80 @@ __global__ void __launch_bounds__(kThreads) ssim_stats_kernel(const float* __res
     stage(xp, H, W, x0, y0, xs);
     stage(tp, H, W, x0, y0, ts);
     __syncthreads();
-    // rows: five moments of every staged row at every output column
-    for (int idx = threadIdx.x; idx < kE * kT; idx += kThreads) {
-        const int r = idx / kT, c = idx - r * kT;
-        float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f, m3 = 0.0f, m4 = 0.0f;
+    // rows: five moments of every staged row at every output column; a thread takes 4 consecutive columns of a row
+    // (14 staged values feed its 4 outputs)
+    for (int job = threadIdx.x; job < kE * (kT / 4); job += kThreads) {
+        const int r = job / (kT / 4), c0 = (job - r * (kT / 4)) * 4;
+        float xa[4 + 2 * kR], ta[4 + 2 * kR];
+#pragma unroll
+        for (int j = 0; j < 4 + 2 * kR; j++) {
+            xa[j] = xs[r * (kE + 1) + c0 + j];
+            ta[j] = ts[r * (kE + 1) + c0 + j];
+        }
+        float m[5][4];
+#pragma unroll
+        for (int o = 0; o < 4; o++) m[0][o] = m[1][o] = m[2][o] = m[3][o] = m[4][o] = 0.0f;
 #pragma unroll
         for (int k = 0; k <= 2 * kR; k++) {
-            const float a = xs[r * (kE + 1) + c + k], b = ts[r * (kE + 1) + c + k], w = win.w[k];
-            m0 += w * a;
-            m1 += w * b;
-            m2 += w * (a * a);
-            m3 += w * (b * b);
-            m4 += w * (a * b);
+            const float w = win.w[k];
+#pragma unroll
+            for (int o = 0; o < 4; o++) {
+                const float a = xa[o + k], b = ta[o + k];
+                m[0][o] += w * a;
+                m[1][o] += w * b;
+                m[2][o] += w * (a * a);
+                m[3][o] += w * (b * b);
+                m[4][o] += w * (a * b);
+            }
         }
-        hs[0][idx] = m0;
-        hs[1][idx] = m1;
-        hs[2][idx] = m2;
-        hs[3][idx] = m3;
-        hs[4][idx] = m4;
+#pragma unroll
+        for (int q = 0; q < 5; q++)
+            *reinterpret_cast<float4*>(&hs[q][r * kT + c0]) = make_float4(m[q][0], m[q][1], m[q][2], m[q][3]);
     }
     __syncthreads();
+    // columns: a thread takes 4 consecutive rows of one column (14 row-pass values per moment feed them)
     float sum_s = 0.0f, sum_l1 = 0.0f;
-    const int c = threadIdx.x & (kT - 1);
-    for (int r = threadIdx.x / kT; r < kT; r += kThreads / kT) {
-        float mu_x = 0.0f, mu_y = 0.0f, exx = 0.0f, eyy = 0.0f, exy = 0.0f;
+    {
+        const int c = threadIdx.x & (kT - 1), r0 = (threadIdx.x / kT) * 4;
+        float mu_x[4], mu_y[4], exx[4], eyy[4], exy[4];
 #pragma unroll
-        for (int k = 0; k <= 2 * kR; k++) {
-            const int o = (r + k) * kT + c;
-            const float w = win.w[k];
-            mu_x += w * hs[0][o];
-            mu_y += w * hs[1][o];
-            exx += w * hs[2][o];
-            eyy += w * hs[3][o];
-            exy += w * hs[4][o];
+        for (int o = 0; o < 4; o++) mu_x[o] = mu_y[o] = exx[o] = eyy[o] = exy[o] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4 + 2 * kR; j++) {
+            const int i = (r0 + j) * kT + c;
+            const float h0 = hs[0][i], h1 = hs[1][i], h2 = hs[2][i], h3 = hs[3][i], h4 = hs[4][i];
+#pragma unroll
+            for (int o = 0; o < 4; o++) {
+                const int k = j - o;
+                if (k < 0 || k > 2 * kR) continue;
+                const float w = win.w[k];
+                mu_x[o] += w * h0;
+                mu_y[o] += w * h1;
+                exx[o] += w * h2;
+                eyy[o] += w * h3;
+                exy[o] += w * h4;
+            }
         }
-        const int gy = y0 + r, gx = x0 + c;
-        if (gy >= H || gx >= W) continue;
-        const float sxx = exx - mu_x * mu_x, syy = eyy - mu_y * mu_y, sxy = exy - mu_x * mu_y;
-        const float a1 = 2.0f * mu_x * mu_y + kC1, a2 = 2.0f * sxy + kC2;
-        const float b1 = mu_x * mu_x + mu_y * mu_y + kC1, b2 = sxx + syy + kC2;
-        const float den = b1 * b2;
-        const float s = a1 * a2 / den;
-        const float ds_dmu = 2.0f * mu_y * a2 / den - s * 2.0f * mu_x / b1;
-        const float ds_dsxx = -s / b2;
-        const float ds_dsxy = 2.0f * a1 / den;
-        const size_t p = ch * plane + static_cast<size_t>(gy) * W + gx;
-        A[p] = ds_dmu - 2.0f * mu_x * ds_dsxx - mu_y * ds_dsxy;
-        B[p] = ds_dsxx;
-        Cm[p] = ds_dsxy;
-        sum_s += s;
-        sum_l1 += fabsf(xs[(r + kR) * (kE + 1) + c + kR] - ts[(r + kR) * (kE + 1) + c + kR]);
+#pragma unroll
+        for (int o = 0; o < 4; o++) {
+            const int r = r0 + o;
+            const int gy = y0 + r, gx = x0 + c;
+            if (gy >= H || gx >= W) continue;
+            const float sxx = exx[o] - mu_x[o] * mu_x[o], syy = eyy[o] - mu_y[o] * mu_y[o], sxy = exy[o] - mu_x[o] * mu_y[o];
+            const float a1 = 2.0f * mu_x[o] * mu_y[o] + kC1, a2 = 2.0f * sxy + kC2;
+            const float b1 = mu_x[o] * mu_x[o] + mu_y[o] * mu_y[o] + kC1, b2 = sxx + syy + kC2;
+            const float den = b1 * b2;
+            const float s = a1 * a2 / den;
+            const float ds_dmu = 2.0f * mu_y[o] * a2 / den - s * 2.0f * mu_x[o] / b1;
+            const float ds_dsxx = -s / b2;
+            const float ds_dsxy = 2.0f * a1 / den;
+            const size_t p = ch * plane + static_cast<size_t>(gy) * W + gx;
+            A[p] = ds_dmu - 2.0f * mu_x[o] * ds_dsxx - mu_y[o] * ds_dsxy;
+            B[p] = ds_dsxx;
+            Cm[p] = ds_dsxy;
+            sum_s += s;
+            sum_l1 += fabsf(xs[(r + kR) * (kE + 1) + c + kR] - ts[(r + kR) * (kE + 1) + c + kR]);
+        }
     }
     for (int o = 16; o > 0; o >>= 1) {
         sum_s += __shfl_down_sync(0xffffffffu, sum_s, o);
@@ -127,46 +151,63 @@ __global__ void __launch_bounds__(kThreads) ssim_grad_kernel(const float* __rest
                                                              const float* __restrict__ A, const float* __restrict__ B, const float* __restrict__ Cm,
                                                              float l1_scale, float ssim_scale, float* __restrict__ grad) {
     __shared__ float as[kE * (kE + 1)], bs[kE * (kE + 1)], cs[kE * (kE + 1)];
-    __shared__ float hs[3][kE * kT];
+    __shared__ __align__(16) float hs[3][kE * kT];  // 16-byte aligned rows: float4 stores
     const int x0 = blockIdx.x * kT, y0 = blockIdx.y * kT, ch = blockIdx.z;
     const size_t plane = static_cast<size_t>(H) * W;
     stage(A + ch * plane, H, W, x0, y0, as);
     stage(B + ch * plane, H, W, x0, y0, bs);
     stage(Cm + ch * plane, H, W, x0, y0, cs);
     __syncthreads();
-    for (int idx = threadIdx.x; idx < kE * kT; idx += kThreads) {
-        const int r = idx / kT, c = idx - r * kT;
-        float m0 = 0.0f, m1 = 0.0f, m2 = 0.0f;
+    for (int job = threadIdx.x; job < kE * (kT / 4); job += kThreads) {
+        const int r = job / (kT / 4), c0 = (job - r * (kT / 4)) * 4;
+        float m[3][4];
 #pragma unroll
-        for (int k = 0; k <= 2 * kR; k++) {
-            const int o = r * (kE + 1) + c + k;
-            const float w = win.w[k];
-            m0 += w * as[o];
-            m1 += w * bs[o];
-            m2 += w * cs[o];
+        for (int o = 0; o < 4; o++) m[0][o] = m[1][o] = m[2][o] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4 + 2 * kR; j++) {
+            const int i = r * (kE + 1) + c0 + j;
+            const float va = as[i], vb = bs[i], vc = cs[i];
+#pragma unroll
+            for (int o = 0; o < 4; o++) {
+                const int k = j - o;
+                if (k < 0 || k > 2 * kR) continue;
+                const float w = win.w[k];
+                m[0][o] += w * va;
+                m[1][o] += w * vb;
+                m[2][o] += w * vc;
+            }
         }
-        hs[0][idx] = m0;
-        hs[1][idx] = m1;
-        hs[2][idx] = m2;
+#pragma unroll
+        for (int q = 0; q < 3; q++)
+            *reinterpret_cast<float4*>(&hs[q][r * kT + c0]) = make_float4(m[q][0], m[q][1], m[q][2], m[q][3]);
     }
     __syncthreads();
-    const int c = threadIdx.x & (kT - 1);
-    for (int r = threadIdx.x / kT; r < kT; r += kThreads / kT) {
-        const int gy = y0 + r, gx = x0 + c;
-        if (gy >= H || gx >= W) continue;
-        float ga = 0.0f, gb = 0.0f, gc = 0.0f;
+    const int c = threadIdx.x & (kT - 1), r0 = (threadIdx.x / kT) * 4;
+    float ga[4], gb[4], gc[4];
 #pragma unroll
-        for (int k = 0; k <= 2 * kR; k++) {
-            const int o = (r + k) * kT + c;
+    for (int o = 0; o < 4; o++) ga[o] = gb[o] = gc[o] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4 + 2 * kR; j++) {
+        const int i = (r0 + j) * kT + c;
+        const float h0 = hs[0][i], h1 = hs[1][i], h2 = hs[2][i];
+#pragma unroll
+        for (int o = 0; o < 4; o++) {
+            const int k = j - o;
+            if (k < 0 || k > 2 * kR) continue;
             const float w = win.w[k];
-            ga += w * hs[0][o];
-            gb += w * hs[1][o];
-            gc += w * hs[2][o];
+            ga[o] += w * h0;
+            gb[o] += w * h1;
+            gc[o] += w * h2;
         }
+    }
+#pragma unroll
+    for (int o = 0; o < 4; o++) {
+        const int gy = y0 + r0 + o, gx = x0 + c;
+        if (gy >= H || gx >= W) continue;
         const size_t p = ch * plane + static_cast<size_t>(gy) * W + gx;
         const float xv = x[p], tv = t[p], d = xv - tv;
         const float sgn = d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f);
-        grad[p] = l1_scale * sgn - ssim_scale * (ga + 2.0f * xv * gb + tv * gc);
+        grad[p] = l1_scale * sgn - ssim_scale * (ga[o] + 2.0f * xv * gb[o] + tv * gc[o]);
     }
 }
 
