@@ -92,21 +92,27 @@ __global__ void ranges_kernel(const K* __restrict__ keys, uint2* __restrict__ ra
     if (j == n - 1 || static_cast<uint32_t>(keys[j + 1]) != k) ranges[k].y = static_cast<uint32_t>(j + 1);
 }
 
-// buckets of 32 instances per tile, inclusive scan (one CTA)
+// buckets of 32 instances per tile, inclusive scan (one CTA; a thread scans 8 consecutive tiles per round, so a
+// 1080p grid takes one round)
 __global__ void __launch_bounds__(1024) bucket_scan_kernel(const uint2* __restrict__ ranges, uint32_t* __restrict__ off, uint32_t n_tiles) {
+    constexpr int kPer = 8;
     __shared__ uint32_t warp_sums[32];
-    __shared__ uint32_t carry;
-    if (threadIdx.x == 0) carry = 0;
-    __syncthreads();
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (uint32_t base = 0; base < n_tiles; base += 1024) {
-        const uint32_t t = base + threadIdx.x;
-        uint32_t cnt = 0;
-        if (t < n_tiles) {
-            const uint2 rg = ranges[t];
-            cnt = (rg.y - rg.x + 31) / 32;
+    uint32_t carry = 0;
+    for (uint32_t base = 0; base < n_tiles; base += 1024 * kPer) {
+        const uint32_t first = base + threadIdx.x * kPer;
+        uint32_t cnt[kPer], sum = 0;
+#pragma unroll
+        for (int j = 0; j < kPer; j++) {
+            cnt[j] = 0;
+            if (first + j < n_tiles) {
+                const uint2 rg = ranges[first + j];
+                cnt[j] = (rg.y - rg.x + 31) / 32;
+            }
+            sum += cnt[j];
         }
-        uint32_t x = cnt;
+        uint32_t x = sum;
+#pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
             if (lane >= static_cast<uint32_t>(o)) x += y;
@@ -115,6 +121,7 @@ __global__ void __launch_bounds__(1024) bucket_scan_kernel(const uint2* __restri
         __syncthreads();
         if (warp == 0) {
             uint32_t v = warp_sums[lane];
+#pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
                 if (lane >= static_cast<uint32_t>(o)) v += y;
@@ -122,10 +129,13 @@ __global__ void __launch_bounds__(1024) bucket_scan_kernel(const uint2* __restri
             warp_sums[lane] = v;
         }
         __syncthreads();
-        const uint32_t incl = x + (warp > 0 ? warp_sums[warp - 1] : 0u) + carry;
-        if (t < n_tiles) off[t] = incl;
-        __syncthreads();
-        if (threadIdx.x == 1023) carry = incl;
+        uint32_t run = carry + x - sum + (warp > 0 ? warp_sums[warp - 1] : 0u);
+#pragma unroll
+        for (int j = 0; j < kPer; j++) {
+            run += cnt[j];
+            if (first + j < n_tiles) off[first + j] = run;
+        }
+        carry += warp_sums[31];
         __syncthreads();
     }
 }

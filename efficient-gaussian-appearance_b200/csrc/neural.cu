@@ -838,7 +838,7 @@ __global__ void __launch_bounds__(kFastWarps * 32, 2) neural_bwd_vis_kernel(Para
 
 // geometry chain rule of the visible primitives (one thread per row, rows in primitive order): mean (added to the
 // view-direction part written by the MLP backward), log-scale, rotation and opacity gradients, densification
-__global__ void __launch_bounds__(256) neural_geometry_bwd_kernel(Params P, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
+__global__ void __launch_bounds__(256, 3) neural_geometry_bwd_kernel(Params P, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
                                                                   const uint32_t* __restrict__ rank_of, const Record* __restrict__ sorted_rec,
                                                                   const GradRecord* __restrict__ grads, GradOut O) {
     const uint32_t gi = blockIdx.x * blockDim.x + threadIdx.x;

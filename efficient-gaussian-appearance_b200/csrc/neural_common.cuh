@@ -127,22 +127,11 @@ __device__ inline f3 view_dir(const View& v, f3 m, float* rn_out) {
     return rn * dv;
 }
 
-__device__ inline void put1(float* p, size_t k, float v, int acc) { if (acc) p[k] += v; else p[k] = v; }
-__device__ inline void put3n(float* p, uint32_t i, f3 v, int acc) { put1(p, 3ull * i, v.x, acc); put1(p, 3ull * i + 1, v.y, acc); put1(p, 3ull * i + 2, v.z, acc); }
-// as put3n, accumulating with reductions: each element receives one addition per launch, so the result is the
-// load-add-store value of put3n (a float atomic may flush a subnormal sum to zero), without the load on the thread's
-// critical path
-__device__ inline void add3n(float* p, uint32_t i, f3 v, int acc) {
-    float* q = p + 3ull * i;
-    if (acc) {
-        atomicAdd(q, v.x);
-        atomicAdd(q + 1, v.y);
-        atomicAdd(q + 2, v.z);
-    } else {
-        q[0] = v.x;
-        q[1] = v.y;
-        q[2] = v.z;
-    }
+// store, or add with a reduction (one addition per element and launch: deterministic, no load on the critical path)
+__device__ inline void put1(float* p, size_t k, float v, int acc) {
+    if (acc) atomicAdd(p + k, v);
+    else p[k] = v;
 }
+__device__ inline void put3n(float* p, uint32_t i, f3 v, int acc) { put1(p, 3ull * i, v.x, acc); put1(p, 3ull * i + 1, v.y, acc); put1(p, 3ull * i + 2, v.z, acc); }
 
 }  // namespace fgs

@@ -712,11 +712,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
                 gbase = mk3(base_act_grad(A.base_act, bb.x), base_act_grad(A.base_act, bb.y), base_act_grad(A.base_act, bb.z)) * gpre;
             }
             if (A.base_input) gbase = gbase + gbase_in;
-            add3n(O.base, i, gbase, O.accumulate);
+            put3n(O.base, i, gbase, O.accumulate);
         }
         if ((own & kOwnDir) && valid) {
             const f3 gmean_color = A.dir_grad ? rn * (gd - dot3(gd, d) * d) : mk3(0.0f, 0.0f, 0.0f);
-            add3n(O.means, i, gmean_color, O.accumulate);
+            put3n(O.means, i, gmean_color, O.accumulate);
         }
         sync_tile();
         cur = nxt;

@@ -20,7 +20,12 @@ __device__ inline void blend_sums_to_grads(const GradRecord& g, const Record& q,
     gop = proper_aa ? g.g2.x : (o - o * o) * g.g2.x;
 }
 
-__device__ inline void put(float* p, size_t k, float v, int acc) { if (acc) p[k] += v; else p[k] = v; }
+// store, or add with a reduction (every element receives one addition per launch, so the result is the load-add-store
+// value, deterministic, and the thread does not wait for the load)
+__device__ inline void put(float* p, size_t k, float v, int acc) {
+    if (acc) atomicAdd(p + k, v);
+    else p[k] = v;
+}
 __device__ inline void put3(float* p, uint32_t i, f3 v, int acc) { put(p, 3ull * i, v.x, acc); put(p, 3ull * i + 1, v.y, acc); put(p, 3ull * i + 2, v.z, acc); }
 
 // chain rule from the 2D gradients (mean2d, conic) to mean, log-scale and quaternion

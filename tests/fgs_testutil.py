@@ -88,6 +88,7 @@ def gpu_forward_stages(F, prims_dev: dict, settings, grad_image=None, densificat
     out['final_T'] = ft.transpose(0, 2, 1, 3).reshape(f.grid_h * 12, f.grid_w * 16)[:H, :W]
     out['n_contrib'] = nc.transpose(0, 2, 1, 3).reshape(f.grid_h * 12, f.grid_w * 16)[:H, :W]
     out['tile_max'] = view_tensor(st.tile_ws, v.tile_max_contributors, T, torch.int32).cpu().numpy().view(np.uint32)
+    out['bucket_off'] = view_tensor(st.tile_ws, v.bucket_offsets, T, torch.int32).cpu().numpy().view(np.uint32)
     return out
 
 

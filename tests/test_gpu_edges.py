@@ -19,6 +19,8 @@ def _check(F, cuda, prims, cam, degree=3):
     assert g['n_visible'] == o['n_visible'] and g['n_instances'] == o['n_instances']
     for k in ('n_touched', 'sorted_idx', 'tile_keys', 'ranks', 'ranges', 'n_contrib', 'image', 'final_T'):
         np.testing.assert_array_equal(g[k], o[k], err_msg=k)
+    lengths = o['ranges'][:, 1].astype(np.int64) - o['ranges'][:, 0].astype(np.int64)
+    np.testing.assert_array_equal(g['bucket_off'], np.cumsum((lengths + 31) // 32).astype(np.uint32), err_msg='bucket offsets')
     return g, o
 
 

@@ -43,6 +43,9 @@ def _compare_forward(g, o, exact_image):
     np.testing.assert_array_equal(g['tile_keys'], o['tile_keys'])
     np.testing.assert_array_equal(g['ranks'], o['ranks'])
     np.testing.assert_array_equal(g['ranges'], o['ranges'])
+    # bucket offsets: inclusive scan of ceil(tile list length / 32) (kernels_forward.cuh:14-24, forward.cu:204-219)
+    lengths = o['ranges'][:, 1].astype(np.int64) - o['ranges'][:, 0].astype(np.int64)
+    np.testing.assert_array_equal(g['bucket_off'], np.cumsum((lengths + 31) // 32).astype(np.uint32))
     rec_o = oracle_records_in_rank_order(o)
     rec_g = g['records']
     # geometry fields bit-exact: mean2d, opacity, power threshold, conic, bounds
