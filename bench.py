@@ -47,10 +47,21 @@ METRIC = {'c3': 'render FPS (inference, NASG 8 lobes, 3M Gaussians, 64 ring view
           'c3sv': 'render FPS (inference, Spherical Voronoi 8 sites, 3M Gaussians, 64 ring views @1920x1080, views sharded over the GPUs)','c1': 'train steps/s (forward + backward + fused Adam), fused SH-3 appearance, 1M Gaussians @1280x720',
           'c4': 'train steps/s (8 views @1920x1080, forward + loss + backward + gradient reduce-scatter + sharded fused Adam + '
                 'parameter all-gather), Neural appearance, 6M Gaussians'}
-# this library's kernels per rendered view (preprocess, chunk scan, compaction, reorder, emit, ranges, bucket scan,
-# forward blend, backward blend, backward preprocess) plus one fused Adam per step; CUB sort / scan kernels, torch's
-# loss kernels and NCCL are not counted
-OWN_KERNELS_PER_VIEW = 10
+# this library's kernel launches per view: preprocess 1, compaction 4 (group sums, group scan, chunk offsets, compact),
+# depth sort 4 passes x 3 (upsweep, row scan, downsweep), depth reorder 1, offset scan 3, emission 1, tile sort
+# 2 passes x 3 (end_bit 13 or 14 at these sizes), ranges + bucket scan 2, blend 1; training adds the fused loss 3
+# (c4), the backward blend 1 and the backward preprocess (SH: 1; Neural: tcgen05 backward + geometry 2), plus the
+# Neural colour pass 1 in the forward. Per step: c4 adds one zeroing of the untouched gradients and one fused Adam
+# (or the fused exchange kernel); c1 one fused Adam. NCCL and torch's own kernels are not counted.
+RENDER_LAUNCHES_PER_VIEW = 1 + 4 + 12 + 1 + 3 + 1 + 6 + 2 + 1
+
+
+def own_launches(wl_name: str, views: int) -> int:
+    if wl_name in RENDER:
+        return RENDER_LAUNCHES_PER_VIEW * views
+    if wl_name == 'c4':
+        return (RENDER_LAUNCHES_PER_VIEW + 1 + 3 + 1 + 2) * views + 2
+    return RENDER_LAUNCHES_PER_VIEW + 1 + 1 + 1
 
 
 def _peaks() -> tuple[float, str]:
@@ -323,13 +334,19 @@ def run_b200(args, wl_name: str) -> dict | None:
     barrier()
     ms_e2e = e2.elapsed_time(e3) / args.steps
 
-    # per-stage timing pass (CUDA events on the launching stream), averaged per step
+    # per-stage timing pass (CUDA events on the launching stream), averaged per step; the training step runs its views
+    # one after another here (no second stream), so every stage's events bracket only that stage's kernels
+    overlapped = wl_name == 'c4' and trainer.overlap_views
+    if overlapped:
+        trainer.overlap_views = False
     _lib.profile_enable(True)
     n_prof = 2
     for _ in range(n_prof):
         step()
     torch.cuda.synchronize()
     _lib.profile_enable(False)
+    if overlapped:
+        trainer.overlap_views = True
     stage_ms = {k: v / n_prof for k, v in _lib.profile_collect().items()}
 
     # frame statistics of one view
@@ -379,7 +396,7 @@ def run_b200(args, wl_name: str) -> dict | None:
                                    f'dp{world} (reduce-scatter / sharded Adam / all-gather: {exchange_desc})' if strong else f'replicas x{world}'),
                    'l2': 'inputs larger than L2 (parameters alone exceed 126 MB)'},
         'e2e': {'value': e2e_per_s, 'unit': 'frames/s' if render else 'steps/s', 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
-        'gpu_launches': ((8 * views_per_step) if render else (OWN_KERNELS_PER_VIEW * views_per_step + 1)) * args.steps,
+        'gpu_launches': own_launches(wl_name, views_per_step) * args.steps,
         'clocks': clocks,
         'stage_ms_per_step': {k: round(v, 4) for k, v in stage_ms.items()},
         'roofline': {'kernel': dominant, 'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'peak_kind': peak_kind, 'unit': 'GB/s',

@@ -112,8 +112,9 @@ class Trainer:
     """Holds the flat parameter / gradient buffers of one replica and runs data-parallel steps."""
 
     def __init__(self, prims: dict[str, torch.Tensor], lrs: dict[str, float | list], device: torch.device, group=None,
-                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool = False) -> None:
+                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool = False, overlap_views: bool = True) -> None:
         self.device = device
+        self.overlap_views = overlap_views
         self.pg = group
         self.world = torch.distributed.get_world_size(group) if group is not None else 1
         self.rank = torch.distributed.get_rank(group) if group is not None else 0
@@ -150,9 +151,10 @@ class Trainer:
         self.grad_shard = self.grads[self.rank * shard:(self.rank + 1) * shard] if self.world == 1 else torch.empty(shard, device=device)
         self.step_count = 0
         self.n = prims['means'].shape[0]
-        self.loss_fn = FusedLoss()
-        self._image = None
-        self._grad_image = None
+        self.loss_fns = (FusedLoss(), FusedLoss())
+        self._images = [None, None]
+        self._grad_images = [None, None]
+        self._side_stream = None
 
     def _setup_peer_buffers(self) -> None:
         """Flat buffers in symmetric memory: every rank's buffers mapped on every device (peer pointers), plus the
@@ -199,22 +201,46 @@ class Trainer:
                               p(v('residual_params')), p(v('mlp_weights')))
 
     def backward_views(self, settings_list: list, targets: list) -> torch.Tensor:
-        """Renders the local views and accumulates their gradients into the flat gradient buffer; returns the summed loss."""
+        """Renders the local views and accumulates their gradients into the flat gradient buffer; returns the summed loss.
+
+        With overlap_views (and more than one view) consecutive views alternate between the current stream and a side
+        stream, each with its own workspaces, image and loss buffers: the forward, loss and binning of view k + 1 run
+        while view k's backward runs. The backward passes stay chained in view order (each waits for the previous
+        one's event), so gradients accumulate view by view as in the sequential order."""
         cp = self._prims()
         cg = self._grads()
-        total = torch.zeros((), device=self.device)
+        main = torch.cuda.current_stream(self.device)
+        overlap = self.overlap_views and len(settings_list) > 1
+        if overlap and self._side_stream is None:
+            self._side_stream = torch.cuda.Stream(self.device)
+        streams = (main, self._side_stream if overlap else main)
+        totals = [torch.zeros((), device=self.device) for _ in range(2)]
+        if overlap:
+            streams[1].wait_stream(main)  # parameters, targets and totals are ready
+        prev_backward = None
+        states = [None, None]  # a view's workspaces live until the next view on the same stream replaces them
         for k, (settings, target) in enumerate(zip(settings_list, targets)):
-            st = R.ForwardState(R._rasterizer, cp, settings, self.device)
-            st.preprocess(cp)
-            shape = (3, settings.height, settings.width)
-            if self._image is None or tuple(self._image.shape) != shape:
-                self._image = torch.empty(shape, device=self.device)
-                self._grad_image = torch.empty(shape, device=self.device)
-            st.render_train(self._image)
-            loss, _ = self.loss_fn(self._image, target, grad_out=self._grad_image)
-            total += loss
-            st.backward(cp, self._image, self._grad_image, cg, None, accumulate=k > 0)
-        return total
+            j = k % 2
+            with torch.cuda.stream(streams[j]):
+                st = R.ForwardState(R._rasterizer, cp, settings, self.device)
+                st.preprocess(cp)
+                shape = (3, settings.height, settings.width)
+                if self._images[j] is None or tuple(self._images[j].shape) != shape:
+                    self._images[j] = torch.empty(shape, device=self.device)
+                    self._grad_images[j] = torch.empty(shape, device=self.device)
+                st.render_train(self._images[j])
+                loss, _ = self.loss_fns[j](self._images[j], target, grad_out=self._grad_images[j])
+                totals[j] += loss
+                if prev_backward is not None:
+                    streams[j].wait_event(prev_backward)
+                st.backward(cp, self._images[j], self._grad_images[j], cg, None, accumulate=k > 0)
+                if overlap:
+                    prev_backward = torch.cuda.Event()
+                    prev_backward.record(streams[j])
+                states[j] = st
+        if overlap:
+            main.wait_stream(streams[1])
+        return totals[0] + totals[1]
 
     def adam_segments(self, grad_slice: torch.Tensor | None = None) -> list:
         """Adam segments of this rank's slice [rank*S, (rank+1)*S), split at parameter-group boundaries (gradients from
