@@ -171,6 +171,11 @@ def settings_of(cam, degree: int, dev):
                                 cam.focal_y, cam.center_x, cam.center_y, cam.near_plane, cam.far_plane, False, True, True)
 
 
+# DRAM bytes (read + write) per visible row measured by ncu on the small c4 case (2M Gaussians, one view; profiles/
+# neural_tcgen05_small_case.md): MLP backward 570 + geometry backward 414; scaled by the view's visible rows
+TRAFFIC_PER_VISIBLE_ROW = {('c4', 'preprocess_backward'): 570.0 + 414.0}
+
+
 def stage_bytes(stage: str, s: dict) -> float:
     """Algorithmic DRAM bytes of one occurrence of each stage per view (per-unit figures x the frame's units)."""
     N, V, I, P, A = s['N'], s['V'], s['I'], s['pixels'], s['appearance_bytes']
@@ -361,6 +366,10 @@ def run_b200(args, wl_name: str) -> dict | None:
     peak, peak_kind = _peaks()
     bytes_dom = stage_bytes(dominant, stats)
     achieved = bytes_dom / (per_view[dominant] * 1e-3) / 1e9 if bytes_dom else 0.0
+    per_row = TRAFFIC_PER_VISIBLE_ROW.get((wl_name, dominant))
+    traffic = per_row * stats['V'] if per_row else None
+    traffic_src = ('ncu dram__bytes_read.sum + dram__bytes_write.sum per visible row on the 2M-Gaussian one-view case, x visible rows '
+                   'of view 0 (per view launch)') if per_row else None
     fracs = {k: round(stage_bytes(k, stats) / (per_view[k] * 1e-3) / 1e9 / peak, 4) for k in per_view if stage_bytes(k, stats) and per_view[k] > 0}
 
     if world > 1:
@@ -400,7 +409,8 @@ def run_b200(args, wl_name: str) -> dict | None:
         'clocks': clocks,
         'stage_ms_per_step': {k: round(v, 4) for k, v in stage_ms.items()},
         'roofline': {'kernel': dominant, 'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'peak_kind': peak_kind, 'unit': 'GB/s',
-                     'frac': achieved / peak, 'traffic': None, 'algorithmic_bytes': bytes_dom, 'frac_by_stage': fracs},
+                     'frac': achieved / peak, 'traffic': traffic, 'traffic_source': traffic_src, 'algorithmic_bytes': bytes_dom,
+                     'frac_by_stage': fracs},
     }
     if world > 1:
         torch.distributed.destroy_process_group()
