@@ -21,7 +21,8 @@ and writes the new parameters into every rank's buffer, between two device-side 
 symmetric memory can be set up on the group and falls back to 'nccl' otherwise. The switch-multicast variant
 (multimem) is opt-in (multicast=True).
 """
-from __future__ import annotations
+from __future__ import warnings
+import annotations
 
 import ctypes
 import math
@@ -162,7 +163,9 @@ class Trainer:
         import torch.distributed._symmetric_memory as symm
         name = self.pg.group_name
         if hasattr(symm, 'enable_symm_mem_for_group') and not symm.is_symm_mem_enabled_for_group(name):
-            symm.enable_symm_mem_for_group(name)
+            with warnings.catch_warnings():  # newer torch enables symmetric memory for every group and deprecates the call
+                warnings.simplefilter('ignore', FutureWarning)
+                symm.enable_symm_mem_for_group(name)
         self.params = symm.empty(self.total, dtype=torch.float32, device=self.device)
         self.grads = symm.empty(self.total, dtype=torch.float32, device=self.device)
         self.params.zero_()
