@@ -21,8 +21,9 @@ and writes the new parameters into every rank's buffer, between two device-side 
 symmetric memory can be set up on the group and falls back to 'nccl' otherwise. The switch-multicast variant
 (multimem) is opt-in (multicast=True).
 """
-from __future__ import warnings
-import annotations
+from __future__ import annotations
+
+import warnings
 
 import ctypes
 import math
