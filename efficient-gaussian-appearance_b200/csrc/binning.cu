@@ -92,6 +92,39 @@ __global__ void ranges_kernel(const K* __restrict__ keys, uint2* __restrict__ ra
     if (j == n - 1 || static_cast<uint32_t>(keys[j + 1]) != k) ranges[k].y = static_cast<uint32_t>(j + 1);
 }
 
+// the same with 8 consecutive keys per thread read as 16-byte vectors (keys 16-byte aligned)
+template <typename K>
+__global__ void __launch_bounds__(256) ranges8_kernel(const K* __restrict__ keys, uint2* __restrict__ ranges, uint64_t n) {
+    constexpr int kVec = 16 / sizeof(K);  // keys per 16-byte vector
+    const uint64_t j0 = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+    if (j0 >= n) return;
+    uint32_t k[8];
+    if (j0 + 8 <= n) {
+#pragma unroll
+        for (int v = 0; v < 8 / kVec; v++) {
+            const uint4 q = reinterpret_cast<const uint4*>(keys + j0)[v];
+            const K* e = reinterpret_cast<const K*>(&q);
+#pragma unroll
+            for (int i = 0; i < kVec; i++) k[v * kVec + i] = e[i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) k[i] = j0 + i < n ? static_cast<uint32_t>(keys[j0 + i]) : 0u;
+    }
+    uint32_t prev = j0 > 0 ? static_cast<uint32_t>(keys[j0 - 1]) : 0u;
+    const uint32_t after = j0 + 8 < n ? static_cast<uint32_t>(keys[j0 + 8]) : 0u;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint64_t j = j0 + i;
+        if (j >= n) break;
+        const uint32_t cur = k[i];
+        if (j == 0 || prev != cur) ranges[cur].x = static_cast<uint32_t>(j);
+        const uint32_t next = i < 7 ? k[i + 1] : after;
+        if (j == n - 1 || next != cur) ranges[cur].y = static_cast<uint32_t>(j + 1);
+        prev = cur;
+    }
+}
+
 // buckets of 32 instances per tile, inclusive scan (one CTA; a thread scans 8 consecutive tiles per round, so a
 // 1080p grid takes one round)
 __global__ void __launch_bounds__(1024) bucket_scan_kernel(const uint2* __restrict__ ranges, uint32_t* __restrict__ off, uint32_t n_tiles) {
@@ -153,9 +186,15 @@ cudaError_t launch_ranges(const void* keys, uint64_t n, bool wide, const TileBuf
     cudaError_t e = cudaMemsetAsync(T.ranges, 0, sizeof(uint2) * n_tiles, s);
     if (e != cudaSuccess) return e;
     if (n > 0) {
-        const unsigned grid = static_cast<unsigned>((n + 255) / 256);
-        if (wide) ranges_kernel<uint32_t><<<grid, 256, 0, s>>>(static_cast<const uint32_t*>(keys), T.ranges, n);
-        else ranges_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(keys), T.ranges, n);
+        if ((reinterpret_cast<uintptr_t>(keys) & 15u) == 0) {
+            const unsigned grid = static_cast<unsigned>((n + 8 * 256 - 1) / (8 * 256));
+            if (wide) ranges8_kernel<uint32_t><<<grid, 256, 0, s>>>(static_cast<const uint32_t*>(keys), T.ranges, n);
+            else ranges8_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(keys), T.ranges, n);
+        } else {
+            const unsigned grid = static_cast<unsigned>((n + 255) / 256);
+            if (wide) ranges_kernel<uint32_t><<<grid, 256, 0, s>>>(static_cast<const uint32_t*>(keys), T.ranges, n);
+            else ranges_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(keys), T.ranges, n);
+        }
     }
     bucket_scan_kernel<<<1, 1024, 0, s>>>(T.ranges, T.bucket_off, static_cast<uint32_t>(n_tiles));
     return cudaGetLastError();

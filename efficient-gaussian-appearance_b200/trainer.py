@@ -23,10 +23,9 @@ symmetric memory can be set up on the group and falls back to 'nccl' otherwise. 
 """
 from __future__ import annotations
 
-import warnings
-
 import ctypes
 import math
+import warnings
 from dataclasses import dataclass
 
 import torch
