@@ -87,6 +87,10 @@ PROTOTYPES = {
                              c_size_t, c_void_p, c_void_p, _P(Gradients), c_void_p, c_int, c_int, c_void_p]),
     'fgs_frame_buffers': (c_int, [_P(Frame), c_void_p, c_void_p, c_void_p, _P(FrameViews)]),
     'fgs_pruning_scores': (c_int, [_P(Settings), _P(Frame), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    'fgs_relocation_adjustment': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    'fgs_add_noise': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_float, ctypes.c_uint64, ctypes.c_uint64, c_void_p]),
+    'fgs_update_3d_filter': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_float, c_float, c_float, c_float, c_float,
+                                     c_float, c_float, c_float, c_void_p]),
     'fgs_adam_step': (c_int, [_P(AdamSegment), c_int, c_void_p]),
     'fgs_profile_enable': (c_int, [c_int]),
     'fgs_inference_noalloc': (c_int, [c_void_p, _P(Primitives), _P(Settings), c_void_p, c_int, c_int, c_void_p, _P(c_int64), _P(c_int64)]),

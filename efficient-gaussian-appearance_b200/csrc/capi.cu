@@ -589,6 +589,45 @@ int fgs_pruning_scores(const fgs_settings* settings, const fgs_frame* frame, voi
     return FGS_OK;
 }
 
+int fgs_relocation_adjustment(const float* old_opacities, const float* old_scales, const int64_t* n_samples, float* new_opacities,
+                              float* new_scales, int64_t n, void* stream) {
+    if (n < 0 || n > 0xFFFFFFFFll) return fail(FGS_ERR_INVALID_ARGUMENT, "n out of range");
+    if (n > 0 && (!old_opacities || !old_scales || !n_samples || !new_opacities || !new_scales)) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    FGS_CUDA(fgs::launch_relocation(old_opacities, old_scales, n_samples, new_opacities, new_scales, static_cast<uint32_t>(n),
+                                    static_cast<cudaStream_t>(stream)),
+             "relocation adjustment");
+    return FGS_OK;
+}
+
+int fgs_add_noise(const float* raw_scales, const float* raw_rotations, const float* raw_opacities, float* means, int64_t n, float current_lr,
+                  uint64_t seed, uint64_t offset, void* stream) {
+    if (n < 0 || n > 0xFFFFFFFFll) return fail(FGS_ERR_INVALID_ARGUMENT, "n out of range");
+    if (n > 0 && (!raw_scales || !raw_rotations || !raw_opacities || !means)) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (reinterpret_cast<uintptr_t>(raw_rotations) % 16 != 0) return fail(FGS_ERR_INVALID_ARGUMENT, "rotations must be 16-byte aligned");
+    FGS_CUDA(fgs::launch_add_noise(raw_scales, raw_rotations, raw_opacities, means, static_cast<uint32_t>(n), current_lr, seed, offset,
+                                   static_cast<cudaStream_t>(stream)),
+             "add noise");
+    return FGS_OK;
+}
+
+int fgs_update_3d_filter(const float* positions, const float* w2c, float* filter_3d, uint8_t* visibility_mask, int64_t n, int width, int height,
+                         float focal_x, float focal_y, float center_x, float center_y, float near_plane, float far_plane,
+                         float clipping_tolerance, float distance2filter, void* stream) {
+    if (n < 0 || n > 0xFFFFFFFFll) return fail(FGS_ERR_INVALID_ARGUMENT, "n out of range");
+    if (n > 0 && (!positions || !w2c || !filter_3d || !visibility_mask)) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (reinterpret_cast<uintptr_t>(w2c) % 16 != 0) return fail(FGS_ERR_INVALID_ARGUMENT, "w2c must be 16-byte aligned");
+    // frustum slopes of the image widened by the clipping tolerance (filter3d/src/filter3d.cu:63-73)
+    const float bounds = clipping_tolerance + 0.5f;
+    const float w = static_cast<float>(width), h = static_cast<float>(height);
+    const float ox = center_x - 0.5f * w, oy = center_y - 0.5f * h;
+    const float left = (-(bounds * w) - ox) / focal_x, right = (bounds * w - ox) / focal_x;
+    const float top = (-(bounds * h) - oy) / focal_y, bottom = (bounds * h - oy) / focal_y;
+    FGS_CUDA(fgs::launch_filter3d(positions, w2c, filter_3d, visibility_mask, static_cast<uint32_t>(n), left, right, top, bottom, near_plane,
+                                  far_plane, distance2filter, static_cast<cudaStream_t>(stream)),
+             "3d filter");
+    return FGS_OK;
+}
+
 int fgs_frame_buffers(const fgs_frame* frame, void* prim_ws, void* tile_ws, void* inst_ws, fgs_frame_views* out) {
     if (!frame || !out) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
     std::memset(out, 0, sizeof(fgs_frame_views));

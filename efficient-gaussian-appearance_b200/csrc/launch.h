@@ -94,4 +94,12 @@ cudaError_t launch_adam(const AdamSegment* segs, int n_segs, cudaStream_t s);
 cudaError_t launch_dp_shard_adam(const AdamSegment* segs, int n_segs, const float* const* grads, float* const* params, int n_ranks,
                                  const float* local_params, const float* mc_grads, float* mc_params, cudaStream_t s);
 
+// densification.cu
+cudaError_t launch_relocation(const float* old_opacity, const float* old_scale, const int64_t* n_samples, float* new_opacity, float* new_scale,
+                              uint32_t n, cudaStream_t s);
+cudaError_t launch_add_noise(const float* raw_scales, const float* raw_rotations, const float* raw_opacities, float* means, uint32_t n, float lr,
+                             uint64_t seed, uint64_t offset, cudaStream_t s);
+cudaError_t launch_filter3d(const float* positions, const float* w2c, float* filter, uint8_t* visible, uint32_t n, float left, float right,
+                            float top, float bottom, float near_plane, float far_plane, float distance2filter, cudaStream_t s);
+
 }  // namespace fgs

@@ -15,6 +15,9 @@
  *   _C.pruning_scores (rasterization/src/rasterization_api.cu:337-416, src/pruning_scores.cu:11-204)
  *                     -> fgs_forward_preprocess + fgs_forward_render + fgs_pruning_scores
  *   _C.adam_step (adam/src/adam.cu:44-87)                          -> fgs_adam_step (several tensors per launch)
+ *   _C.relocation_adjustment / _C.add_noise (densification/src/densification_api.cu:13-72)
+ *                                                                  -> fgs_relocation_adjustment, fgs_add_noise
+ *   _C.update_3d_filter (filter3d/src/filter3d.cu:43-90)           -> fgs_update_3d_filter
  * The reference's forward reads the visible-primitive and instance counts back to the host in the middle
  * of the call (rasterization/src/forward.cu:82-85) to size its buffers; here that point is the boundary
  * between fgs_forward_preprocess and fgs_forward_render, so the caller allocates the instance and bucket
@@ -186,6 +189,22 @@ int fgs_pruning_scores(const fgs_settings* settings, const fgs_frame* frame, voi
 
 /* fused Adam over up to 12 segments in one launch (adam/src/adam.cu:18-42 per element) */
 int fgs_adam_step(const fgs_adam_segment* segments, int n_segments, void* stream);
+
+/* 3DGS-MCMC relocation (densification/include/kernels_mcmc.cuh:10-54): for each of n primitives duplicated into
+ * n_samples[i] copies (clamped to 1..50), the new opacity keeps the composite opacity and the scales are rescaled.
+ * old_opacities [n] activated, old_scales [n,3] activated; outputs new_opacities [n], new_scales [n,3]. */
+int fgs_relocation_adjustment(const float* old_opacities, const float* old_scales, const int64_t* n_samples, float* new_opacities,
+                              float* new_scales, int64_t n, void* stream);
+/* 3DGS-MCMC position noise, in place on means [n,3] (kernels_mcmc.cuh:64-146): raw (pre-activation) scales [n,3],
+ * quaternions [n,4] (16-byte aligned) and opacity logits [n]; one Philox4x32-10 draw per primitive with counter
+ * (offset / 4, primitive index) and key `seed` (the reference takes seed and offset from torch's CUDA generator). */
+int fgs_add_noise(const float* raw_scales, const float* raw_rotations, const float* raw_opacities, float* means, int64_t n, float current_lr,
+                  uint64_t seed, uint64_t offset, void* stream);
+/* 3D filter update of one view (filter3d/src/filter3d.cu:11-90): positions [n,3], w2c [4,4] row-major (16-byte
+ * aligned), filter_3d [n] and visibility_mask [n] (bytes) updated in place. */
+int fgs_update_3d_filter(const float* positions, const float* w2c, float* filter_3d, uint8_t* visibility_mask, int64_t n, int width, int height,
+                         float focal_x, float focal_y, float center_x, float center_y, float near_plane, float far_plane,
+                         float clipping_tolerance, float distance2filter, void* stream);
 
 /* Data-parallel training (no reference counterpart: the reference trains on one GPU, Renderer.py:62-65): the
  * gradient reduce-scatter, the sharded Adam and the parameter all-gather of one step in one kernel over NVLink.
