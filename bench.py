@@ -213,6 +213,12 @@ def run_b200(args, wl_name: str) -> dict | None:
         pg = torch.distributed.group.WORLD
     configure(wl)
     prims = scene(wl)
+    if getattr(args, 'order', 'morton') == 'morton':
+        # a scene in training is kept in Morton order by the reference's trainer (Trainer.py:165-169, every 5000
+        # iterations): the same Gaussians, reordered so that neighbours in space are neighbours in memory
+        from trainer import morton_order
+        order = morton_order(prims['means'].to(dev)).cpu()
+        prims = {k: (v if k == 'mlp_weights' else v[order].contiguous()) for k, v in prims.items()}
     cams = S.ring_cameras(wl['views'] if wl_name in RENDER else 8, wl['width'], wl['height'])
 
     def barrier():
@@ -403,7 +409,8 @@ def run_b200(args, wl_name: str) -> dict | None:
                    'n_visible_view0': fr.n_visible, 'n_instances_view0': fr.n_instances,
                    'parallelism': (f'{world} GPU(s), views split, no collective' if render else
                                    f'dp{world} (reduce-scatter / sharded Adam / all-gather: {exchange_desc})' if strong else f'replicas x{world}'),
-                   'l2': 'inputs larger than L2 (parameters alone exceed 126 MB)'},
+                   'l2': 'inputs larger than L2 (parameters alone exceed 126 MB)',
+                   'gaussian_order': getattr(args, 'order', 'morton')},
         'e2e': {'value': e2e_per_s, 'unit': 'frames/s' if render else 'steps/s', 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
         'gpu_launches': own_launches(wl_name, views_per_step) * args.steps,
         'clocks': clocks,
@@ -520,6 +527,8 @@ def main() -> None:
     ap.add_argument('--multicast', action='store_true', help='peer exchange through NVSwitch multicast (multimem)')
     ap.add_argument('--gaussians', type=int, default=0, help='override the workload\'s Gaussian count (small profiling cases)')
     ap.add_argument('--views', type=int, default=0, help='override the workload\'s global batch of views (c4)')
+    ap.add_argument('--order', default='morton', choices=['morton', 'generated'],
+                    help='order of the Gaussians in memory: Morton order of the means (as the reference trainer keeps them) or as generated')
     args = ap.parse_args()
     if args.gaussians:
         WORKLOADS[args.workload]['n'] = args.gaussians

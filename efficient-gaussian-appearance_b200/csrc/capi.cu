@@ -610,6 +610,13 @@ int fgs_add_noise(const float* raw_scales, const float* raw_rotations, const flo
     return FGS_OK;
 }
 
+int fgs_morton_codes(const float* means, int64_t n, const float* box_min, const float* box_max, uint64_t* codes, void* stream) {
+    if (n < 0 || n > 0xFFFFFFFFll) return fail(FGS_ERR_INVALID_ARGUMENT, "n out of range");
+    if (!box_min || !box_max || (n > 0 && (!means || !codes))) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    FGS_CUDA(fgs::launch_morton(means, codes, static_cast<uint32_t>(n), box_min, box_max, static_cast<cudaStream_t>(stream)), "morton codes");
+    return FGS_OK;
+}
+
 int fgs_update_3d_filter(const float* positions, const float* w2c, float* filter_3d, uint8_t* visibility_mask, int64_t n, int width, int height,
                          float focal_x, float focal_y, float center_x, float center_y, float near_plane, float far_plane,
                          float clipping_tolerance, float distance2filter, void* stream) {

@@ -10,7 +10,9 @@
 //     through Box-Muller, s(o) = 1 / (1 + exp(100 o - 0.5)) of the activated opacity o; primitives with a degenerate
 //     quaternion are left unchanged);
 //   3D filter: filter3d/src/filter3d.cu:11-90 (for points inside the view frustum with the clipping tolerance, the
-//     filter becomes min(filter, distance2filter * depth) and the point is marked visible).
+//     filter becomes min(filter, distance2filter * depth) and the point is marked visible);
+//   Morton codes of the means for the periodic reordering of the Gaussians (Model.py:449-453 with NeRFICG's
+//     morton_encode, absent here): each coordinate quantised to 21 bits over the given box, bits interleaved x, y, z.
 // The relocation coefficients are evaluated in double on the host and kept in each device's constant memory.
 #include <curand_philox4x32_x.h>
 
@@ -145,6 +147,32 @@ __global__ void __launch_bounds__(256) filter3d_kernel(const float* __restrict__
     visible[i] = 1;
 }
 
+// 21 bits of x spread to every third bit of a 63-bit word
+__device__ inline uint64_t spread3(uint64_t x) {
+    x &= 0x1fffffull;
+    x = (x | (x << 32)) & 0x1f00000000ffffull;
+    x = (x | (x << 16)) & 0x1f0000ff0000ffull;
+    x = (x | (x << 8)) & 0x100f00f00f00f00full;
+    x = (x | (x << 4)) & 0x10c30c30c30c30c3ull;
+    x = (x | (x << 2)) & 0x1249249249249249ull;
+    return x;
+}
+
+__device__ inline uint64_t quantize21(float v, float lo, float scale) {
+    const float q = (v - lo) * scale;  // [0, 2^21) inside the box
+    return q <= 0.0f ? 0ull : (q >= 2097151.0f ? 2097151ull : static_cast<uint64_t>(q));
+}
+
+__global__ void __launch_bounds__(256) morton_kernel(const float* __restrict__ means, uint64_t* __restrict__ codes, uint32_t n, float3 lo,
+                                                     float3 scale) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint64_t qx = quantize21(means[3ull * i], lo.x, scale.x);
+    const uint64_t qy = quantize21(means[3ull * i + 1], lo.y, scale.y);
+    const uint64_t qz = quantize21(means[3ull * i + 2], lo.z, scale.z);
+    codes[i] = spread3(qx) | (spread3(qy) << 1) | (spread3(qz) << 2);
+}
+
 unsigned blocks_of(uint64_t n) { return static_cast<unsigned>((n + 255) / 256); }
 
 }  // namespace
@@ -163,6 +191,17 @@ cudaError_t launch_add_noise(const float* raw_scales, const float* raw_rotations
     if (n == 0) return cudaSuccess;
     add_noise_kernel<<<blocks_of(n), 256, 0, s>>>(raw_scales, reinterpret_cast<const float4*>(raw_rotations), raw_opacities, means, n, lr, seed,
                                                   offset);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_morton(const float* means, uint64_t* codes, uint32_t n, const float lo[3], const float hi[3], cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    float sc[3];
+    for (int a = 0; a < 3; a++) {
+        const float ext = hi[a] - lo[a];
+        sc[a] = ext > 0.0f ? 2097152.0f / ext : 0.0f;
+    }
+    morton_kernel<<<blocks_of(n), 256, 0, s>>>(means, codes, n, make_float3(lo[0], lo[1], lo[2]), make_float3(sc[0], sc[1], sc[2]));
     return cudaGetLastError();
 }
 

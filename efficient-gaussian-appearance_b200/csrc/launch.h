@@ -99,6 +99,7 @@ cudaError_t launch_relocation(const float* old_opacity, const float* old_scale, 
                               uint32_t n, cudaStream_t s);
 cudaError_t launch_add_noise(const float* raw_scales, const float* raw_rotations, const float* raw_opacities, float* means, uint32_t n, float lr,
                              uint64_t seed, uint64_t offset, cudaStream_t s);
+cudaError_t launch_morton(const float* means, uint64_t* codes, uint32_t n, const float lo[3], const float hi[3], cudaStream_t s);
 cudaError_t launch_filter3d(const float* positions, const float* w2c, float* filter, uint8_t* visible, uint32_t n, float left, float right,
                             float top, float bottom, float near_plane, float far_plane, float distance2filter, cudaStream_t s);
 

@@ -83,6 +83,21 @@ def loss_and_grad_reference(img: torch.Tensor, target: torch.Tensor, l1_weight: 
     return loss.detach(), x.grad
 
 
+def morton_order(means: torch.Tensor) -> torch.Tensor:
+    """Permutation that sorts Gaussians by the Morton code of their means (21 bits per axis over the means' bounding
+    box, fgs_morton_codes), ties kept in index order: the reordering the reference's trainer applies every 5000
+    iterations (Trainer.py:165-169, Model.py:449-453) so that Gaussians close in space are close in memory."""
+    m = means.detach().reshape(-1, 3).contiguous().float()
+    n = m.shape[0]
+    codes = torch.empty(n, dtype=torch.int64, device=m.device)
+    if n == 0:
+        return codes
+    lo, hi = m.min(0).values.tolist(), m.max(0).values.tolist()
+    _lib.check(_lib.lib.fgs_morton_codes(m.data_ptr(), n, (ctypes.c_float * 3)(*lo), (ctypes.c_float * 3)(*hi), codes.data_ptr(),
+                                         torch.cuda.current_stream(m.device).cuda_stream))
+    return torch.argsort(codes, stable=True)  # codes < 2^63: the signed order is the code order
+
+
 class FusedLoss:
     """The same loss through the library's fused CUDA kernels (fgs_l1_dssim): loss value and image gradient stay on
     the device; the workspace is kept between calls of the same image size."""
@@ -244,6 +259,30 @@ class Trainer:
         if overlap:
             main.wait_stream(streams[1])
         return totals[0] + totals[1]
+
+    @torch.no_grad()
+    def apply_morton_ordering(self) -> None:
+        """Reorders every per-Gaussian parameter group and its Adam moments by the Morton order of the means (the same
+        permutation on every rank: all replicas hold the same means). A rank's moments cover only its slice, so with
+        several ranks the moments are gathered, permuted and sliced again."""
+        order = morton_order(self.view(self.params, 'means'))
+        if self.world > 1:
+            full_m = torch.empty(self.total, dtype=torch.float32, device=self.device)
+            full_v = torch.empty(self.total, dtype=torch.float32, device=self.device)
+            torch.distributed.all_gather_into_tensor(full_m, self.exp_avg, group=self.pg)
+            torch.distributed.all_gather_into_tensor(full_v, self.exp_avg_sq, group=self.pg)
+        else:
+            full_m, full_v = self.exp_avg, self.exp_avg_sq
+        for g in self.groups:
+            if g.name == 'mlp_weights':
+                continue
+            for buf in (self.params, full_m, full_v):
+                rows = buf[g.offset:g.offset + g.numel].view(g.shape[0], -1)
+                rows.copy_(rows[order])
+        if self.world > 1:
+            lo = self.rank * self.shard
+            self.exp_avg.copy_(full_m[lo:lo + self.shard])
+            self.exp_avg_sq.copy_(full_v[lo:lo + self.shard])
 
     def adam_segments(self, grad_slice: torch.Tensor | None = None) -> list:
         """Adam segments of this rank's slice [rank*S, (rank+1)*S), split at parameter-group boundaries (gradients from

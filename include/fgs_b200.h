@@ -200,6 +200,10 @@ int fgs_relocation_adjustment(const float* old_opacities, const float* old_scale
  * (offset / 4, primitive index) and key `seed` (the reference takes seed and offset from torch's CUDA generator). */
 int fgs_add_noise(const float* raw_scales, const float* raw_rotations, const float* raw_opacities, float* means, int64_t n, float current_lr,
                   uint64_t seed, uint64_t offset, void* stream);
+/* Morton codes of means [n,3] for reordering the Gaussians (Model.py:449-453 sorts by NeRFICG's morton_encode, which
+ * is absent here): box_min / box_max are 3 host floats; each coordinate is quantised to 21 bits over the box and the
+ * bits are interleaved (x lowest), giving codes [n] (uint64) to argsort. */
+int fgs_morton_codes(const float* means, int64_t n, const float* box_min, const float* box_max, uint64_t* codes, void* stream);
 /* 3D filter update of one view (filter3d/src/filter3d.cu:11-90): positions [n,3], w2c [4,4] row-major (16-byte
  * aligned), filter_3d [n] and visibility_mask [n] (bytes) updated in place. */
 int fgs_update_3d_filter(const float* positions, const float* w2c, float* filter_3d, uint8_t* visibility_mask, int64_t n, int width, int height,

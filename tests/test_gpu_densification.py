@@ -79,3 +79,44 @@ def test_update_3d_filter_matches_oracle_bitwise(cuda):
     np.testing.assert_array_equal(flt_d.cpu().numpy(), rf)
     np.testing.assert_array_equal(vis_d.cpu().numpy(), rv)
     assert rv.sum() > 1000
+
+
+def _spread3(x):
+    out = np.zeros_like(x, dtype=np.uint64)
+    for b in range(21):
+        out |= ((x >> np.uint64(b)) & np.uint64(1)) << np.uint64(3 * b)
+    return out
+
+
+def test_morton_codes_and_reordering(cuda):
+    import FasterGSVDACudaBackend as F
+    from trainer import morton_order, Trainer
+    g = torch.Generator().manual_seed(3)
+    n = 50000
+    means = torch.randn(n, 3, generator=g) * torch.tensor([4.0, 1.0, 9.0])
+    order = morton_order(means.to(cuda)).cpu().numpy()
+    # codes restated: 21 bits per axis over the bounding box (float32 as the kernel), interleaved x lowest
+    m = means.numpy()
+    lo, hi = m.min(0), m.max(0)
+    q = np.empty((n, 3), np.uint64)
+    for a in range(3):
+        scale = np.float32(2097152.0) / (np.float32(hi[a]) - np.float32(lo[a]))
+        v = (m[:, a].astype(np.float32) - np.float32(lo[a])) * scale
+        q[:, a] = np.clip(np.floor(v), 0, 2097151).astype(np.uint64)
+    codes = _spread3(q[:, 0]) | (_spread3(q[:, 1]) << np.uint64(1)) | (_spread3(q[:, 2]) << np.uint64(2))
+    np.testing.assert_array_equal(order, np.argsort(codes, kind='stable'))
+    # the trainer permutes every per-Gaussian group (and its moments) by that order; the MLP weights stay
+    F.initialize_appearance('sh', 3, 'none', 'none', 'relu', True)
+    prims = {'means': means, 'scales': torch.randn(n, 3, generator=g) - 4.0, 'rotations': torch.randn(n, 4, generator=g),
+             'opacities': torch.randn(n, 1, generator=g), 'base_colors': torch.randn(n, 3, generator=g),
+             'residual_params': torch.randn(n, 45, generator=g)}
+    lrs = {k: 1e-3 for k in prims}
+    tr = Trainer({k: v.to(cuda) for k, v in prims.items()}, lrs, cuda)
+    tr.exp_avg.copy_(torch.arange(tr.shard, dtype=torch.float32, device=cuda))
+    before = tr.exp_avg.clone()
+    tr.apply_morton_ordering()
+    for k, v in prims.items():
+        assert torch.equal(tr.view(tr.params, k).cpu(), v[order])
+        gi = next(x for x in tr.groups if x.name == k)
+        moved = before[gi.offset:gi.offset + gi.numel].view(n, -1)[torch.from_numpy(order).to(cuda)]
+        assert torch.equal(tr.exp_avg[gi.offset:gi.offset + gi.numel].view(n, -1), moved)
