@@ -171,9 +171,9 @@ def settings_of(cam, degree: int, dev):
                                 cam.focal_y, cam.center_x, cam.center_y, cam.near_plane, cam.far_plane, False, True, True)
 
 
-# DRAM bytes (read + write) per visible row measured by ncu on the small c4 case (2M Gaussians, one view; profiles/
-# neural_tcgen05_small_case.md): MLP backward 570 + geometry backward 414; scaled by the view's visible rows
-TRAFFIC_PER_VISIBLE_ROW = {('c4', 'preprocess_backward'): 570.0 + 414.0}
+# DRAM bytes (read + write) per visible row measured by ncu on the small c4 case (2M Gaussians in Morton order, one
+# view; profiles/neural_tcgen05_small_case.md): MLP backward 415 + geometry backward 190; scaled by the view's visible rows
+TRAFFIC_PER_VISIBLE_ROW = {('c4', 'preprocess_backward'): 415.0 + 190.0}
 
 
 def stage_bytes(stage: str, s: dict) -> float:
@@ -374,7 +374,7 @@ def run_b200(args, wl_name: str) -> dict | None:
     achieved = bytes_dom / (per_view[dominant] * 1e-3) / 1e9 if bytes_dom else 0.0
     per_row = TRAFFIC_PER_VISIBLE_ROW.get((wl_name, dominant))
     traffic = per_row * stats['V'] if per_row else None
-    traffic_src = ('ncu dram__bytes_read.sum + dram__bytes_write.sum per visible row on the 2M-Gaussian one-view case, x visible rows '
+    traffic_src = ('ncu dram__bytes_read.sum + dram__bytes_write.sum per visible row on the 2M-Gaussian one-view case (Morton order), x visible rows '
                    'of view 0 (per view launch)') if per_row else None
     fracs = {k: round(stage_bytes(k, stats) / (per_view[k] * 1e-3) / 1e9 / peak, 4) for k in per_view if stage_bytes(k, stats) and per_view[k] > 0}
 
