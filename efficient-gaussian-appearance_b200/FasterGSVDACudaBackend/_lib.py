@@ -89,6 +89,7 @@ PROTOTYPES = {
     'fgs_pruning_scores': (c_int, [_P(Settings), _P(Frame), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     'fgs_relocation_adjustment': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     'fgs_add_noise': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_float, ctypes.c_uint64, ctypes.c_uint64, c_void_p]),
+    'fgs_tc_timeout': (c_int, [_P(c_int), c_int]),
     'fgs_morton_codes': (c_int, [c_void_p, c_int64, _P(c_float), _P(c_float), c_void_p, c_void_p]),
     'fgs_update_3d_filter': (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_float, c_float, c_float, c_float, c_float,
                                      c_float, c_float, c_float, c_void_p]),

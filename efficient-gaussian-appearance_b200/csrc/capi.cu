@@ -399,7 +399,20 @@ int fgs_forward_preprocess(fgs_rasterizer* r, const fgs_primitives* prims, const
     unsigned long long* host = pinned_counters();
     if (!host) return fail(FGS_ERR_CUDA, "pinned host buffer");
     FGS_CUDA(cudaMemcpyAsync(host, B.counters, 2 * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s), "counter readback");
+    // the tensor-core MLP kernels' timeout flag rides along with the counters (Neural appearance only)
+    const bool neural = !precomputed && r->cfg.model == fgs::kNeural;
+    int* tc_flag = nullptr;
+    host[2] = 0;
+    if (neural) {
+        FGS_CUDA(fgs::tc_timeout_flag(&tc_flag), "tensor-core timeout flag");
+        FGS_CUDA(cudaMemcpyAsync(&host[2], tc_flag, sizeof(int), cudaMemcpyDeviceToHost, s), "tensor-core timeout flag");
+    }
     FGS_CUDA(cudaStreamSynchronize(s), "counter readback");
+    if (neural && (host[2] & 0xffffffffull)) {
+        FGS_CUDA(cudaMemsetAsync(tc_flag, 0, sizeof(int), s), "tensor-core timeout flag");
+        return fail(FGS_ERR_CUDA, "a tensor-core MLP kernel launched earlier on this device gave up a bounded wait for its MMAs; "
+                                  "the gradients or colours it produced are invalid (the flag is now cleared)");
+    }
     const uint64_t n_visible = host[0], n_inst = host[1];
     if (n_inst > 0x7fffff00ULL) return fail(FGS_ERR_UNSUPPORTED, "more than 2^31 instances");
     frame->n_visible = static_cast<int64_t>(n_visible);
@@ -735,6 +748,15 @@ int fgs_l1_dssim(const float* image, const float* target, int channels, int heig
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     ProfScope p_("loss", s);
     FGS_CUDA(fgs::launch_l1_dssim(image, target, channels, height, width, l1_weight, dssim_weight, grad_image, loss, workspace, s), "loss");
+    return FGS_OK;
+}
+
+int fgs_tc_timeout(int* timed_out, int clear) {
+    if (!timed_out) return fail(FGS_ERR_INVALID_ARGUMENT, "NULL argument");
+    int* flag = nullptr;
+    FGS_CUDA(fgs::tc_timeout_flag(&flag), "tensor-core timeout flag");
+    FGS_CUDA(cudaMemcpy(timed_out, flag, sizeof(int), cudaMemcpyDeviceToHost), "tensor-core timeout flag");
+    if (clear && *timed_out) FGS_CUDA(cudaMemset(flag, 0, sizeof(int)), "tensor-core timeout flag");
     return FGS_OK;
 }
 

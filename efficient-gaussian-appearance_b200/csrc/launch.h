@@ -78,6 +78,9 @@ cudaError_t launch_tc_backward(const Params& P, const AppearanceConfig& A, const
 constexpr int kTcSelftestFloats = 14400;
 constexpr int kTcSelftestStatus = 14336;
 cudaError_t tc_selftest(float* scratch, int* mismatches, cudaStream_t s);
+// device address of the flag the tcgen05 kernels set when a bounded mbarrier wait ran out (their outputs are then
+// invalid); it stays set until cleared
+cudaError_t tc_timeout_flag(int** flag);
 
 // adam.cu
 struct AdamSegment {

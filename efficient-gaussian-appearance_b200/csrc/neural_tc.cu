@@ -17,6 +17,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdint>
+#include <mutex>
 #include <vector>
 
 #include "launch.h"
@@ -863,6 +864,25 @@ cudaError_t launch_tc_backward(const Params& P, const AppearanceConfig& A, const
     if (e != cudaSuccess) return e;
     tc_bwd_kernel<<<grid, kTcThreads, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, p);
     return cudaGetLastError();
+}
+
+// device address of this device's timeout flag (cached per device)
+cudaError_t tc_timeout_flag(int** flag) {
+    static std::mutex mu;
+    static int* addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_tc_timeout);
+        if (e != cudaSuccess) return e;
+        addr[dev] = static_cast<int*>(p);
+    }
+    *flag = addr[dev];
+    return cudaSuccess;
 }
 
 }  // namespace fgs

@@ -244,6 +244,10 @@ int fgs_l1_dssim(const float* image, const float* target, int channels, int heig
  * floats. Synchronises the stream. */
 #define FGS_TC_SELFTEST_FLOATS 14400
 int fgs_tc_selftest(float* scratch, int* mismatches, void* stream);
+/* (no reference counterpart) whether a tcgen05 MLP kernel on the current device gave up a bounded wait for its MMAs
+ * since the flag was last cleared (its outputs are then invalid; fgs_forward_preprocess of a Neural configuration
+ * also reports it as an error and clears it). Synchronous; clear != 0 resets the flag. */
+int fgs_tc_timeout(int* timed_out, int clear);
 
 /* Optional per-stage timing: while enabled, every stage above records a CUDA event pair on its stream;
  * fgs_profile_collect waits for them, returns the summed milliseconds per stage since the last collect

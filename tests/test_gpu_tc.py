@@ -14,3 +14,12 @@ def test_tcgen05_selftest(cuda):
     bad = ctypes.c_int(-1)
     _lib.check(_lib.lib.fgs_tc_selftest(scratch.data_ptr(), ctypes.byref(bad), torch.cuda.current_stream().cuda_stream))
     assert bad.value == 0
+
+
+@pytest.mark.gpu
+def test_no_tensor_core_wait_ran_out(cuda):
+    """The tcgen05 kernels report a bounded mbarrier wait that ran out through a device flag (fgs_tc_timeout); after
+    the self-test and the earlier tests' Neural renders it must be clear."""
+    flag = ctypes.c_int(-1)
+    _lib.check(_lib.lib.fgs_tc_timeout(ctypes.byref(flag), 0))
+    assert flag.value == 0
