@@ -268,10 +268,18 @@ def run_b200(args, wl_name: str) -> dict | None:
         def step():
             return trainer.step(settings, tg_dev)
 
+        copy_stream = torch.cuda.Stream(dev)
+        arrived = [torch.cuda.Event() for _ in tg_dev]
+
         def step_e2e():
-            for h, d in zip(tg_host, tg_dev):
-                d.copy_(h, non_blocking=True)
-            loss = trainer.step(settings, tg_dev)
+            # the step's targets go up on a copy stream, one event per view, so the first views render while the later
+            # targets are still in flight; the previous step's losses were the last readers of the device buffers
+            copy_stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(copy_stream):
+                for h, d, ev in zip(tg_host, tg_dev, arrived):
+                    d.copy_(h, non_blocking=True)
+                    ev.record(copy_stream)
+            loss = trainer.step(settings, tg_dev, ready=arrived)
             return loss.to('cpu', non_blocking=True)
 
         h2d = sum(t.numel() * 4 for t in tg_host)

@@ -218,13 +218,14 @@ class Trainer:
         return _lib.Gradients(p(v('means')), p(v('scales')), p(v('rotations')), p(v('opacities')), None, p(v('base_colors')),
                               p(v('residual_params')), p(v('mlp_weights')))
 
-    def backward_views(self, settings_list: list, targets: list) -> torch.Tensor:
+    def backward_views(self, settings_list: list, targets: list, ready: list | None = None) -> torch.Tensor:
         """Renders the local views and accumulates their gradients into the flat gradient buffer; returns the summed loss.
 
         With overlap_views (and more than one view) consecutive views alternate between the current stream and a side
         stream, each with its own workspaces, image and loss buffers: the forward, loss and binning of view k + 1 run
         while view k's backward runs. The backward passes stay chained in view order (each waits for the previous
-        one's event), so gradients accumulate view by view as in the sequential order."""
+        one's event), so gradients accumulate view by view as in the sequential order. `ready` (optional, one CUDA
+        event per view) lets the targets arrive asynchronously: view k's loss waits for ready[k], its render does not."""
         cp = self._prims()
         cg = self._grads()
         main = torch.cuda.current_stream(self.device)
@@ -247,6 +248,8 @@ class Trainer:
                     self._images[j] = torch.empty(shape, device=self.device)
                     self._grad_images[j] = torch.empty(shape, device=self.device)
                 st.render_train(self._images[j])
+                if ready is not None:
+                    streams[j].wait_event(ready[k])
                 loss, _ = self.loss_fns[j](self._images[j], target, grad_out=self._grad_images[j])
                 totals[j] += loss
                 if prev_backward is not None:
@@ -317,7 +320,7 @@ class Trainer:
             torch.distributed.all_gather_into_tensor(self.params, self.params[self.rank * self.shard:(self.rank + 1) * self.shard],
                                                      group=self.pg)
 
-    def step(self, settings_list: list, targets: list) -> torch.Tensor:
-        loss = self.backward_views(settings_list, targets)
+    def step(self, settings_list: list, targets: list, ready: list | None = None) -> torch.Tensor:
+        loss = self.backward_views(settings_list, targets, ready)
         self.apply_gradients()
         return loss
