@@ -243,9 +243,19 @@ def run_b200(args, wl_name: str) -> dict | None:
             for s0 in settings:
                 render(s0)
 
+        copy_stream = torch.cuda.Stream(dev)
+
         def step_e2e():
+            # each image goes down on a copy stream while the next view renders; the step ends with the last image on
+            # the host
+            main = torch.cuda.current_stream()
             for k, s0 in enumerate(settings):
-                imgs_host[k % 2].copy_(render(s0), non_blocking=True)
+                img = render(s0)
+                copy_stream.wait_stream(main)
+                with torch.cuda.stream(copy_stream):
+                    imgs_host[k % 2].copy_(img, non_blocking=True)
+                img.record_stream(copy_stream)
+            main.wait_stream(copy_stream)
 
         h2d = 0
         d2h = len(mine) * wl['height'] * wl['width'] * 3 * 4
@@ -311,10 +321,28 @@ def run_b200(args, wl_name: str) -> dict | None:
         def step():
             return run(grad_dev)
 
+        copy_stream = torch.cuda.Stream(dev)
+        grad_in = torch.empty_like(grad_dev)
+        grad_ready = torch.cuda.Event()
+
         def step_e2e():
-            g = grad_host.to(dev, non_blocking=True)
-            img = run(g)
-            img_host.copy_(img.detach(), non_blocking=True)
+            # the upstream gradient goes up on a copy stream during the forward; the image goes down during the backward
+            main = torch.cuda.current_stream()
+            copy_stream.wait_stream(main)
+            with torch.cuda.stream(copy_stream):
+                grad_in.copy_(grad_host, non_blocking=True)
+                grad_ready.record(copy_stream)
+            img = F.diff_rasterize(params['means'], params['scales'], params['rotations'], params['opacities'], empty, s0,
+                                   base_colors=params['base_colors'], residual_params=params['residual_params'])
+            copy_stream.wait_stream(main)
+            with torch.cuda.stream(copy_stream):
+                img_host.copy_(img.detach(), non_blocking=True)
+            main.wait_event(grad_ready)
+            img.backward(grad_in)
+            opt.step()
+            for p in params.values():
+                p.grad = None
+            main.wait_stream(copy_stream)
             return img_host
 
         h2d = grad_host.numel() * 4
