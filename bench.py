@@ -465,8 +465,9 @@ def run_b200(args, wl_name: str) -> dict | None:
 # ------------------------------------------------------------------------------------------------------------
 # CPU restatement (reference arm and cpu_baseline)
 
-def cpu_step(wl_name: str, tile_sample: float = 0.05) -> dict:
-    """Time of one step of the CPU restatement (oracle/, one thread), on a bounded sample:
+def cpu_step(wl_name: str, tile_sample: float = 0.05, threads: int = 0) -> dict:
+    """Time of one step of the CPU restatement (oracle/, its per-primitive and per-pixel loops on `threads` OpenMP
+    threads, by default every host core), on a bounded sample:
     c1: preprocess / depth order / binning / backward preprocess / Adam of all Gaussians, blends on a random
         `tile_sample` fraction of the tiles (scaled to all tiles).
     c4: one view of a scene with 1/64 of the Gaussians (same distributions) with blends on `tile_sample` of the tiles;
@@ -483,6 +484,16 @@ def cpu_step(wl_name: str, tile_sample: float = 0.05) -> dict:
     prims = scene(wl)
     cam = S.ring_cameras(8, wl['width'], wl['height'])[0]
     lib = O.load(False)
+    threads = threads or os.cpu_count() or 1
+    O.set_threads(threads)
+    try:
+        return _cpu_step_timed(wl_name, wl, prims, cam, lib, O, scale, tile_sample, threads)
+    finally:
+        O.set_threads(1)
+
+
+def _cpu_step_timed(wl_name, wl, prims, cam, lib, O, scale, tile_sample, threads) -> dict:
+    import ctypes
     if wl['model'] in ('sh', 'nasg', 'sv'):
         a = O.make_appearance(wl['model'], wl['degree'], 0, 0, 1, True)
     else:
@@ -521,8 +532,8 @@ def cpu_step(wl_name: str, tile_sample: float = 0.05) -> dict:
         t2 = time.perf_counter()
         frame_s = (t1 - t0) * scale + (t2 - t1) * scale / frac
         sample = (f'{wl_name} frame estimated from one view of a {n}-Gaussian scene (1/32 of 3M) at 1920x1080 with the blend on '
-                  f'{int(keep.sum())} of {T} tiles, scaled x32 (x{32 / frac:.0f} for the blend); single-threaded C restatement')
-        return {'value': 1.0 / frame_s, 'unit': 'frames/s', 'cores': 1, 'kind': 'port', 'sample': sample}
+                  f'{int(keep.sum())} of {T} tiles, scaled x32 (x{32 / frac:.0f} for the blend); C restatement on {threads} threads')
+        return {'value': 1.0 / frame_s, 'unit': 'frames/s', 'cores': threads, 'kind': 'port', 'sample': sample}
     gimg = np.ascontiguousarray((np.random.default_rng(2).standard_normal((3, H, W)) * 0.01).astype(np.float32))
     rg = np.zeros((max(V, 1), 12))
     lib.orc_blend_backward(V, O._p(sidx), O._p(rec), O._p(ranks), O._p(ranges_s), ctypes.byref(v), O._p(nc), O._p(gimg), O._p(rg))
@@ -543,11 +554,11 @@ def cpu_step(wl_name: str, tile_sample: float = 0.05) -> dict:
     step_s = view_s * wl['views'] + (t4 - t3) * scale
     if wl_name == 'c4':
         sample = (f'c4 step estimated from one view of a {n}-Gaussian scene (1/64 of 6M) at 1920x1080 with blends on {int(keep.sum())} of '
-                  f'{T} tiles, scaled x64 (x{64 / frac:.0f} for blends), x8 views, plus Adam; single-threaded C restatement')
+                  f'{T} tiles, scaled x64 (x{64 / frac:.0f} for blends), x8 views, plus Adam; C restatement on {threads} threads')
     else:
         sample = (f'c1 step: preprocess/binning/backward-preprocess/Adam on all {n} Gaussians, blends on {int(keep.sum())} of {T} tiles scaled '
-                  f'x{1 / frac:.1f}; single-threaded C restatement')
-    return {'value': 1.0 / step_s, 'unit': 'steps/s', 'cores': 1, 'kind': 'port', 'sample': sample}
+                  f'x{1 / frac:.1f}; C restatement on {threads} threads')
+    return {'value': 1.0 / step_s, 'unit': 'steps/s', 'cores': threads, 'kind': 'port', 'sample': sample}
 
 
 def main() -> None:

@@ -29,6 +29,9 @@
 #include <stdlib.h>
 #include <string.h>
 #include <tgmath.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 #ifndef ORC_DOUBLE
 typedef float real;
@@ -410,12 +413,28 @@ static v3_r fused_color(const orc_appearance* A, const orc_view* v, int64_t i, c
     return col;
 }
 
+/* Threads of the per-primitive and per-pixel loops (OpenMP). 1 (the default, used by the parity tests) runs every loop
+ * in order; more threads give the same per-element results, and sums over elements (the MLP weight gradient, the
+ * blend backward's per-primitive sums) are then added per thread and combined in thread order. */
+static int g_threads = 1;
+void orc_set_threads(int n) { g_threads = n < 1 ? 1 : n; }
+int orc_threads(void) { return g_threads; }
+
+static inline int thread_id(void) {
+#ifdef _OPENMP
+    return omp_get_thread_num();
+#else
+    return 0;
+#endif
+}
+
 /* Forward preprocess of all primitives. Outputs (primitive order): n_touched[N], depth_key[N] (float bits
  * of the depth in working precision; only meaningful where n_touched > 0), rec[N*14] as doubles
  * (mx, my, opacity, thr, ca, cb, cc, r, g, b, xmin, xmax, ymin, ymax). */
 int orc_preprocess(const orc_appearance* A, const orc_view* v, int64_t n, const inreal* means, const inreal* scales, const inreal* rots,
                    const inreal* opac, const inreal* precomputed, const inreal* base, const inreal* residual, const inreal* mlp,
                    uint32_t* n_touched, uint32_t* depth_key, double* rec) {
+#pragma omp parallel for schedule(dynamic, 64) num_threads(g_threads) if (g_threads > 1)
     for (int64_t i = 0; i < n; i++) {
         orc_rec q;
         memset(&q, 0, sizeof(q));
@@ -471,34 +490,50 @@ static void rec_of(const double* rec, uint32_t i, orc_rec* q) {
 int64_t orc_bin(int64_t n_visible, const uint32_t* sorted_idx, const double* rec, int width, int height, uint32_t* tile_keys,
                 uint32_t* ranks, uint32_t* ranges) {
     const int gw = (width + TILE_W - 1) / TILE_W, gh = (height + TILE_H - 1) / TILE_H, T = gw * gh;
-    int64_t n_inst = 0;
-    int64_t* counts = (int64_t*)calloc((size_t)T + 1, sizeof(int64_t));
-    /* pass 1: count per tile; pass 2: place (counting sort keeps emission order inside a tile) */
+    /* emission: per depth rank the touched tiles of its primitive in row-major order (the exact tile test), ranks in
+     * order; then a stable counting sort by tile keeps the emission order inside every tile list */
+    int64_t* off = (int64_t*)calloc((size_t)n_visible + 1, sizeof(int64_t));
     for (int pass = 0; pass < 2; pass++) {
-        int64_t* pos = 0;
-        if (pass == 1) {
-            pos = (int64_t*)malloc(sizeof(int64_t) * ((size_t)T + 1));
-            int64_t acc = 0;
-            for (int t = 0; t < T; t++) { pos[t] = acc; ranges[2 * t] = (uint32_t)acc; acc += counts[t]; ranges[2 * t + 1] = (uint32_t)acc; }
-            for (int t = 0; t < T; t++) if (counts[t] == 0) { ranges[2 * t] = 0; ranges[2 * t + 1] = 0; }
-        }
+        uint32_t* em = pass == 1 ? (uint32_t*)malloc(sizeof(uint32_t) * ((size_t)off[n_visible] + 1)) : 0;
+#pragma omp parallel for schedule(dynamic, 256) num_threads(g_threads) if (g_threads > 1)
         for (int64_t r = 0; r < n_visible; r++) {
             orc_rec q;
             rec_of(rec, sorted_idx[r], &q);
             const uint32_t tx0 = q.xmin / TILE_W, tx1 = (q.xmax + TILE_W - 1) / TILE_W, ty0 = q.ymin / TILE_H, ty1 = (q.ymax + TILE_H - 1) / TILE_H;
             const uint32_t bw = tx1 - tx0, nmax = bw * (ty1 - ty0);
             const real sx = q.mx - R(0.5), sy = q.my - R(0.5);
+            int64_t k = 0;
             for (uint32_t t = 0; t < nmax; t++) {
                 const uint32_t tx = tx0 + t % bw, ty = ty0 + t / bw;
                 if (!tile_overlaps_r(sx, sy, q.ca, q.cb, q.cc, tx, ty, q.thr)) continue;
-                const uint32_t tile = ty * (uint32_t)gw + tx;
-                if (pass == 0) { counts[tile]++; n_inst++; }
-                else { const int64_t p = pos[tile]++; tile_keys[p] = tile; ranks[p] = (uint32_t)r; }
+                if (pass == 1) em[off[r] + k] = ty * (uint32_t)gw + tx;
+                k++;
             }
+            if (pass == 0) off[r + 1] = k;
         }
+        if (pass == 0) {
+            for (int64_t r = 0; r < n_visible; r++) off[r + 1] += off[r];
+            continue;
+        }
+        const int64_t n_inst = off[n_visible];
+        int64_t* pos = (int64_t*)calloc((size_t)T + 1, sizeof(int64_t));
+        for (int64_t i = 0; i < n_inst; i++) pos[em[i] + 1]++;
+        for (int t = 0; t < T; t++) {
+            ranges[2 * t] = pos[t + 1] ? (uint32_t)pos[t] : 0;
+            pos[t + 1] += pos[t];
+            ranges[2 * t + 1] = pos[t + 1] - pos[t] ? (uint32_t)pos[t + 1] : 0;
+        }
+        for (int64_t r = 0; r < n_visible; r++)
+            for (int64_t i = off[r]; i < off[r + 1]; i++) {
+                const int64_t p2 = pos[em[i]]++;
+                tile_keys[p2] = em[i];
+                ranks[p2] = (uint32_t)r;
+            }
         free(pos);
+        free(em);
     }
-    free(counts);
+    const int64_t n_inst = off[n_visible];
+    free(off);
     return n_inst;
 }
 
@@ -522,6 +557,7 @@ int orc_blend(int64_t n_visible, const uint32_t* sorted_idx, const double* rec, 
               const orc_view* v, real* image, real* final_T, uint32_t* n_contrib, int chw, int clamp_out) {
     (void)n_visible;
     const int W = v->width, H = v->height, gw = (W + TILE_W - 1) / TILE_W;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(g_threads) if (g_threads > 1)
     for (int py = 0; py < H; py++) {
         for (int px = 0; px < W; px++) {
             const int tx = px / TILE_W, ty = py / TILE_H, tile = ty * gw + tx;
@@ -572,8 +608,22 @@ int orc_blend_backward(int64_t n_visible, const uint32_t* sorted_idx, const doub
     memset(grads, 0, sizeof(double) * 12 * (size_t)n_visible);
     const size_t np = (size_t)W * H;
     typedef struct { uint32_t r; double alpha, G, dx, dy; } frag;
+    const int nt = g_threads;
+    /* with several threads each accumulates into its own (lazily zeroed) copy and lists the depth ranks it touched, so
+     * combining costs as much as the contributions, not as the whole copies */
+    double* parts = nt > 1 ? (double*)calloc((size_t)nt * 12 * (size_t)n_visible, sizeof(double)) : 0;
+    uint8_t* seen = nt > 1 ? (uint8_t*)calloc((size_t)nt * (size_t)n_visible, 1) : 0;
+    uint32_t** touched = nt > 1 ? (uint32_t**)calloc((size_t)nt, sizeof(uint32_t*)) : 0;
+    size_t* n_touched_t = nt > 1 ? (size_t*)calloc((size_t)nt, sizeof(size_t)) : 0;
+#pragma omp parallel num_threads(nt) if (nt > 1)
+    {
+    const int tid = thread_id();
+    double* acc = parts ? parts + (size_t)tid * 12 * (size_t)n_visible : grads;
+    uint8_t* my_seen = seen ? seen + (size_t)tid * (size_t)n_visible : 0;
+    size_t list_cap = 0;
     frag* fr = (frag*)malloc(sizeof(frag) * 1);
     size_t cap = 1;
+#pragma omp for schedule(dynamic, 1)
     for (int py = 0; py < H; py++) {
         for (int px = 0; px < W; px++) {
             const int tx = px / TILE_W, ty = py / TILE_H, tile = ty * gw + tx;
@@ -612,7 +662,15 @@ int orc_blend_backward(int64_t n_visible, const uint32_t* sorted_idx, const doub
             T = 1.0;
             for (size_t k = 0; k < nf; k++) {
                 const double* o = rec + 14 * (size_t)sorted_idx[fr[k].r];
-                double* gr = grads + 12 * (size_t)fr[k].r;
+                double* gr = acc + 12 * (size_t)fr[k].r;
+                if (my_seen && !my_seen[fr[k].r]) {
+                    my_seen[fr[k].r] = 1;
+                    if (n_touched_t[tid] == list_cap) {
+                        list_cap = list_cap ? 2 * list_cap : 1024;
+                        touched[tid] = (uint32_t*)realloc(touched[tid], list_cap * sizeof(uint32_t));
+                    }
+                    touched[tid][n_touched_t[tid]++] = fr[k].r;
+                }
                 const double a = fr[k].alpha, w = T * a;
                 for (int c = 0; c < 3; c++) { gr[5 + c] += w * g[c]; after[c] -= w * o[7 + c]; }
                 const double rcp = 1.0 / fmax(1.0 - a, 1e-6);
@@ -633,6 +691,21 @@ int orc_blend_backward(int64_t n_visible, const uint32_t* sorted_idx, const doub
         }
     }
     free(fr);
+    }
+    if (parts) {
+        for (int t = 0; t < nt; t++) {
+            const double* pt = parts + (size_t)t * 12 * (size_t)n_visible;
+            for (size_t j = 0; j < n_touched_t[t]; j++) {
+                const size_t r = touched[t][j];
+                for (int k = 0; k < 12; k++) grads[12 * r + k] += pt[12 * r + k];
+            }
+            free(touched[t]);
+        }
+        free(parts);
+        free(seen);
+        free(touched);
+        free(n_touched_t);
+    }
     for (int64_t r = 0; r < n_visible; r++) {
         double* gr = grads + 12 * (size_t)r;
         const double o = rec[14 * (size_t)sorted_idx[r] + 2];
@@ -728,7 +801,14 @@ int orc_preprocess_backward(const orc_appearance* A, const orc_view* v, int64_t 
     double wd[16];
     for (int k = 0; k < 16; k++) wd[k] = v->w2c[k];
     w = wd;
-    if (g_mlp && A->model == 5) memset(g_mlp, 0, sizeof(double) * (size_t)neural_param_count(A));
+    const size_t n_mlp = (g_mlp && A->model == 5) ? (size_t)neural_param_count(A) : 0;
+    if (n_mlp) memset(g_mlp, 0, sizeof(double) * n_mlp);
+    const int nt = g_threads;
+    double* mlp_parts = (nt > 1 && n_mlp) ? (double*)calloc((size_t)nt * n_mlp, sizeof(double)) : 0;
+#pragma omp parallel num_threads(nt) if (nt > 1)
+    {
+    double* my_mlp = mlp_parts ? mlp_parts + (size_t)thread_id() * n_mlp : g_mlp;
+#pragma omp for schedule(dynamic, 64)
     for (int64_t i = 0; i < n; i++) {
         const uint32_t r = rank_of[i];
         if (r == 0xffffffffu) {
@@ -768,7 +848,7 @@ int orc_preprocess_backward(const orc_appearance* A, const orc_view* v, int64_t 
                 case 2: gd = sv_backward_d(rp, gpre, d, deg, A->res_act, local); break;
                 case 3: gd = lobes_backward_d(rp, gpre, d, deg, A->res_act, 0, local); break;
                 case 4: gd = lobes_backward_d(rp, gpre, d, deg, A->res_act, 1, local); break;
-                case 5: gd = neural_backward_d(A, rp, base + 3 * i, gpre, d, deg, mlp, local, g_mlp, g_base + 3 * i); break;
+                case 5: gd = neural_backward_d(A, rp, base + 3 * i, gpre, d, deg, mlp, local, my_mlp, g_base + 3 * i); break;
                 default: break;
             }
             const int active = residual_active(A, deg);
@@ -871,6 +951,12 @@ int orc_preprocess_backward(const orc_appearance* A, const orc_view* v, int64_t 
             g_rots[4 * i + 3] = t * (qr * g_rz + qx * g_xz + qy * g_yz - 2.0 * qz * g_zz - qz * h);
         }
     }
+    }
+    if (mlp_parts) {
+        for (int t = 0; t < nt; t++)
+            for (size_t k = 0; k < n_mlp; k++) g_mlp[k] += mlp_parts[(size_t)t * n_mlp + k];
+        free(mlp_parts);
+    }
     return 0;
 }
 
@@ -884,6 +970,7 @@ void orc_adam(int64_t n, float* param, const float* grad, float* m, float* v, in
     float lr[7];
     for (int k = 0; k < n_lr; k++) lr[k] = (float)(lrs[k] * bc1);
     const float b1 = (float)beta1, b2 = (float)beta2, e = (float)eps, c2 = (float)bc2;
+    #pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
     for (int64_t j = 0; j < n; j++) {
         const float g = grad[j], g2 = g * g;
         const float mm = fmaf(b1, m[j] - g, g);

@@ -60,6 +60,8 @@ def load(double: bool = False) -> ctypes.CDLL:
     lib.orc_blend.argtypes = [i64, P, P, P, P, P, P, P, P, ctypes.c_int, ctypes.c_int]
     lib.orc_blend_backward.argtypes = [i64, P, P, P, P, P, P, P, P]
     lib.orc_pruning_scores.argtypes = [i64, P, P, P, P, P, P, P]
+    lib.orc_set_threads.argtypes = [ctypes.c_int]
+    lib.orc_threads.restype = ctypes.c_int
     lib.orc_preprocess_backward.argtypes = [P, P, i64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, ctypes.c_int]
     lib.orc_adam.argtypes = [i64, P, P, P, P, i64, P, ctypes.c_int, i64, ctypes.c_double, ctypes.c_double, ctypes.c_double]
     lib.orc_adam.restype = None
@@ -226,3 +228,11 @@ def appearance(app: Appearance, means, cam_pos, base, residual, degree: int, ups
         lib.orc_appearance_grad(ctypes.byref(app), n, _p(means), _p(cam), _p(base), _p(residual), int(degree), _p(up), _p(gb), _p(gr), _p(gm))
         out.update(grad_base=gb, grad_residual=gr, grad_means=gm)
     return out
+
+
+def set_threads(n: int) -> None:
+    """Threads of the oracle's per-primitive and per-pixel loops (both builds); 1, the default, keeps every loop in
+    order. Used by the CPU-baseline timing; the parity tests run with one thread."""
+    for double in (False, True):
+        load(double).orc_set_threads(int(n))
+
