@@ -93,8 +93,8 @@ fgs::PrimBuffers carve_prim(void* ws, uint64_t n, size_t* bytes) {
     size_t tb = fgs::depth_sort_temp_bytes(static_cast<uint32_t>(n));
     const size_t sb = fgs::exclusive_scan_temp_bytes(static_cast<uint32_t>(n));
     if (sb > tb) tb = sb;
-    B.cub_temp = c.take<char>(tb);
-    B.cub_temp_bytes = tb;
+    B.sort_temp = c.take<char>(tb);
+    B.sort_temp_bytes = tb;
     if (bytes) *bytes = c.off;
     return B;
 }
@@ -429,7 +429,7 @@ int fgs_forward_preprocess(fgs_rasterizer* r, const fgs_primitives* prims, const
         frame->depth_selector = B.sorted_idx == B.idx_b ? 1 : 0;
         ProfScope p_("reorder_scan", s);
         FGS_CUDA(fgs::launch_reorder(B, static_cast<uint32_t>(n_visible), s), "reorder");
-        FGS_CUDA(fgs::exclusive_scan_u32(B.inst_off, static_cast<uint32_t>(n_visible), B.cub_temp, B.cub_temp_bytes, s), "offset scan");
+        FGS_CUDA(fgs::exclusive_scan_u32(B.inst_off, static_cast<uint32_t>(n_visible), B.sort_temp, B.sort_temp_bytes, s), "offset scan");
     }
     return FGS_OK;
 }
@@ -878,7 +878,7 @@ int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const 
     if (nv > 0) {
         FGS_CUDA(fgs::depth_sort(B, static_cast<uint32_t>(nv), s), "depth sort");
         FGS_CUDA(fgs::launch_reorder(B, static_cast<uint32_t>(nv), s), "reorder");
-        FGS_CUDA(fgs::exclusive_scan_u32(B.inst_off, static_cast<uint32_t>(nv), B.cub_temp, B.cub_temp_bytes, s), "offset scan");
+        FGS_CUDA(fgs::exclusive_scan_u32(B.inst_off, static_cast<uint32_t>(nv), B.sort_temp, B.sort_temp_bytes, s), "offset scan");
         FGS_CUDA(fgs::launch_emit(B.sorted_rec, B.inst_off, I.keys_a, I.vals_a, static_cast<uint32_t>(nv), g.gw, g.wide, s), "emit");
     }
     const void* keys = nullptr;

@@ -55,7 +55,7 @@ struct PrimBuffers {
     uint32_t* vis_idx;     // [V] visible primitives in primitive order (the compaction's list, kept past the depth sort)
     Record* sorted_rec;    // [V] records in depth order
     uint32_t* inst_off;    // [V] exclusive instance offsets in depth order
-    void* cub_temp; size_t cub_temp_bytes;
+    void* sort_temp; size_t sort_temp_bytes;
     const uint32_t* sorted_idx;  // set after the depth sort (points at idx_a or idx_b)
 };
 

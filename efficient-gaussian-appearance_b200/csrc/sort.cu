@@ -297,7 +297,7 @@ size_t depth_sort_temp_bytes(uint32_t n) { return sort_temp_bytes(n); }
 cudaError_t depth_sort(PrimBuffers& B, uint32_t n_visible, cudaStream_t s) {
     uint32_t* kout = nullptr;
     uint32_t* vout = nullptr;
-    const cudaError_t e = radix_sort_pairs<uint32_t>(B.keys_a, B.keys_b, B.idx_a, B.idx_b, n_visible, 32, B.cub_temp, B.cub_temp_bytes, &kout, &vout, s);
+    const cudaError_t e = radix_sort_pairs<uint32_t>(B.keys_a, B.keys_b, B.idx_a, B.idx_b, n_visible, 32, B.sort_temp, B.sort_temp_bytes, &kout, &vout, s);
     B.sorted_idx = vout;
     return e;
 }
