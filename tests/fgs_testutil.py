@@ -103,3 +103,53 @@ def rel_err(a, b) -> float:
 
 def oracle_records_in_rank_order(o: dict) -> np.ndarray:
     return o['records'][o['sorted_idx']]
+
+
+def compare_forward(g, o, exact_image):
+    """Every forward stage of a GPU run (gpu_forward_stages) against an oracle run: integer stages, geometry fields
+    and contributor counts bit for bit; colors, image and transmittance bit for bit when `exact_image`, else within
+    1e-5 relative (colors), 1e-4 max abs (image) and 1e-6 (transmittance)."""
+    assert g['n_visible'] == o['n_visible']
+    assert g['n_instances'] == o['n_instances']
+    np.testing.assert_array_equal(g['n_touched'], o['n_touched'])
+    vis = o['n_touched'] > 0
+    np.testing.assert_array_equal(g['depth_key'][vis], o['depth_key'][vis])
+    np.testing.assert_array_equal(g['sorted_idx'], o['sorted_idx'])
+    np.testing.assert_array_equal(g['instance_offsets'], o['instance_offsets'])
+    np.testing.assert_array_equal(g['tile_keys'], o['tile_keys'])
+    np.testing.assert_array_equal(g['ranks'], o['ranks'])
+    np.testing.assert_array_equal(g['ranges'], o['ranges'])
+    # bucket offsets: inclusive scan of ceil(tile list length / 32) (kernels_forward.cuh:14-24, forward.cu:204-219)
+    lengths = o['ranges'][:, 1].astype(np.int64) - o['ranges'][:, 0].astype(np.int64)
+    np.testing.assert_array_equal(g['bucket_off'], np.cumsum((lengths + 31) // 32).astype(np.uint32))
+    rec_o = oracle_records_in_rank_order(o)
+    rec_g = g['records']
+    # geometry fields bit-exact: mean2d, opacity, power threshold, conic, bounds
+    for gi, oi in ((0, 0), (1, 1), (2, 2), (3, 3), (4, 4), (5, 5), (6, 6)):
+        np.testing.assert_array_equal(rec_g[:, gi], rec_o[:, oi].astype(np.float32))
+    bx = rec_g[:, 7].view(np.uint32)
+    by = rec_g[:, 11].view(np.uint32)
+    np.testing.assert_array_equal(bx & 0xffff, rec_o[:, 10].astype(np.uint32))
+    np.testing.assert_array_equal(bx >> 16, rec_o[:, 11].astype(np.uint32))
+    np.testing.assert_array_equal(by & 0xffff, rec_o[:, 12].astype(np.uint32))
+    np.testing.assert_array_equal(by >> 16, rec_o[:, 13].astype(np.uint32))
+    np.testing.assert_array_equal(g['n_contrib'], o['n_contrib'])
+    colors_g = rec_g[:, 8:11]
+    colors_o = rec_o[:, 7:10].astype(np.float32)
+    if exact_image:
+        np.testing.assert_array_equal(colors_g, colors_o)
+        np.testing.assert_array_equal(g['image'], o['image'])
+        np.testing.assert_array_equal(g['final_T'], o['final_T'])
+    else:
+        assert np.abs(colors_g - colors_o).max() <= 1e-5 * max(1.0, np.abs(colors_o).max())
+        assert np.abs(g['image'] - o['image']).max() <= 1e-4
+        assert np.abs(g['final_T'] - o['final_T']).max() <= 1e-6
+
+
+def gpu_colors_by_primitive(g: dict, n: int) -> np.ndarray:
+    """The blended colors of a GPU run (record fields 8-10, depth-rank order) scattered back to primitive order
+    [n, 3]; zero for culled primitives. Fed to the oracle as precomputed colors, they make its blend see the GPU's
+    inputs exactly."""
+    out = np.zeros((n, 3), np.float32)
+    out[g['sorted_idx']] = g['records'][:, 8:11]
+    return out

@@ -9,7 +9,7 @@ import torch
 
 import synthetic as S
 from oracle import oracle as O
-from fgs_testutil import ACT, scene, to_dev, settings_for, gpu_forward_stages, rel_err, oracle_records_in_rank_order
+from fgs_testutil import ACT, scene, to_dev, settings_for, gpu_forward_stages, rel_err, compare_forward
 
 pytestmark = pytest.mark.gpu
 
@@ -32,44 +32,6 @@ def _configure(F, model, degree, base, res, col):
         F.initialize_appearance('sh', 3, 'none', 'none', 'relu', True)
 
 
-def _compare_forward(g, o, exact_image):
-    assert g['n_visible'] == o['n_visible']
-    assert g['n_instances'] == o['n_instances']
-    np.testing.assert_array_equal(g['n_touched'], o['n_touched'])
-    vis = o['n_touched'] > 0
-    np.testing.assert_array_equal(g['depth_key'][vis], o['depth_key'][vis])
-    np.testing.assert_array_equal(g['sorted_idx'], o['sorted_idx'])
-    np.testing.assert_array_equal(g['instance_offsets'], o['instance_offsets'])
-    np.testing.assert_array_equal(g['tile_keys'], o['tile_keys'])
-    np.testing.assert_array_equal(g['ranks'], o['ranks'])
-    np.testing.assert_array_equal(g['ranges'], o['ranges'])
-    # bucket offsets: inclusive scan of ceil(tile list length / 32) (kernels_forward.cuh:14-24, forward.cu:204-219)
-    lengths = o['ranges'][:, 1].astype(np.int64) - o['ranges'][:, 0].astype(np.int64)
-    np.testing.assert_array_equal(g['bucket_off'], np.cumsum((lengths + 31) // 32).astype(np.uint32))
-    rec_o = oracle_records_in_rank_order(o)
-    rec_g = g['records']
-    # geometry fields bit-exact: mean2d, opacity, power threshold, conic, bounds
-    for gi, oi in ((0, 0), (1, 1), (2, 2), (3, 3), (4, 4), (5, 5), (6, 6)):
-        np.testing.assert_array_equal(rec_g[:, gi], rec_o[:, oi].astype(np.float32))
-    bx = rec_g[:, 7].view(np.uint32)
-    by = rec_g[:, 11].view(np.uint32)
-    np.testing.assert_array_equal(bx & 0xffff, rec_o[:, 10].astype(np.uint32))
-    np.testing.assert_array_equal(bx >> 16, rec_o[:, 11].astype(np.uint32))
-    np.testing.assert_array_equal(by & 0xffff, rec_o[:, 12].astype(np.uint32))
-    np.testing.assert_array_equal(by >> 16, rec_o[:, 13].astype(np.uint32))
-    np.testing.assert_array_equal(g['n_contrib'], o['n_contrib'])
-    colors_g = rec_g[:, 8:11]
-    colors_o = rec_o[:, 7:10].astype(np.float32)
-    if exact_image:
-        np.testing.assert_array_equal(colors_g, colors_o)
-        np.testing.assert_array_equal(g['image'], o['image'])
-        np.testing.assert_array_equal(g['final_T'], o['final_T'])
-    else:
-        assert np.abs(colors_g - colors_o).max() <= 1e-5 * max(1.0, np.abs(colors_o).max())
-        assert np.abs(g['image'] - o['image']).max() <= 1e-4
-        assert np.abs(g['final_T'] - o['final_T']).max() <= 1e-6
-
-
 @pytest.mark.parametrize('case', CASES, ids=[f'{c[0]}{c[1]}-{c[2]}-{c[3]}-{c[4]}' for c in CASES])
 def test_forward_backward_parity(cuda, case):
     import FasterGSVDACudaBackend as F
@@ -86,7 +48,7 @@ def test_forward_backward_parity(cuda, case):
     grad_image = torch.randn(3, H, W, generator=torch.Generator().manual_seed(2)) * 0.01
     o = O.run(a, O.make_view(cam, degree), prims, grad_image=grad_image)
     assert o['n_visible'] > 1000 and o['n_instances'] > o['n_visible']
-    _compare_forward(g, o, exact)
+    compare_forward(g, o, exact)
 
     # backward through autograd
     leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
@@ -118,7 +80,7 @@ def test_variants_proper_aa_render_base_densification(cuda):
         a = O.make_appearance('sh', 3, 0, 0, 1, True)
         grad_image = torch.randn(3, H, W, generator=torch.Generator().manual_seed(2)) * 0.01
         o = O.run(a, O.make_view(cam, 3, proper_aa=proper_aa, render_base=render_base), prims, grad_image=grad_image, densification_rows=3)
-        _compare_forward(g, o, exact_image=True)
+        compare_forward(g, o, exact_image=True)
         leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
         dens = torch.zeros(3, n, device=cuda)
         img = F.diff_rasterize(leaves['means'], leaves['scales'], leaves['rotations'], leaves['opacities'], dens, settings,
