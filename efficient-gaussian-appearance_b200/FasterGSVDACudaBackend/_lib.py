@@ -37,7 +37,7 @@ class Frame(ctypes.Structure):
     _fields_ = [('n_primitives', c_int64), ('n_visible', c_int64), ('n_instances', c_int64), ('n_buckets', c_int64),
                 ('width', c_int32), ('height', c_int32), ('grid_w', c_int32), ('grid_h', c_int32), ('end_bit', c_int32),
                 ('wide_keys', c_int32), ('depth_selector', c_int32), ('tile_selector', c_int32), ('precomputed', c_int32),
-                ('reserved', c_int32)]
+                ('mlp_activations', c_int32)]
 
 
 class Gradients(ctypes.Structure):

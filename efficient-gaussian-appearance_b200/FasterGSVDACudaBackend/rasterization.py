@@ -207,14 +207,17 @@ def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
 class ForwardState:
     """Workspaces and frame record of one forward pass (kept by autograd for the backward)."""
 
-    def __init__(self, rasterizer: Rasterizer, prims: _lib.Primitives, settings: RasterizerSettings, device: torch.device) -> None:
+    def __init__(self, rasterizer: Rasterizer, prims: _lib.Primitives, settings: RasterizerSettings, device: torch.device,
+                 training: bool = True) -> None:
+        """`training`: a backward follows, so the primitive workspace also holds the tensor-core MLP's activations
+        (Neural appearance), which the backward then reads instead of recomputing them."""
         self.rasterizer = rasterizer
         self.settings = settings
         self.device = device
         self.c_settings, self.keep = _c_settings(settings, device)
         self.frame = _lib.Frame()
         n = prims.n_primitives
-        self.prim_ws = _workspace(size_out(lib.fgs_primitive_workspace_bytes, rasterizer.handle, n), device)
+        self.prim_ws = _workspace(size_out(lib.fgs_primitive_workspace_bytes, rasterizer.handle if training else None, n), device)
         self.tile_ws = _workspace(size_out(lib.fgs_tile_workspace_bytes, int(settings.width), int(settings.height)), device)
         self.inst_ws = None
         self.bucket_ws = None
@@ -368,7 +371,7 @@ def rasterize(
                           precomputed_colors.detach() if precomputed_colors is not None else None,
                           base_colors.detach() if base_colors is not None else None,
                           residual_params.detach() if residual_params is not None else None, mlp)
-    state = ForwardState(_rasterizer, prims, rasterizer_settings, device)
+    state = ForwardState(_rasterizer, prims, rasterizer_settings, device, training=False)
     state.preprocess(prims)
     h, w = int(rasterizer_settings.height), int(rasterizer_settings.width)
     image = torch.empty((3, h, w) if to_chw else (h, w, 3), dtype=torch.float32, device=device)
@@ -401,7 +404,7 @@ def update_pruning_scores(
                           precomputed_colors.detach() if precomputed_colors is not None else None,
                           base_colors.detach() if base_colors is not None else None,
                           residual_params.detach() if residual_params is not None else None, mlp)
-    state = ForwardState(_rasterizer, prims, rasterizer_settings, device)
+    state = ForwardState(_rasterizer, prims, rasterizer_settings, device, training=False)
     state.preprocess(prims)
     image = torch.empty((3, int(rasterizer_settings.height), int(rasterizer_settings.width)), dtype=torch.float32, device=device)
     state.render_train(image)

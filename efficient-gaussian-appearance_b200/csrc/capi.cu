@@ -70,7 +70,7 @@ Grid grid_of(int width, int height) {
     return g;
 }
 
-fgs::PrimBuffers carve_prim(void* ws, uint64_t n, size_t* bytes) {
+fgs::PrimBuffers carve_prim(void* ws, uint64_t n, size_t* bytes, size_t act_bytes = 0) {
     Carver c(ws);
     const uint64_t chunks = (n + fgs::kChunk - 1) / fgs::kChunk;
     fgs::PrimBuffers B{};
@@ -95,8 +95,17 @@ fgs::PrimBuffers carve_prim(void* ws, uint64_t n, size_t* bytes) {
     if (sb > tb) tb = sb;
     B.sort_temp = c.take<char>(tb);
     B.sort_temp_bytes = tb;
+    // the tensor-core MLP's activation store (training workspaces) comes last, so every other buffer keeps its offset
+    B.mlp_act = act_bytes ? c.take<unsigned char>(act_bytes) : nullptr;
+    B.mlp_act_bytes = act_bytes;
     if (bytes) *bytes = c.off;
     return B;
+}
+
+// bytes of the activation store for n primitives: nonzero only for a Neural MLP that runs on the tcgen05 kernels
+size_t mlp_act_bytes(const fgs_rasterizer* r, uint64_t n) {
+    if (!r || !r->appearance_set || !r->mlp_set || r->cfg.model != fgs::kNeural) return 0;
+    return fgs::tc_activation_bytes(r->cfg, n);
 }
 
 fgs::TileBuffers carve_tile(void* ws, const Grid& g, size_t* bytes) {
@@ -190,6 +199,7 @@ fgs::Params make_params(const fgs_primitives* p) {
     P.means = p->means; P.scales = p->scales; P.rotations = p->rotations; P.opacities = p->opacities;
     P.precomputed = p->precomputed_colors; P.base = p->base_colors; P.residual = p->residual_params; P.mlp = p->mlp_weights;
     P.n = static_cast<uint32_t>(p->n_primitives);
+    P.mlp_act = nullptr;
     return P;
 }
 
@@ -330,9 +340,9 @@ int fgs_residual_stride(const fgs_rasterizer* r, int64_t* out) {
     return FGS_OK;
 }
 
-int fgs_primitive_workspace_bytes(const fgs_rasterizer*, int64_t n, size_t* out) {
+int fgs_primitive_workspace_bytes(const fgs_rasterizer* r, int64_t n, size_t* out) {
     if (!out || n < 0) return fail(FGS_ERR_INVALID_ARGUMENT, "bad argument");
-    carve_prim(nullptr, static_cast<uint64_t>(n), out);
+    carve_prim(nullptr, static_cast<uint64_t>(n), out, mlp_act_bytes(r, static_cast<uint64_t>(n)));
     return FGS_OK;
 }
 
@@ -371,12 +381,18 @@ int fgs_forward_preprocess(fgs_rasterizer* r, const fgs_primitives* prims, const
     rc = check_prims(r, prims, &precomputed);
     if (rc) return rc;
     const uint64_t n = static_cast<uint64_t>(prims->n_primitives);
-    size_t need = 0;
-    fgs::PrimBuffers B = carve_prim(prim_ws, n, &need);
+    // a workspace that also covers the activation store (the size fgs_primitive_workspace_bytes gives for this
+    // rasterizer) keeps the tensor-core MLP's activations for fgs_backward
+    const size_t act_bytes = precomputed ? 0 : mlp_act_bytes(r, n);
+    size_t need = 0, need_act = 0;
+    carve_prim(nullptr, n, &need_act, act_bytes);
+    const bool keep_act = act_bytes > 0 && prim_ws && prim_ws_bytes >= need_act;
+    fgs::PrimBuffers B = carve_prim(prim_ws, n, &need, keep_act ? act_bytes : 0);
     if (!prim_ws || prim_ws_bytes < need) return fail(FGS_ERR_WORKSPACE, "primitive workspace too small");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const fgs::View v = make_view(settings);
-    const fgs::Params P = make_params(prims);
+    fgs::Params P = make_params(prims);
+    P.mlp_act = keep_act ? B.mlp_act : nullptr;
     const Grid g = grid_of(settings->width, settings->height);
     std::memset(frame, 0, sizeof(fgs_frame));
     frame->n_primitives = static_cast<int64_t>(n);
@@ -387,6 +403,7 @@ int fgs_forward_preprocess(fgs_rasterizer* r, const fgs_primitives* prims, const
     frame->end_bit = g.end_bit;
     frame->wide_keys = g.wide ? 1 : 0;
     frame->precomputed = precomputed ? 1 : 0;
+    frame->mlp_activations = keep_act ? 1 : 0;
     if (n == 0) return FGS_OK;
     {
         ProfScope p_("preprocess", s);
@@ -537,12 +554,14 @@ int fgs_backward(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_setti
     size_t need = 0;
     GradBuffers gb = carve_grad(grad_ws, nv, n_mlp, &need);
     if (!grad_ws || grad_ws_bytes < need) return fail(FGS_ERR_WORKSPACE, "gradient workspace too small");
-    fgs::PrimBuffers B = carve_prim(prim_ws, n, nullptr);
+    const size_t act_bytes = neural && frame->mlp_activations ? mlp_act_bytes(r, n) : 0;
+    fgs::PrimBuffers B = carve_prim(prim_ws, n, nullptr, act_bytes);
     const fgs::TileBuffers T = carve_tile(tile_ws, g, nullptr);
     InstBuffers I = carve_inst(inst_ws, static_cast<uint64_t>(frame->n_instances), g, nullptr);
     (void)bucket_ws;
     const fgs::View v = make_view(settings);
-    const fgs::Params P = make_params(prims);
+    fgs::Params P = make_params(prims);
+    P.mlp_act = B.mlp_act;  // the forward's activation store, or null (recomputed)
     if (nv > 0) {
         FGS_CUDA(cudaMemsetAsync(gb.rec, 0, nv * sizeof(fgs::GradRecord), s), "gradient clear");
         fgs::BlendArgs a;

@@ -71,6 +71,9 @@ cudaError_t launch_l1_dssim(const float* image, const float* target, int C, int 
 // neural_tc.cu
 bool tc_mlp_supported(const AppearanceConfig& A);  // 64-wide MLP with hidden layers: the tcgen05 kernels apply
 size_t tc_mlp_smem_bytes(const AppearanceConfig& A);  // their largest dynamic shared memory (0 when unsupported)
+// bytes of the activation store the tcgen05 colour pass fills for the backward (Params::mlp_act) for up to n_rows
+// visible rows; 0 when the tcgen05 kernels do not apply
+size_t tc_activation_bytes(const AppearanceConfig& A, uint64_t n_rows);
 cudaError_t launch_tc_color(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis_idx, uint32_t n_visible,
                             Record* rec, cudaStream_t s);
 cudaError_t launch_tc_backward(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis_idx, uint32_t n_visible,

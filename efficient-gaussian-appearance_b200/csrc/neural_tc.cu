@@ -142,6 +142,10 @@ constexpr int kTcThreads = 256;
 constexpr int kTcWidth = 64;
 constexpr int kTcMaxLayers = 8;
 constexpr int kPrefetchFeatures = 32;  // rows of up to 32 latent floats are prefetched into registers (16 per thread)
+// Activation store of the colour pass (training): per 128-row tile, every hidden activation as the 16 KB K-major fp16
+// block the backward's shared slot holds, then the fp16-rounded raw outputs (4 halves per row, the last one zero).
+constexpr uint32_t kTcActLayerBytes = kTcRows * kTcWidth * 2;
+constexpr uint32_t kTcActOutBytes = kTcRows * 8;
 
 // one MLP configuration laid out for the tensor-core kernels
 struct TcPlan {
@@ -153,6 +157,7 @@ struct TcPlan {
     int h_slots;                                 // activation buffers: 1 (forward, rewritten in place) or layers - 1
     uint32_t wg_col[kTcMaxLayers];               // TMEM column of each layer's weight-gradient accumulator
     uint32_t tmem_cols;                          // allocated TMEM columns (power of two)
+    uint32_t act_tile_bytes;                     // activation store bytes per tile
 };
 
 __device__ __forceinline__ uint32_t h_slot(const TcPlan& p, int j) { return p.h_smem + static_cast<uint32_t>(j % p.h_slots) * (kTcRows * kTcWidth * 2); }
@@ -173,6 +178,14 @@ __device__ inline float2 unpack2(uint32_t w) {
     const __half2 h = *reinterpret_cast<const __half2*>(&w);
     return __half22float2(h);
 }
+// 16-byte global -> shared copies that complete in the background without registers. cp_async_wait makes a thread's
+// copies visible to that thread; the proxy fence and barrier of sync_tile then publish them to the tensor cores like
+// ordinary shared stores.
+__device__ inline void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ inline void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ inline void cp_async_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // fp32 master weights -> fp16 K-major copies in shared memory
 __device__ inline void stage_weights_tc(const TcPlan& p, const float* __restrict__ w, unsigned char* smem) {
@@ -223,6 +236,7 @@ struct RowData {
     float4 f[kPrefetchFeatures / 8];  // this thread's half of the latent features (fast path)
     float4 q2, g1;                    // colour of the record and its blend gradient sums (backward)
     f3 base;                          // base colour parameters
+    uint2 y;                          // stored fp16 raw outputs (backward with an activation store)
 };
 
 // The prefetch of a row runs in three stages placed in different phases of the current tile, because each stage's
@@ -323,8 +337,9 @@ __device__ inline void issue_forward(const TcPlan& p, uint32_t sbase, uint32_t t
     for (uint32_t ks = 0; ks < K / 16; ks++) tc::mma(tb, tc::desc_advance(a, ks * 256), tc::desc_advance(b, ks * 256), id, ks > 0);
 }
 
-// hidden-layer epilogue, this thread's 32 columns: accumulator -> activation -> fp16 K-major row of the slot
-__device__ inline void hidden_epilogue(uint32_t t_addr, uint32_t row_base, int half, bool relu) {
+// hidden-layer epilogue, this thread's 32 columns: accumulator -> activation -> fp16 K-major row of the slot (and,
+// with g_row, the same 64 bytes at the same offsets of the activation store)
+__device__ inline void hidden_epilogue(uint32_t t_addr, uint32_t row_base, int half, bool relu, unsigned char* g_row) {
     float a[32];
     tc::ld32(t_addr + 32 * half, a);
 #pragma unroll
@@ -333,8 +348,40 @@ __device__ inline void hidden_epilogue(uint32_t t_addr, uint32_t row_base, int h
         if (relu)
 #pragma unroll
             for (int k = 0; k < 8; k++) x[k] = fmaxf(x[k], 0.0f);
-        st_shared_v4(row_base + (4 * half + q) * 128, pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+        const uint4 h = make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+        st_shared_v4(row_base + (4 * half + q) * 128, h.x, h.y, h.z, h.w);
+        if (g_row) *reinterpret_cast<uint4*>(g_row + (4 * half + q) * 128) = h;
     }
+}
+
+// loss-scaled output gradient of a row (fp16, K-major, 16 columns) from the fp16-rounded raw outputs yh
+__device__ inline void write_output_grad(const TcPlan& p, const AppearanceConfig& A, uint32_t sbase, int row, bool valid, f3 gpre,
+                                         const float (&yh)[3]) {
+    float dy[3] = {0.0f, 0.0f, 0.0f};
+    if (valid) {
+        const float gv[3] = {gpre.x, gpre.y, gpre.z};
+        for (int c = 0; c < 3; c++) dy[c] = gv[c] * residual_act_grad_from_y(A.res_act, residual_act(A.res_act, yh[c]));
+    }
+    const uint32_t yrow = sbase + p.y_smem + tc::kmajor_offset(row, 0, 16);
+    st_shared_v4(yrow, pack2(kLossScale * dy[0], kLossScale * dy[1]), pack2(kLossScale * dy[2], 0.0f), 0u, 0u);
+    st_shared_v4(yrow + 128, 0u, 0u, 0u, 0u);
+}
+
+// the activation store of tile `tl`
+__device__ inline const unsigned char* act_tile(const TcPlan& p, const unsigned char* act, uint32_t tl) {
+    return act + static_cast<size_t>(tl) * p.act_tile_bytes;
+}
+// stored hidden activation j of tile `tl` into its shared slot (this thread's half of its row), asynchronously
+__device__ inline void fetch_activation(const TcPlan& p, uint32_t sbase, const unsigned char* act, uint32_t tl, int j, int row, int half) {
+    const uint32_t off = tc::kmajor_offset(row, 0, kTcWidth);
+    const unsigned char* src = act_tile(p, act, tl) + static_cast<size_t>(j) * kTcActLayerBytes + off;
+    const uint32_t dst = sbase + h_slot(p, j) + off;
+#pragma unroll
+    for (int q = 0; q < 4; q++) cp_async16(dst + (4 * half + q) * 128, src + (4 * half + q) * 128);
+}
+// stored raw outputs of row `row` of tile `tl`
+__device__ inline uint2 load_outputs(const TcPlan& p, const unsigned char* act, uint32_t tl, int row) {
+    return *reinterpret_cast<const uint2*>(act_tile(p, act, tl) + static_cast<size_t>(p.layers - 1) * kTcActLayerBytes + row * 8);
 }
 
 // data-gradient epilogue of a hidden layer, this thread's 32 columns: dL/d(activation), masked by the ReLU of the
@@ -403,6 +450,7 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
     const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows;
     const bool fast = fast_features(P, A);
     const uint32_t x_row = sbase + plan.x_smem + tc::kmajor_offset(row, 0, plan.kin);
+    const uint32_t h_row = tc::kmajor_offset(row, 0, kTcWidth);
     RowData cur, nxt;
     if (blockIdx.x < n_tiles) {
         load_row_index(vis, n_rows, blockIdx.x * kTcRows + row, cur);
@@ -411,6 +459,7 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
         const uint32_t next = tile + gridDim.x;
         const bool more = next < n_tiles;
+        unsigned char* const act = P.mlp_act ? P.mlp_act + static_cast<size_t>(tile) * plan.act_tile_bytes : nullptr;
         if (more) load_row_index(vis, n_rows, next * kTcRows + row, nxt);
         write_input_row(P, A, v, deg, cur, fast, half, x_row, plan.kin, nullptr, row);
         sync_tile();
@@ -424,10 +473,14 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
             alive = wait_all(&bar, phase);
             if (!alive) break;
             if (l < plan.layers - 1) {
-                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(row, 0, kTcWidth), half, A.hidden_act == 1);
+                hidden_epilogue(t_row, sbase + h_slot(plan, l) + h_row, half, A.hidden_act == 1,
+                                act ? act + static_cast<size_t>(l) * kTcActLayerBytes + h_row : nullptr);
             } else if (half == 0) {  // whole warps: the TMEM load is warp-collective
                 float y[16];
                 tc::ld16(t_row, y);
+                if (act)
+                    *reinterpret_cast<uint2*>(act + static_cast<size_t>(l) * kTcActLayerBytes + row * 8) =
+                        make_uint2(pack2(y[0], y[1]), pack2(y[2], 0.0f));
                 if (cur.valid) {
                     const f3 res = residual_act3(A.res_act, mk3(__half2float(__float2half_rn(y[0])), __half2float(__float2half_rn(y[1])),
                                                                  __half2float(__float2half_rn(y[2]))));
@@ -637,16 +690,28 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
     const bool fast = fast_features(P, A) && (reinterpret_cast<uintptr_t>(O.residual) & 15u) == 0;  // 16-byte gradient stores
     float* trig = fast && plan.trig_smem ? reinterpret_cast<float*>(smem + plan.trig_smem) : nullptr;
     const uint32_t x_row = sbase + plan.x_smem + tc::kmajor_offset(row, 0, plan.kin);
+    // With an activation store (the colour pass's hidden activations and raw outputs) the forward is not recomputed:
+    // a tile's activations are copied into their slots while the previous tile finishes (slot j as soon as the MMAs
+    // of layer j, its last reader, completed) and its raw outputs come with the row prefetch.
+    const unsigned char* const act = P.mlp_act;
     RowData cur, nxt;
     if (blockIdx.x < n_tiles) {
         load_row_index(vis, n_rows, blockIdx.x * kTcRows + row, cur);
+        if (act) {
+            cur.y = load_outputs(plan, act, blockIdx.x, row);
+            for (int j = 0; j < last; j++) fetch_activation(plan, sbase, act, blockIdx.x, j, row, half);
+            cp_async_commit();
+        }
         load_row_params(P, A, fast, half, rank_of, cur);
         load_row_rank(sorted_rec, grads, cur);
     }
     for (uint32_t tile = blockIdx.x; tile < n_tiles && alive; tile += gridDim.x) {
         const uint32_t next = tile + gridDim.x;
         const bool more = next < n_tiles;
-        if (more) load_row_index(vis, n_rows, next * kTcRows + row, nxt);
+        if (more) {
+            load_row_index(vis, n_rows, next * kTcRows + row, nxt);
+            if (act) nxt.y = load_outputs(plan, act, next, row);
+        }
         const bool valid = cur.valid;
         const uint32_t i = cur.i;
         f3 gpre = mk3(0.0f, 0.0f, 0.0f);
@@ -654,9 +719,17 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
             gpre = mk3(cur.g1.y, cur.g1.z, cur.g1.w) * mk3(color_act_grad_from_y(A.color_act, cur.q2.x), color_act_grad_from_y(A.color_act, cur.q2.y),
                                                            color_act_grad_from_y(A.color_act, cur.q2.z));
         write_input_row(P, A, v, deg, cur, fast, half, x_row, plan.kin, trig, row);
+        if (act) {
+            if (half == 0) {
+                const float2 y01 = unpack2(cur.y.x);
+                const float yh[3] = {y01.x, y01.y, unpack2(cur.y.y).x};
+                write_output_grad(plan, A, sbase, row, valid, gpre, yh);
+            }
+            cp_async_wait();  // this tile's activation slots
+        }
         sync_tile();
-        // recomputed forward; the last layer's outputs become the scaled output gradient
-        for (int l = 0; l < plan.layers && alive; l++) {
+        // recomputed forward (no activation store); the last layer's outputs become the scaled output gradient
+        for (int l = 0; l < plan.layers && alive && !act; l++) {
             if (t == 0) {
                 issue_forward(plan, sbase, tb, l);
                 tc::commit(&bar);
@@ -666,21 +739,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
             alive = wait_all(&bar, phase);
             if (!alive) break;
             if (l < last) {
-                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(row, 0, kTcWidth), half, relu);
+                hidden_epilogue(t_row, sbase + h_slot(plan, l) + tc::kmajor_offset(row, 0, kTcWidth), half, relu, nullptr);
             } else if (half == 0) {
                 float y[16];
                 tc::ld16(t_row, y);
-                float dy[3] = {0.0f, 0.0f, 0.0f};
-                if (valid) {
-                    const float gv[3] = {gpre.x, gpre.y, gpre.z};
-                    for (int c = 0; c < 3; c++) {
-                        const float yh = __half2float(__float2half_rn(y[c]));
-                        dy[c] = gv[c] * residual_act_grad_from_y(A.res_act, residual_act(A.res_act, yh));
-                    }
-                }
-                const uint32_t yrow = sbase + plan.y_smem + tc::kmajor_offset(row, 0, 16);
-                st_shared_v4(yrow, pack2(kLossScale * dy[0], kLossScale * dy[1]), pack2(kLossScale * dy[2], 0.0f), 0u, 0u);
-                st_shared_v4(yrow + 128, 0u, 0u, 0u, 0u);
+                const float yh[3] = {__half2float(__float2half_rn(y[0])), __half2float(__float2half_rn(y[1])), __half2float(__float2half_rn(y[2]))};
+                write_output_grad(plan, A, sbase, row, valid, gpre, yh);
             }
             sync_tile();
         }
@@ -691,9 +755,21 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
                 tc::commit(&bar);
             }
             __syncwarp();
-            if (l == last && more) load_row_rank(sorted_rec, grads, nxt);
+            if (more) {
+                if (!act) {
+                    if (l == last) load_row_rank(sorted_rec, grads, nxt);
+                } else if (l == last) {
+                    load_row_params(P, A, fast, half, rank_of, nxt);
+                } else if (l == last - 1) {
+                    load_row_rank(sorted_rec, grads, nxt);
+                }
+            }
             alive = wait_all(&bar, phase);
             if (!alive) break;
+            if (act && more && l < last) {  // slot l is free: the next tile's activation l
+                fetch_activation(plan, sbase, act, next, l, row, half);
+                cp_async_commit();
+            }
             if (l > 0) {
                 hidden_grad_epilogue(t_row, sbase + h_slot(plan, l - 1) + tc::kmajor_offset(row, 0, kTcWidth), half, relu);
                 sync_tile();
@@ -745,6 +821,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
         tc::mbar_wait(&bar, phase ^ 1u);  // the timed-out MMAs must not be in flight when the columns are freed
         if (t == 0) atomicExch(&g_tc_timeout, 1);
     }
+    cp_async_wait();  // no activation copy outlives the CTA (only a timeout leaves one in flight)
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -757,6 +834,7 @@ bool make_plan(const AppearanceConfig& A, bool backward, TcPlan& p) {
     p.layers = A.n_hidden + 1;
     p.kin = A.n_input_pad;
     p.backward = backward ? 1 : 0;
+    p.act_tile_bytes = static_cast<uint32_t>(p.layers - 1) * kTcActLayerBytes + kTcActOutBytes;
     if (p.kin % 16 != 0 || p.kin > 256) return false;
     uint32_t off = 0, w = 0;
     for (int l = 0; l < p.layers; l++) {
@@ -834,6 +912,12 @@ cudaError_t tc_grid(K kernel, const TcPlan& p, uint32_t n_tiles, int max_per_sm,
 bool tc_mlp_supported(const AppearanceConfig& A) {
     TcPlan p;
     return make_plan(A, true, p) && make_plan(A, false, p);
+}
+
+size_t tc_activation_bytes(const AppearanceConfig& A, uint64_t n_rows) {
+    TcPlan p;
+    if (!make_plan(A, true, p) || !make_plan(A, false, p)) return 0;
+    return static_cast<size_t>((n_rows + kTcRows - 1) / kTcRows) * p.act_tile_bytes;
 }
 
 size_t tc_mlp_smem_bytes(const AppearanceConfig& A) {

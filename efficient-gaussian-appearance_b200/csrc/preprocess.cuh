@@ -37,6 +37,8 @@ struct Params {
     const float* residual;     // [N, stride] or null
     const float* mlp;          // fp32 master MLP weights or null
     uint32_t n;
+    unsigned char* mlp_act;    // training only: the tensor-core colour pass's hidden activations and raw outputs per
+                               // 128-row tile, kept for the backward (null: not kept, the backward recomputes them)
 };
 
 // buffers of the primitive stage (all sized for N)
@@ -57,6 +59,7 @@ struct PrimBuffers {
     uint32_t* inst_off;    // [V] exclusive instance offsets in depth order
     void* sort_temp; size_t sort_temp_bytes;
     const uint32_t* sorted_idx;  // set after the depth sort (points at idx_a or idx_b)
+    unsigned char* mlp_act; size_t mlp_act_bytes;  // tensor-core MLP activation store (training workspaces), or null
 };
 
 // gradient outputs of the backward preprocess

@@ -93,7 +93,8 @@ typedef struct {
     int32_t depth_selector;  /* which half of the depth double buffer holds the sorted indices */
     int32_t tile_selector;   /* which half of the tile double buffer holds the sorted instances */
     int32_t precomputed;
-    int32_t reserved;
+    int32_t mlp_activations; /* 1: fgs_forward_preprocess kept the tensor-core MLP's activations in the primitive
+                                workspace, and fgs_backward reads them instead of recomputing the MLP forward */
 } fgs_frame;
 
 /* Gradient outputs (rasterization_api.cu:170-183). Arrays are overwritten (or added to when
@@ -154,7 +155,10 @@ int fgs_set_residual_mlp(fgs_rasterizer* r, int n_input_dims, int n_output_dims,
 int fgs_mlp_param_count(const fgs_rasterizer* r, int64_t* out);
 int fgs_residual_stride(const fgs_rasterizer* r, int64_t* out);
 
-/* workspace sizes (the reference's grow-on-demand blobs, rasterization/include/buffer_utils.h:35-152) */
+/* workspace sizes (the reference's grow-on-demand blobs, rasterization/include/buffer_utils.h:35-152).
+ * The primitive workspace size for a rasterizer whose Neural MLP runs on the tensor cores includes a store for the
+ * MLP's hidden activations (about 264 bytes per primitive for two 64-wide hidden layers); with r = NULL the size
+ * excludes it, which suits a forward that no backward follows (inference, pruning scores). */
 int fgs_primitive_workspace_bytes(const fgs_rasterizer* r, int64_t n_primitives, size_t* out);
 int fgs_tile_workspace_bytes(int width, int height, size_t* out);
 int fgs_instance_workspace_bytes(int64_t n_instances, int width, int height, size_t* out);

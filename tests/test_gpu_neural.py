@@ -8,6 +8,8 @@ sum lands on an fp16 rounding boundary in a different order (tensor-core accumul
 1e-3 max-abs and 1e-5 mean-abs. The backward rounds the loss-scaled output and hidden gradients to fp16 as the
 reference does, while the oracle differentiates in double: gradients are compared at 1e-2 relative L2 for the
 MLP weights and features and 1e-3 for the geometry."""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -139,6 +141,50 @@ def test_neural_accumulate_two_views(cuda):
         ref = (g0[k] + g1[k]).cpu().numpy()
         err = rel_err(both[k].cpu().numpy(), ref)
         assert err <= 1e-5, f'{k}: relative error {err:.2e}'
+
+
+@pytest.mark.parametrize('cfg', [(16, 0, 64, 1, False, 'none'), (32, 1, 64, 2, False, 'tanh'), (8, 2, 64, 3, True, 'softplus')],
+                         ids=['1-hidden', '2-hidden', '3-hidden-base'])
+def test_neural_stored_activations_match_recompute(cuda, cfg):
+    """A training forward keeps the tensor-core MLP's activations for the backward (frame.mlp_activations); a forward
+    whose workspace excludes the store (training=False) leaves the backward to recompute them. Both give the same
+    image and the same gradients (up to the order of the fp32 atomics), over enough rows that every CTA fetches
+    several tiles' activations."""
+    import FasterGSVDACudaBackend as F
+    from FasterGSVDACudaBackend import rasterization as R, _lib
+    feat, nf, nn, nh, base_input, res_act = cfg
+    neural, shapes = _setup(F, feat, nf, nn, nh, base_input, res_act)
+    n, W, H = 160000, 256, 192
+    prims = {**S.geometry(n, seed=3), **S.neural_appearance(n, feature_dim=feat, layer_shapes=shapes, seed=4)}
+    dev = to_dev(prims, cuda)
+    cam = S.ring_cameras(4, W, H)[1]
+    gi = (torch.randn(3, H, W, generator=torch.Generator().manual_seed(6)) * 0.01).to(cuda)
+    cp = R._c_primitives(dev['means'], dev['scales'], dev['rotations'], dev['opacities'], None, dev['base_colors'], dev['residual_params'],
+                         dev['mlp_weights'])
+    names = ('means', 'scales', 'rotations', 'opacities', 'precomputed_colors', 'base_colors', 'residual_params', 'mlp_weights')
+
+    def run(training):
+        out = {k: torch.zeros_like(v) for k, v in dev.items()}
+        cg = _lib.Gradients(*[out[k].data_ptr() if k in out else None for k in names])
+        st = R.ForwardState(R._rasterizer, cp, settings_for(F, cam, 3, cuda), cuda, training=training)
+        st.preprocess(cp)
+        image = torch.empty(3, H, W, device=cuda)
+        st.render_train(image)
+        st.backward(cp, image, gi, cg, None)
+        torch.cuda.synchronize()
+        return st.frame, image.cpu().numpy(), out
+
+    f1, img1, g1 = run(True)
+    f0, img0, g0 = run(False)
+    assert f1.mlp_activations == 1 and f0.mlp_activations == 0
+    assert f1.n_visible > 2 * 148 * 128, f1.n_visible
+    np.testing.assert_array_equal(img1, img0)
+    for k in g1:
+        err = rel_err(g1[k].cpu().numpy(), g0[k].cpu().numpy())
+        assert err <= 1e-5, f'{k}: relative error {err:.2e}'
+    flag = ctypes.c_int(-1)
+    _lib.check(_lib.lib.fgs_tc_timeout(ctypes.byref(flag), 0))
+    assert flag.value == 0
 
 
 def test_neural_degree_zero_backward(cuda):
