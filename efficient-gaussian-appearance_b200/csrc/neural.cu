@@ -126,7 +126,7 @@ __device__ inline void assemble_inputs(const Params& P, const AppearanceConfig& 
         } else {
             for (int f = 0; f < nf; f++) {
                 float s, c;
-                det_sincos(octave(val, f), &s, &c);
+                enc_sincos(octave(val, f), &s, &c);
                 row[o++] = __float2half_rn(s);
                 row[o++] = __float2half_rn(c);
             }
@@ -203,7 +203,7 @@ __device__ inline void encode_rows(const Params& P, const AppearanceConfig& A, u
             } else {
                 for (int f = 0; f < nf; f++) {
                     float sn, cs;
-                    det_sincos(octave(val, f), &sn, &cs);
+                    enc_sincos(octave(val, f), &sn, &cs);
                     *reinterpret_cast<__half2*>(row + e * per + 2 * f) = __floats2half2_rn(sn, cs);
                 }
             }
@@ -255,7 +255,7 @@ __device__ inline void feature_grads(const Params& P, const AppearanceConfig& A,
             else
                 for (int f = 0; f < nf; f++) {
                     float sn, cs;
-                    det_sincos(octave(val, f), &sn, &cs);
+                    enc_sincos(octave(val, f), &sn, &cs);
                     gv += static_cast<float>(1 << f) * (cs * g[e * per + 2 * f] - sn * g[e * per + 2 * f + 1]);
                 }
             gv *= inv;
@@ -561,7 +561,7 @@ __global__ void __launch_bounds__(kBwdRows) neural_bwd_kernel(Params P, Appearan
                     else
                         for (int f = 0; f < A.n_freq; f++) {
                             float sn, cs;
-                            det_sincos(octave(val, f), &sn, &cs);
+                            enc_sincos(octave(val, f), &sn, &cs);
                             gv += static_cast<float>(1 << f) * (cs * gx[j * per + 2 * f] - sn * gx[j * per + 2 * f + 1]);
                         }
                     gv *= inv;

@@ -294,10 +294,10 @@ __device__ inline void write_input_row(const Params& P, const AppearanceConfig& 
             if (4 * q >= F / 2) break;
             const float4 x = d.f[q];
             float s0, c0, s1, c1, s2, c2, s3, c3;
-            det_sincos(x.x, &s0, &c0);
-            det_sincos(x.y, &s1, &c1);
-            det_sincos(x.z, &s2, &c2);
-            det_sincos(x.w, &s3, &c3);
+            enc_sincos(x.x, &s0, &c0);
+            enc_sincos(x.y, &s1, &c1);
+            enc_sincos(x.z, &s2, &c2);
+            enc_sincos(x.w, &s3, &c3);
             w.push8(pack2(s0, c0), pack2(s1, c1), pack2(s2, c2), pack2(s3, c3));
             if (trig) {
                 float* tq = trig + (2 * (jb + 4 * q)) * kTcRows + row;
@@ -317,7 +317,7 @@ __device__ inline void write_input_row(const Params& P, const AppearanceConfig& 
         } else {
             for (int f = 0; f < nf; f++) {
                 float sn, cs;
-                det_sincos(octave(val, f), &sn, &cs);
+                enc_sincos(octave(val, f), &sn, &cs);
                 w.push(sn);
                 w.push(cs);
             }
@@ -544,10 +544,10 @@ __device__ inline int input_grad_row(const Params& P, const AppearanceConfig& A,
                 }
             } else {
                 const float4 x = *reinterpret_cast<const float4*>(feat + j);
-                det_sincos(x.x, &sn[0], &cs[0]);
-                det_sincos(x.y, &sn[1], &cs[1]);
-                det_sincos(x.z, &sn[2], &cs[2]);
-                det_sincos(x.w, &sn[3], &cs[3]);
+                enc_sincos(x.x, &sn[0], &cs[0]);
+                enc_sincos(x.y, &sn[1], &cs[1]);
+                enc_sincos(x.z, &sn[2], &cs[2]);
+                enc_sincos(x.w, &sn[3], &cs[3]);
             }
             float gv[4];
 #pragma unroll
@@ -611,7 +611,7 @@ __device__ inline int input_grad_row(const Params& P, const AppearanceConfig& A,
                 } else {
                     const int f = q >> 1;
                     if ((q & 1) == 0) {
-                        det_sincos(octave(val, f), &sn, &cs);
+                        enc_sincos(octave(val, f), &sn, &cs);
                         g_even = g[k];
                     } else {
                         gacc += static_cast<float>(1 << f) * (cs * g_even - sn * g[k]);

@@ -69,8 +69,10 @@ static float det_exp_f(float x) {
     return p * f_from_bits((uint32_t)((int)n + 127) << 23);
 }
 
-/* sine and cosine as the kernels' det_sincos (fgs_common.cuh): Cody-Waite reduction modulo pi/2 in three parts,
- * Taylor series of sin through r^9 and cos through r^10, quadrant rotation; libm beyond |x| = 8192 */
+/* sine and cosine of the Neural encoding in the float build: Cody-Waite reduction modulo pi/2 in three parts,
+ * Taylor series of sin through r^9 and cos through r^10, quadrant rotation; libm beyond |x| = 8192. Within 2.5e-7 of
+ * exact; the kernels use the GPU's hardware approximation (what the reference's fast-math build evaluates), so an
+ * encoded fp16 input can differ from this one by a rounding, which the Neural tolerances cover. */
 static void det_sincos_f(float x, float* sp, float* cp) {
     if (!(fabsf(x) <= 8192.0f)) {
         *sp = sinf(x);

@@ -42,9 +42,9 @@ def test_binning_invariants():
 
 
 def test_det_sincos_error_bound():
-    """The deterministic sine / cosine of the Neural encoding (Cody-Waite reduction + Taylor series, restated from
-    the kernels' det_sincos) against double-precision libm: at most 2.5e-7 absolute error on [-8192, 8192] and at
-    the quadrant boundaries; libm beyond (the kernels use sincosf there)."""
+    """The oracle's deterministic sine / cosine of the Neural encoding (Cody-Waite reduction + Taylor series) against
+    double-precision libm: at most 2.5e-7 absolute error on [-8192, 8192] and at the quadrant boundaries; libm
+    beyond."""
     import ctypes
     lib = O.load(False)
     rng = np.random.default_rng(0)
