@@ -171,9 +171,11 @@ def settings_of(cam, degree: int, dev):
                                 cam.focal_y, cam.center_x, cam.center_y, cam.near_plane, cam.far_plane, False, True, True)
 
 
-# DRAM bytes (read + write) per visible row measured by ncu on the small c4 case (2M Gaussians in Morton order, one
-# view; profiles/neural_tcgen05_small_case.md): MLP backward 415 + geometry backward 190; scaled by the view's visible rows
-TRAFFIC_PER_VISIBLE_ROW = {('c4', 'preprocess_backward'): 415.0 + 190.0}
+# DRAM bytes (read + write) measured by ncu on the small c4 case (2M Gaussians in Morton order, one view: 945,337
+# visible rows, 3,455,846 instances; profiles/neural_tcgen05_small_case.md), as (bytes per visible row, bytes per
+# instance): backward preprocess = MLP backward 706.5 (it reads the colour pass's activation store) + geometry backward
+# 187.2 per visible row; blend backward 168.9 MB over the instances. Scaled by the view's visible rows and instances.
+TRAFFIC_PER_UNIT = {('c4', 'preprocess_backward'): (706.5 + 187.2, 0.0), ('c4', 'blend_backward'): (0.0, 168885.0e3 / 3455846)}
 
 
 def stage_bytes(stage: str, s: dict) -> float:
@@ -408,10 +410,10 @@ def run_b200(args, wl_name: str) -> dict | None:
     peak, peak_kind = _peaks()
     bytes_dom = stage_bytes(dominant, stats)
     achieved = bytes_dom / (per_view[dominant] * 1e-3) / 1e9 if bytes_dom else 0.0
-    per_row = TRAFFIC_PER_VISIBLE_ROW.get((wl_name, dominant))
-    traffic = per_row * stats['V'] if per_row else None
-    traffic_src = ('ncu dram__bytes_read.sum + dram__bytes_write.sum per visible row on the 2M-Gaussian one-view case (Morton order), x visible rows '
-                   'of view 0 (per view launch)') if per_row else None
+    per_unit = TRAFFIC_PER_UNIT.get((wl_name, dominant))
+    traffic = per_unit[0] * stats['V'] + per_unit[1] * stats['I'] if per_unit else None
+    traffic_src = ('ncu dram__bytes_read.sum + dram__bytes_write.sum per visible row and per instance on the 2M-Gaussian one-view case (Morton '
+                   'order), x visible rows and instances of view 0 (per view launch)') if per_unit else None
     fracs = {k: round(stage_bytes(k, stats) / (per_view[k] * 1e-3) / 1e9 / peak, 4) for k in per_view if stage_bytes(k, stats) and per_view[k] > 0}
 
     if world > 1:
