@@ -70,9 +70,10 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
         const uint32_t bs = min(static_cast<uint32_t>(kTilePixels), n - start);
         for (uint32_t g = 0; g < bs; g += 32) {
             const bool ov = g + lane < bs && overlaps_subtile(st[g + lane].bnd, sx0, sy0);
-            uint32_t pending = __ballot_sync(0xffffffffu, ov);
+            // `done` changes only where a fragment is accepted, so the warp votes on it once per group of 32
+            // records and after each accepted fragment
+            uint32_t pending = __all_sync(0xffffffffu, done) ? 0u : __ballot_sync(0xffffffffu, ov);
             while (pending) {
-                if (__all_sync(0xffffffffu, done)) break;
                 const uint32_t k = g + __ffs(pending) - 1;
                 pending &= pending - 1;
                 const float4 a = st[k].a;
@@ -123,6 +124,7 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
                     atomicAdd(gp + 8, s8);
                     if (kAbs) { atomicAdd(gp + 9, sax); atomicAdd(gp + 10, say); }
                 }
+                if (__all_sync(0xffffffffu, done)) break;
             }
         }
     }
@@ -178,9 +180,10 @@ __global__ void __launch_bounds__(kTilePixels) pruning_scores_kernel(BlendArgs A
         const uint32_t bs = min(static_cast<uint32_t>(kTilePixels), n - start);
         for (uint32_t g = 0; g < bs; g += 32) {
             const bool ov = g + lane < bs && overlaps_subtile(sbnd[g + lane], sx0, sy0);
-            uint32_t pending = __ballot_sync(0xffffffffu, ov);
+            // `done` changes only where a fragment is accepted, so the warp votes on it once per group of 32
+            // records and after each accepted fragment
+            uint32_t pending = __all_sync(0xffffffffu, done) ? 0u : __ballot_sync(0xffffffffu, ov);
             while (pending) {
-                if (__all_sync(0xffffffffu, done)) break;
                 const uint32_t k = g + __ffs(pending) - 1;
                 pending &= pending - 1;
                 const float4 a = sa[k];
@@ -207,6 +210,7 @@ __global__ void __launch_bounds__(kTilePixels) pruning_scores_kernel(BlendArgs A
                 }
                 const float total = warp_sum(score);
                 if (lane == 0) atomicAdd(scores + sprim[k], total);
+                if (__all_sync(0xffffffffu, done)) break;
             }
         }
     }

@@ -521,7 +521,8 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
 constexpr int kOwnDir = 1, kOwnBase = 2;
 
 __device__ inline int input_grad_row(const Params& P, const AppearanceConfig& A, const GradOut& O, uint32_t t_row, const RowData& d, bool fast,
-                                     int half, const float* trig, int row, int kin, int deg, f3 dir, f3& gbase_in, f3& gdir) {
+                                     int half, const float* trig, int row, int kin, int deg, f3 dir, f3& gbase_in, f3& gdir,
+                                     float* stage_row) {
     const float inv = 1.0f / kLossScale;
     const int F = A.feature_dim, nf = A.n_freq, per = nf > 0 ? 2 * nf : 1, nraw = F + (A.base_input ? 3 : 0);
     const int enc = nraw * per;
@@ -553,6 +554,10 @@ __device__ inline int input_grad_row(const Params& P, const AppearanceConfig& A,
 #pragma unroll
             for (int k = 0; k < 4; k++) gv[k] = (cs[k] * g[2 * k] - sn[k] * g[2 * k + 1]) * inv;
             const float4 o = make_float4(gv[0], gv[1], gv[2], gv[3]);
+            if (stage_row) {  // written out by whole rows afterwards (store_staged_features)
+                *reinterpret_cast<float4*>(stage_row + j) = o;
+                return;
+            }
             float4* dst = reinterpret_cast<float4*>(gout + j);
             if (acc) atomicAdd(dst, o);  // one addition per element and launch (deterministic)
             else *dst = o;
@@ -638,6 +643,28 @@ __device__ inline int input_grad_row(const Params& P, const AppearanceConfig& A,
     return kOwnDir | kOwnBase;
 }
 
+// Feature gradients of 32-feature rows leave through shared memory: each row's two threads put their halves into a
+// staging block (rows of 36 floats, so the 16-byte stores of a warp's rows fall in different banks), and the CTA then
+// writes whole 128-byte rows, four per warp instruction, instead of 32 rows 16 bytes each. The staging block lives in
+// the input operand slot, free between the layer-0 MMAs and the next tile's input row.
+constexpr int kStageStride = 36;
+constexpr uint32_t kStageBytes = kTcRows * kStageStride * 4;
+__device__ inline bool stage_features(const TcPlan& p, bool fast, const AppearanceConfig& A) {
+    return fast && A.feature_dim == 32 && static_cast<uint32_t>(p.kin) * kTcRows * 2 >= kStageBytes + kTcRows * 4;
+}
+__device__ inline void store_staged_features(const GradOut& O, const float* stage, const uint32_t* rows_prim, int t) {
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+        const int c = t + kTcThreads * m, r = c >> 3, q = c & 7;
+        const uint32_t pi = rows_prim[r];
+        if (pi == 0xffffffffu) continue;
+        const float4 v = *reinterpret_cast<const float4*>(stage + r * kStageStride + 4 * q);
+        float4* dst = reinterpret_cast<float4*>(O.residual + static_cast<size_t>(pi) * 32 + 4 * q);
+        if (O.accumulate) atomicAdd(dst, v);  // one addition per element and launch (deterministic)
+        else *dst = v;
+    }
+}
+
 // backward MMAs of layer l: weight gradient (M = 64, accumulated in TMEM) and data gradient (layer accumulator)
 __device__ inline void issue_backward(const TcPlan& p, uint32_t sbase, uint32_t tb, int l, bool wg_accumulate) {
     const int last = p.layers - 1;
@@ -690,6 +717,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
     const bool fast = fast_features(P, A) && (reinterpret_cast<uintptr_t>(O.residual) & 15u) == 0;  // 16-byte gradient stores
     float* trig = fast && plan.trig_smem ? reinterpret_cast<float*>(smem + plan.trig_smem) : nullptr;
     const uint32_t x_row = sbase + plan.x_smem + tc::kmajor_offset(row, 0, plan.kin);
+    const bool staged = stage_features(plan, fast, A);
+    float* const fstage = reinterpret_cast<float*>(smem + plan.x_smem);
+    uint32_t* const fstage_prim = reinterpret_cast<uint32_t*>(smem + plan.x_smem + kStageBytes);
     // With an activation store (the colour pass's hidden activations and raw outputs) the forward is not recomputed:
     // a tile's activations are copied into their slots while the previous tile finishes (slot j as soon as the MMAs
     // of layer j, its last reader, completed) and its raw outputs come with the row prefetch.
@@ -781,7 +811,13 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
         float rn = 1.0f;
         const f3 d = valid ? view_dir(v, cur.mean, &rn) : mk3(0.0f, 0.0f, 1.0f);
         f3 gbase_in = mk3(0.0f, 0.0f, 0.0f), gd = mk3(0.0f, 0.0f, 0.0f);
-        const int own = input_grad_row(P, A, O, t_row, cur, fast, half, trig, row, plan.kin, deg, d, gbase_in, gd);
+        const int own = input_grad_row(P, A, O, t_row, cur, fast, half, trig, row, plan.kin, deg, d, gbase_in, gd,
+                                       staged ? fstage + row * kStageStride : nullptr);
+        if (staged) {
+            if (half == 0) fstage_prim[row] = valid ? i : 0xffffffffu;
+            __syncthreads();
+            store_staged_features(O, fstage, fstage_prim, t);
+        }
         if ((own & kOwnBase) && valid) {
             f3 gbase = mk3(0.0f, 0.0f, 0.0f);
             if (v.render_base) {
