@@ -1,15 +1,18 @@
 // Neural appearance MLP on the sm_100a tensor cores (tcgen05 + TMEM); see tc.cuh for the operand layouts.
 //
 // Semantics as in neural.cu (appearance_neural.cuh:10-407 of the reference: encoding, SH inputs, fp16 network
-// without biases, loss scale 128 in the backward). Design: one CTA of 128 threads handles tiles of 128 visible
-// rows, thread t owning row t of the tile (the 32x32b TMEM load gives each thread its row). Per layer one thread
-// issues the K/16 MMAs (M = 128 rows, N = layer width, fp16 operands from shared memory in the canonical layouts,
-// fp32 accumulator in TMEM) and commits them to an mbarrier; the threads read their row from TMEM, apply the
-// activation, round to fp16 and store the next layer's operand. The backward issues, per layer, the data-gradient
-// MMAs (into the layer accumulator) and the weight-gradient MMAs (M = 64, reduction over the tile's rows) into
-// TMEM accumulators that persist over every tile the CTA processes; they are read out and added to the weight
-// gradient once per CTA. Hidden gradients overwrite their activations in place after the MMAs that read them
-// completed. Used for 64-wide networks with at least one hidden layer (neural.cu keeps the other shapes).
+// without biases, loss scale 128 in the backward). Design: one CTA of 256 threads handles tiles of 128 visible
+// rows, two threads per row (warps w and w + 4 read the same TMEM lane quarter, each taking half of the columns).
+// Per layer one thread issues the K/16 MMAs (M = 128 rows, N = layer width, fp16 operands from shared memory in the
+// canonical layouts, fp32 accumulator in TMEM) and commits them to an mbarrier; the threads read their row from
+// TMEM, apply the activation, round to fp16 and store the next layer's operand. In training the colour pass also
+// writes every hidden activation and the raw outputs of a tile to an activation store, which the backward copies
+// back into its shared slots (cp.async, one tile ahead) instead of recomputing the forward. The backward issues,
+// per layer, the data-gradient MMAs (into the layer accumulator) and the weight-gradient MMAs (M = 64, reduction
+// over the tile's rows) into TMEM accumulators that persist over every tile the CTA processes; they are read out
+// and added to the weight gradient once per CTA. Hidden gradients overwrite their activations in place after the
+// MMAs that read them completed. Used for 64-wide networks with at least one hidden layer (neural.cu keeps the
+// other shapes).
 //
 // This file also holds the tensor-core self-test behind fgs_tc_selftest: three small GEMMs covering every operand
 // orientation the MLP kernels use (forward: A and B K-major; data gradient: B MN-major; weight gradient: M = 64,

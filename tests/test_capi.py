@@ -54,6 +54,32 @@ def test_workspace_queries():
         size_out(lib.fgs_tile_workspace_bytes, 0, 10)
 
 
+def test_workspace_activation_store_size():
+    """A rasterizer whose Neural MLP runs on the tensor cores (64 neurons) sizes the primitive workspace with the
+    activation store: per 128-row tile one 16 KB block per hidden layer plus 1 KB of raw outputs, after the other
+    buffers (one 256-byte alignment step at most); NULL, SH and 16-wide networks size it without."""
+    import FasterGSVDACudaBackend as F
+    from FasterGSVDACudaBackend._lib import lib, size_out
+    from FasterGSVDACudaBackend import rasterization as R
+    n = 100_000
+    tiles = (n + 127) // 128
+    for hidden in (1, 2, 3):
+        F.initialize_appearance('neural', 0, 'none', 'tanh', 'relu', True)
+        F.initialize_residual_mlp(80, 3, {'otype': 'Identity'}, {'otype': 'FullyFusedMLP', 'activation': 'ReLU', 'output_activation': 'None',
+                                                                  'n_neurons': 64, 'n_hidden_layers': hidden}, False, 1, [0, 1, 2, 3])
+        with_store = size_out(lib.fgs_primitive_workspace_bytes, R._rasterizer.handle, n)
+        without = size_out(lib.fgs_primitive_workspace_bytes, None, n)
+        extra = with_store - without
+        store = tiles * (hidden * 128 * 64 * 2 + 128 * 8)
+        assert store <= extra < store + 256, (hidden, extra, store)
+    F.initialize_residual_mlp(80, 3, {'otype': 'Identity'}, {'otype': 'FullyFusedMLP', 'activation': 'ReLU', 'output_activation': 'None',
+                                                              'n_neurons': 16, 'n_hidden_layers': 2}, False, 1, [0, 1, 2, 3])
+    assert size_out(lib.fgs_primitive_workspace_bytes, R._rasterizer.handle, n) == size_out(lib.fgs_primitive_workspace_bytes, None, n)
+    F.initialize_appearance('sh', 3, 'none', 'none', 'relu', True)
+    assert size_out(lib.fgs_primitive_workspace_bytes, R._rasterizer.handle, n) == size_out(lib.fgs_primitive_workspace_bytes, None, n)
+    assert [f[0] for f in F._lib.Frame._fields_][-1] == 'mlp_activations'
+
+
 def test_settings_field_order_matches_reference():
     import FasterGSVDACudaBackend as F
     assert F.RasterizerSettings._fields == ('w2c', 'cam_position', 'bg_color', 'appearance_degree', 'width', 'height', 'focal_x', 'focal_y',
