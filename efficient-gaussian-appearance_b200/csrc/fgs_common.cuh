@@ -7,9 +7,9 @@
 // -fmad=false, so nvcc never contracts a*b+c on its own, and the transcendental functions below are
 // polynomial evaluations built from the same basic operations. A C implementation that performs the
 // same operations in the same order (compiled with -ffp-contract=off) therefore produces bit-identical
-// results, which is what makes keys, tile lists, ranges and images reproducible outside the GPU. The Neural
-// encoding's sine and cosine (enc_sincos) are the one hardware approximation: they feed only colours, which are
-// compared within tolerances.
+// results, which is what makes keys, tile lists, ranges and images reproducible outside the GPU. Two hardware
+// approximations stay off those paths: the Neural encoding's sine and cosine (enc_sincos), which feed only colours,
+// and the backward blend's reciprocal of 1 - alpha in gradient terms; both are compared within tolerances.
 #pragma once
 
 #include <cstdint>
