@@ -1,12 +1,11 @@
 """Generates the appearance golden vectors from the reference's own PyTorch modules.
 
-Imports Appearance/SH.py, SV.py, NASG.py and NASGabor.py from the reference checkout (default /root/reference, or
-$FGS_REFERENCE) unmodified, with small stand-ins for the NeRFICG framework modules they import but that are absent
-from the checkout (Framework, Logging, Datasets.utils, Optim.*, Thirdparty.TinyCudaNN and the backend package).
-For each model it evaluates AppearanceModel.forward (color_activation(base_activation(base) + residual(dir)))
-on seeded inputs on the CPU in float64 and records the colors and the autograd gradients for a seeded upstream
-gradient. The fixtures are written to tests/golden/appearance_<model>.npz and committed; the tests never read the
-reference at run time.
+Imports Appearance/SH.py, SV.py, NASG.py and NASGabor.py from the reference checkout ($FGS_REFERENCE) unmodified,
+with small stand-ins for the NeRFICG framework modules they import but that are absent from the checkout
+(Framework, Logging, Datasets.utils, Optim.*, Thirdparty.TinyCudaNN and the backend package). For each model it
+evaluates AppearanceModel.forward (color_activation(base_activation(base) + residual(dir))) on seeded inputs on the
+CPU in float64 and records the colors and the autograd gradients for a seeded upstream gradient. The fixtures are
+written to tests/golden/appearance_<model>.npz and committed; the tests never read the reference at run time.
 
 Run: python tests/golden/make_golden.py
 """
