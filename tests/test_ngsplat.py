@@ -79,3 +79,23 @@ def test_rejects_unrepresentable_neural_configs(tmp_path):
         ngsplat.export_ngsplat(tmp_path / 'x.ngsplat', z['means'], z['scales'], z['rotations'], z['opacities'], z['base_colors'],
                                z['residual_params'], ngsplat.ViewerAppearance('neural', residual_activation='tanh'),
                                mlp_weights=z['mlp_weights'][:-16])
+
+
+def test_header_options_and_test_cameras(tmp_path):
+    """Proper-antialiasing flag, orbit-hint overrides and baked test cameras land in the header; the splat and
+    residual payloads stay those of the reference file for the same parameters."""
+    z = np.load(GOLDEN / 'ngsplat_sv3.npz')
+    meta = json.loads(str(z['meta']))
+    cams = np.arange(2 * 18, dtype=np.float32).reshape(2, 18)
+    out = tmp_path / 'opts.ngsplat'
+    ngsplat.export_ngsplat(out, z['means'], z['scales'], z['rotations'], z['opacities'], z['base_colors'], z['residual_params'],
+                           _appearance(meta), proper_antialiasing=True, center=(1.0, 2.0, 3.0), up=(0.0, 0.0, 2.0), distance=7.5,
+                           test_cameras=cams)
+    f = ngsplat.read_ngsplat(out)
+    r = ngsplat.read_ngsplat_bytes(z['ngsplat'].tobytes())
+    assert f['flags'] == r['flags'] | 1
+    assert f['center'] == (1.0, 2.0, 3.0) and f['up'] == (0.0, 0.0, 1.0) and f['distance'] == 7.5
+    np.testing.assert_array_equal(f['test_cameras'], cams)
+    np.testing.assert_array_equal(f['geometry'], r['geometry'])
+    for a, b in zip(f['textures'], r['textures']):
+        np.testing.assert_array_equal(a, b)
