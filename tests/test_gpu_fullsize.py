@@ -8,6 +8,8 @@ over several 4096-key tiles per digit, hundreds of tensor-core tiles per CTA.
 - c3 (NASG-8 inference, 3,000,000 Gaussians, 1920x1080): integer stages bit for bit, colors within 1e-5 relative, the
   clamped HWC inference image within 1e-4 of the oracle; and, with the GPU's own colors given to the oracle as
   precomputed colors, the blended image bit for bit.
+- c2 (Neural 80-64-64-3, 1,000,000 Gaussians, 1264x832): against the full oracle run, integer stages bit for bit, the
+  image within 1e-3 max / 1e-5 mean, gradients within 1e-3 (geometry) / 1e-2 (base colours, features, weights).
 - c4 (Neural 80-64-64-3, 6,000,000 Gaussians, 1920x1080, view 0 of the training batch): culling, depth order, binning,
   records and the blended image bit for bit against the oracle fed the GPU's colors; the colors themselves against the
   oracle's fp16-semantics MLP on a seeded sample of 20,000 Gaussians (1e-3 max abs, 2e-5 mean abs: the tensor cores
@@ -104,6 +106,39 @@ def _neural_c4(F):
     neural = dict(feature_dim=feat, base_input=0, n_freq=n_freq, sh_mask=15, n_input=n_in, n_input_pad=pad, n_neurons=neurons, n_hidden=hidden,
                   hidden_act=1)
     return neural, S.mlp_layer_shapes(pad, neurons, hidden)
+
+
+def test_c2_full_size_neural_forward_backward(cuda, oracle_threads):
+    """c2: Neural appearance (32 latent features, 80 inputs, 2x64 hidden), 1,000,000 Gaussians at 1264x832, compared
+    with the full oracle run (no sampling): integer stages bit for bit, image within the Neural tolerances, gradients
+    within 1e-3 (geometry) / 1e-2 (base colours, features, MLP weights) relative L2."""
+    import FasterGSVDACudaBackend as F
+    n, W, H = 1_000_000, 1264, 832
+    neural, shapes = _neural_c4(F)
+    prims = {**S.geometry(n), **S.neural_appearance(n, 32, layer_shapes=shapes)}
+    cam = S.ring_cameras(1, W, H)[0]
+    settings = settings_for(F, cam, 3, cuda)
+    dev = {k: v.to(cuda).contiguous() for k, v in prims.items()}
+    g = gpu_forward_stages(F, dev, settings)
+    grad_image = torch.randn(3, H, W, generator=torch.Generator().manual_seed(2)) * 0.01
+    o = O.run(O.make_appearance('neural', 0, 0, 1, 1, True, neural=neural), O.make_view(cam, 3), prims, grad_image=grad_image)
+    assert o['n_visible'] > 500_000 and o['n_instances'] > 1_200_000
+    assert g['n_visible'] == o['n_visible'] and g['n_instances'] == o['n_instances']
+    for k in ('n_touched', 'sorted_idx', 'tile_keys', 'ranks', 'ranges', 'n_contrib'):
+        np.testing.assert_array_equal(g[k], o[k], err_msg=k)
+    err = np.abs(g['image'] - o['image'])
+    assert err.max() <= 1e-3 and err.mean() <= 1e-5, (err.max(), err.mean())
+    del g
+
+    leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
+    img = F.diff_rasterize(leaves['means'], leaves['scales'], leaves['rotations'], leaves['opacities'], torch.empty(0, device=cuda), settings,
+                           base_colors=leaves['base_colors'], residual_params=leaves['residual_params'], mlp_weights=leaves['mlp_weights'])
+    img.backward(grad_image.to(cuda))
+    tol = {'means': 1e-3, 'scales': 1e-3, 'rotations': 1e-3, 'opacities': 1e-3, 'base_colors': 1e-2, 'residual_params': 1e-2, 'mlp_weights': 1e-2}
+    for k, t in leaves.items():
+        ref = o['grads'][k]
+        e = rel_err(t.grad.cpu().numpy().reshape(ref.shape), ref)
+        assert e <= tol[k], f'{k}: relative error {e:.2e}'
 
 
 def test_c4_full_size_neural_view(cuda, oracle_threads):
