@@ -119,3 +119,58 @@ def test_failed_rank_surfaces_as_error():
     assert all(not p.is_alive() for p in procs)
     assert procs[1].exitcode != 0
     assert procs[0].exitcode == 3
+
+
+def _position_order(means: torch.Tensor) -> torch.Tensor:
+    """Stand-in for the Morton order on CPU ranks (the codes come from a GPU kernel): any fixed permutation of the
+    Gaussians exercises the same gather / permute / re-slice logic."""
+    m = means.reshape(-1, 3)
+    return torch.argsort(m[:, 0] + 0.37 * m[:, 1] - 0.11 * m[:, 2], stable=True)
+
+
+def _morton_worker(rank, world, port, out_dir):
+    for p in (str(ROOT), str(ROOT / 'efficient-gaussian-appearance_b200'), str(ROOT / 'tests')):
+        sys.path.insert(0, p)
+    import datetime
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    torch.distributed.init_process_group('gloo', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    import trainer as T
+    T.morton_order = _position_order
+    t = T.Trainer(_prims(), LRS, torch.device('cpu'), group=torch.distributed.group.WORLD)
+    lo = rank * t.shard
+    t.exp_avg.copy_(torch.arange(lo, lo + t.shard, dtype=torch.float32))
+    t.exp_avg_sq.copy_(-torch.arange(lo, lo + t.shard, dtype=torch.float32))
+    t.apply_morton_ordering()
+    torch.save({'params': t.params.clone(), 'm': t.exp_avg.clone(), 'v': t.exp_avg_sq.clone(), 'shard': t.shard},
+               os.path.join(out_dir, f'morton_{rank}.pt'))
+    torch.distributed.destroy_process_group()
+
+
+def test_morton_ordering_two_ranks_matches_single_process(tmp_path):
+    """Every rank holds only its slice of the Adam moments: the ordering gathers them, permutes every per-Gaussian
+    group (the MLP weights stay) and hands each rank its slice again, as one process permuting everything would."""
+    for p in (str(ROOT), str(ROOT / 'efficient-gaussian-appearance_b200')):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import trainer as T
+    world = 2
+    mp.start_processes(_morton_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method='spawn', join=True)
+    parts = [torch.load(tmp_path / f'morton_{r}.pt') for r in range(world)]
+    saved, T.morton_order = T.morton_order, _position_order
+    try:
+        ref = T.Trainer(_prims(), LRS, torch.device('cpu'))
+        ref.exp_avg.copy_(torch.arange(ref.shard, dtype=torch.float32))
+        ref.exp_avg_sq.copy_(-torch.arange(ref.shard, dtype=torch.float32))
+        ref.apply_morton_ordering()
+    finally:
+        T.morton_order = saved
+    n = sum((g.numel + 63) // 64 * 64 for g in ref.groups)
+    assert torch.equal(parts[0]['params'], parts[1]['params'])
+    assert torch.equal(parts[0]['params'][:n], ref.params[:n])
+    m = torch.cat([p['m'] for p in parts])
+    v = torch.cat([p['v'] for p in parts])
+    assert torch.equal(m[:n], ref.exp_avg[:n]) and torch.equal(v[:n], ref.exp_avg_sq[:n])
+    means = _prims()['means']
+    g = next(x for x in ref.groups if x.name == 'means')
+    assert torch.equal(ref.params[g.offset:g.offset + g.numel].view(-1, 3), means[_position_order(means)])
