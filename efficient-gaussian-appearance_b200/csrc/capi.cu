@@ -4,6 +4,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 #include <utility>
@@ -834,11 +835,14 @@ int fgs_profile_collect(char* names, size_t names_bytes, double* ms, int max_ent
 // output image.
 //
 // The device address of the array is looked up once per device, on that device's first call (with the device
-// current), so the first call on each device should happen before any stream capture. All calls share the
-// array and it keeps the previous call's contents; every buffer the kernels read is either fully rewritten by
-// the call or cleared by it (the tile ranges are set to zero before they are filled). Two calls whose work
-// overlaps on the GPU (different streams or threads without synchronisation) race on the array.
+// current), so the first call on each device should happen before any stream capture. The cached address
+// belongs to the device's primary context: after cudaDeviceReset on that device it is stale and the process
+// must not call this entry point again on that device. All calls share the array and it keeps the previous
+// call's contents; every buffer the kernels read is either fully rewritten by the call or cleared by it (the
+// tile ranges are set to zero before they are filled). Two calls whose work overlaps on the GPU (different
+// streams or threads without synchronisation) race on the array.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[FGS_NOALLOC_SCRATCH_BYTES];
+static std::mutex g_noalloc_mu;
 static void* g_noalloc_ptr[64] = {nullptr};
 
 int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_settings* settings, float* image, int to_chw,
@@ -852,12 +856,16 @@ int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const 
     int dev = 0;
     FGS_CUDA(cudaGetDevice(&dev), "noalloc device");
     if (dev < 0 || dev >= 64) return fail(FGS_ERR_UNSUPPORTED, "device index beyond 63");
-    if (!g_noalloc_ptr[dev]) {
-        void* p = nullptr;
-        FGS_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "noalloc scratch address");
-        g_noalloc_ptr[dev] = p;
+    char* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void* p = nullptr;
+            FGS_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "noalloc scratch address");
+            g_noalloc_ptr[dev] = p;
+        }
+        base = static_cast<char*>(g_noalloc_ptr[dev]);
     }
-    char* base = static_cast<char*>(g_noalloc_ptr[dev]);
     const uint64_t n = static_cast<uint64_t>(prims->n_primitives);
     const Grid g = grid_of(settings->width, settings->height);
     size_t prim_bytes = 0, tile_bytes = 0;
@@ -916,6 +924,20 @@ int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const 
     a.grid_w = g.gw;
     a.grid_h = g.gh;
     FGS_CUDA(fgs::launch_blend_inference(a, image, to_chw, clamp_output, s), "blend");
+    if (nv > 0 && !precomputed && r->cfg.model == fgs::kNeural) {
+        // the tensor-core colour pass gives up a bounded wait by setting a device flag instead of faulting; read it
+        // (pageable host memory, no allocation) so invalid colours never come back with FGS_OK
+        int* tc_flag = nullptr;
+        int flag_host = 0;
+        FGS_CUDA(fgs::tc_timeout_flag(&tc_flag), "tensor-core timeout flag");
+        FGS_CUDA(cudaMemcpyAsync(&flag_host, tc_flag, sizeof(int), cudaMemcpyDeviceToHost, s), "tensor-core timeout flag");
+        FGS_CUDA(cudaStreamSynchronize(s), "tensor-core timeout flag");
+        if (flag_host) {
+            FGS_CUDA(cudaMemsetAsync(tc_flag, 0, sizeof(int), s), "tensor-core timeout flag");
+            return fail(FGS_ERR_CUDA, "fgs_inference_noalloc: a tensor-core MLP kernel gave up a bounded wait for its MMAs; the image "
+                                      "is invalid (the flag is now cleared)");
+        }
+    }
     if (n_visible) *n_visible = static_cast<int64_t>(nv);
     if (n_instances) *n_instances = static_cast<int64_t>(ni);
     return FGS_OK;

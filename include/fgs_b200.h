@@ -265,9 +265,16 @@ int fgs_profile_collect(char* names, size_t names_bytes, double* ms, int max_ent
  * running inside a host application that owns a fixed device-memory budget, where a cudaMalloc in the middle of a
  * frame may stall it or fail. All workspaces live in one static device array of FGS_NOALLOC_SCRATCH_BYTES that
  * every GPU loading the library holds until exit; inputs and the output image stay caller-owned. The call rejects,
- * with FGS_ERR_WORKSPACE and a message, any scene whose workspaces do not fit (roughly: 100k primitives at 720p
- * with up to ~1M tile instances fit). Each device's first call looks up the array's address, so make it before any
- * stream capture. Calls share the array: calls that overlap on the GPU race. Output as fgs_inference_render. */
+ * with FGS_ERR_WORKSPACE and a message, any scene whose workspaces do not fit. The workspaces are those of
+ * fgs_primitive_workspace_bytes(NULL, N) + fgs_tile_workspace_bytes(W, H) + fgs_instance_workspace_bytes(I, W, H):
+ * about 132.3 bytes per primitive, 1552 bytes per 16x12 tile (8.1 per pixel) and 12.25 bytes per tile instance
+ * (16.25 beyond 65536 tiles), each sub-buffer rounded up to 256 bytes; 100,000 primitives at 1280x720 leave room for
+ * 1,000,000 tile instances. Each device's first call looks up the array's address (with that device current), so
+ * make it before any stream capture; after cudaDeviceReset of a device the looked-up address is stale and this entry
+ * point must not be called on that device again. A Neural colour pass that gave up a bounded wait is reported as
+ * FGS_ERR_CUDA (and the flag cleared), never as an image. Calls share the array, which keeps the last call's
+ * contents (every buffer a call reads is rewritten or cleared by it): calls that overlap on the GPU race. Output as
+ * fgs_inference_render. */
 #define FGS_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const fgs_settings* settings, float* image, int to_chw,
                           int clamp_output, void* stream, int64_t* n_visible, int64_t* n_instances);

@@ -7,7 +7,7 @@ evaluates AppearanceModel.forward (color_activation(base_activation(base) + resi
 CPU in float64 and records the colors and the autograd gradients for a seeded upstream gradient. The fixtures are
 written to tests/golden/appearance_<model>.npz and committed; the tests never read the reference at run time.
 
-Run: python tests/golden/make_golden.py
+Run: python tests/golden/make_golden.py <reference checkout>   (or set $FGS_REFERENCE)
 """
 import importlib
 import os
@@ -18,7 +18,9 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get('FGS_REFERENCE', '/root/reference'))
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('FGS_REFERENCE', ''))
+if not str(REF) or not (REF / 'Appearance').is_dir():
+    raise SystemExit('pass the reference checkout (the directory holding Appearance/) as the first argument or in $FGS_REFERENCE')
 OUT = Path(__file__).resolve().parent
 
 

@@ -7,7 +7,7 @@ so no dataset or NeRFICG framework is needed) and stores the inputs together wit
 tests/golden/ngsplat_<case>.npz. The tests compare this library's writer (ngsplat.py) with those bytes and never read
 the reference at run time.
 
-Run: python tests/golden/make_ngsplat_golden.py   (the reference checkout is taken from $FGS_REFERENCE)
+Run: python tests/golden/make_ngsplat_golden.py <reference checkout>   (or set $FGS_REFERENCE)
 """
 import json
 import os
@@ -19,7 +19,9 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get('FGS_REFERENCE', '/root/reference'))
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('FGS_REFERENCE', ''))
+if not str(REF) or not (REF / 'Appearance').is_dir():
+    raise SystemExit('pass the reference checkout (the directory holding Appearance/) as the first argument or in $FGS_REFERENCE')
 OUT = Path(__file__).resolve().parent
 N = 300
 

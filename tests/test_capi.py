@@ -101,3 +101,21 @@ def test_size_validation_rejects_mismatched_tensors():
                        R._rasterizer)
     R._check_sizes(n, torch.zeros(n, 3), torch.zeros(n, 4), torch.zeros(n, 1), None, torch.zeros(n, 3), torch.zeros(n, 15, 3), None,
                    R._rasterizer)
+
+
+def test_noalloc_size_example_fits():
+    """The allocation-free entry point's documented example (100,000 primitives at 1280x720 with 1,000,000 tile
+    instances) fits its static array, and 1.1M instances do not: the same workspace queries size both."""
+    from FasterGSVDACudaBackend._lib import lib, size_out
+    limit = 32 * 1024 * 1024
+    header = (ROOT / 'include' / 'fgs_b200.h').read_text()
+    assert '#define FGS_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)' in header
+    rnd = lambda b: (b + 255) // 256 * 256
+    base = rnd(size_out(lib.fgs_primitive_workspace_bytes, None, 100_000)) + rnd(size_out(lib.fgs_tile_workspace_bytes, 1280, 720))
+    assert base + size_out(lib.fgs_instance_workspace_bytes, 1_000_000, 1280, 720) <= limit
+    assert base + size_out(lib.fgs_instance_workspace_bytes, 1_100_000, 1280, 720) > limit
+    # the per-item costs the header states
+    per_prim = (size_out(lib.fgs_primitive_workspace_bytes, None, 2_000_000) - size_out(lib.fgs_primitive_workspace_bytes, None, 1_000_000)) / 1e6
+    per_inst = (size_out(lib.fgs_instance_workspace_bytes, 2_000_000, 1280, 720) - size_out(lib.fgs_instance_workspace_bytes, 1_000_000, 1280, 720)) / 1e6
+    assert abs(per_prim - 132.3) < 0.1 and abs(per_inst - 12.25) < 0.01
+    assert size_out(lib.fgs_tile_workspace_bytes, 16 * 80, 12 * 60) // (80 * 60) == 1552

@@ -68,6 +68,7 @@ def test_neural_parity(cuda, cfg):
     for k in ('n_touched', 'sorted_idx', 'tile_keys', 'ranks', 'ranges'):
         np.testing.assert_array_equal(g[k], o[k], err_msg=k)
     img_err = np.abs(g['image'] - o['image'])
+    print(f'\n[neural {cfg}] image max-abs {img_err.max():.3e} mean-abs {img_err.mean():.3e}')
     assert img_err.max() <= 1e-3 and img_err.mean() <= 1e-5, (img_err.max(), img_err.mean())
 
     leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
@@ -79,6 +80,7 @@ def test_neural_parity(cuda, cfg):
     for k, t in leaves.items():
         ref = o['grads'][k]
         err = rel_err(t.grad.cpu().numpy().reshape(ref.shape), ref)
+        print(f'[neural {cfg}] grad {k} rel {err:.3e}')
         assert err <= tol[k], f'{k}: relative error {err:.2e}'
 
 
