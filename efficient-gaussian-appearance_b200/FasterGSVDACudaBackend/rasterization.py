@@ -243,9 +243,15 @@ class ForwardState:
                                        image.data_ptr(), int(bool(to_chw)), int(bool(clamp_output)), _stream()))
 
     def backward(self, prims: _lib.Primitives, image: torch.Tensor, grad_image: torch.Tensor, grads: _lib.Gradients,
-                 densification_info: torch.Tensor | None, accumulate: bool = False) -> None:
+                 densification_info: torch.Tensor | None, accumulate: bool = False, grad_ws: torch.Tensor | None = None) -> None:
+        """`grad_ws`: a caller-owned gradient workspace (uint8, at least fgs_gradient_workspace_bytes) that keeps the
+        per-primitive blend sums of this backward (48-byte records in depth-rank order at its start) for inspection."""
         f = self.frame
-        grad_ws = _workspace(size_out(lib.fgs_gradient_workspace_bytes, self.rasterizer.handle, f.n_visible), self.device)
+        need = size_out(lib.fgs_gradient_workspace_bytes, self.rasterizer.handle, f.n_visible)
+        if grad_ws is None:
+            grad_ws = _workspace(need, self.device)
+        elif grad_ws.numel() < need:
+            raise ValueError('gradient workspace too small')
         dens = ptr(densification_info)
         rows = densification_info.shape[0] if dens is not None else 0
         check(lib.fgs_backward(self.rasterizer.handle, ctypes.byref(prims), ctypes.byref(self.c_settings), ctypes.byref(f),

@@ -24,7 +24,12 @@ FLAGS = ['-O3', '-std=c++17', '-lineinfo', '-fmad=false', '-Xcompiler', '-fPIC',
 # tensor-core MLP of the neural appearance, whose backward also carries the geometry chain rule; the photometric loss,
 # checked against its fp32 PyTorch definition; the blend backward, whose fragment decisions are written with explicit
 # single-rounding intrinsics): contraction allowed.
-CONTRACTED = {'neural.cu', 'neural_tc.cu', 'loss.cu', 'blend_bwd.cu'}
+CONTRACTED = {'neural.cu', 'neural_tc.cu', 'loss.cu'}
+# Sources that evaluate the rasterizer's forward decisions (projection, culling, tile bounds and overlap, fragment
+# acceptance, transmittance) and must compute them exactly as the reference's own build does: its kernels are
+# compiled with -use_fast_math (FasterGSVDACudaBackend/setup.py:125-129, and tiny-cuda-nn's runtime compiler with
+# fast math for the preprocess), so these are too, with the reference's expressions.
+FAST_MATH = {'preprocess.cu', 'binning.cu', 'blend.cu', 'blend_bwd.cu'}
 
 
 def _digest(paths):
@@ -32,7 +37,7 @@ def _digest(paths):
     for p in sorted(paths):
         h.update(p.name.encode())
         h.update(p.read_bytes())
-    h.update(' '.join(FLAGS + ARCH + sorted(CONTRACTED)).encode())
+    h.update(' '.join(FLAGS + ARCH + sorted(CONTRACTED) + sorted(FAST_MATH)).encode())
     return h.hexdigest()
 
 
@@ -43,6 +48,8 @@ def _compile(src: Path, headers_digest: str) -> Path:
     if obj.exists() and stamp.exists() and stamp.read_text() == key:
         return obj
     flags = [f if not (f == '-fmad=false' and src.name in CONTRACTED) else '-fmad=true' for f in FLAGS]
+    if src.name in FAST_MATH:
+        flags = [f for f in flags if f != '-fmad=false'] + ['-use_fast_math']
     cmd = [NVCC, *ARCH, *flags, '-c', str(src), '-o', str(obj)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:

@@ -10,18 +10,20 @@ namespace fgs {
 // row-major) are laid end to end and every lane tests one candidate per round, so a warp spends
 // ceil(sum of candidates / 32) rounds whatever the mix of footprint sizes. A hit of primitive L goes to
 // inst_off[L] + (hits of L before it), which keeps depth order across primitives and row-major tile order within one;
-// consecutive hits of one primitive are consecutive lanes and consecutive addresses.
+// consecutive hits of one primitive are consecutive lanes and consecutive addresses. A primitive never writes past
+// the instances its tile count reserved (inst_off of the next rank, or n_instances for the last): the count and the
+// emission evaluate the same tile test on the same record values, and the bound keeps the buffers safe regardless.
 template <typename K>
 __global__ void __launch_bounds__(256) emit_kernel(const Record* __restrict__ rec, const uint32_t* __restrict__ inst_off,
                                                    K* __restrict__ keys, uint32_t* __restrict__ vals, uint32_t n_visible,
-                                                   uint32_t grid_w) {
+                                                   uint32_t grid_w, uint32_t n_instances) {
     const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t lane = threadIdx.x & 31;
     const bool active = r < n_visible;
     if (__ballot_sync(0xffffffffu, active) == 0) return;
     float sx = 0.0f, sy = 0.0f, ca = 0.0f, cb = 0.0f, cc = 0.0f, thr = 0.0f;
     uint4 tb = make_uint4(0, 0, 0, 0);
-    uint32_t n_max = 0, w = 0;
+    uint32_t n_max = 0, w = 0, lim = 0;
     if (active) {
         const Record q = rec[r];
         sx = q.q0.x - 0.5f;
@@ -32,6 +34,7 @@ __global__ void __launch_bounds__(256) emit_kernel(const Record* __restrict__ re
         tb = tile_bounds_of(bx & 0xffffu, bx >> 16, by & 0xffffu, by >> 16);
         n_max = (tb.y - tb.x) * (tb.w - tb.z);
         w = inst_off[r];
+        lim = r + 1 < n_visible ? inst_off[r + 1] : n_instances;
     }
     const uint32_t bw = tb.y - tb.x;
     // candidate ranges [excl, incl) of the lanes' primitives in the warp's flattened list
@@ -61,6 +64,7 @@ __global__ void __launch_bounds__(256) emit_kernel(const Record* __restrict__ re
         const uint32_t qx0 = __shfl_sync(0xffffffffu, tb.x, owner), qy0 = __shfl_sync(0xffffffffu, tb.z, owner);
         const uint32_t qw = __shfl_sync(0xffffffffu, bw, owner);
         const uint32_t qpos = __shfl_sync(0xffffffffu, w, owner) + __shfl_sync(0xffffffffu, emitted, owner);
+        const uint32_t qlim = __shfl_sync(0xffffffffu, lim, owner);
         const bool valid = c < total;  // then the owner has candidates and qw >= 1
         const uint32_t t = c - o_excl, qw1 = valid ? qw : 1u;
         const uint32_t tx = qx0 + t % qw1, ty = qy0 + t / qw1;
@@ -69,8 +73,8 @@ __global__ void __launch_bounds__(256) emit_kernel(const Record* __restrict__ re
         // lanes of this round that belong to the owner: from the owner's first candidate in the round up to this lane
         const uint32_t first = o_excl > base ? o_excl - base : 0u;
         const uint32_t before = hits & ((1u << lane) - 1u) & ~((1u << first) - 1u);
-        if (hit) {
-            const uint32_t o = qpos + __popc(before);
+        const uint32_t o = qpos + __popc(before);
+        if (hit && o < qlim) {
             keys[o] = static_cast<K>(ty * grid_w + tx);
             vals[o] = (r & ~31u) + owner;  // the owner's depth rank
         }
@@ -81,6 +85,13 @@ __global__ void __launch_bounds__(256) emit_kernel(const Record* __restrict__ re
             emitted += __popc(hits & top & ~((1u << lo) - 1u));
         }
     }
+    // reserved slots left unwritten (only if the count had found more tiles than the emission) get the primitive's
+    // first candidate tile, so no stale key or rank reaches the range extraction or the blend
+    if (active)
+        for (uint32_t o = w + emitted; o < lim; o++) {
+            keys[o] = static_cast<K>(tb.z * grid_w + tb.x);
+            vals[o] = r;
+        }
 }
 
 template <typename K>
@@ -174,11 +185,12 @@ __global__ void __launch_bounds__(1024) bucket_scan_kernel(const uint2* __restri
 }
 
 cudaError_t launch_emit(const Record* sorted_rec, const uint32_t* inst_off, void* keys, uint32_t* vals, uint32_t n_visible, int grid_w,
-                        bool wide, cudaStream_t s) {
+                        bool wide, uint64_t n_instances, cudaStream_t s) {
     if (n_visible == 0) return cudaSuccess;
     const int grid = static_cast<int>((n_visible + 255) / 256);
-    if (wide) emit_kernel<uint32_t><<<grid, 256, 0, s>>>(sorted_rec, inst_off, static_cast<uint32_t*>(keys), vals, n_visible, grid_w);
-    else emit_kernel<uint16_t><<<grid, 256, 0, s>>>(sorted_rec, inst_off, static_cast<uint16_t*>(keys), vals, n_visible, grid_w);
+    const uint32_t ni = static_cast<uint32_t>(n_instances);
+    if (wide) emit_kernel<uint32_t><<<grid, 256, 0, s>>>(sorted_rec, inst_off, static_cast<uint32_t*>(keys), vals, n_visible, grid_w, ni);
+    else emit_kernel<uint16_t><<<grid, 256, 0, s>>>(sorted_rec, inst_off, static_cast<uint16_t*>(keys), vals, n_visible, grid_w, ni);
     return cudaGetLastError();
 }
 

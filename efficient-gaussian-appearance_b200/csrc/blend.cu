@@ -49,15 +49,14 @@ __global__ void __launch_bounds__(kTilePixels) blend_kernel(BlendArgs A, float* 
                 pending &= pending - 1;
                 const float4 a = st[k].a;
                 const float dx = a.x - pxf, dy = a.y - pyf;
-                const float e = gauss_exponent(dx, dy, st[k].h);
-                if (e < a.z) continue;
-                const float alpha = a.w * det_exp_blend(fminf(e, 0.0f));
+                const float alpha = __fmul_rn(a.w, fragment_gaussian(gauss_exponent(dx, dy, st[k].h)));
+                if (alpha < kMinAlpha) continue;
                 const float4 c = st[k].c;
                 const float w = tr * alpha;
                 cr = fmaf(w, c.x, cr);
                 cg = fmaf(w, c.y, cg);
                 cbl = fmaf(w, c.z, cbl);
-                tr = tr * (1.0f - alpha);
+                tr = __fmul_rn(tr, __fsub_rn(1.0f, alpha));
                 last = start + k + 1;
                 if (tr < kTransmittanceThreshold) done = true;
             }

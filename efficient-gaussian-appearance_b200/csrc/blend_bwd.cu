@@ -1,13 +1,13 @@
 // Backward of the tile blend: for every pixel, the fragments of its tile are walked front to back again (the same
 // acceptance and termination decisions as the forward: the exponent, alpha, 1 - alpha and the transmittance are
-// evaluated with the forward's single-rounding operations), and the gradient terms of each accepted fragment are
+// evaluated with the forward's operations, blend_common.cuh), and the gradient terms of each accepted fragment are
 // summed over the warp and added to the primitive's gradient record.
 //
 // Semantics: FasterGSVDACudaBackend/.../rasterization/include/kernels_backward.cuh:12-231 (the reference processes
 // buckets of 32 instances with the pixels pipelined through the lanes, which for small footprints spends most issue
 // slots on pairs that do not overlap); here each warp walks its subtile's fragments front to back like the forward.
-// This translation unit is compiled with contraction (its outputs are checked within a tolerance); the decisions
-// above use explicit intrinsics so they do not depend on it.
+// This translation unit is compiled with -use_fast_math like the forward (its gradients are checked within a
+// tolerance); the decisions above use the forward's explicit operations so they do not depend on contraction.
 #include "blend_common.cuh"
 #include "launch.h"
 
@@ -61,8 +61,8 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
             const uint32_t r = A.vals[range.x + start + t];
             const Record q = A.rec[r];
             StagedB& s = st[t];
-            s.a = make_float4(q.q0.x, q.q0.y, -q.q0.w, q.q0.z);
-            s.h = make_float4(-0.5f * q.q1.x, -q.q1.y, -0.5f * q.q1.z, __uint_as_float(r));
+            s.a = make_float4(q.q0.x, q.q0.y, 0.0f, q.q0.z);
+            s.h = make_float4(kHalfConic * q.q1.x, kCrossConic * q.q1.y, kHalfConic * q.q1.z, __uint_as_float(r));
             s.c = make_float4(q.q2.x, q.q2.y, q.q2.z, 0.0f);
             s.bnd = make_uint2(__float_as_uint(q.q1.w), __float_as_uint(q.q2.w));
         }
@@ -80,17 +80,16 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
                 const float4 h = st[k].h;
                 const float dx = a.x - pxf, dy = a.y - pyf;
                 bool acc = !done && start + k < last;
-                float e = 0.0f;
+                float G = 0.0f, alpha = 0.0f;
                 if (acc) {
-                    e = gauss_exponent(dx, dy, h);
-                    acc = e >= a.z;
+                    G = fragment_gaussian(gauss_exponent(dx, dy, h));
+                    alpha = __fmul_rn(a.w, G);
+                    acc = !(alpha < kMinAlpha);
                 }
                 if (!__any_sync(0xffffffffu, acc)) continue;
                 float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
                 float v8 = 0.0f, ax = 0.0f, ay = 0.0f;
                 if (acc) {
-                    const float G = det_exp_blend(fminf(e, 0.0f));
-                    const float alpha = __fmul_rn(a.w, G);
                     const float4 c = st[k].c;
                     const float w = tr * alpha;
                     const float cg = c.x * gr + c.y * gg + c.z * gb;
@@ -105,8 +104,8 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
                     v[4] = hy * dy; v[5] = w * gr; v[6] = w * gg; v[7] = w * gb;
                     v8 = G * dl_da;
                     if (kAbs) {
-                        // |dL/dmean2d| of this fragment, with the raw conic recovered exactly from the staged halves
-                        const float ca = -2.0f * h.x, cb = -h.y, cc = -2.0f * h.z;
+                        // |dL/dmean2d| of this fragment, with the raw conic recovered from the staged scaled conic
+                        const float ca = h.x / kHalfConic, cb = h.y / kCrossConic, cc = h.z / kHalfConic;
                         ax = fabsf(ca * hx + cb * hy);
                         ay = fabsf(cb * hx + cc * hy);
                     }
@@ -170,8 +169,8 @@ __global__ void __launch_bounds__(kTilePixels) pruning_scores_kernel(BlendArgs A
         if (start + t < n) {
             const uint32_t r = A.vals[range.x + start + t];
             const Record q = A.rec[r];
-            sa[t] = make_float4(q.q0.x, q.q0.y, -q.q0.w, q.q0.z);
-            sh[t] = make_float4(-0.5f * q.q1.x, -q.q1.y, -0.5f * q.q1.z, 0.0f);
+            sa[t] = make_float4(q.q0.x, q.q0.y, 0.0f, q.q0.z);
+            sh[t] = make_float4(kHalfConic * q.q1.x, kCrossConic * q.q1.y, kHalfConic * q.q1.z, 0.0f);
             sc[t] = q.q2.x + q.q2.y + q.q2.z;
             sbnd[t] = make_uint2(__float_as_uint(q.q1.w), __float_as_uint(q.q2.w));
             sprim[t] = rank_to_prim[r];
@@ -189,15 +188,14 @@ __global__ void __launch_bounds__(kTilePixels) pruning_scores_kernel(BlendArgs A
                 const float4 a = sa[k];
                 const float dx = a.x - pxf, dy = a.y - pyf;
                 bool acc = !done && start + k < last;
-                float e = 0.0f;
+                float alpha = 0.0f;
                 if (acc) {
-                    e = gauss_exponent(dx, dy, sh[k]);
-                    acc = e >= a.z;
+                    alpha = __fmul_rn(a.w, fragment_gaussian(gauss_exponent(dx, dy, sh[k])));
+                    acc = !(alpha < kMinAlpha);
                 }
                 if (!__any_sync(0xffffffffu, acc)) continue;
                 float score = 0.0f;
                 if (acc) {
-                    const float alpha = __fmul_rn(a.w, det_exp_blend(fminf(e, 0.0f)));
                     const float cg = sc[k];
                     accd = fmaf(tr * alpha, cg, accd);
                     const float oma = __fsub_rn(1.0f, alpha);

@@ -6,16 +6,22 @@
 
 namespace fgs {
 
+// -0.5 log2(e) and -log2(e): folded into the conic so that a fragment's Gaussian is one exp2 of the exponent
+// (rasterization/include/kernels_common.cuh:13-17)
+constexpr float kLog2eBlend = 1.44269504089f;
+constexpr float kHalfConic = -0.5f * kLog2eBlend;
+constexpr float kCrossConic = -kLog2eBlend;
+
 struct Staged {
-    float4 a;   // mean2d.x, mean2d.y, -power_threshold, opacity
-    float4 h;   // -0.5 conic.x, -conic.y, -0.5 conic.z, unused
+    float4 a;   // mean2d.x, mean2d.y, unused, opacity
+    float4 h;   // conic scaled for exp2: kHalfConic conic.x, kCrossConic conic.y, kHalfConic conic.z, unused
     float4 c;   // color rgb, unused
     uint2 bnd;  // bounds x (lo | hi << 16), y (lo | hi << 16)
 };
 
 __device__ inline void stage_record(const Record& q, Staged& s) {
-    s.a = make_float4(q.q0.x, q.q0.y, -q.q0.w, q.q0.z);
-    s.h = make_float4(-0.5f * q.q1.x, -q.q1.y, -0.5f * q.q1.z, 0.0f);
+    s.a = make_float4(q.q0.x, q.q0.y, 0.0f, q.q0.z);
+    s.h = make_float4(kHalfConic * q.q1.x, kCrossConic * q.q1.y, kHalfConic * q.q1.z, 0.0f);
     s.c = make_float4(q.q2.x, q.q2.y, q.q2.z, 0.0f);
     s.bnd = make_uint2(__float_as_uint(q.q1.w), __float_as_uint(q.q2.w));
 }
@@ -25,11 +31,17 @@ __device__ inline bool overlaps_subtile(uint2 bnd, uint32_t sx0, uint32_t sy0) {
     return xlo < sx0 + kSubtileW && sx0 < xhi && ylo < sy0 + kSubtileH && sy0 < yhi;
 }
 
-// exponent of the Gaussian at the pixel: dx * (h.x dx + h.y dy) + (h.z dy) dy
-// (single-rounding operations spelled out, so the value is the same whether or not a translation unit contracts)
+// base-2 exponent of the Gaussian at the pixel, dx (h.x dx + h.y dy) + h.z dy dy with the scaled conic h
+// (kernels_forward.cuh:119-121), in the single-rounding operations the reference's contracting build evaluates it
+// with inside its blend (measured against the reference kernels' transmittance), spelled out so that the forward and
+// the backward blend take identical decisions
 __device__ inline float gauss_exponent(float dx, float dy, float4 h) {
-    return fmaf(dx, fmaf(h.x, dx, __fmul_rn(h.y, dy)), __fmul_rn(__fmul_rn(h.z, dy), dy));
+    return fmaf(__fmul_rn(h.z, dy), dy, __fmul_rn(dx, fmaf(h.x, dx, __fmul_rn(h.y, dy))));
 }
+
+// the Gaussian of a fragment from its base-2 exponent; alpha = opacity * Gaussian (one rounding), and the reference
+// skips the fragment when alpha is below 1/255 (kernels_forward.cuh:122-127, original opacity interpretation)
+__device__ inline float fragment_gaussian(float e) { return exp2f(fminf(e, 0.0f)); }
 
 
 
@@ -61,8 +73,8 @@ __device__ inline float warp_sum(float x) {
 }
 
 struct StagedB {
-    float4 a;   // mean2d.x, mean2d.y, -power_threshold, opacity
-    float4 h;   // -0.5 conic.x, -conic.y, -0.5 conic.z, bits(rank)
+    float4 a;   // mean2d.x, mean2d.y, unused, opacity
+    float4 h;   // conic scaled for exp2 (as Staged), bits(rank)
     float4 c;   // color rgb, unused
     uint2 bnd;
 };

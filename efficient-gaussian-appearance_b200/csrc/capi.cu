@@ -468,7 +468,7 @@ static int render_common(const fgs_settings* settings, fgs_frame* frame, void* p
     if (ni > 0 && (!inst_ws || inst_ws_bytes < need)) return fail(FGS_ERR_WORKSPACE, "instance workspace too small");
     {
         ProfScope p_("emit", s);
-        FGS_CUDA(fgs::launch_emit(B.sorted_rec, B.inst_off, I.keys_a, I.vals_a, static_cast<uint32_t>(frame->n_visible), g.gw, g.wide, s), "emit");
+        FGS_CUDA(fgs::launch_emit(B.sorted_rec, B.inst_off, I.keys_a, I.vals_a, static_cast<uint32_t>(frame->n_visible), g.gw, g.wide, ni, s), "emit");
     }
     const void* keys = nullptr;
     const uint32_t* vals = nullptr;
@@ -906,7 +906,7 @@ int fgs_inference_noalloc(fgs_rasterizer* r, const fgs_primitives* prims, const 
         FGS_CUDA(fgs::depth_sort(B, static_cast<uint32_t>(nv), s), "depth sort");
         FGS_CUDA(fgs::launch_reorder(B, static_cast<uint32_t>(nv), s), "reorder");
         FGS_CUDA(fgs::exclusive_scan_u32(B.inst_off, static_cast<uint32_t>(nv), B.sort_temp, B.sort_temp_bytes, s), "offset scan");
-        FGS_CUDA(fgs::launch_emit(B.sorted_rec, B.inst_off, I.keys_a, I.vals_a, static_cast<uint32_t>(nv), g.gw, g.wide, s), "emit");
+        FGS_CUDA(fgs::launch_emit(B.sorted_rec, B.inst_off, I.keys_a, I.vals_a, static_cast<uint32_t>(nv), g.gw, g.wide, ni, s), "emit");
     }
     const void* keys = nullptr;
     const uint32_t* vals = nullptr;

@@ -119,10 +119,49 @@ __device__ inline float det_log(float x) {
     return fmaf(kf, kLn2Hi, fmaf(kf, kLn2Lo, ln_m));
 }
 
-// sine and cosine of the Neural frequency encoding: the hardware approximation (MUFU), which is what the reference's
-// sincosf becomes under its -use_fast_math build (appearance_neural.cuh:27-32, setup.py:130-134). Its absolute error
-// on [-pi, pi] is about 4e-7, below the fp16 resolution of the encoded MLP inputs.
-__device__ inline void enc_sincos(float x, float* sp, float* cp) { __sincosf(x, sp, cp); }
+// sine and cosine of the Neural frequency encoding, deterministic: Cody-Waite reduction x = k (pi/2) + r with pi/2
+// split into three floats (P1 = float(pi/2), P2 = float(pi/2 - P1), P3 = float(pi/2 - P1 - P2); fused multiply-adds),
+// |r| <= pi/4, then the Taylor series of sin r through r^9 and of cos r through r^10 (truncation below 2e-9), rotated by
+// the quadrant k mod 4. Every operation is an explicit single-rounding operation, so the oracle's C restatement gives
+// the same bits, and the fp16 inputs of the MLP are identical on both sides. Arguments with |x| <= 0.78 (the latent
+// features, which stay small) have k = 0 and r = x + 0, so they skip the reduction; beyond |x| = 8192 the three-part
+// reduction loses accuracy and sincosf is used.
+constexpr float kTwoOverPi = 0.636619746685028076171875f;
+constexpr float kPio2P1 = 1.57079637050628662109375f;
+constexpr float kPio2P2 = -4.371138828673792886547744274139404296875e-08f;
+constexpr float kPio2P3 = -1.7151245100058819e-15f;
+static __device__ __noinline__ void enc_sincos_large(float x, float* sp, float* cp) { sincosf(x, sp, cp); }
+__device__ inline void enc_sincos(float x, float* sp, float* cp) {
+    float k = 0.0f, r;
+    if (fabsf(x) <= 0.78f) {
+        r = __fadd_rn(x, 0.0f);
+    } else if (!(fabsf(x) <= 8192.0f)) {
+        enc_sincos_large(x, sp, cp);
+        return;
+    } else {
+        k = rintf(__fmul_rn(x, kTwoOverPi));
+        r = fmaf(-k, kPio2P1, x);
+        r = fmaf(-k, kPio2P2, r);
+        r = fmaf(-k, kPio2P3, r);
+    }
+    const float r2 = __fmul_rn(r, r);
+    float ps = 1.0f / 362880.0f;
+    ps = fmaf(ps, r2, -1.0f / 5040.0f);
+    ps = fmaf(ps, r2, 1.0f / 120.0f);
+    ps = fmaf(ps, r2, -1.0f / 6.0f);
+    const float sn = fmaf(ps, __fmul_rn(r2, r), r);
+    float pc = -1.0f / 3628800.0f;
+    pc = fmaf(pc, r2, 1.0f / 40320.0f);
+    pc = fmaf(pc, r2, -1.0f / 720.0f);
+    pc = fmaf(pc, r2, 1.0f / 24.0f);
+    pc = fmaf(pc, r2, -0.5f);
+    const float cs = fmaf(pc, r2, 1.0f);
+    // quadrant q = k mod 4: (sin, cos) = (s, c), (c, -s), (-s, -c), (-c, s)
+    const int q = static_cast<int>(k);
+    const float so = (q & 1) ? cs : sn, co = (q & 1) ? sn : cs;
+    *sp = (q & 2) ? -so : so;
+    *cp = ((q + 1) & 2) ? -co : co;
+}
 
 __device__ inline float det_sigmoid(float x) { return 1.0f / (1.0f + det_exp(-x)); }
 

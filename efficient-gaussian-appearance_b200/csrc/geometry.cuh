@@ -1,8 +1,10 @@
 // Per-primitive projection, culling, EWA covariance, screen bounds and the exact tile-overlap test.
 // Follows FasterGSVDACudaBackend/.../rasterization/rtc/preprocess_forward.cu:62-199 (forward geometry),
 // include/tile_culling.cuh:13-65 (tile bounds and the StopThePop ellipse-vs-tile test) and
-// rtc/preprocess_common.cuh:144-252 (quaternion -> rotation, exact tile count). All operations are
-// written out explicitly (this file is compiled with -fmad=false) so the C oracle reproduces them.
+// rtc/preprocess_common.cuh:144-252 (quaternion -> rotation, exact tile count). The expressions are the reference's,
+// term by term and in the same order, and the translation units that project (preprocess.cu) and emit (binning.cu)
+// are compiled with -use_fast_math like the reference's kernels, so the opacity, covariance, conic, screen mean,
+// power threshold, bounds and tile overlap decisions come out as the reference computes them.
 #pragma once
 
 #include "fgs_common.cuh"
@@ -25,6 +27,9 @@ struct View {
 
 struct Mat3 { float m11, m12, m13, m21, m22, m23, m31, m32, m33; };
 
+// opacity activation of the forward projection (rtc/preprocess_common.cuh:70)
+__device__ inline float opacity_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
 __device__ inline Mat3 quat_to_rot(float r, float x, float y, float z, float& norm_sq) {
     const float xx = x * x, yy = y * y, zz = z * z;
     const float xy = x * y, xz = x * z, yz = y * z;
@@ -43,27 +48,32 @@ __device__ inline uint4 tile_bounds_of(uint32_t xmin, uint32_t xmax, uint32_t ym
     return make_uint4(xmin / kTileW, (xmax + kTileW - 1) / kTileW, ymin / kTileH, (ymax + kTileH - 1) / kTileH);
 }
 
-// exact test whether the ellipse {power <= threshold} reaches the tile; m = mean2d - 0.5
+// exact test whether the ellipse {power <= threshold} reaches the tile; m = mean2d - 0.5. The products and sums are
+// the single-rounding operations the reference's contracting build evaluates tile_culling.cuh:47-62 with, written
+// out so that the tile count (preprocess.cu) and the instance emission (binning.cu) take the same decisions whatever
+// either translation unit contracts; the two divisions are the build's (fast-math) division in both.
 __device__ inline bool tile_overlaps(float mx, float my, float cx, float cy, float cz, uint32_t tx, uint32_t ty, float thr) {
     const float rminx = static_cast<float>(tx * kTileW), rminy = static_cast<float>(ty * kTileH);
     const float rmaxx = static_cast<float>((tx + 1) * kTileW - 1), rmaxy = static_cast<float>((ty + 1) * kTileH - 1);
-    const float xmd = rminx - mx;
+    const float xmd = __fsub_rn(rminx, mx);
     const float xl = xmd >= 0.0f ? 1.0f : 0.0f;
     const float nx = xl + (mx > rmaxx ? 1.0f : 0.0f);
-    const float ymd = rminy - my;
+    const float ymd = __fsub_rn(rminy, my);
     const float ya = ymd >= 0.0f ? 1.0f : 0.0f;
     const float ny = ya + (my > rmaxy ? 1.0f : 0.0f);
     if (ny + nx == 0.0f) return true;
-    const float kx = rmaxx + xl * (rminx - rmaxx);
-    const float ky = rmaxy + ya * (rminy - rmaxy);
-    const float dfx = mx - kx, dfy = my - ky;
+    const float kx = __fmaf_rn(xl, __fsub_rn(rminx, rmaxx), rmaxx);
+    const float ky = __fmaf_rn(ya, __fsub_rn(rminy, rmaxy), rmaxy);
+    const float dfx = __fsub_rn(mx, kx), dfy = __fsub_rn(my, ky);
     const float dx = copysignf(static_cast<float>(kTileW - 1), xmd);
     const float dy = copysignf(static_cast<float>(kTileH - 1), ymd);
-    const float tx_ = ny * sat((dx * cx * dfx + dx * cy * dfy) / (dx * cx * dx));
-    const float ty_ = nx * sat((dy * cy * dfx + dy * cz * dfy) / (dy * cz * dy));
-    const float px = kx + tx_ * dx, py = ky + ty_ * dy;
-    const float ex = mx - px, ey = my - py;
-    const float maxp = 0.5f * (cx * ex * ex + cz * ey * ey) + cy * ex * ey;
+    const float dxcx = __fmul_rn(dx, cx), dycz = __fmul_rn(dy, cz);
+    const float tx_ = __fmul_rn(ny, sat(__fmaf_rn(dxcx, dfx, __fmul_rn(__fmul_rn(dx, cy), dfy)) / __fmul_rn(dxcx, dx)));
+    const float ty_ = __fmul_rn(nx, sat(__fmaf_rn(__fmul_rn(dy, cy), dfx, __fmul_rn(dycz, dfy)) / __fmul_rn(dycz, dy)));
+    const float px = __fmaf_rn(tx_, dx, kx), py = __fmaf_rn(ty_, dy, ky);
+    const float ex = __fsub_rn(mx, px), ey = __fsub_rn(my, py);
+    const float inner = __fmaf_rn(__fmul_rn(cx, ex), ex, __fmul_rn(__fmul_rn(cz, ey), ey));
+    const float maxp = __fmaf_rn(__fmul_rn(cy, ex), ey, __fmul_rn(0.5f, inner));
     return maxp <= thr;
 }
 
@@ -107,10 +117,10 @@ __device__ inline Geometry project_primitive(const float* __restrict__ means, co
     G.depth = depth;
     float opacity = 0.0f, ca = 0.0f, cb = 0.0f, cc = 0.0f, a = 0.0f, c = 0.0f, mx = 0.0f, my = 0.0f;
     if (active) {
-        opacity = det_sigmoid(opacities[idx]);
+        opacity = opacity_sigmoid(opacities[idx]);
         if (opacity < kMinAlpha) active = false;
         const f3 s = ld3(scales, idx);
-        const float vx = det_exp(2.0f * s.x), vy = det_exp(2.0f * s.y), vz = det_exp(2.0f * s.z);
+        const float vx = expf(2.0f * s.x), vy = expf(2.0f * s.y), vz = expf(2.0f * s.z);
         const float4 q = reinterpret_cast<const float4*>(rotations)[idx];
         float nsq;
         const Mat3 R = quat_to_rot(q.x, q.y, q.z, q.w, nsq);
@@ -156,7 +166,7 @@ __device__ inline Geometry project_primitive(const float* __restrict__ means, co
     float thr = 0.0f;
     uint32_t n_max = 0;
     if (active) {
-        thr = det_log(opacity * kMinAlphaRcp);
+        thr = logf(opacity * kMinAlphaRcp);
         const float cutoff = 2.0f * thr;
         const float ex = fmaxf(sqrtf(a * cutoff) - 0.5f, 0.0f);
         const float ey = fmaxf(sqrtf(c * cutoff) - 0.5f, 0.0f);

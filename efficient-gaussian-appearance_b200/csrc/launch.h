@@ -44,7 +44,7 @@ struct TileBuffers {
     uint32_t* n_contrib;    // [T * 192]
 };
 cudaError_t launch_emit(const Record* sorted_rec, const uint32_t* inst_off, void* keys, uint32_t* vals, uint32_t n_visible,
-                        int grid_w, bool wide, cudaStream_t s);
+                        int grid_w, bool wide, uint64_t n_instances, cudaStream_t s);
 cudaError_t launch_ranges(const void* keys, uint64_t n_instances, bool wide, const TileBuffers& T, int n_tiles, cudaStream_t s);
 
 // blend.cu

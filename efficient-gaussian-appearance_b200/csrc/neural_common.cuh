@@ -43,36 +43,42 @@ __host__ __device__ inline MlpShape mlp_shape(const AppearanceConfig& A) {
 }
 
 // SH band values of the MLP's direction input (bands 0..3 selected by mask; band l >= 1 is zero unless it is among
-// the first `deg` selected bands), passed to out(k, value) in input order; returns the number written
+// the first `deg` selected bands), passed to out(k, value) in input order; returns the number written. Every product
+// and sum is an explicit single-rounding operation (this file is compiled with contraction), so the values, and the
+// fp16 inputs rounded from them, are the oracle's bit for bit.
 template <typename Out>
 __device__ inline int sh_band_values(int mask, int deg, f3 d, Out&& out) {
     const float x = d.x, y = d.y, z = d.z;
-    const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z;
+    const float xx = __fmul_rn(x, x), yy = __fmul_rn(y, y), zz = __fmul_rn(z, z);
+    const float xy = __fmul_rn(x, y), xz = __fmul_rn(x, z), yz = __fmul_rn(y, z);
     int o = 0, rank = 0;
     if (mask & 1) out(o++, kShC0);
     if (mask & 2) {
         const float m = rank++ < deg ? 1.0f : 0.0f;
-        out(o++, m * (-kShC1 * y));
-        out(o++, m * (kShC1 * z));
-        out(o++, m * (-kShC1 * x));
+        out(o++, __fmul_rn(m, __fmul_rn(-kShC1, y)));
+        out(o++, __fmul_rn(m, __fmul_rn(kShC1, z)));
+        out(o++, __fmul_rn(m, __fmul_rn(-kShC1, x)));
     }
     if (mask & 4) {
         const float m = rank++ < deg ? 1.0f : 0.0f;
-        out(o++, m * (kShC2a * xy));
-        out(o++, m * (-kShC2a * yz));
-        out(o++, m * (kShC2b * zz - kShC2c));
-        out(o++, m * (-kShC2a * xz));
-        out(o++, m * (kShC2d * xx - kShC2d * yy));
+        out(o++, __fmul_rn(m, __fmul_rn(kShC2a, xy)));
+        out(o++, __fmul_rn(m, __fmul_rn(-kShC2a, yz)));
+        out(o++, __fmul_rn(m, __fsub_rn(__fmul_rn(kShC2b, zz), kShC2c)));
+        out(o++, __fmul_rn(m, __fmul_rn(-kShC2a, xz)));
+        out(o++, __fmul_rn(m, __fsub_rn(__fmul_rn(kShC2d, xx), __fmul_rn(kShC2d, yy))));
     }
     if (mask & 8) {
         const float m = rank++ < deg ? 1.0f : 0.0f;
-        out(o++, m * (0.59004358992664352f * y * (-3.0f * xx + yy)));
-        out(o++, m * (2.8906114426405538f * xy * z));
-        out(o++, m * (0.45704579946446572f * y * (1.0f - 5.0f * zz)));
-        out(o++, m * (0.3731763325901154f * z * (5.0f * zz - 3.0f)));
-        out(o++, m * (0.45704579946446572f * x * (1.0f - 5.0f * zz)));
-        out(o++, m * (1.4453057213202769f * z * (xx - yy)));
-        out(o++, m * (0.59004358992664352f * x * (-xx + 3.0f * yy)));
+        const float A = 0.59004358992664352f, B = 2.8906114426405538f, C = 0.45704579946446572f;
+        const float D = 0.3731763325901154f, E = 1.4453057213202769f;
+        const float one_5zz = __fsub_rn(1.0f, __fmul_rn(5.0f, zz));
+        out(o++, __fmul_rn(m, __fmul_rn(__fmul_rn(A, y), __fadd_rn(__fmul_rn(-3.0f, xx), yy))));
+        out(o++, __fmul_rn(m, __fmul_rn(__fmul_rn(B, xy), z)));
+        out(o++, __fmul_rn(m, __fmul_rn(__fmul_rn(C, y), one_5zz)));
+        out(o++, __fmul_rn(m, __fmul_rn(__fmul_rn(D, z), __fsub_rn(__fmul_rn(5.0f, zz), 3.0f))));
+        out(o++, __fmul_rn(m, __fmul_rn(__fmul_rn(C, x), one_5zz)));
+        out(o++, __fmul_rn(m, __fmul_rn(__fmul_rn(E, z), __fsub_rn(xx, yy))));
+        out(o++, __fmul_rn(m, __fmul_rn(__fmul_rn(A, x), __fadd_rn(-xx, __fmul_rn(3.0f, yy)))));
     }
     return o;
 }
@@ -119,12 +125,14 @@ __device__ inline f3 sh_band_grad(int mask, int deg, f3 d, const float* g) {
     return r;
 }
 
+// unit view direction from the camera to m (and 1 / distance), in explicit single-rounding IEEE operations: the MLP's
+// SH inputs depend on it bit for bit
 __device__ inline f3 view_dir(const View& v, f3 m, float* rn_out) {
-    const f3 cam = mk3(v.cam_pos[0], v.cam_pos[1], v.cam_pos[2]);
-    const f3 dv = m - cam;
-    const float rn = rnorm3(dv);
+    const f3 dv = mk3(__fsub_rn(m.x, v.cam_pos[0]), __fsub_rn(m.y, v.cam_pos[1]), __fsub_rn(m.z, v.cam_pos[2]));
+    const float d2 = __fadd_rn(__fadd_rn(__fmul_rn(dv.x, dv.x), __fmul_rn(dv.y, dv.y)), __fmul_rn(dv.z, dv.z));
+    const float rn = __fdiv_rn(1.0f, __fsqrt_rn(fmaxf(d2, 1e-24f)));
     if (rn_out) *rn_out = rn;
-    return rn * dv;
+    return mk3(__fmul_rn(rn, dv.x), __fmul_rn(rn, dv.y), __fmul_rn(rn, dv.z));
 }
 
 // store, or add with a reduction (one addition per element and launch: deterministic, no load on the critical path)

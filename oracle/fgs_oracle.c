@@ -149,6 +149,20 @@ static float det_log_f(float x) {
 #define DLOG(x) log(x)
 #endif
 
+/* Fragment acceptance of the blend (kernels_forward.cuh:119-127 with the conic folded by -0.5 log2(e) and -log2(e),
+ * kernels_common.cuh:13-17): base-2 exponent in the operation order the reference's build evaluates it with, the
+ * Gaussian 2^min(e, 0), alpha = opacity * Gaussian, and the fragment is skipped when alpha < 1/255. The kernels take
+ * the power of two from the GPU's exp2; this restatement takes it from the host's exp2 in double, rounded to the
+ * working precision, so a fragment whose alpha lies within a rounding of 1/255 can be decided differently. Returns
+ * alpha, or -1 for a skipped fragment. */
+static inline real fragment_alpha_r(real opacity, real ca, real cb, real cc, real dx, real dy) {
+    const real kh = (real)(-0.5f * 1.44269504089f), kc = (real)(-1.44269504089f);
+    const real hx = kh * ca, hy = kc * cb, hz = kh * cc;
+    const real ex = RFMA(hz * dy, dy, dx * RFMA(hx, dx, hy * dy));
+    const real alpha = opacity * (real)exp2((double)fmin(ex, R(0.0)));
+    return alpha < (real)(1.0f / 255.0f) ? R(-1.0) : alpha;
+}
+
 /* ------------------------------------------------------------------------------------------------ */
 /* appearance models                                                                                 */
 
@@ -265,16 +279,19 @@ static int tile_overlaps_r(real mx, real my, real cx, real cy, real cz, uint32_t
     const real ya = ymd >= R(0.0) ? R(1.0) : R(0.0);
     const real ny = ya + (my > rmaxy ? R(1.0) : R(0.0));
     if (ny + nx == R(0.0)) return 1;
-    const real kx = rmaxx + xl * (rminx - rmaxx);
-    const real ky = rmaxy + ya * (rminy - rmaxy);
+    /* the kernels' single-rounding operations (geometry.cuh tile_overlaps); their divisions are the GPU build's */
+    const real kx = RFMA(xl, rminx - rmaxx, rmaxx);
+    const real ky = RFMA(ya, rminy - rmaxy, rmaxy);
     const real dfx = mx - kx, dfy = my - ky;
     const real dx = copysign((real)(TILE_W - 1), xmd);
     const real dy = copysign((real)(TILE_H - 1), ymd);
-    const real tx_ = ny * sat_r((dx * cx * dfx + dx * cy * dfy) / (dx * cx * dx));
-    const real ty_ = nx * sat_r((dy * cy * dfx + dy * cz * dfy) / (dy * cz * dy));
-    const real px = kx + tx_ * dx, py = ky + ty_ * dy;
+    const real dxcx = dx * cx, dycz = dy * cz;
+    const real tx_ = ny * sat_r(RFMA(dxcx, dfx, (dx * cy) * dfy) / (dxcx * dx));
+    const real ty_ = nx * sat_r(RFMA(dy * cy, dfx, dycz * dfy) / (dycz * dy));
+    const real px = RFMA(tx_, dx, kx), py = RFMA(ty_, dy, ky);
     const real ex = mx - px, ey = my - py;
-    const real maxp = R(0.5) * (cx * ex * ex + cz * ey * ey) + cy * ex * ey;
+    const real inner = RFMA(cx * ex, ex, (cz * ey) * ey);
+    const real maxp = RFMA(cy * ex, ey, R(0.5) * inner);
     return maxp <= thr;
 }
 
@@ -574,10 +591,8 @@ int orc_blend(int64_t n_visible, const uint32_t* sorted_idx, const double* rec, 
                 rec_of(rec, sorted_idx[ranks[j]], &q);
                 if (!overlaps_subtile(&q, sx0, sy0)) continue;
                 const real dx = q.mx - pxf, dy = q.my - pyf;
-                const real hx = R(-0.5) * q.ca, hy = -q.cb, hz = R(-0.5) * q.cc;
-                const real ex = RFMA(dx, RFMA(hx, dx, hy * dy), (hz * dy) * dy);
-                if (ex < -q.thr) continue;
-                const real alpha = q.opacity * DEXP_BLEND(fmin(ex, R(0.0)));
+                const real alpha = fragment_alpha_r(q.opacity, q.ca, q.cb, q.cc, dx, dy);
+                if (alpha < R(0.0)) continue;
                 const real w = tr * alpha;
                 cr = RFMA(w, q.r, cr);
                 cg = RFMA(w, q.g, cg);
@@ -640,8 +655,7 @@ int orc_blend_backward(int64_t n_visible, const uint32_t* sorted_idx, const doub
                 if (!overlaps_subtile(&q, sx0, sy0)) continue;
                 const real pxf = (real)px + R(0.5), pyf = (real)py + R(0.5);
                 const real dxr = q.mx - pxf, dyr = q.my - pyf;
-                const real ex = RFMA(dxr, RFMA(R(-0.5) * q.ca, dxr, -q.cb * dyr), (R(-0.5) * q.cc * dyr) * dyr);
-                if (ex < -q.thr) continue;
+                if (fragment_alpha_r(q.opacity, q.ca, q.cb, q.cc, dxr, dyr) < R(0.0)) continue;
                 const double* o = rec + 14 * (size_t)sorted_idx[ranks[j]];
                 const double dx = o[0] - ((double)px + 0.5), dy = o[1] - ((double)py + 0.5);
                 const double e = -0.5 * (o[4] * dx * dx + o[6] * dy * dy) - o[5] * dx * dy;
@@ -746,8 +760,7 @@ int orc_pruning_scores(int64_t n_visible, const uint32_t* sorted_idx, const doub
                 if (!overlaps_subtile(&q, sx0, sy0)) continue;
                 const real pxf = (real)px + R(0.5), pyf = (real)py + R(0.5);
                 const real dxr = q.mx - pxf, dyr = q.my - pyf;
-                const real ex = RFMA(dxr, RFMA(R(-0.5) * q.ca, dxr, -q.cb * dyr), (R(-0.5) * q.cc * dyr) * dyr);
-                if (ex < -q.thr) continue;
+                if (fragment_alpha_r(q.opacity, q.ca, q.cb, q.cc, dxr, dyr) < R(0.0)) continue;
                 const double* o = rec + 14 * (size_t)pi;
                 const double dx = o[0] - ((double)px + 0.5), dy = o[1] - ((double)py + 0.5);
                 const double e = -0.5 * (o[4] * dx * dx + o[6] * dy * dy) - o[5] * dx * dy;
@@ -840,6 +853,9 @@ int orc_preprocess_backward(const orc_appearance* A, const orc_view* v, int64_t 
             const v3_d dv = sub_d(m, mk_d(v->cam[0], v->cam[1], v->cam[2]));
             const double rn = 1.0 / sqrt(fmax(dot_d(dv, dv), 1e-24));
             const v3_d d = scl_d(rn, dv);
+            /* the direction as the forward computed it (working precision), for the Neural inputs */
+            const v3_r dv_r = sub_r(mk_r(means[3 * i], means[3 * i + 1], means[3 * i + 2]), mk_r(v->cam[0], v->cam[1], v->cam[2]));
+            const v3_r d_r = scl_r(R(1.0) / sqrt(fmax(dot_r(dv_r, dv_r), R(1e-24))), dv_r);
             const int deg = v->degree < A->max_degree ? v->degree : A->max_degree;
             const inreal* rp = residual ? residual + (size_t)i * stride : 0;
             double local[128];
@@ -850,7 +866,7 @@ int orc_preprocess_backward(const orc_appearance* A, const orc_view* v, int64_t 
                 case 2: gd = sv_backward_d(rp, gpre, d, deg, A->res_act, local); break;
                 case 3: gd = lobes_backward_d(rp, gpre, d, deg, A->res_act, 0, local); break;
                 case 4: gd = lobes_backward_d(rp, gpre, d, deg, A->res_act, 1, local); break;
-                case 5: gd = neural_backward_d(A, rp, base + 3 * i, gpre, d, deg, mlp, local, my_mlp, g_base + 3 * i); break;
+                case 5: gd = neural_backward_d(A, rp, base + 3 * i, gpre, d, d_r, deg, mlp, local, my_mlp, g_base + 3 * i); break;
                 default: break;
             }
             const int active = residual_active(A, deg);

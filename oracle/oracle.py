@@ -126,10 +126,12 @@ def make_appearance(model: str, max_degree: int = 0, base_act: int = 0, res_act:
 
 
 def run(app: Appearance, view: View, prims: dict, grad_image=None, double: bool = False, densification_rows: int = 0,
-        pruning: bool = False) -> dict:
+        pruning: bool = False, rank_grads=None) -> dict:
     """Runs the restated pipeline; prims holds numpy/torch arrays (means, scales, rotations, opacities and the
     appearance inputs). Returns intermediates, the image [3,H,W], with pruning the per-primitive pruning scores and,
-    with grad_image, all gradients."""
+    with grad_image, all gradients. With rank_grads ([V, 12] per depth rank of this run, in the blend backward's
+    layout {mean2d x, y, conic a, b, c, colour r, g, b, opacity, |mean2d x|, |mean2d y|, 0}) the backward preprocess
+    runs on those per-primitive blend sums instead of the restated blend backward."""
     lib = load(double)
     means, scales, rots, opac = (_in(prims[k], double) for k in ('means', 'scales', 'rotations', 'opacities'))
     pre = _in(prims.get('precomputed_colors'), double)
@@ -174,11 +176,14 @@ def run(app: Appearance, view: View, prims: dict, grad_image=None, double: bool 
         scores = np.zeros(max(n, 1), np.float64)
         lib.orc_pruning_scores(V, _p(sorted_idx), _p(rec), _p(ranks), _p(ranges), ctypes.byref(view), _p(n_contrib), _p(scores))
         out['pruning_scores'] = scores[:n]
-    if grad_image is None:
+    if grad_image is None and rank_grads is None:
         return out
-    gimg = _f32(grad_image)
     grads = np.zeros((max(V, 1), 12), np.float64)
-    lib.orc_blend_backward(V, _p(sorted_idx), _p(rec), _p(ranks), _p(ranges), ctypes.byref(view), _p(n_contrib), _p(gimg), _p(grads))
+    if rank_grads is not None:
+        grads[:V] = np.asarray(rank_grads, np.float64).reshape(V, 12)
+    else:
+        gimg = _f32(grad_image)
+        lib.orc_blend_backward(V, _p(sorted_idx), _p(rec), _p(ranks), _p(ranges), ctypes.byref(view), _p(n_contrib), _p(gimg), _p(grads))
     rank_of = np.full(n, 0xffffffff, np.uint32)
     rank_of[sorted_idx] = np.arange(V, dtype=np.uint32)
     stride = res.shape[1] if res is not None and res.ndim == 2 else (int(np.prod(res.shape[1:])) if res is not None else 0)

@@ -105,45 +105,98 @@ def oracle_records_in_rank_order(o: dict) -> np.ndarray:
     return o['records'][o['sorted_idx']]
 
 
-def compare_forward(g, o, exact_image):
-    """Every forward stage of a GPU run (gpu_forward_stages) against an oracle run: integer stages, geometry fields
-    and contributor counts bit for bit; colors, image and transmittance bit for bit when `exact_image`, else within
-    1e-5 relative (colors), 1e-4 max abs (image) and 1e-6 (transmittance)."""
-    assert g['n_visible'] == o['n_visible']
-    assert g['n_instances'] == o['n_instances']
-    np.testing.assert_array_equal(g['n_touched'], o['n_touched'])
-    vis = o['n_touched'] > 0
-    np.testing.assert_array_equal(g['depth_key'][vis], o['depth_key'][vis])
-    np.testing.assert_array_equal(g['sorted_idx'], o['sorted_idx'])
-    np.testing.assert_array_equal(g['instance_offsets'], o['instance_offsets'])
-    np.testing.assert_array_equal(g['tile_keys'], o['tile_keys'])
-    np.testing.assert_array_equal(g['ranks'], o['ranks'])
-    np.testing.assert_array_equal(g['ranges'], o['ranges'])
-    # bucket offsets: inclusive scan of ceil(tile list length / 32) (kernels_forward.cuh:14-24, forward.cu:204-219)
-    lengths = o['ranges'][:, 1].astype(np.int64) - o['ranges'][:, 0].astype(np.int64)
+def compare_forward(g, o, image_max=5e-2, flips=1e-3):
+    """Every forward stage of a GPU run (gpu_forward_stages) against the oracle's C restatement. The kernels evaluate
+    the projection, tile test and fragment acceptance with the reference build's fast-math arithmetic (approximate
+    division, square root, exp, log and exp2; bit for bit the reference's, tests/test_gpu_reference.py), which a C
+    program cannot reproduce, while the restatement uses IEEE arithmetic; the two agree within rounding, and a decision
+    that sits within a rounding of its threshold (a culled primitive, a tile at the edge of a footprint, a fragment at
+    alpha = 1/255) can go either way, which changes a pixel by up to the fragment's share of it. Bounds: visible and
+    instance counts and tiles touched per primitive differ on at most a fraction `flips` of the primitives; for
+    primitives visible on both sides the screen means agree within 1e-3 px, conics within 1e-3 of their magnitude,
+    opacities within 1e-5, colours within 1e-4 relative; the depth order agrees wherever the depth keys and visibility
+    do; contributor counts differ on at most a fraction `flips` of the pixels; the image within 5e-6 mean-abs, with at
+    most a fraction `flips` of the pixels off by more than 1e-4 and none by more than `image_max` (a flipped fragment
+    has alpha near 1/255 and moves its pixel by at most that share of a colour difference). Returns the measured
+    figures."""
+    n = len(o['n_touched'])
+    tol = 2 + flips * n
+    m = {'visible': (g['n_visible'], o['n_visible']), 'instances': (g['n_instances'], o['n_instances']),
+         'touched_mismatch': int((g['n_touched'] != o['n_touched']).sum())}
+    assert abs(g['n_visible'] - o['n_visible']) <= tol, m
+    assert abs(g['n_instances'] - o['n_instances']) <= 10 + flips * max(o['n_instances'], 1), m
+    assert m['touched_mismatch'] <= tol, m
+    both = (g['n_touched'] > 0) & (o['n_touched'] > 0)
+    if both.any():
+        rec_g = np.zeros((n, 12), np.float32)
+        rec_g[g['sorted_idx']] = g['records']
+        rec_o = o['records']
+        m['mean2d'] = float(np.abs(rec_g[both, 0:2] - rec_o[both, 0:2]).max())
+        cg, co = rec_g[both, 4:7].astype(np.float64), rec_o[both, 4:7]
+        m['conic'] = float((np.abs(cg - co).max(1) / np.maximum(np.abs(co[:, 0]), np.abs(co[:, 2]))).max())
+        m['opacity'] = float(np.abs(rec_g[both, 2] - rec_o[both, 2]).max())
+        colo = rec_o[both, 7:10]
+        m['colour'] = float(np.abs(rec_g[both, 8:11].astype(np.float64) - colo).max() / max(1.0, np.abs(colo).max()))
+        assert m['mean2d'] <= 1e-3 and m['conic'] <= 1e-3 and m['opacity'] <= 1e-5 and m['colour'] <= 1e-4, m
+    if np.array_equal(g['depth_key'][both], o['depth_key'][both]) and np.array_equal(g['n_touched'] > 0, o['n_touched'] > 0):
+        np.testing.assert_array_equal(g['sorted_idx'], o['sorted_idx'])
+    # bucket offsets: inclusive scan of ceil(tile list length / 32) of this run's own ranges (kernels_forward.cuh:14-24)
+    lengths = g['ranges'][:, 1].astype(np.int64) - g['ranges'][:, 0].astype(np.int64)
     np.testing.assert_array_equal(g['bucket_off'], np.cumsum((lengths + 31) // 32).astype(np.uint32))
-    rec_o = oracle_records_in_rank_order(o)
-    rec_g = g['records']
-    # geometry fields bit-exact: mean2d, opacity, power threshold, conic, bounds
-    for gi, oi in ((0, 0), (1, 1), (2, 2), (3, 3), (4, 4), (5, 5), (6, 6)):
-        np.testing.assert_array_equal(rec_g[:, gi], rec_o[:, oi].astype(np.float32))
-    bx = rec_g[:, 7].view(np.uint32)
-    by = rec_g[:, 11].view(np.uint32)
-    np.testing.assert_array_equal(bx & 0xffff, rec_o[:, 10].astype(np.uint32))
-    np.testing.assert_array_equal(bx >> 16, rec_o[:, 11].astype(np.uint32))
-    np.testing.assert_array_equal(by & 0xffff, rec_o[:, 12].astype(np.uint32))
-    np.testing.assert_array_equal(by >> 16, rec_o[:, 13].astype(np.uint32))
-    np.testing.assert_array_equal(g['n_contrib'], o['n_contrib'])
-    colors_g = rec_g[:, 8:11]
-    colors_o = rec_o[:, 7:10].astype(np.float32)
+    m['contrib_mismatch'] = float((g['n_contrib'] != o['n_contrib']).mean())
+    d = np.abs(g['image'] - o['image'])
+    m['image_mean'], m['image_max'], m['pixels_over_1e-4'] = float(d.mean()), float(d.max()), float((d.max(0) > 1e-4).mean())
+    print('\n[vs oracle]', m)
+    assert m['contrib_mismatch'] <= flips and m['pixels_over_1e-4'] <= flips, m
+    assert m['image_mean'] <= 5e-6 and m['image_max'] <= image_max, m
+    return m
+
+
+def assert_matches_reference(g, r, img_ref, exact_image=False, image_max=2e-6):
+    """This library's forward stages (gpu_forward_stages) against the reference's own kernels run on the same inputs
+    (oracle/reference.py buffers()): visible and instance counts, tiles touched per primitive, screen means, conics and
+    opacities bit for bit; every tile's list of primitives bit for bit once the reference's order of equal-depth
+    primitives is made canonical (its compaction orders depth ties by atomic scheduling; this library by primitive
+    index); contributor counts and final transmittance bit for bit outside the tiles where such a tie reordered the
+    list; the image bit for bit there (`exact_image`, identical colours) or within `image_max` (colours evaluated in
+    another order). Returns the number of tiles whose raw lists differ only in the order of depth ties, and the [H, W]
+    mask of the pixels outside them."""
+    n = len(g['n_touched'])
+    assert g['n_visible'] == r['n_visible'] and g['n_instances'] == r['n_instances'], \
+        ((g['n_visible'], r['n_visible']), (g['n_instances'], r['n_instances']))
+    np.testing.assert_array_equal(g['n_touched'], r['n_touched'], err_msg='tiles touched per primitive')
+    vis = g['n_touched'] > 0
+    rec = np.zeros((n, 12), np.float32)
+    rec[g['sorted_idx']] = g['records']
+    np.testing.assert_array_equal(rec[vis, 0:2], r['mean2d'][vis], err_msg='screen means')
+    np.testing.assert_array_equal(rec[vis, 4:7], r['conic_opacity'][vis, 0:3], err_msg='conics')
+    np.testing.assert_array_equal(rec[vis, 2], r['conic_opacity'][vis, 3], err_msg='opacities')
+    np.testing.assert_array_equal(g['ranges'], r['ranges'], err_msg='tile ranges')
+    mine = g['sorted_idx'][g['ranks']] if g['n_instances'] else np.zeros(0, np.uint32)
+    theirs = r['instance_prims']
+    key = g['depth_key'].astype(np.uint64)
+    tie_tiles = []
+    for t, (a, b) in enumerate(g['ranges']):
+        if a == b or np.array_equal(mine[a:b], theirs[a:b]):
+            continue
+        lst = theirs[a:b]
+        canon = lst[np.lexsort((lst, key[lst]))]
+        np.testing.assert_array_equal(mine[a:b], canon, err_msg=f'tile {t}')
+        tie_tiles.append(t)
+    H, W = g['image'].shape[1:]
+    gw = (W + 15) // 16
+    mask = np.ones((H, W), bool)
+    for t in tie_tiles:
+        ty, tx = divmod(t, gw)
+        mask[ty * 12:(ty + 1) * 12, tx * 16:(tx + 1) * 16] = False
+    np.testing.assert_array_equal(g['n_contrib'][mask], r['n_contrib'][mask], err_msg='contributor counts')
+    np.testing.assert_array_equal(g['final_T'][mask], r['final_T'][mask], err_msg='final transmittance')
+    ref = img_ref.cpu().numpy() if hasattr(img_ref, 'cpu') else img_ref
     if exact_image:
-        np.testing.assert_array_equal(colors_g, colors_o)
-        np.testing.assert_array_equal(g['image'], o['image'])
-        np.testing.assert_array_equal(g['final_T'], o['final_T'])
+        np.testing.assert_array_equal(g['image'][:, mask], ref[:, mask], err_msg='image')
     else:
-        assert np.abs(colors_g - colors_o).max() <= 1e-5 * max(1.0, np.abs(colors_o).max())
-        assert np.abs(g['image'] - o['image']).max() <= 1e-4
-        assert np.abs(g['final_T'] - o['final_T']).max() <= 1e-6
+        assert np.abs(g['image'][:, mask] - ref[:, mask]).max() <= image_max
+    return len(tie_tiles), mask
 
 
 def gpu_colors_by_primitive(g: dict, n: int) -> np.ndarray:

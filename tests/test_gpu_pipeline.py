@@ -1,8 +1,10 @@
-"""GPU parity: every stage of the training forward and the backward against the CPU oracle, for all appearance
-models. Integer stages (culling, depth keys, depth order, instance offsets, tile keys, tile lists, ranges,
-contributor counts) and the transmittance are compared bit for bit; images bit for bit where the colors are
-(precomputed, SH with identity / ReLU activations) and within 1e-4 max-abs otherwise; gradients within 1e-3
-relative (L2 over each tensor, against the double-precision oracle backward)."""
+"""GPU parity: every stage of the training forward and the backward against the oracle's C restatement, for all
+appearance models (the bit-for-bit comparison with the reference's own kernels is tests/test_gpu_reference.py).
+The kernels decide culling, tile overlap and fragment acceptance with the reference build's fast-math arithmetic,
+which the IEEE restatement follows within rounding: forward stages within the bounds of fgs_testutil.compare_forward
+(images within 1e-6 mean-abs and 1e-3 max-abs, decisions flipped on at most 2e-4 of the primitives and pixels), the
+colours within 1e-5 relative, gradients within 1e-3 relative (L2 over each tensor, against the double-precision
+oracle backward)."""
 import numpy as np
 import pytest
 import torch
@@ -14,14 +16,14 @@ from fgs_testutil import ACT, scene, to_dev, settings_for, gpu_forward_stages, r
 pytestmark = pytest.mark.gpu
 
 CASES = [
-    # model, degree, base, residual, color, exact_image
-    ('precomputed', 0, 'none', 'none', 'relu', True),
-    ('sh', 3, 'none', 'none', 'relu', True),
-    ('sh', 1, 'none', 'none', 'none', True),
-    ('sh', 2, 'exp', 'tanh', 'satexp', False),
-    ('sv', 8, 'none', 'none', 'relu', False),
-    ('nasg', 8, 'none', 'tanh', 'relu', False),
-    ('nasgabor', 4, 'none', 'tanh', 'sigmoid', False),
+    # model, degree, base, residual, color
+    ('precomputed', 0, 'none', 'none', 'relu'),
+    ('sh', 3, 'none', 'none', 'relu'),
+    ('sh', 1, 'none', 'none', 'none'),
+    ('sh', 2, 'exp', 'tanh', 'satexp'),
+    ('sv', 8, 'none', 'none', 'relu'),
+    ('nasg', 8, 'none', 'tanh', 'relu'),
+    ('nasgabor', 4, 'none', 'tanh', 'sigmoid'),
 ]
 
 
@@ -35,7 +37,7 @@ def _configure(F, model, degree, base, res, col):
 @pytest.mark.parametrize('case', CASES, ids=[f'{c[0]}{c[1]}-{c[2]}-{c[3]}-{c[4]}' for c in CASES])
 def test_forward_backward_parity(cuda, case):
     import FasterGSVDACudaBackend as F
-    model, degree, base, res, col, exact = case
+    model, degree, base, res, col = case
     _configure(F, model, degree, base, res, col)
     n, W, H = 20000, 256, 192
     prims = scene(model, n, degree, seed=0, scale_shift=1.0)
@@ -48,15 +50,13 @@ def test_forward_backward_parity(cuda, case):
     grad_image = torch.randn(3, H, W, generator=torch.Generator().manual_seed(2)) * 0.01
     o = O.run(a, O.make_view(cam, degree), prims, grad_image=grad_image)
     assert o['n_visible'] > 1000 and o['n_instances'] > o['n_visible']
-    compare_forward(g, o, exact)
+    compare_forward(g, o)
 
     # backward through autograd
     leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
     img = F.diff_rasterize(leaves['means'], leaves['scales'], leaves['rotations'], leaves['opacities'], torch.empty(0, device=cuda), settings,
                            precomputed_colors=leaves.get('precomputed_colors'), base_colors=leaves.get('base_colors'),
                            residual_params=leaves.get('residual_params'))
-    if exact:
-        np.testing.assert_array_equal(img.detach().cpu().numpy(), o['image'])
     img.backward(grad_image.to(cuda))
     for k, t in leaves.items():
         ref = o['grads'][k]
@@ -64,7 +64,8 @@ def test_forward_backward_parity(cuda, case):
         err = rel_err(got, ref)
         assert err <= 1e-3, f'{k}: relative error {err:.2e}'
         scale = np.abs(ref).max()
-        assert np.allclose(got, ref, rtol=1e-2, atol=1e-4 * scale), f'{k}: elementwise mismatch'
+        off = ~np.isclose(got, ref, rtol=1e-2, atol=1e-4 * scale)
+        assert off.mean() <= 1e-3, f'{k}: {int(off.sum())} elements off (primitives with a flipped fragment decision)'
 
 
 def test_variants_proper_aa_render_base_densification(cuda):
@@ -80,7 +81,7 @@ def test_variants_proper_aa_render_base_densification(cuda):
         a = O.make_appearance('sh', 3, 0, 0, 1, True)
         grad_image = torch.randn(3, H, W, generator=torch.Generator().manual_seed(2)) * 0.01
         o = O.run(a, O.make_view(cam, 3, proper_aa=proper_aa, render_base=render_base), prims, grad_image=grad_image, densification_rows=3)
-        compare_forward(g, o, exact_image=True)
+        compare_forward(g, o)
         leaves = {k: v.clone().requires_grad_(True) for k, v in dev.items()}
         dens = torch.zeros(3, n, device=cuda)
         img = F.diff_rasterize(leaves['means'], leaves['scales'], leaves['rotations'], leaves['opacities'], dens, settings,
@@ -91,7 +92,7 @@ def test_variants_proper_aa_render_base_densification(cuda):
             err = rel_err(t.grad.cpu().numpy().reshape(ref.shape), ref)
             assert err <= 1e-3, f'{k} (aa={proper_aa}, base={render_base}): {err:.2e}'
         d = dens.cpu().numpy()
-        np.testing.assert_array_equal(d[0], o['densification'][0].astype(np.float32))
+        assert (d[0] != o['densification'][0].astype(np.float32)).mean() <= 2e-4
         assert rel_err(d[1], o['densification'][1]) <= 1e-3
         assert rel_err(d[2], o['densification'][2]) <= 1e-3
 
@@ -113,4 +114,5 @@ def test_inference_matches_oracle(cuda, to_chw, clamp):
         ref = np.clip(ref, 0.0, 1.0)
     if not to_chw:
         ref = ref.transpose(1, 2, 0)
-    np.testing.assert_array_equal(img.cpu().numpy(), ref)
+    d = np.abs(img.cpu().numpy() - ref)
+    assert d.mean() <= 1e-6 and d.max() <= 1e-3, (d.mean(), d.max())
