@@ -35,16 +35,25 @@ import torch
 
 WORKLOADS = {
     'c1': dict(n=1_000_000, width=1280, height=720, model='sh', degree=3, views=1),
+    'c2': dict(n=1_000_000, width=1264, height=832, model='neural', degree=3, views=1, feature_dim=32, n_freq=1, neurons=64, hidden=2),
+    # the paper's default network (550 of the reference's 559 paper configurations): 8 features, 1 octave, 2 x 16 hidden
+    'c2paper': dict(n=1_000_000, width=1264, height=832, model='neural', degree=3, views=1, feature_dim=8, n_freq=1, neurons=16, hidden=2),
     'c4': dict(n=6_000_000, width=1920, height=1080, model='neural', degree=3, views=8, feature_dim=32, n_freq=1, neurons=64, hidden=2),
     'c3': dict(n=3_000_000, width=1920, height=1080, model='nasg', degree=8, views=64),
     'c3sv': dict(n=3_000_000, width=1920, height=1080, model='sv', degree=8, views=64),
 }
 C1_LRS = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 'base_colors': 0.000705237, 'residual_params': 0.000125}
+C2_LRS = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 'base_colors': 0.00025, 'residual_params': 0.008,
+          'mlp_weights': 0.003}
+SINGLE_VIEW = ('c1', 'c2', 'c2paper')
 C4_LRS = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 'base_colors': 0.00025, 'residual_params': 0.008,
           'mlp_weights': 0.003}
 RENDER = ('c3', 'c3sv')
 METRIC = {'c3': 'render FPS (inference, NASG 8 lobes, 3M Gaussians, 64 ring views @1920x1080, views sharded over the GPUs)',
-          'c3sv': 'render FPS (inference, Spherical Voronoi 8 sites, 3M Gaussians, 64 ring views @1920x1080, views sharded over the GPUs)','c1': 'train steps/s (forward + backward + fused Adam), fused SH-3 appearance, 1M Gaussians @1280x720',
+          'c3sv': 'render FPS (inference, Spherical Voronoi 8 sites, 3M Gaussians, 64 ring views @1920x1080, views sharded over the GPUs)',
+          'c1': 'train steps/s (forward + backward + fused Adam), fused SH-3 appearance, 1M Gaussians @1280x720',
+          'c2': 'train steps/s (forward + backward + fused Adam), Neural appearance (32 features, 2x64 MLP), 1M Gaussians @1264x832',
+          'c2paper': 'train steps/s (forward + backward + fused Adam), Neural appearance (8 features, 2x16 MLP), 1M Gaussians @1264x832',
           'c4': 'train steps/s (8 views @1920x1080, forward + loss + backward + gradient reduce-scatter + sharded fused Adam + '
                 'parameter all-gather), Neural appearance, 6M Gaussians'}
 # this library's kernel launches per view: preprocess 1, compaction 4 (group sums, group scan, chunk offsets, compact),
@@ -61,6 +70,8 @@ def own_launches(wl_name: str, views: int) -> int:
         return RENDER_LAUNCHES_PER_VIEW * views
     if wl_name == 'c4':
         return (RENDER_LAUNCHES_PER_VIEW + 1 + 3 + 1 + 2) * views + 2
+    if WORKLOADS[wl_name]['model'] == 'neural':  # colour pass, blend backward, MLP backward + geometry + zeroing, Adam
+        return RENDER_LAUNCHES_PER_VIEW + 1 + 1 + 3 + 1
     return RENDER_LAUNCHES_PER_VIEW + 1 + 1 + 1
 
 
@@ -171,29 +182,110 @@ def settings_of(cam, degree: int, dev):
                                 cam.focal_y, cam.center_x, cam.center_y, cam.near_plane, cam.far_plane, False, True, True)
 
 
-# DRAM bytes (read + write) measured by ncu on the small c4 case (2M Gaussians in Morton order, one view: 945,337
-# visible rows, 3,455,846 instances; profiles/neural_tcgen05_small_case.md), as (bytes per visible row, bytes per
-# instance): backward preprocess = MLP backward 706.5 (it reads the colour pass's activation store) + geometry backward
-# 187.2 per visible row; blend backward 168.9 MB over the instances. Scaled by the view's visible rows and instances.
+# DRAM bytes (read + write) measured by ncu on the small c4 case (2M Gaussians in Morton order, one view), per visible
+# row and per instance: backward preprocess = MLP backward (it reads the colour pass's activation store) + geometry
+# backward, per visible row; blend backward over the instances. Scaled by the view's visible rows and instances.
 TRAFFIC_PER_UNIT = {('c4', 'preprocess_backward'): (706.5 + 187.2, 0.0), ('c4', 'blend_backward'): (0.0, 168885.0e3 / 3455846)}
+# how each stage is bound at these sizes (ncu): the blends issue-bound (8x4 subtile warps, one fragment per lane step),
+# the tensor-core MLP stages latency-bound on their per-tile MMA -> epilogue chains; the rest streams HBM
+BOUND = {'blend_forward': 'issue', 'blend_inference': 'issue', 'blend_backward': 'issue', 'appearance_mlp': 'latency',
+         'preprocess_backward': 'latency'}
 
 
 def stage_bytes(stage: str, s: dict) -> float:
-    """Algorithmic DRAM bytes of one occurrence of each stage per view (per-unit figures x the frame's units)."""
-    N, V, I, P, A = s['N'], s['V'], s['I'], s['pixels'], s['appearance_bytes']
-    if stage == 'preprocess':
-        return N * (44 + A) + N * 8 + V * 52
+    """Algorithmic DRAM bytes of one occurrence of each stage per view (per-unit figures x the frame's units): N
+    Gaussians, V visible, I instances, P pixels, A appearance bytes read per visible Gaussian by the fused preprocess
+    (0 for Neural, whose colour pass reads the latent), F latent floats, K key bytes (2 or 4), T tiles."""
+    N, V, I, P, A, F, K, T = s['N'], s['V'], s['I'], s['pixels'], s['appearance_bytes'], s['features'], s['key_bytes'], s['tiles']
+    neural = s['model'] == 'neural'
+    if stage == 'preprocess':  # geometry of every Gaussian, appearance of the visible ones; counts and keys, records
+        return N * 44 + (0 if neural else V * A) + N * 8 + V * 52
+    if stage == 'compaction':
+        return N * 8 + V * 8
+    if stage == 'appearance_mlp':  # index, mean, latent, base in; colour out; activation store (training) out
+        return V * (4 + 12 + 4 * F + 12 + 12) + V * s['store_bytes']
+    if stage == 'depth_sort':  # 4 passes of 8 bits over (key, value) pairs, read and written
+        return 4 * V * 16
+    if stage == 'reorder_scan':
+        return V * (48 + 48 + 12) + V * 12
+    if stage == 'emit':
+        return V * 52 + I * (K + 4)
+    if stage == 'tile_sort':
+        return 2 * I * (K + 4) * 2
+    if stage == 'ranges':
+        return I * K + T * 12
     if stage == 'blend_forward':
         return I * 52 + P * 20
     if stage == 'blend_inference':
         return I * 52 + P * 12
+    if stage == 'loss':
+        return 3 * P * 44
     if stage == 'blend_backward':
         return I * 52 + P * 32 + V * 48
     if stage == 'preprocess_backward':
-        return 2 * N * (44 + A) + N * 4 + V * 96
+        if neural:  # touched rows: MLP backward + geometry backward; zero gradients of the untouched rows
+            return V * (128 + 8 * F) + V * 192 + (N - V) * (56 + 4 * F) + N * 4
+        return N * 4 + V * (44 + A + 96) + N * (44 + A)
     if stage == 'adam':
         return 28 * s['params']
     return 0.0
+
+
+def stage_flops(stage: str, s: dict) -> float:
+    """Tensor-core FLOPs of the Neural MLP stages per view: 2 x (multiply-adds of every layer, the output padded to 16
+    rows) per visible row forward; twice that backward (data and weight gradients; the activations come from the store)."""
+    if s['model'] != 'neural':
+        return 0.0
+    if stage == 'appearance_mlp':
+        return s['V'] * s['mlp_flops']
+    if stage == 'preprocess_backward':
+        return 2.0 * s['V'] * s['mlp_flops']
+    return 0.0
+
+
+def frame_stats(wl: dict, n_visible: int, n_instances: int, n_params: int) -> dict:
+    """The per-view units the byte and FLOP counts scale with."""
+    model = wl['model']
+    stride = {'sh': 45, 'neural': wl.get('feature_dim', 0), 'nasg': 8 * wl['degree'], 'sv': 7 * wl['degree']}[model]
+    tiles = ((wl['width'] + 15) // 16) * ((wl['height'] + 11) // 12)
+    out = dict(N=wl['n'], V=n_visible, I=n_instances, pixels=wl['width'] * wl['height'], params=n_params, model=model,
+               appearance_bytes=0 if model == 'neural' else 12 + 4 * stride, features=wl.get('feature_dim', 0),
+               key_bytes=2 if tiles <= 65536 else 4, tiles=tiles, store_bytes=0, mlp_flops=0)
+    if model == 'neural':
+        nn, hidden = wl['neurons'], wl['hidden']
+        kin = (wl['feature_dim'] * 2 * wl['n_freq'] + 16 + 15) // 16 * 16
+        out['mlp_flops'] = 2 * (kin * nn + (hidden - 1) * nn * nn + nn * 16)
+        out['store_bytes'] = 128 * hidden + 8 if nn == 64 else 0  # the tensor-core kernels' activation store (training)
+    return out
+
+
+def static_config(wl_name: str, world: int, args, exchange_desc: str = 'none') -> dict:
+    """The workload description both arms print (no measured quantities)."""
+    wl = WORKLOADS[wl_name]
+    render, strong = wl_name in RENDER, wl_name == 'c4' or wl_name in RENDER
+    if render:
+        desc = f"{wl['model']}-{wl['degree']} {wl['n'] / 1e6:g}M Gaussians, {wl['views']} views {wl['width']}x{wl['height']}, inference, views sharded"
+    elif strong:
+        desc = f"Neural {wl['n'] / 1e6:g}M Gaussians, {wl['views']} views {wl['width']}x{wl['height']} global batch, data-parallel"
+    elif wl['model'] == 'neural':
+        desc = (f"Neural ({wl['feature_dim']} features, {wl['hidden']}x{wl['neurons']} MLP) {wl['n'] / 1e6:g}M Gaussians, 1 view "
+                f"{wl['width']}x{wl['height']} per GPU")
+    else:
+        desc = f"SH-3 {wl['n'] / 1e6:g}M Gaussians, 1 view {wl['width']}x{wl['height']} per GPU"
+    views_per_gpu = ((wl['views'] + world - 1) // world) if render else (wl['views'] // world if strong else 1)
+    return {'workload': f'{wl_name}: {desc}', 'n_gaussians': wl['n'], 'width': wl['width'], 'height': wl['height'], 'views_per_gpu': views_per_gpu,
+            'parallelism': (f'{world} GPU(s), views split, no collective' if render else
+                            f'dp{world} (reduce-scatter / sharded Adam / all-gather: {exchange_desc})' if strong else f'replicas x{world}'),
+            'l2': 'inputs larger than L2 (parameters alone exceed 126 MB)', 'gaussian_order': getattr(args, 'order', 'morton')}
+
+
+def _tensor_peak() -> float:
+    """Sustained dense bf16/fp16 tensor TFLOP/s of this pool's B200s (the MLP stages run inside a long step)."""
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get('bf16_tflops_sustained', d.get('bf16_tflops', 1400.0)))
+    return 1400.0
 
 
 # ------------------------------------------------------------------------------------------------------------
@@ -275,7 +367,7 @@ def run_b200(args, wl_name: str) -> dict | None:
         settings = [settings_of(cams[v], wl['degree'], dev) for v in mine]
         tg_host = [t.pin_memory() for t in [targets(wl)[v] for v in mine]]
         tg_dev = [t.to(dev) for t in tg_host]
-        n_params = trainer.shard  # parameters this rank's Adam updates
+        n_params = trainer.shard + (trainer.mlp.numel if trainer.mlp_moments is not None else 0)  # parameters this rank's Adam updates
 
         def step():
             return trainer.step(settings, tg_dev)
@@ -304,7 +396,9 @@ def run_b200(args, wl_name: str) -> dict | None:
         cam = cams[rank % len(cams)]
         s0 = settings_of(cam, wl['degree'], dev)
         params = {k: torch.nn.Parameter(v.to(dev).contiguous()) for k, v in prims.items()}
-        opt = F.FusedAdam([{'params': [params[k]], 'lr': lr} for k, lr in C1_LRS.items()], lr=0.0, eps=1e-15)
+        lrs = C1_LRS if wl['model'] == 'sh' else C2_LRS
+        opt = F.FusedAdam([{'params': [params[k]], 'lr': lr} for k, lr in lrs.items()], lr=0.0, eps=1e-15)
+        mlp = params.get('mlp_weights')
         grad_host = (torch.randn(3, wl['height'], wl['width'], generator=torch.Generator().manual_seed(2)) * 0.01).pin_memory()
         grad_dev = grad_host.to(dev)
         img_host = torch.empty((3, wl['height'], wl['width']), pin_memory=True)
@@ -313,7 +407,7 @@ def run_b200(args, wl_name: str) -> dict | None:
 
         def run(g):
             img = F.diff_rasterize(params['means'], params['scales'], params['rotations'], params['opacities'], empty, s0,
-                                   base_colors=params['base_colors'], residual_params=params['residual_params'])
+                                   base_colors=params['base_colors'], residual_params=params['residual_params'], mlp_weights=mlp)
             img.backward(g)
             opt.step()
             for p in params.values():
@@ -335,7 +429,7 @@ def run_b200(args, wl_name: str) -> dict | None:
                 grad_in.copy_(grad_host, non_blocking=True)
                 grad_ready.record(copy_stream)
             img = F.diff_rasterize(params['means'], params['scales'], params['rotations'], params['opacities'], empty, s0,
-                                   base_colors=params['base_colors'], residual_params=params['residual_params'])
+                                   base_colors=params['base_colors'], residual_params=params['residual_params'], mlp_weights=mlp)
             copy_stream.wait_stream(main)
             with torch.cuda.stream(copy_stream):
                 img_host.copy_(img.detach(), non_blocking=True)
@@ -352,7 +446,8 @@ def run_b200(args, wl_name: str) -> dict | None:
         views_per_step = 1
         stat_settings = s0
         stat_prims = R._c_primitives(params['means'].detach(), params['scales'].detach(), params['rotations'].detach(),
-                                     params['opacities'].detach(), None, params['base_colors'].detach(), params['residual_params'].detach(), None)
+                                     params['opacities'].detach(), None, params['base_colors'].detach(), params['residual_params'].detach(),
+                                     mlp.detach() if mlp is not None else None)
 
     exchange_desc = 'none'
     if wl_name == 'c4' and world > 1:
@@ -402,9 +497,8 @@ def run_b200(args, wl_name: str) -> dict | None:
     st = R.ForwardState(R._rasterizer, stat_prims, stat_settings, dev)
     st.preprocess(stat_prims)
     fr = st.frame
-    stride = {'sh': 45, 'neural': wl.get('feature_dim', 0), 'nasg': 8 * wl['degree'], 'sv': 7 * wl['degree']}[wl['model']]
-    stats = dict(N=wl['n'], V=fr.n_visible, I=fr.n_instances, pixels=wl['width'] * wl['height'], params=n_params, appearance_bytes=12 + 4 * stride)
     del st
+    stats = frame_stats(wl, fr.n_visible, fr.n_instances, n_params)
     per_view = {k: (v if k == 'adam' else v / views_per_step) for k, v in stage_ms.items()}
     dominant = max(stage_ms, key=stage_ms.get)
     peak, peak_kind = _peaks()
@@ -415,6 +509,9 @@ def run_b200(args, wl_name: str) -> dict | None:
     traffic_src = ('ncu dram__bytes_read.sum + dram__bytes_write.sum per visible row and per instance on the 2M-Gaussian one-view case (Morton '
                    'order), x visible rows and instances of view 0 (per view launch)') if per_unit else None
     fracs = {k: round(stage_bytes(k, stats) / (per_view[k] * 1e-3) / 1e9 / peak, 4) for k in per_view if stage_bytes(k, stats) and per_view[k] > 0}
+    tflops_peak = _tensor_peak()
+    tensor_fracs = {k: round(stage_flops(k, stats) / (per_view[k] * 1e-3) / 1e12 / tflops_peak, 4) for k in per_view
+                    if stage_flops(k, stats) and per_view[k] > 0}
 
     if world > 1:
         t = torch.tensor([ms, ms_e2e], device=dev)
@@ -438,60 +535,95 @@ def run_b200(args, wl_name: str) -> dict | None:
         'vs_baseline': None,
         'dtype': 'f32 (MLP fp16 operands, fp32 accumulation)' if wl['model'] == 'neural' else 'f32',
         'data': 'synthetic (seeded scene with the configuration shapes and distributions; no dataset available)',
-        'config': {'workload': wl_name + (f": {wl['model']}-{wl['degree']} {wl['n'] / 1e6:g}M Gaussians, {wl['views']} views 1920x1080, inference, "
-                                          f"views sharded" if render else
-                                          f": Neural {wl['n'] / 1e6:g}M Gaussians, {wl['views']} views 1920x1080 global batch, data-parallel"
-                                          if strong else f": SH-3 {wl['n'] / 1e6:g}M Gaussians, 1 view 1280x720 per GPU"),
-                   'mpix_per_s': steps_per_s * wl['width'] * wl['height'] / 1e6 if render else None,
-                   'n_gaussians': wl['n'], 'width': wl['width'], 'height': wl['height'], 'views_per_gpu': views_per_step,
-                   'n_visible_view0': fr.n_visible, 'n_instances_view0': fr.n_instances,
-                   'parallelism': (f'{world} GPU(s), views split, no collective' if render else
-                                   f'dp{world} (reduce-scatter / sharded Adam / all-gather: {exchange_desc})' if strong else f'replicas x{world}'),
-                   'l2': 'inputs larger than L2 (parameters alone exceed 126 MB)',
-                   'gaussian_order': getattr(args, 'order', 'morton')},
+        'config': static_config(wl_name, world, args, exchange_desc),
+        'frame': {'n_visible_view0': fr.n_visible, 'n_instances_view0': fr.n_instances,
+                  'mpix_per_s': steps_per_s * wl['width'] * wl['height'] / 1e6 if render else None},
         'e2e': {'value': e2e_per_s, 'unit': 'frames/s' if render else 'steps/s', 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
         'gpu_launches': own_launches(wl_name, views_per_step) * args.steps,
         'clocks': clocks,
         'stage_ms_per_step': {k: round(v, 4) for k, v in stage_ms.items()},
         'roofline': {'kernel': dominant, 'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'peak_kind': peak_kind, 'unit': 'GB/s',
                      'frac': achieved / peak, 'traffic': traffic, 'traffic_source': traffic_src, 'algorithmic_bytes': bytes_dom,
-                     'frac_by_stage': fracs},
+                     'frac_by_stage': fracs, 'tensor_frac_by_stage': tensor_fracs, 'tensor_peak_tflops': tflops_peak,
+                     'bound_by_stage': {k: BOUND.get(k, 'hbm') for k in per_view}},
     }
     if world > 1:
         torch.distributed.destroy_process_group()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out['cpu_baseline'] = cpu_step(wl_name, args.cpu_sample)
+        prep = cpu_prepare(wl_name, args.cpu_sample)
+        runs = [cpu_step(prep) for _ in range(3)]
+        base = {k: runs[0][k] for k in ('unit', 'cores', 'kind', 'sample')}
+        base['value'] = float(np.median([r['value'] for r in runs]))
+        out['cpu_baseline'] = base
+        out['cpu_baseline_appearance'] = cpu_appearance_baseline()
     return out if rank == 0 else None
 
 
 # ------------------------------------------------------------------------------------------------------------
 # CPU restatement (reference arm and cpu_baseline)
 
-def cpu_step(wl_name: str, tile_sample: float = 0.05, threads: int = 0) -> dict:
-    """Time of one step of the CPU restatement (oracle/, its per-primitive and per-pixel loops on `threads` OpenMP
-    threads, by default every host core), on a bounded sample:
+def cpu_prepare(wl_name: str, tile_sample: float = 0.05, threads: int = 0) -> dict:
+    """The bounded sample of the CPU restatement (oracle/, its per-primitive and per-pixel loops on `threads` OpenMP
+    threads, by default every host core), prepared once:
     c1: preprocess / depth order / binning / backward preprocess / Adam of all Gaussians, blends on a random
         `tile_sample` fraction of the tiles (scaled to all tiles).
-    c4: one view of a scene with 1/64 of the Gaussians (same distributions) with blends on `tile_sample` of the tiles;
-        preprocess, binning and backward-preprocess times scaled x64, blend times x64 / tile_sample, times 8 views,
-        plus Adam over all 6M-Gaussian parameters (timed on 1/64 and scaled)."""
-    import ctypes
+    c2 / c4: one view of a scene with 1/64 of the Gaussians (same distributions) with blends on `tile_sample` of the
+        tiles; preprocess, binning and backward-preprocess times scaled x64, blend times x64 / tile_sample, times the
+        views, plus Adam over all the workload's parameters (timed on 1/64 and scaled).
+    c3: one frame of a 1/32 scene with the blend on `tile_sample` of the tiles, scaled x32 (x32 / tile_sample)."""
     import synthetic as S
     from oracle import oracle as O
     wl = dict(WORKLOADS[wl_name])
     scale = 1
-    if wl_name == 'c4' or wl_name in RENDER:
-        scale = 64 if wl_name == 'c4' else 32
+    if wl['model'] == 'neural' or wl_name in RENDER:
+        scale = 32 if wl_name in RENDER else 64
         wl['n'] = wl['n'] // scale
     prims = scene(wl)
     cam = S.ring_cameras(8, wl['width'], wl['height'])[0]
-    lib = O.load(False)
     threads = threads or os.cpu_count() or 1
-    O.set_threads(threads)
+    return dict(wl_name=wl_name, wl=wl, prims=prims, cam=cam, lib=O.load(False), O=O, scale=scale, tile_sample=tile_sample, threads=threads)
+
+
+def cpu_step(prep: dict) -> dict:
+    """One timed sample: the scaled estimate in the metric's unit, and the sample's own wall time."""
+    O = prep['O']
+    O.set_threads(prep['threads'])
     try:
-        return _cpu_step_timed(wl_name, wl, prims, cam, lib, O, scale, tile_sample, threads)
+        t0 = time.perf_counter()
+        out = _cpu_step_timed(prep['wl_name'], prep['wl'], prep['prims'], prep['cam'], prep['lib'], O, prep['scale'], prep['tile_sample'],
+                              prep['threads'])
+        out['sample_ms'] = (time.perf_counter() - t0) * 1e3
+        return out
     finally:
         O.set_threads(1)
+
+
+def cpu_appearance_baseline(n: int = 100_000, reps: int = 5) -> dict:
+    """Configuration c0: the reference's CPU-runnable path, its unfused PyTorch appearance (SH degree 3, activations
+    none / none / relu) forward plus autograd backward for N Gaussians on the host cores, timed through the PyTorch
+    restatement oracle/appearance_torch.py (pinned to the reference modules' own outputs). Inputs as configs[0]: base
+    ~N(0,1), rest ~N(0,0.3), means uniform in a radius-5 ball, camera at distance 8, upstream gradient ~N(0,1)."""
+    from oracle import appearance_torch as AT
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(1)
+    base = torch.randn(n, 3, generator=g).requires_grad_(True)
+    rest = (torch.randn(n, 15, 3, generator=g) * 0.3).requires_grad_(True)
+    d = torch.nn.functional.normalize(torch.randn(n, 3, generator=g))
+    means = (d * 5.0 * torch.rand(n, 1, generator=g) ** (1.0 / 3.0)).requires_grad_(True)
+    cam = torch.tensor([0.0, 0.0, 8.0])
+    up = torch.randn(n, 3, generator=torch.Generator().manual_seed(2))
+    times = []
+    for r in range(reps + 1):
+        t0 = time.perf_counter()
+        AT.sh_colors(means, cam, base, rest, 3).backward(up)
+        times.append(time.perf_counter() - t0)
+        for t in (base, rest, means):
+            t.grad = None
+    t = float(np.median(times[1:]))
+    return {'value': 1.0 / t, 'unit': 'c0 steps/s (SH-3 colours of 100,000 Gaussians, forward + autograd backward)', 'cores': threads,
+            'kind': 'port', 'sample': f'full c0 workload, median of {reps} after 1 warm-up; PyTorch restatement of the reference\'s unfused '
+                                      f'Appearance/SH.py path'}
 
 
 def _cpu_step_timed(wl_name, wl, prims, cam, lib, O, scale, tile_sample, threads) -> dict:
@@ -554,9 +686,10 @@ def _cpu_step_timed(wl_name, wl, prims, cam, lib, O, scale, tile_sample, threads
     t4 = time.perf_counter()
     view_s = (t1 - t0) * scale + (t2 - t1) * scale / frac + (t3 - t2) * scale
     step_s = view_s * wl['views'] + (t4 - t3) * scale
-    if wl_name == 'c4':
-        sample = (f'c4 step estimated from one view of a {n}-Gaussian scene (1/64 of 6M) at 1920x1080 with blends on {int(keep.sum())} of '
-                  f'{T} tiles, scaled x64 (x{64 / frac:.0f} for blends), x8 views, plus Adam; C restatement on {threads} threads')
+    if wl['model'] == 'neural':
+        sample = (f'{wl_name} step estimated from one view of a {n}-Gaussian scene (1/64 of {n * 64 / 1e6:g}M) at {W}x{H} with blends on '
+                  f'{int(keep.sum())} of {T} tiles, scaled x64 (x{64 / frac:.0f} for blends), x{wl["views"]} views, plus Adam; C restatement on '
+                  f'{threads} threads')
     else:
         sample = (f'c1 step: preprocess/binning/backward-preprocess/Adam on all {n} Gaussians, blends on {int(keep.sum())} of {T} tiles scaled '
                   f'x{1 / frac:.1f}; C restatement on {threads} threads')
@@ -586,14 +719,23 @@ def main() -> None:
     if args.impl == 'reference':
         if int(os.environ.get('RANK', '0')) != 0:
             return
-        runs = [cpu_step(args.workload, args.cpu_sample) for _ in range(max(1, min(args.steps, 2)))]
+        prep = cpu_prepare(args.workload, args.cpu_sample)
+        for _ in range(args.warmup):
+            cpu_step(prep)
+        runs = [cpu_step(prep) for _ in range(args.steps)]
         v = float(np.median([r['value'] for r in runs]))
-        base = dict(runs[0], value=v)
+        ms = float(np.median([r['sample_ms'] for r in runs]))
         unit = 'frames/s' if args.workload in RENDER else 'steps/s'
+        base = {k: runs[0][k] for k in ('unit', 'cores', 'kind', 'sample')}
+        base['value'] = v
         print(json.dumps({'impl': 'reference', 'metric': METRIC[args.workload], 'value': v, 'unit': unit, 'n_gpus': args.gpus,
-                          'steps': len(runs), 'warmup': 0, 'ms_per_step': 1000.0 / v, 'higher_is_better': True,
-                          'scaling': 'strong' if args.workload in ('c4',) + RENDER else 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-                          'config': {'workload': args.workload}, 'cpu_baseline': base,
+                          'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms, 'higher_is_better': True,
+                          'scaling': 'strong' if args.workload in ('c4',) + RENDER else 'weak', 'vs_baseline': None, 'dtype': 'f32',
+                          'data': 'synthetic (seeded scene with the configuration shapes and distributions; no dataset available)',
+                          'config': static_config(args.workload, args.gpus, args),
+                          'estimate': {'value_is_estimate': True, 'timed': 'each of the steps is one bounded sample of the workload (ms_per_step is '
+                                       'its measured wall time); value is the sample scaled to one full step of the workload', 'sample': base['sample']},
+                          'cpu_baseline': base, 'cpu_baseline_appearance': cpu_appearance_baseline(),
                           'e2e': {'value': v, 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}))
         return
     out = run_b200(args, args.workload)

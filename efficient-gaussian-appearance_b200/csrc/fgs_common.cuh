@@ -124,21 +124,19 @@ __device__ inline float det_log(float x) {
 // |r| <= pi/4, then the Taylor series of sin r through r^9 and of cos r through r^10 (truncation below 2e-9), rotated by
 // the quadrant k mod 4. Every operation is an explicit single-rounding operation, so the oracle's C restatement gives
 // the same bits, and the fp16 inputs of the MLP are identical on both sides. Arguments with |x| <= 0.78 (the latent
-// features, which stay small) have k = 0 and r = x + 0, so they skip the reduction; beyond |x| = 8192 the three-part
-// reduction loses accuracy and sincosf is used.
+// features, which stay small) have k = 0 and r = x + 0, so they skip the reduction. Arguments are clamped to
+// |x| <= 8192, where the three-part reduction stays accurate (the latent features never come near it); the function
+// is inline arithmetic only, with no call in the MLP kernels' hot loops.
 constexpr float kTwoOverPi = 0.636619746685028076171875f;
 constexpr float kPio2P1 = 1.57079637050628662109375f;
 constexpr float kPio2P2 = -4.371138828673792886547744274139404296875e-08f;
 constexpr float kPio2P3 = -1.7151245100058819e-15f;
-static __device__ __noinline__ void enc_sincos_large(float x, float* sp, float* cp) { sincosf(x, sp, cp); }
 __device__ inline void enc_sincos(float x, float* sp, float* cp) {
     float k = 0.0f, r;
     if (fabsf(x) <= 0.78f) {
         r = __fadd_rn(x, 0.0f);
-    } else if (!(fabsf(x) <= 8192.0f)) {
-        enc_sincos_large(x, sp, cp);
-        return;
     } else {
+        x = fminf(fmaxf(x, -8192.0f), 8192.0f);
         k = rintf(__fmul_rn(x, kTwoOverPi));
         r = fmaf(-k, kPio2P1, x);
         r = fmaf(-k, kPio2P2, r);

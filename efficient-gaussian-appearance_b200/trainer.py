@@ -5,21 +5,25 @@ over the ranks of a torch.distributed group (one process per GPU); every rank ho
 Per step and rank:
   1. render its views and backpropagate the loss, accumulating the gradients of all local views into one flat
      fp32 gradient buffer (the backward kernels write the first view and add the following ones);
-  2. reduce-scatter (sum) the flat gradient buffer: rank r receives the summed gradients of the contiguous slice
-     [r*S, (r+1)*S) of the flat parameter vector;
-  3. fused Adam on that slice only (the optimizer moments exist only for the slice);
-  4. all-gather the updated slices back into every replica's flat parameter buffer.
-The flat buffer holds the parameter groups one after another (means, scales, rotations, opacities, base colors,
-residual parameters, MLP weights), each padded to a multiple of 64 floats, so a rank's slice can span several
-groups; the Adam segments carry each group's learning rate(s), betas and column offset.
-With one rank the collectives are skipped and the result equals the sequential accumulation over the same views.
+  2. reduce the gradients by Gaussian range: rank r receives the summed gradients of Gaussians [r*R, (r+1)*R) of
+     every per-Gaussian parameter group (R = ceil(N / ranks), rounded up to a multiple of 4 rows);
+  3. fused Adam on that range only (the optimizer moments of the per-Gaussian groups exist only for the range);
+  4. gather the updated ranges back into every replica's parameters.
+The MLP weights (a few thousand values shared by all Gaussians) are one more segment: owned by the last rank in the
+peer exchange, all-reduced with a replicated Adam in the NCCL exchange.
+The flat buffers hold the parameter groups one after another (means, scales, rotations, opacities, base colors,
+residual parameters, MLP weights), each per-Gaussian group padded to ranks * R rows, so every group stays one
+contiguous [N, ...] tensor for the kernels and every rank's rows of a group are one contiguous range. Padding rows
+have zero gradients and stay zero. With one rank the collectives are skipped and the result equals the sequential
+accumulation over the same views.
 
-Exchange modes: 'nccl' runs steps 2-4 as NCCL reduce-scatter, the fused Adam kernel and NCCL all-gather; 'peer'
-keeps the flat buffers in symmetric memory (mapped into every rank) and runs steps 2-4 as one kernel
-(fgs_dp_shard_adam) that sums the slice's gradients over NVLink (or through the switch with multicast), applies Adam
-and writes the new parameters into every rank's buffer, between two device-side barriers. 'auto' picks 'peer' when
-symmetric memory can be set up on the group and falls back to 'nccl' otherwise. The switch-multicast variant
-(multimem) is opt-in (multicast=True).
+Exchange modes: 'nccl' runs steps 2-4 as one NCCL reduce-scatter and one all-gather per per-Gaussian group, an
+all-reduce of the MLP gradient, and the fused Adam kernel; 'peer' keeps the flat buffers in symmetric memory (mapped
+into every rank) and runs steps 2-4 as one kernel (fgs_dp_shard_adam) that, for every element of the rank's
+segments, sums the gradients of all ranks over NVLink (or through the switch with multicast), applies Adam and writes
+the new parameter into every rank's buffer, between two device-side barriers. 'auto' picks 'peer' when symmetric
+memory can be set up on the group and falls back to 'nccl' otherwise. The switch-multicast variant (multimem) is
+opt-in (multicast=True).
 """
 from __future__ import annotations
 
@@ -45,6 +49,8 @@ class Group:
     shape: tuple
     lr: float | list
     betas: tuple = (0.9, 0.999)
+    cols: int = 0    # floats per Gaussian (0 for the MLP weights)
+    shard_offset: int = 0  # in floats, within a rank's moment buffer (per-Gaussian groups)
 
 
 def gaussian_window(size: int, sigma: float, device, dtype=torch.float32) -> torch.Tensor:
@@ -135,17 +141,27 @@ class Trainer:
         self.world = torch.distributed.get_world_size(group) if group is not None else 1
         self.rank = torch.distributed.get_rank(group) if group is not None else 0
         self.groups: list[Group] = []
-        off = 0
+        self.n = prims['means'].shape[0]
+        # rows per rank, a multiple of 4 so that every rank's range of every group starts 16-byte aligned
+        self.rows = (max(self.n, 1) + 4 * self.world - 1) // (4 * self.world) * 4
+        padded = self.rows * self.world
+        off, soff = 0, 0
         for name in GROUP_ORDER:
             t = prims.get(name)
             if t is None or t.numel() == 0:
                 continue
-            betas = mlp_betas if name == 'mlp_weights' else (0.9, 0.999)
-            self.groups.append(Group(name, off, t.numel(), tuple(t.shape), lrs[name], betas))
-            off += (t.numel() + 63) // 64 * 64
-        shard = (off + 64 * self.world - 1) // (64 * self.world) * 64
-        self.shard = shard
-        self.total = shard * self.world
+            if name == 'mlp_weights':
+                self.groups.append(Group(name, off, t.numel(), tuple(t.shape), lrs[name], mlp_betas))
+                off += (t.numel() + 63) // 64 * 64
+                continue
+            cols = t.numel() // self.n
+            self.groups.append(Group(name, off, t.numel(), tuple(t.shape), lrs[name], (0.9, 0.999), cols, soff))
+            off += padded * cols
+            soff += self.rows * cols
+        self.total = off
+        self.shard = soff  # floats of the per-Gaussian moments a rank holds
+        self.mlp = next((g for g in self.groups if g.name == 'mlp_weights'), None)
+        self.mlp_owner = self.world - 1
         self.exchange = 'nccl'
         self.peers = None
         self.use_multicast = multicast
@@ -162,11 +178,15 @@ class Trainer:
             self.grads = torch.zeros(self.total, dtype=torch.float32, device=device)
         for g in self.groups:
             self.params[g.offset:g.offset + g.numel].copy_(prims[g.name].reshape(-1))
-        self.exp_avg = torch.zeros(shard, dtype=torch.float32, device=device)
-        self.exp_avg_sq = torch.zeros(shard, dtype=torch.float32, device=device)
-        self.grad_shard = self.grads[self.rank * shard:(self.rank + 1) * shard] if self.world == 1 else torch.empty(shard, device=device)
+        self.exp_avg = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        self.exp_avg_sq = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        # MLP moments: on the owning rank (peer exchange) or on every rank (replicated Adam after the all-reduce)
+        self.mlp_moments = None
+        if self.mlp is not None and (self.exchange != 'peer' or self.rank == self.mlp_owner):
+            self.mlp_moments = (torch.zeros(self.mlp.numel, dtype=torch.float32, device=device),
+                                torch.zeros(self.mlp.numel, dtype=torch.float32, device=device))
+        self.grad_shard = torch.empty(self.shard, dtype=torch.float32, device=device) if self.world > 1 else None
         self.step_count = 0
-        self.n = prims['means'].shape[0]
         self.loss_fns = (FusedLoss(), FusedLoss())
         self._images = [None, None]
         self._grad_images = [None, None]
@@ -200,10 +220,23 @@ class Trainer:
         self.peers = pb
 
     def view(self, buf: torch.Tensor, name: str) -> torch.Tensor | None:
+        """Parameter group `name` of a flat parameter or gradient buffer, as its [N, ...] tensor."""
         for g in self.groups:
             if g.name == name:
                 return buf[g.offset:g.offset + g.numel].view(g.shape)
         return None
+
+    def range_view(self, buf: torch.Tensor, name: str, rank: int | None = None) -> torch.Tensor:
+        """Rows [rank * R, (rank + 1) * R) of per-Gaussian group `name` in a flat buffer, as an [R, cols] tensor."""
+        g = next(x for x in self.groups if x.name == name)
+        r = self.rank if rank is None else rank
+        lo = g.offset + r * self.rows * g.cols
+        return buf[lo:lo + self.rows * g.cols].view(self.rows, g.cols)
+
+    def shard_view(self, buf: torch.Tensor, name: str) -> torch.Tensor:
+        """This rank's part of per-Gaussian group `name` in a moment-layout buffer (exp_avg, exp_avg_sq, grad_shard)."""
+        g = next(x for x in self.groups if x.name == name)
+        return buf[g.shard_offset:g.shard_offset + self.rows * g.cols].view(self.rows, g.cols)
 
     def _prims(self) -> tuple:
         v = lambda k: self.view(self.params, k)
@@ -266,59 +299,80 @@ class Trainer:
     @torch.no_grad()
     def apply_morton_ordering(self) -> None:
         """Reorders every per-Gaussian parameter group and its Adam moments by the Morton order of the means (the same
-        permutation on every rank: all replicas hold the same means). A rank's moments cover only its slice, so with
-        several ranks the moments are gathered, permuted and sliced again."""
+        permutation on every rank: all replicas hold the same means). A rank's moments cover only its Gaussian range,
+        so with several ranks the moments are gathered, permuted and split into ranges again."""
         order = morton_order(self.view(self.params, 'means'))
-        if self.world > 1:
-            full_m = torch.empty(self.total, dtype=torch.float32, device=self.device)
-            full_v = torch.empty(self.total, dtype=torch.float32, device=self.device)
+        n, rows, world = self.n, self.rows, self.world
+        if world > 1:
+            full_m = torch.empty(self.shard * world, dtype=torch.float32, device=self.device)
+            full_v = torch.empty(self.shard * world, dtype=torch.float32, device=self.device)
             torch.distributed.all_gather_into_tensor(full_m, self.exp_avg, group=self.pg)
             torch.distributed.all_gather_into_tensor(full_v, self.exp_avg_sq, group=self.pg)
-        else:
-            full_m, full_v = self.exp_avg, self.exp_avg_sq
         for g in self.groups:
             if g.name == 'mlp_weights':
                 continue
-            for buf in (self.params, full_m, full_v):
-                rows = buf[g.offset:g.offset + g.numel].view(g.shape[0], -1)
-                rows.copy_(rows[order])
-        if self.world > 1:
-            lo = self.rank * self.shard
-            self.exp_avg.copy_(full_m[lo:lo + self.shard])
-            self.exp_avg_sq.copy_(full_v[lo:lo + self.shard])
+            p_rows = self.params[g.offset:g.offset + g.numel].view(n, g.cols)
+            p_rows.copy_(p_rows[order])
+            for local, full in ((self.exp_avg, full_m if world > 1 else None), (self.exp_avg_sq, full_v if world > 1 else None)):
+                if full is None:
+                    rows_m = local[g.shard_offset:g.shard_offset + rows * g.cols].view(rows, g.cols)[:n]
+                    rows_m.copy_(rows_m[order])
+                    continue
+                # the group's moments of all ranks in row order: rank r's part sits at r * shard + shard_offset
+                parts = full.view(world, self.shard)[:, g.shard_offset:g.shard_offset + rows * g.cols]
+                allrows = parts.reshape(world * rows, g.cols)
+                allrows[:n] = allrows[:n][order]
+                local[g.shard_offset:g.shard_offset + rows * g.cols].copy_(allrows[self.rank * rows:(self.rank + 1) * rows].reshape(-1))
 
-    def adam_segments(self, grad_slice: torch.Tensor | None = None) -> list:
-        """Adam segments of this rank's slice [rank*S, (rank+1)*S), split at parameter-group boundaries (gradients from
-        grad_slice, by default the reduce-scattered shard)."""
-        grad_shard = self.grad_shard if grad_slice is None else grad_slice
-        lo, hi = self.rank * self.shard, (self.rank + 1) * self.shard
+    def adam_segments(self, grads: torch.Tensor | None = None, with_mlp: bool = True) -> list:
+        """Adam segments of this rank: its Gaussian range of every per-Gaussian group (gradients from `grads`, a
+        moment-layout buffer, by default the local flat gradient buffer's rows of the range) and, with_mlp, the MLP
+        weights."""
         segs = []
         for g in self.groups:
-            a, b = max(lo, g.offset), min(hi, g.offset + g.numel)
-            if a >= b:
+            if g.name == 'mlp_weights':
                 continue
-            s0 = a - lo
-            segs.append(_segment(self.params[a:b], grad_shard[s0:s0 + (b - a)], self.exp_avg[s0:s0 + (b - a)],
-                                 self.exp_avg_sq[s0:s0 + (b - a)], self.step_count, g.lr, g.betas, 1e-15, column_offset=a - g.offset))
+            lo = g.offset + self.rank * self.rows * g.cols
+            size = self.rows * g.cols
+            grad = self.grads[lo:lo + size] if grads is None else grads[g.shard_offset:g.shard_offset + size]
+            segs.append(_segment(self.params[lo:lo + size], grad, self.exp_avg[g.shard_offset:g.shard_offset + size],
+                                 self.exp_avg_sq[g.shard_offset:g.shard_offset + size], self.step_count, g.lr, g.betas, 1e-15,
+                                 column_offset=self.rank * self.rows * g.cols))
+        if with_mlp and self.mlp is not None and self.mlp_moments is not None:
+            g = self.mlp
+            segs.append(_segment(self.params[g.offset:g.offset + g.numel], self.grads[g.offset:g.offset + g.numel], self.mlp_moments[0],
+                                 self.mlp_moments[1], self.step_count, g.lr, g.betas, 1e-15))
         return segs
 
     def apply_gradients(self, adam_fn=None) -> None:
-        """Exchange step: reduce-scatter of the gradients, Adam on this rank's slice, all-gather of the parameters.
-        `adam_fn(segments)` replaces the fused GPU Adam (used by the CPU tests with the checker's Adam)."""
+        """Exchange step: gradients reduced by Gaussian range, Adam on this rank's range (and the MLP weights), the
+        ranges gathered back into every replica. `adam_fn(segments)` replaces the fused GPU Adam (used by the CPU tests
+        with the checker's Adam)."""
         self.step_count += 1
         if self.exchange == 'peer':
             self.h_grads.barrier(channel=0)  # every rank's gradients are final
-            segs = self.adam_segments(self.grads[self.rank * self.shard:(self.rank + 1) * self.shard])
+            segs = self.adam_segments(with_mlp=self.rank == self.mlp_owner)
             arr = (_lib.AdamSegment * len(segs))(*segs)
             _lib.check(_lib.lib.fgs_dp_shard_adam(arr, len(segs), ctypes.byref(self.peers), torch.cuda.current_stream(self.device).cuda_stream))
             self.h_params.barrier(channel=1)  # every rank's parameters are written
             return
-        if self.world > 1:
-            torch.distributed.reduce_scatter_tensor(self.grad_shard, self.grads, group=self.pg)
-        (adam_fn or adam_step_segments)(self.adam_segments())
-        if self.world > 1:
-            torch.distributed.all_gather_into_tensor(self.params, self.params[self.rank * self.shard:(self.rank + 1) * self.shard],
-                                                     group=self.pg)
+        if self.world == 1:
+            (adam_fn or adam_step_segments)(self.adam_segments())
+            return
+        for g in self.groups:
+            if g.name == 'mlp_weights':
+                torch.distributed.all_reduce(self.grads[g.offset:g.offset + g.numel], group=self.pg)
+                continue
+            size = self.rows * g.cols
+            torch.distributed.reduce_scatter_tensor(self.grad_shard[g.shard_offset:g.shard_offset + size],
+                                                    self.grads[g.offset:g.offset + size * self.world], group=self.pg)
+        (adam_fn or adam_step_segments)(self.adam_segments(self.grad_shard))
+        for g in self.groups:
+            if g.name == 'mlp_weights':
+                continue
+            size = self.rows * g.cols
+            full = self.params[g.offset:g.offset + size * self.world]
+            torch.distributed.all_gather_into_tensor(full, full[self.rank * size:(self.rank + 1) * size], group=self.pg)
 
     def step(self, settings_list: list, targets: list, ready: list | None = None) -> torch.Tensor:
         loss = self.backward_views(settings_list, targets, ready)

@@ -70,19 +70,20 @@ static float det_exp_f(float x) {
 }
 
 /* sine and cosine of the Neural encoding in the float build: Cody-Waite reduction modulo pi/2 in three parts,
- * Taylor series of sin through r^9 and cos through r^10, quadrant rotation; libm beyond |x| = 8192. Within 2.5e-7 of
- * exact; the kernels use the GPU's hardware approximation (what the reference's fast-math build evaluates), so an
- * encoded fp16 input can differ from this one by a rounding, which the Neural tolerances cover. */
+ * Taylor series of sin through r^9 and cos through r^10, quadrant rotation, arguments clamped to |x| <= 8192; the
+ * kernels' enc_sincos (fgs_common.cuh) performs the same single-rounding operations, so both give the same bits (within
+ * 2.5e-7 of exact). */
 static void det_sincos_f(float x, float* sp, float* cp) {
-    if (!(fabsf(x) <= 8192.0f)) {
-        *sp = sinf(x);
-        *cp = cosf(x);
-        return;
+    float k = 0.0f, r;
+    if (fabsf(x) <= 0.78f) {
+        r = x + 0.0f;
+    } else {
+        x = fminf(fmaxf(x, -8192.0f), 8192.0f);
+        k = rintf(x * 0.636619746685028076171875f);
+        r = fmaf(-k, 1.57079637050628662109375f, x);
+        r = fmaf(-k, -4.371138828673792886547744274139404296875e-08f, r);
+        r = fmaf(-k, -1.7151245100058819e-15f, r);
     }
-    const float k = rintf(x * 0.636619746685028076171875f);
-    float r = fmaf(-k, 1.57079637050628662109375f, x);
-    r = fmaf(-k, -4.371138828673792886547744274139404296875e-08f, r);
-    r = fmaf(-k, -1.7151245100058819e-15f, r);
     const float r2 = r * r;
     float ps = 1.0f / 362880.0f;
     ps = fmaf(ps, r2, -1.0f / 5040.0f);

@@ -1,7 +1,8 @@
-"""Data-parallel exchange step on CPU ranks (gloo, world size 2): reduce-scatter of the flat gradient buffer, Adam on
-each rank's slice (the checker's float Adam, same operations as the kernel) and all-gather of the parameters give
-bit-identical parameters to a single process applying Adam to the summed gradients. Also a rank that fails before
-the collective makes the others fail with an error instead of hanging (short process-group timeout)."""
+"""Data-parallel exchange step on CPU ranks (gloo, world size 2): gradients reduced by Gaussian range (a reduce-scatter
+per parameter group, an all-reduce of the MLP weights), Adam on each rank's Gaussian range (the checker's float Adam,
+same operations as the kernel) and the ranges gathered back give bit-identical parameters to a single process applying
+Adam to the summed gradients. Also a rank that fails before the collective makes the others fail with an error
+instead of hanging (short process-group timeout)."""
 import os
 import socket
 import sys
@@ -33,7 +34,7 @@ def _oracle_adam(segments):
                      seg.beta1, seg.beta2, seg.eps)
 
 
-def _prims(n=1000, feat=7):
+def _prims(n=1001, feat=7):
     g = torch.Generator().manual_seed(0)
     return {'means': torch.randn(n, 3, generator=g), 'scales': torch.randn(n, 3, generator=g), 'rotations': torch.randn(n, 4, generator=g),
             'opacities': torch.randn(n, 1, generator=g), 'base_colors': torch.randn(n, 3, generator=g),
@@ -44,9 +45,15 @@ LRS = {'means': 1.6e-4, 'scales': 0.005, 'rotations': 0.001, 'opacities': 0.05, 
        'residual_params': [0.002] * 3 + [0.006] + [0.0008] * 3, 'mlp_weights': 0.003}
 
 
-def _grads(trainer, rank, step):
+def _grads(trainer, rank, step, fill=True):
+    """Per-group random gradients of one rank and step (padding rows of the flat buffer stay zero)."""
     g = torch.Generator().manual_seed(1000 * step + rank)
-    trainer.grads.copy_(torch.randn(trainer.total, generator=g))
+    out = {}
+    for grp in trainer.groups:
+        out[grp.name] = torch.randn(grp.shape, generator=g)
+        if fill:
+            trainer.view(trainer.grads, grp.name).copy_(out[grp.name])
+    return out
 
 
 def _worker(rank, world, port, out_dir):
@@ -58,10 +65,11 @@ def _worker(rank, world, port, out_dir):
     torch.distributed.init_process_group('gloo', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
     from trainer import Trainer
     t = Trainer(_prims(), LRS, torch.device('cpu'), group=torch.distributed.group.WORLD)
+    assert t.rows * world >= t.n and t.rows % 4 == 0
     for step in range(3):
         _grads(t, rank, step)
         t.apply_gradients(adam_fn=_oracle_adam)
-    torch.save(t.params.clone(), os.path.join(out_dir, f'params_{rank}.pt'))
+    torch.save({g.name: t.view(t.params, g.name).clone() for g in t.groups}, os.path.join(out_dir, f'params_{rank}.pt'))
     torch.distributed.destroy_process_group()
 
 
@@ -73,23 +81,18 @@ def test_sharded_adam_matches_single_process(tmp_path):
     world = 2
     port = _free_port()
     mp.start_processes(_worker, args=(world, port, str(tmp_path)), nprocs=world, start_method='spawn', join=True)
-    # single process: same flat layout (padded for 2 ranks), gradients summed over the ranks
+    # single process: the gradients summed over the ranks
     ref = Trainer(_prims(), LRS, torch.device('cpu'))
-    dist_total = (ref.total + 64 * world - 1) // (64 * world) * (64 * world)
     for step in range(3):
-        total = None
-        for rank in range(world):
-            g = torch.Generator().manual_seed(1000 * step + rank)
-            x = torch.randn(dist_total, generator=g)
-            total = x if total is None else total + x
-        # the distributed run pads the flat buffer to a multiple of 64 * world; use the same prefix
-        ref.grads.copy_(total[:ref.total])
+        parts = [_grads(ref, rank, step, fill=False) for rank in range(world)]
+        for grp in ref.groups:
+            ref.view(ref.grads, grp.name).copy_(parts[0][grp.name] + parts[1][grp.name])
         ref.apply_gradients(adam_fn=_oracle_adam)
     p0 = torch.load(tmp_path / 'params_0.pt')
     p1 = torch.load(tmp_path / 'params_1.pt')
-    assert torch.equal(p0, p1)
-    n = ref.total
-    assert torch.equal(p0[:n], ref.params[:n])
+    for grp in ref.groups:
+        assert torch.equal(p0[grp.name], p1[grp.name]), grp.name
+        assert torch.equal(p0[grp.name], ref.view(ref.params, grp.name)), grp.name
 
 
 def _failing_worker(rank, world, port):
@@ -128,6 +131,12 @@ def _position_order(means: torch.Tensor) -> torch.Tensor:
     return torch.argsort(m[:, 0] + 0.37 * m[:, 1] - 0.11 * m[:, 2], stable=True)
 
 
+def _moments(name, rows_total, cols, sign):
+    """A known full moment tensor of one group: row-major counting values (negated for the second moment)."""
+    base = {'means': 0, 'scales': 1e5, 'rotations': 2e5, 'opacities': 3e5, 'base_colors': 4e5, 'residual_params': 5e5}[name]
+    return sign * (base + torch.arange(rows_total * cols, dtype=torch.float32)).view(rows_total, cols)
+
+
 def _morton_worker(rank, world, port, out_dir):
     for p in (str(ROOT), str(ROOT / 'efficient-gaussian-appearance_b200'), str(ROOT / 'tests')):
         sys.path.insert(0, p)
@@ -138,18 +147,21 @@ def _morton_worker(rank, world, port, out_dir):
     import trainer as T
     T.morton_order = _position_order
     t = T.Trainer(_prims(), LRS, torch.device('cpu'), group=torch.distributed.group.WORLD)
-    lo = rank * t.shard
-    t.exp_avg.copy_(torch.arange(lo, lo + t.shard, dtype=torch.float32))
-    t.exp_avg_sq.copy_(-torch.arange(lo, lo + t.shard, dtype=torch.float32))
+    groups = [g for g in t.groups if g.name != 'mlp_weights']
+    for g in groups:
+        for buf, sign in ((t.exp_avg, 1.0), (t.exp_avg_sq, -1.0)):
+            t.shard_view(buf, g.name).copy_(_moments(g.name, t.rows * world, g.cols, sign)[rank * t.rows:(rank + 1) * t.rows])
     t.apply_morton_ordering()
-    torch.save({'params': t.params.clone(), 'm': t.exp_avg.clone(), 'v': t.exp_avg_sq.clone(), 'shard': t.shard},
-               os.path.join(out_dir, f'morton_{rank}.pt'))
+    torch.save({'params': {g.name: t.view(t.params, g.name).clone() for g in t.groups},
+                'm': {g.name: t.shard_view(t.exp_avg, g.name).clone() for g in groups},
+                'v': {g.name: t.shard_view(t.exp_avg_sq, g.name).clone() for g in groups}}, os.path.join(out_dir, f'morton_{rank}.pt'))
     torch.distributed.destroy_process_group()
 
 
 def test_morton_ordering_two_ranks_matches_single_process(tmp_path):
-    """Every rank holds only its slice of the Adam moments: the ordering gathers them, permutes every per-Gaussian
-    group (the MLP weights stay) and hands each rank its slice again, as one process permuting everything would."""
+    """Every rank holds only its Gaussian range of the Adam moments: the ordering gathers them, permutes every
+    per-Gaussian group (the MLP weights stay) and hands each rank its range again, as one process permuting everything
+    would (the first N rows; the ranges' padding rows differ between the layouts and are not used)."""
     for p in (str(ROOT), str(ROOT / 'efficient-gaussian-appearance_b200')):
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -160,17 +172,20 @@ def test_morton_ordering_two_ranks_matches_single_process(tmp_path):
     saved, T.morton_order = T.morton_order, _position_order
     try:
         ref = T.Trainer(_prims(), LRS, torch.device('cpu'))
-        ref.exp_avg.copy_(torch.arange(ref.shard, dtype=torch.float32))
-        ref.exp_avg_sq.copy_(-torch.arange(ref.shard, dtype=torch.float32))
+        groups = [g for g in ref.groups if g.name != 'mlp_weights']
+        for g in groups:
+            ref.shard_view(ref.exp_avg, g.name).copy_(_moments(g.name, ref.rows, g.cols, 1.0))
+            ref.shard_view(ref.exp_avg_sq, g.name).copy_(_moments(g.name, ref.rows, g.cols, -1.0))
         ref.apply_morton_ordering()
     finally:
         T.morton_order = saved
-    n = sum((g.numel + 63) // 64 * 64 for g in ref.groups)
-    assert torch.equal(parts[0]['params'], parts[1]['params'])
-    assert torch.equal(parts[0]['params'][:n], ref.params[:n])
-    m = torch.cat([p['m'] for p in parts])
-    v = torch.cat([p['v'] for p in parts])
-    assert torch.equal(m[:n], ref.exp_avg[:n]) and torch.equal(v[:n], ref.exp_avg_sq[:n])
+    n = ref.n
+    for g in ref.groups:
+        assert torch.equal(parts[0]['params'][g.name], parts[1]['params'][g.name])
+        assert torch.equal(parts[0]['params'][g.name], ref.view(ref.params, g.name))
+    for g in groups:
+        for key, buf in (('m', ref.exp_avg), ('v', ref.exp_avg_sq)):
+            dist = torch.cat([p[key][g.name] for p in parts])[:n]
+            assert torch.equal(dist, ref.shard_view(buf, g.name)[:n]), (key, g.name)
     means = _prims()['means']
-    g = next(x for x in ref.groups if x.name == 'means')
-    assert torch.equal(ref.params[g.offset:g.offset + g.numel].view(-1, 3), means[_position_order(means)])
+    assert torch.equal(ref.view(ref.params, 'means'), means[_position_order(means)])

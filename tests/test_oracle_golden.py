@@ -29,3 +29,19 @@ def test_appearance_matches_reference_modules(path, double):
 
 def test_golden_files_present():
     assert len(FILES) == 8
+
+
+@pytest.mark.parametrize('path', [f for f in FILES if '_sh' in Path(f).stem], ids=lambda f: Path(f).stem)
+def test_torch_restatement_matches_reference_modules(path):
+    """The PyTorch restatement of the reference's unfused SH path (the CPU baseline of configuration c0) reproduces
+    the reference modules' colours and autograd gradients."""
+    import torch
+    from oracle import appearance_torch as AT
+    z = np.load(path)
+    t = {k: torch.tensor(z[k], dtype=torch.float64, requires_grad=k in ('base', 'residual', 'means')) for k in ('base', 'residual', 'means')}
+    col = AT.sh_colors(t['means'], torch.tensor(z['cam'], dtype=torch.float64), t['base'], t['residual'], int(z['degree']), str(z['base_act']),
+                       str(z['residual_act']), str(z['color_act']))
+    col.backward(torch.tensor(z['upstream'], dtype=torch.float64))
+    for got, key in ((col.detach(), 'colors'), (t['base'].grad, 'grad_base'), (t['residual'].grad, 'grad_residual'), (t['means'].grad, 'grad_means')):
+        ref = z[key]
+        assert np.abs(got.numpy().reshape(ref.shape) - ref).max() <= 1e-9 * max(1.0, np.abs(ref).max()), key

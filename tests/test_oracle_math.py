@@ -43,16 +43,20 @@ def test_binning_invariants():
 
 def test_det_sincos_error_bound():
     """The oracle's deterministic sine / cosine of the Neural encoding (Cody-Waite reduction + Taylor series) against
-    double-precision libm: at most 2.5e-7 absolute error on [-8192, 8192] and at the quadrant boundaries; libm
-    beyond."""
+    double-precision libm: at most 2.5e-7 absolute error on [-8192, 8192] and at the quadrant boundaries; arguments
+    beyond are clamped to +-8192 (as the kernels do)."""
     import ctypes
     lib = O.load(False)
     rng = np.random.default_rng(0)
     xs = np.concatenate([rng.normal(0, 0.1, 20000), rng.uniform(-10, 10, 20000), rng.uniform(-8192, 8192, 20000),
-                         (np.arange(-64, 65) * np.pi / 4), [0.0, -0.0, 1e-30, 8192.0, -8192.0, 9000.0]]).astype(np.float32)
+                         (np.arange(-64, 65) * np.pi / 4), [0.0, -0.0, 1e-30, 8192.0, -8192.0]]).astype(np.float32)
     s, c = ctypes.c_float(), ctypes.c_float()
     worst = 0.0
     for x in xs:
         lib.orc_det_sincos(ctypes.c_float(x), ctypes.byref(s), ctypes.byref(c))
         worst = max(worst, abs(s.value - np.sin(np.float64(x))), abs(c.value - np.cos(np.float64(x))))
     assert worst <= 2.5e-7, worst
+    s2, c2 = ctypes.c_float(), ctypes.c_float()
+    lib.orc_det_sincos(ctypes.c_float(9000.0), ctypes.byref(s), ctypes.byref(c))
+    lib.orc_det_sincos(ctypes.c_float(8192.0), ctypes.byref(s2), ctypes.byref(c2))
+    assert (s.value, c.value) == (s2.value, c2.value)
