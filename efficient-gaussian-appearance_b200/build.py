@@ -16,14 +16,14 @@ BUILD = HERE / '_build'
 LIB = HERE / 'FasterGSVDACudaBackend' / 'lib' / 'libfgs_b200.so'
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
-# -fmad=false: no implicit contraction of a*b+c (the arithmetic contract of fgs_common.cuh);
-# IEEE division / square root and denormals are nvcc's defaults without --use_fast_math.
+# Default for the remaining sources (sort, adam, densification, the C ABI): -fmad=false, no implicit contraction of
+# a*b+c, with nvcc's IEEE division, square root and denormals.
 FLAGS = ['-O3', '-std=c++17', '-lineinfo', '-fmad=false', '-Xcompiler', '-fPIC', '--expt-relaxed-constexpr',
          '-Xptxas', '-warn-spills']
 # Sources whose outputs are checked against the CPU restatement within a tolerance rather than bit for bit (the fp16
 # tensor-core MLP of the neural appearance, whose backward also carries the geometry chain rule; the photometric loss,
-# checked against its fp32 PyTorch definition; the blend backward, whose fragment decisions are written with explicit
-# single-rounding intrinsics): contraction allowed.
+# checked against its fp32 PyTorch definition): contraction allowed. Their deterministic parts (the frequency encoding,
+# the view direction, the SH band values) are written with explicit single-rounding operations.
 CONTRACTED = {'neural.cu', 'neural_tc.cu', 'loss.cu'}
 # Sources that evaluate the rasterizer's forward decisions (projection, culling, tile bounds and overlap, fragment
 # acceptance, transmittance) and must compute them exactly as the reference's own build does: its kernels are

@@ -1,16 +1,14 @@
-// Tile alpha blending: training forward (with per-32-instance checkpoints for the backward), inference
-// forward, and the per-bucket backward.
+// Tile alpha blending: the training forward (which also stores each pixel's final transmittance and number of
+// contributors, and each tile's largest contributor count, for the backward) and the inference forward.
 //
-// Forward semantics follow FasterGSVDACudaBackend/.../rasterization/include/kernels_forward.cuh:26-166
-// and kernels_inference.cuh:11-126: 16x12 tiles, six warps each owning an 8x4 subtile, instances staged
-// 192 at a time in shared memory, a Gaussian is skipped by a warp when its screen bounds miss the
-// subtile, alpha = opacity * exp(-power), fragments below alpha 1/255 are skipped, blending stops once
-// the transmittance falls below 1e-4. The acceptance test is evaluated as "exponent >= -ln(255 opacity)"
-// against the per-primitive threshold stored by the preprocess (the same threshold the tile test uses),
-// and exp is the deterministic polynomial of fgs_common.cuh.
-// Backward: the gradients of include/kernels_backward.cuh:12-231 (the reference processes buckets of 32
-// instances with the pixels pipelined through the lanes, which for small footprints spends most issue slots
-// on pairs that do not overlap); here each warp walks its subtile's fragments front to back like the forward.
+// Semantics follow FasterGSVDACudaBackend/.../rasterization/include/kernels_forward.cuh:26-166 and
+// kernels_inference.cuh:11-126: 16x12 tiles, six warps each owning an 8x4 subtile, instances staged 192 at a time in
+// shared memory, a Gaussian is skipped by a warp when its screen bounds miss the subtile, alpha = opacity * G with the
+// fragment's Gaussian G = exp2(min(exponent, 0)) (the exponent pre-scaled by log2 e through the staged conic),
+// fragments with alpha below 1/255 are skipped, and blending stops once the transmittance falls below 1e-4. The
+// exponent, alpha and the transmittance update are the reference's expressions written as explicit single-rounding
+// operations (blend_common.cuh); this file is compiled with -use_fast_math like the reference's build, so exp2 is the
+// same hardware approximation, and the accepted fragments and final transmittances equal the reference's bit for bit.
 #include "blend_common.cuh"
 #include "launch.h"
 

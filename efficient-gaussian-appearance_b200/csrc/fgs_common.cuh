@@ -1,15 +1,12 @@
-// Shared constants, small vector helpers and the deterministic transcendental functions used by every
-// kernel of the rasterizer.
+// Shared constants, small vector helpers and the deterministic functions used by the kernels of the rasterizer.
 //
-// Arithmetic contract: every value that decides an integer outcome (culling, screen bounds, tile
-// overlap, per-pixel alpha acceptance, early termination) is computed from IEEE-754 single precision
-// add / mul / div / sqrt and explicit fmaf only. This translation unit family is compiled with
-// -fmad=false, so nvcc never contracts a*b+c on its own, and the transcendental functions below are
-// polynomial evaluations built from the same basic operations. A C implementation that performs the
-// same operations in the same order (compiled with -ffp-contract=off) therefore produces bit-identical
-// results, which is what makes keys, tile lists, ranges and images reproducible outside the GPU. Two hardware
-// approximations stay off those paths: the Neural encoding's sine and cosine (enc_sincos), which feed only colours,
-// and the backward blend's reciprocal of 1 - alpha in gradient terms; both are compared within tolerances.
+// Arithmetic contract. The translation units whose results decide integer outcomes (preprocess.cu, binning.cu,
+// blend.cu, blend_bwd.cu: culling, screen bounds, tile overlap, fragment acceptance, early termination) are compiled
+// with -use_fast_math, like the reference's own build, and write the expressions whose rounding matters as explicit
+// single-rounding operations (__fmul_rn, __fadd_rn, fmaf) in the reference's order, so that the decisions, tile lists
+// and transmittances equal the reference's kernels bit for bit. The Neural MLP units (neural.cu, neural_tc.cu) keep
+// the compiler's default contraction and use the deterministic sine and cosine below, so their fp16 MLP inputs are
+// reproducible by a C restatement. det_exp / det_sigmoid serve gradient terms of the backward preprocess only.
 #pragma once
 
 #include <cstdint>
@@ -52,7 +49,7 @@ __device__ inline float clampf(float x, float lo, float hi) { return fminf(fmaxf
 // [0,1] clamp with NaN -> 0, written with comparisons so that every implementation agrees
 __device__ inline float sat(float x) { return x > 0.0f ? (x < 1.0f ? x : 1.0f) : 0.0f; }
 
-// ---- deterministic exp / log ----
+// ---- deterministic exp ----
 // Cody-Waite reduction x = n*ln2 + r (ln2 split into a high part with trailing zero bits and a low
 // correction), e^r from its Taylor series through r^7 (|r| <= ln2/2, truncation < 6e-9 relative),
 // and the 2^n scale applied through the exponent field. Inputs below -87 return 0, above 88 inf.
@@ -77,46 +74,6 @@ __device__ inline float det_exp(float x) {
     p = fmaf(p, r, 1.0f);
     const int e = static_cast<int>(n) + 127;   // in [1, 254] for the accepted range
     return p * __int_as_float(e << 23);
-}
-
-// e^x for x in [-6, 0] (the blend's accepted exponent range, bounded by ln(255)); same reduction with
-// the series truncated after r^6 (truncation < 1.3e-7 relative, comparable to a hardware exp2)
-__device__ inline float det_exp_blend(float x) {
-    const float n = rintf(x * kLog2e);
-    float r = fmaf(-n, kLn2Hi, x);
-    r = fmaf(-n, kLn2Lo, r);
-    float p = 1.0f / 720.0f;
-    p = fmaf(p, r, 1.0f / 120.0f);
-    p = fmaf(p, r, 1.0f / 24.0f);
-    p = fmaf(p, r, 1.0f / 6.0f);
-    p = fmaf(p, r, 0.5f);
-    p = fmaf(p, r, 1.0f);
-    p = fmaf(p, r, 1.0f);
-    return p * __int_as_float((static_cast<int>(n) + 127) << 23);
-}
-
-// natural log for finite x > 0: x = m * 2^k with m in [sqrt(1/2), sqrt(2)), ln m = 2 atanh(s) with
-// s = (m - 1) / (m + 1) evaluated by its odd series through s^11; non-positive x returns -inf / NaN
-__device__ inline float det_log(float x) {
-    if (!(x > 0.0f)) return x == 0.0f ? __int_as_float(0xff800000) : __int_as_float(0x7fc00000);
-    if (x == __int_as_float(0x7f800000)) return x;
-    int k = 0;
-    if (x < 1.17549435e-38f) { x = x * 16777216.0f; k = -24; }   // subnormal: scale by 2^24
-    const int bits = __float_as_int(x);
-    k += ((bits >> 23) & 0xff) - 127;
-    float m = __int_as_float((bits & 0x007fffff) | 0x3f800000);  // [1, 2)
-    if (m > 1.41421356f) { m = m * 0.5f; k += 1; }
-    const float s = (m - 1.0f) / (m + 1.0f);
-    const float s2 = s * s;
-    float p = 1.0f / 11.0f;
-    p = fmaf(p, s2, 1.0f / 9.0f);
-    p = fmaf(p, s2, 1.0f / 7.0f);
-    p = fmaf(p, s2, 1.0f / 5.0f);
-    p = fmaf(p, s2, 1.0f / 3.0f);
-    p = fmaf(p, s2, 1.0f);
-    const float ln_m = 2.0f * s * p;
-    const float kf = static_cast<float>(k);
-    return fmaf(kf, kLn2Hi, fmaf(kf, kLn2Lo, ln_m));
 }
 
 // sine and cosine of the Neural frequency encoding, deterministic: Cody-Waite reduction x = k (pi/2) + r with pi/2

@@ -76,6 +76,18 @@ size_t tc_mlp_smem_bytes(const AppearanceConfig& A);  // their largest dynamic s
 size_t tc_activation_bytes(const AppearanceConfig& A, uint64_t n_rows);
 cudaError_t launch_tc_color(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis_idx, uint32_t n_visible,
                             Record* rec, cudaStream_t s);
+// Activation store of a training workspace, per 128-row tile: the hidden activations, the raw outputs (4 halves per
+// row) at outputs_off, and a row block at rows_off of kTcRowDataBytes per row that the geometry pass of the
+// warp-specialised MLP backward fills: SH input chunks (2 x 16 bytes of fp16), the loss-scaled output gradient chunk
+// (16 bytes), then primitive index, 1 / distance and the view direction (u32, 4 floats, padded to 32 bytes).
+constexpr uint32_t kTcRowDataBytes = 80;
+struct TcRowLayout {
+    uint32_t tile_bytes, outputs_off, rows_off;
+};
+// whether launch_tc_backward runs the warp-specialised kernel for these inputs (training with an activation store,
+// one octave, full SH input, no base input, 8 / 16 / 32 features, 16-byte aligned features and gradients); then *L
+// is the store's layout
+bool tc_ws_layout(const Params& P, const AppearanceConfig& A, const GradOut& O, TcRowLayout* L);
 cudaError_t launch_tc_backward(const Params& P, const AppearanceConfig& A, const View& v, const uint32_t* vis_idx, uint32_t n_visible,
                                const uint32_t* rank_of, const Record* sorted_rec, const GradRecord* grads, const GradOut& O, cudaStream_t s);
 constexpr int kTcSelftestFloats = 14400;

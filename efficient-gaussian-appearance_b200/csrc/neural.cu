@@ -859,6 +859,66 @@ __global__ void __launch_bounds__(256, 3) neural_geometry_bwd_kernel(Params P, V
     put3n(O.means, i, gmean, 1);
 }
 
+// The geometry chain rule of the visible rows ahead of the warp-specialised MLP backward (tc_bwd_ws_kernel), which
+// also hands that kernel each row's inputs through the activation store's row block (TcRowLayout): the two fp16 chunks
+// of SH inputs, the loss-scaled output gradient chunk (from the colour pass's stored raw outputs) and the primitive
+// index, 1 / distance and view direction; the base-colour gradient is written here. Same values as tc_bwd_kernel
+// computes (the same functions, compiled with the same flags). This kernel writes the mean gradient first; the MLP
+// backward adds its direction part.
+__global__ void __launch_bounds__(256, 3) neural_geometry_rows_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis,
+                                                                   uint32_t n_rows, const uint32_t* __restrict__ rank_of,
+                                                                   const Record* __restrict__ sorted_rec, const GradRecord* __restrict__ grads,
+                                                                   GradOut O, TcRowLayout L) {
+    const uint32_t gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi >= n_rows) return;
+    const uint32_t i = vis[gi];
+    const uint32_t r = rank_of[i];
+    const GradRecord g = grads[r];
+    const Record rq = sorted_rec[r];
+    const f3 m = ld3(P.means, i);
+    float gmx, gmy, gca, gcb, gcc, g_opacity;
+    blend_sums_to_grads(g, rq, v.proper_aa, gmx, gmy, gca, gcb, gcc, g_opacity);
+    const f3 gmean = geometry_backward(P, v, i, m, gmx, gmy, gca, gcb, gcc, g_opacity, O);
+    if (O.densification != nullptr && O.densification_rows == 3) {
+        const float nx = 0.5f * (g.g2.y * static_cast<float>(v.width)), ny = 0.5f * (g.g2.z * static_cast<float>(v.height));
+        O.densification[2ull * P.n + i] += sqrtf(nx * nx + ny * ny);
+    }
+    put1(O.opacities, i, g_opacity, O.accumulate);
+    put3n(O.means, i, gmean, O.accumulate);
+    // colour-activation gradient and the base-colour gradient
+    const f3 gpre = mk3(g.g1.y, g.g1.z, g.g1.w) * mk3(color_act_grad_from_y(A.color_act, rq.q2.x), color_act_grad_from_y(A.color_act, rq.q2.y),
+                                                      color_act_grad_from_y(A.color_act, rq.q2.z));
+    f3 gbase = mk3(0.0f, 0.0f, 0.0f);
+    if (v.render_base) {
+        const f3 bb = ld3(P.base, i);
+        gbase = mk3(base_act_grad(A.base_act, bb.x), base_act_grad(A.base_act, bb.y), base_act_grad(A.base_act, bb.z)) * gpre;
+    }
+    put3n(O.base, i, gbase, O.accumulate);
+    // the MLP backward's row inputs
+    unsigned char* const tile = P.mlp_act + static_cast<size_t>(gi / 128) * L.tile_bytes;
+    const uint32_t row = gi % 128;
+    const uint2 yo = *reinterpret_cast<const uint2*>(tile + L.outputs_off + row * 8);
+    const float yh[3] = {__low2float(*reinterpret_cast<const __half2*>(&yo.x)), __high2float(*reinterpret_cast<const __half2*>(&yo.x)),
+                         __low2float(*reinterpret_cast<const __half2*>(&yo.y))};
+    const float gv[3] = {gpre.x, gpre.y, gpre.z};
+    float dy[3];
+    for (int c = 0; c < 3; c++) dy[c] = gv[c] * residual_act_grad_from_y(A.res_act, residual_act(A.res_act, yh[c]));
+    float rn = 1.0f;
+    const f3 dir = view_dir(v, m, &rn);
+    float sh[16];
+    sh_band_values(15, min(v.degree, A.max_degree), dir, [&](int k, float val) { sh[k] = val; });
+    auto h2 = [](float lo, float hi) {
+        const __half2 h = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    };
+    uint4* const out = reinterpret_cast<uint4*>(tile + L.rows_off + row * kTcRowDataBytes);
+    out[0] = make_uint4(h2(sh[0], sh[1]), h2(sh[2], sh[3]), h2(sh[4], sh[5]), h2(sh[6], sh[7]));
+    out[1] = make_uint4(h2(sh[8], sh[9]), h2(sh[10], sh[11]), h2(sh[12], sh[13]), h2(sh[14], sh[15]));
+    out[2] = make_uint4(h2(kMlpLossScale * dy[0], kMlpLossScale * dy[1]), h2(kMlpLossScale * dy[2], 0.0f), 0u, 0u);
+    out[3] = make_uint4(i, __float_as_uint(rn), __float_as_uint(dir.x), __float_as_uint(dir.y));
+    out[4] = make_uint4(__float_as_uint(dir.z), 0u, 0u, 0u);
+}
+
 // backward of a view rendered at appearance degree 0 (the MLP is not evaluated, the residual is zero): base-colour
 // gradients of the visible rows; features and the view-direction part of the mean gradient are zero
 __global__ void __launch_bounds__(256) neural_base_bwd_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis, uint32_t n_rows,
@@ -1025,6 +1085,13 @@ cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig
         }
         if (n_visible == 0) return cudaSuccess;
         if (tc_mlp_supported(A)) {
+            TcRowLayout L;
+            if (tc_ws_layout(P, A, O, &L)) {  // warp-specialised MLP backward: the geometry pass first hands it the row inputs
+                neural_geometry_rows_kernel<<<(n_visible + 255) / 256, 256, 0, st>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, L);
+                cudaError_t e = cudaGetLastError();
+                if (e != cudaSuccess) return e;
+                return launch_tc_backward(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, st);
+            }
             cudaError_t e = launch_tc_backward(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, st);
             if (e != cudaSuccess) return e;
             neural_geometry_bwd_kernel<<<(n_visible + 255) / 256, 256, 0, st>>>(P, v, vis, n_visible, rank_of, sorted_rec, grads, O);

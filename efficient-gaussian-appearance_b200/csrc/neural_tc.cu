@@ -146,7 +146,8 @@ constexpr int kTcWidth = 64;
 constexpr int kTcMaxLayers = 8;
 constexpr int kPrefetchFeatures = 32;  // rows of up to 32 latent floats are prefetched into registers (16 per thread)
 // Activation store of the colour pass (training): per 128-row tile, every hidden activation as the 16 KB K-major fp16
-// block the backward's shared slot holds, then the fp16-rounded raw outputs (4 halves per row, the last one zero).
+// block the backward's shared slot holds, then the fp16-rounded raw outputs (4 halves per row, the last one zero), then
+// the row block the geometry pass of the warp-specialised backward fills (TcRowLayout).
 constexpr uint32_t kTcActLayerBytes = kTcRows * kTcWidth * 2;
 constexpr uint32_t kTcActOutBytes = kTcRows * 8;
 
@@ -867,13 +868,437 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
     if (warp == 0) tc::tmem_dealloc(tb, plan.tmem_cols);
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Warp-specialised MLP backward (training, with the colour pass's activation store): one CTA per SM, 512 threads.
+//   warps 0-7    producer, two threads per tile row: gathers the row's inputs one tile ahead, encodes the input row
+//                (fp16, K-major) keeping the fp32 sine and cosine for the input gradient, copies the stored activations
+//                into the stage's slots (cp.async); the row's second thread also writes the SH inputs, the loss-scaled
+//                output gradient and the row's view direction and base-colour gradient. Then every producer thread
+//                arrives on the stage's `full` barrier.
+//   warps 8-11   consumer 0 (stage 0: the CTA's even tiles) and warps 12-15 consumer 1 (stage 1: odd tiles), one
+//                thread per row (warp w reads TMEM lanes 32 (w % 4) ..): the group's first thread issues the layer
+//                MMAs, the group runs the data-gradient epilogues and the input-gradient epilogue, then arrives on the
+//                stage's `empty` barrier. Each consumer owns 256 TMEM columns (its layer accumulator and its
+//                weight-gradient accumulators, added to the output once per CTA).
+// Two tiles are in flight per SM, so one consumer's epilogues overlap the other's MMAs and the producer's encoding
+// of the next tiles. Same arithmetic as tc_bwd_kernel, row by row. Every wait is bounded; a wait that ran out makes
+// its whole role stop (the threads of a role agree through a barrier reduction) and sets the timeout flag, and the
+// other roles' bounded waits then run out in turn.
+constexpr int kWsThreads = 512;
+constexpr int kWsProducers = 256;
+
+bool make_plan(const AppearanceConfig& A, bool backward, TcPlan& p);
+
+struct WsRowInfo {      // per row of a stage: the last 32 bytes of the row block (TcRowLayout)
+    uint32_t i;         // primitive index; 0xffffffff for rows past the end
+    float rn;           // 1 / distance to the camera
+    float dx, dy, dz;   // unit view direction
+    float pad[3];
+};
+
+struct WsPlan {
+    TcPlan t;                          // weights: w_smem, w_off, rows, cols, layers, kin
+    uint32_t stage0, stage_bytes;      // first stage, bytes per stage
+    uint32_t x_off, h_off, y_off, trig_off, info_off;  // offsets within a stage
+    uint32_t wg_col[kTcMaxLayers];     // weight-gradient accumulators within a consumer's 256 columns
+    uint32_t smem_bytes;
+};
+
+bool make_ws_plan(const AppearanceConfig& A, WsPlan& w) {
+    if (!make_plan(A, true, w.t)) return false;
+    const int F = A.feature_dim;
+    if (!(A.n_freq == 1 && (F == 8 || F == 16 || F == 32) && !A.base_input && A.sh_mask == 15 && w.t.kin == 2 * F + 16)) return false;
+    uint32_t wbytes = 0;
+    for (int l = 0; l < w.t.layers; l++) wbytes += static_cast<uint32_t>(w.t.rows[l] * w.t.cols[l]) * 2;
+    w.stage0 = (wbytes + 127) & ~127u;
+    uint32_t o = 0;
+    w.x_off = o;
+    o += kTcRows * static_cast<uint32_t>(w.t.kin) * 2;
+    w.h_off = o;
+    o += static_cast<uint32_t>(w.t.layers - 1) * kTcActLayerBytes;
+    w.y_off = o;
+    o += kTcRows * 16 * 2;
+    w.trig_off = o;
+    o += static_cast<uint32_t>(2 * F) * kTcRows * 4;
+    w.info_off = o;
+    o += kTcRows * static_cast<uint32_t>(sizeof(WsRowInfo));
+    w.stage_bytes = o;
+    w.smem_bytes = w.stage0 + 2 * w.stage_bytes;
+    // the feature-gradient staging block (rows of F + 4 floats, then the row's primitive) fits in the input slot
+    if (static_cast<uint32_t>(F + 4) * kTcRows * 4 + kTcRows * 4 > kTcRows * static_cast<uint32_t>(w.t.kin) * 2) return false;
+    uint32_t cols = static_cast<uint32_t>(w.t.kin > kTcWidth ? w.t.kin : kTcWidth);
+    for (int l = 0; l < w.t.layers; l++) {
+        w.wg_col[l] = cols;
+        cols += static_cast<uint32_t>(l == w.t.layers - 1 ? w.t.rows[l] : w.t.cols[l]);
+    }
+    return cols <= 256 && w.smem_bytes + 256 <= 227u * 1024u;
+}
+
+// Split of a row's producer work: the first thread encodes feature chunks [0, kC0) (4 features = one 16-byte chunk of
+// 8 encoded columns), the second thread chunks [kC0, F / 4) and copies the row block (SH inputs, output gradient, row
+// info) into the stage.
+template <int F>
+struct WsSplit {
+    static constexpr int kChunks = F / 4;
+    static constexpr int kC0 = (kChunks + 1) / 2;
+};
+
+// The producer's row buffer of half H (0: first thread of the row, 1: second): the row's primitive and this thread's
+// latent feature chunks.
+template <int F, int H>
+struct WsRow {
+    static constexpr int kN = H ? WsSplit<F>::kChunks - WsSplit<F>::kC0 : WsSplit<F>::kC0;
+    uint32_t i;
+    bool valid;
+    float4 f[kN > 0 ? kN : 1];
+};
+
+template <int F, int H>
+__device__ inline void ws_load_index(const uint32_t* __restrict__ vis, uint32_t n_rows, uint32_t tile, int row, WsRow<F, H>& d) {
+    const uint32_t gi = tile * kTcRows + row;
+    d.valid = gi < n_rows;
+    d.i = d.valid ? vis[gi] : 0u;
+}
+template <int F, int H>
+__device__ inline void ws_load_features(const Params& P, WsRow<F, H>& d) {
+    if (!d.valid) return;
+    const float4* src = reinterpret_cast<const float4*>(P.residual + static_cast<size_t>(d.i) * F) + (H ? WsSplit<F>::kC0 : 0);
+#pragma unroll
+    for (int q = 0; q < WsRow<F, H>::kN; q++) d.f[q] = src[q];
+}
+
+// producer: this thread's feature chunks of one row of a stage (`xs`: the row's first 16-byte chunk of the input
+// slot; the fp32 sine and cosine go to `trig`); the second thread also clears the output gradient's unused chunk and,
+// for rows past the end, the SH chunks, the output gradient and the row info
+template <int F, int H>
+__device__ inline void ws_write_row(const WsRow<F, H>& d, uint4* xs, float* trig, uint4* ys, WsRowInfo* info, int row) {
+    using S = WsSplit<F>;
+    constexpr int c_lo = H ? S::kC0 : 0, n = WsRow<F, H>::kN;
+    if (H) {
+        ys[8] = make_uint4(0u, 0u, 0u, 0u);
+        if (!d.valid) {
+            xs[8 * S::kChunks] = make_uint4(0u, 0u, 0u, 0u);
+            xs[8 * (S::kChunks + 1)] = make_uint4(0u, 0u, 0u, 0u);
+            ys[0] = make_uint4(0u, 0u, 0u, 0u);
+            info[row].i = 0xffffffffu;
+        }
+    }
+    if (!d.valid) {
+#pragma unroll
+        for (int q = 0; q < n; q++) xs[8 * (c_lo + q)] = make_uint4(0u, 0u, 0u, 0u);
+        return;
+    }
+#pragma unroll
+    for (int q = 0; q < n; q++) {
+        const float4 x = d.f[q];
+        float s0, c0, s1, c1, s2, c2, s3, c3;
+        enc_sincos(x.x, &s0, &c0);
+        enc_sincos(x.y, &s1, &c1);
+        enc_sincos(x.z, &s2, &c2);
+        enc_sincos(x.w, &s3, &c3);
+        xs[8 * (c_lo + q)] = make_uint4(pack2(s0, c0), pack2(s1, c1), pack2(s2, c2), pack2(s3, c3));
+        float* tq = trig + (8 * (c_lo + q)) * kTcRows + row;
+        tq[0] = s0; tq[kTcRows] = c0; tq[2 * kTcRows] = s1; tq[3 * kTcRows] = c1;
+        tq[4 * kTcRows] = s2; tq[5 * kTcRows] = c2; tq[6 * kTcRows] = s3; tq[7 * kTcRows] = c3;
+    }
+}
+
+struct WsShared {  // what the producer and consumers share besides the plan
+    unsigned char* smem;
+    uint32_t sbase;
+    uint64_t* full_bar;
+    uint64_t* empty_bar;
+};
+
+// The producer loop of half H over the CTA's tiles. Three row buffers rotate (this tile, the next, the one after the
+// next), so no buffer is copied while its loads are in flight. Loads are issued after the stage's arrival (an arrival
+// orders this thread's earlier memory accesses, so loads issued before it would be waited for there): the features of
+// the tile after the next and the index of the tile after that. Returns false when a wait ran out.
+template <int F, int H>
+__device__ bool ws_producer(const Params& P, const uint32_t* __restrict__ vis, uint32_t n_rows, const WsPlan& plan, const WsShared& sh,
+                            int row) {
+    using S = WsSplit<F>;
+    const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows, G = gridDim.x;
+    const int last = plan.t.layers - 1;
+    const unsigned char* const act = P.mlp_act;
+    const uint32_t rows_off = static_cast<uint32_t>(last) * kTcActLayerBytes + kTcActOutBytes;
+    WsRow<F, H> ra, rb, rc;
+    uint32_t tile = blockIdx.x;
+    if (tile < n_tiles) {
+        ws_load_index(vis, n_rows, tile, row, ra);
+        ws_load_features(P, ra);
+    }
+    if (tile + G < n_tiles) {
+        ws_load_index(vis, n_rows, tile + G, row, rb);
+        ws_load_features(P, rb);
+    }
+    if (tile + 2 * G < n_tiles) ws_load_index(vis, n_rows, tile + 2 * G, row, rc);
+    auto produce = [&](uint32_t k, WsRow<F, H>& cur, WsRow<F, H>& n2) -> bool {
+        const uint32_t s = k & 1u;
+        if (k >= 2 && !tc::mbar_wait(&sh.empty_bar[s], ((k >> 1) - 1) & 1u)) return false;
+        const uint32_t st = sh.sbase + plan.stage0 + s * plan.stage_bytes;
+        unsigned char* const sg = sh.smem + plan.stage0 + s * plan.stage_bytes;
+        const unsigned char* const at = act_tile(plan.t, act, tile);
+        // this thread's half of the row's stored activations into the stage's slots; the second thread also the row
+        // block (SH chunks into the input slot, the output gradient chunk, the row info); complete before the arrival
+        const uint32_t off = tc::kmajor_offset(row, 0, kTcWidth);
+        for (int j = 0; j < last; j++) {
+            const unsigned char* src = at + static_cast<size_t>(j) * kTcActLayerBytes + off;
+            const uint32_t dst = st + plan.h_off + static_cast<uint32_t>(j) * kTcActLayerBytes + off;
+#pragma unroll
+            for (int q = 0; q < 4; q++) cp_async16(dst + (4 * H + q) * 128, src + (4 * H + q) * 128);
+        }
+        const uint32_t x_row = st + plan.x_off + tc::kmajor_offset(row, 0, 2 * F + 16);
+        if (H && cur.valid) {
+            const unsigned char* rb_src = at + rows_off + static_cast<size_t>(row) * kTcRowDataBytes;
+            cp_async16(x_row + S::kChunks * 128, rb_src);
+            cp_async16(x_row + (S::kChunks + 1) * 128, rb_src + 16);
+            cp_async16(st + plan.y_off + tc::kmajor_offset(row, 0, 16), rb_src + 32);
+            cp_async16(st + plan.info_off + row * 32, rb_src + 48);
+            cp_async16(st + plan.info_off + row * 32 + 16, rb_src + 64);
+        }
+        cp_async_commit();
+        ws_write_row(cur, reinterpret_cast<uint4*>(sg + plan.x_off + tc::kmajor_offset(row, 0, 2 * F + 16)), reinterpret_cast<float*>(sg + plan.trig_off),
+                     reinterpret_cast<uint4*>(sg + plan.y_off + tc::kmajor_offset(row, 0, 16)), reinterpret_cast<WsRowInfo*>(sg + plan.info_off), row);
+        cp_async_wait();
+        tc::fence_smem_to_async();
+        tc::mbar_arrive(&sh.full_bar[s]);
+        if (tile + 2 * G < n_tiles) ws_load_features(P, n2);
+        if (tile + 3 * G < n_tiles) ws_load_index(vis, n_rows, tile + 3 * G, row, cur);
+        return true;
+    };
+    for (uint32_t k = 0; tile < n_tiles;) {
+        if (!produce(k, ra, rc)) return false;
+        k++;
+        if ((tile += G) >= n_tiles) break;
+        if (!produce(k, rb, ra)) return false;
+        k++;
+        if ((tile += G) >= n_tiles) break;
+        if (!produce(k, rc, rb)) return false;
+        k++;
+        tile += G;
+    }
+    return true;
+}
+
+// backward MMAs of layer l for a stage (stage base `st`) into a consumer's columns (`cb`)
+__device__ inline void ws_issue_backward(const WsPlan& p, uint32_t sbase, uint32_t st, uint32_t cb, int l, bool wg_accumulate) {
+    const int last = p.t.layers - 1;
+    const uint32_t in = st + (l == 0 ? p.x_off : p.h_off + static_cast<uint32_t>(l - 1) * kTcActLayerBytes);
+    const uint32_t K = p.t.cols[l], in_row_group = 16u * K;
+    const uint32_t dout = st + (l == last ? p.y_off : p.h_off + static_cast<uint32_t>(l) * kTcActLayerBytes);
+    const uint32_t R = p.t.rows[l], dout_row_group = 16u * R;
+    const uint32_t w = sbase + p.t.w_smem[l];
+    const uint32_t dw = cb + p.wg_col[l];
+    const uint64_t in_mn = tc::desc(in, in_row_group, 128), dout_mn = tc::desc(dout, dout_row_group, 128);
+    if (l == last) {
+        const uint32_t id = tc::idesc(64, R, 1, 1);
+        for (uint32_t ks = 0; ks < kTcRows / 16; ks++)
+            tc::mma(dw, tc::desc_advance(in_mn, ks * 2 * in_row_group), tc::desc_advance(dout_mn, ks * 2 * dout_row_group), id,
+                    (wg_accumulate || ks > 0) ? 1u : 0u);
+    } else {
+        const uint32_t id = tc::idesc(64, K, 1, 1);
+        for (uint32_t ks = 0; ks < kTcRows / 16; ks++)
+            tc::mma(dw, tc::desc_advance(dout_mn, ks * 2 * dout_row_group), tc::desc_advance(in_mn, ks * 2 * in_row_group), id,
+                    (wg_accumulate || ks > 0) ? 1u : 0u);
+    }
+    const uint32_t id = tc::idesc(128, K, 0, 1);
+    const uint64_t dk = tc::desc(dout, 128, dout_row_group), wmn = tc::desc(w, in_row_group, 128);
+    for (uint32_t ks = 0; ks < R / 16; ks++)
+        tc::mma(cb, tc::desc_advance(dk, ks * 256), tc::desc_advance(wmn, ks * 2 * in_row_group), id, ks > 0);
+}
+
+// consumer: data-gradient epilogue of a hidden layer for one row (64 columns): dL/d(activation), masked by the ReLU
+// of the stored activation, written over that activation (fp16, in place; `hs`: the row's first 16-byte chunk).
+// The stored chunks are read before any is written, so the loads issue together.
+__device__ inline void ws_hidden_grad(uint32_t t_addr, uint4* hs, bool relu) {
+    float a[64];
+    tc::ld64(t_addr, a);
+    uint4 h[8];
+#pragma unroll
+    for (int q = 0; q < 8; q++) h[q] = hs[8 * q];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        float* x = a + 8 * q;
+        if (relu) {
+            const uint32_t hw[4] = {h[q].x, h[q].y, h[q].z, h[q].w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float2 hv = unpack2(hw[k]);
+                if (!(hv.x > 0.0f)) x[2 * k] = 0.0f;
+                if (!(hv.y > 0.0f)) x[2 * k + 1] = 0.0f;
+            }
+        }
+        hs[8 * q] = make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+    }
+}
+
+// consumer: loss-scaled dL/d(input) of the row (TMEM columns 0 .. 2F + 15) -> feature gradients into the staging row,
+// the direction gradient added to the mean gradient
+template <int F>
+__device__ inline void ws_input_grad(const AppearanceConfig& A, const GradOut& O, uint32_t t_row, const WsRowInfo& ri, const float* trig, int row,
+                                     int deg, float* stage_row) {
+    const float inv = 1.0f / kLossScale;
+    const bool valid = ri.i != 0xffffffffu;
+#pragma unroll
+    for (int h = 0; h < (F + 15) / 16; h++) {  // 16 features (32 columns) per TMEM load
+        constexpr int kf = F < 16 ? F : 16;
+        float g[2 * kf];
+        if constexpr (kf == 16) tc::ld32(t_row + 32 * h, g);
+        else tc::ld16(t_row + 32 * h, g);
+        if (valid) {
+#pragma unroll
+            for (int q = 0; q < kf / 4; q++) {
+                float gv[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int j = 16 * h + 4 * q + k;
+                    const float sn = trig[(2 * j) * kTcRows + row], cs = trig[(2 * j + 1) * kTcRows + row];
+                    gv[k] = (cs * g[2 * (4 * q + k)] - sn * g[2 * (4 * q + k) + 1]) * inv;
+                }
+                *reinterpret_cast<float4*>(stage_row + 16 * h + 4 * q) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+            }
+        }
+    }
+    float gsh[16];
+    tc::ld16(t_row + 2 * F, gsh);
+    if (!valid) return;
+    if (!A.dir_grad) return;
+    const f3 d = mk3(ri.dx, ri.dy, ri.dz);
+    const f3 gd = inv * sh_band_grad(15, deg, d, gsh);
+    put3n(O.means, ri.i, ri.rn * (gd - dot3(gd, d) * d), 1);  // added to the geometry pass's mean gradient
+}
+
+template <int F>
+__global__ void __launch_bounds__(kWsThreads, 1) tc_bwd_ws_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis,
+                                                                  uint32_t n_rows, const uint32_t* __restrict__ rank_of,
+                                                                  const Record* __restrict__ sorted_rec, const GradRecord* __restrict__ grads,
+                                                                  GradOut O, const __grid_constant__ WsPlan plan) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t full_bar[2], empty_bar[2], mma_bar[2];
+    __shared__ uint32_t tbase;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31, row = t & (kTcRows - 1);
+    const int role = t < kWsProducers ? 0 : 1 + ((t - kWsProducers) >> 7);  // 0 producer, 1 / 2 consumer 0 / 1
+    stage_weights_tc(plan.t, P.mlp, smem);
+    if (warp == 0) tc::tmem_alloc(&tbase, 512);
+    if (t == 0)
+        for (int s = 0; s < 2; s++) {
+            tc::mbar_init(&full_bar[s], kWsProducers);
+            tc::mbar_init(&empty_bar[s], kTcRows);
+            tc::mbar_init(&mma_bar[s], 1);
+        }
+    sync_tile();
+    const uint32_t tb = tbase, sbase = tc::smem_addr(smem);
+    const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows, G = gridDim.x;
+    const int deg = min(v.degree, A.max_degree);
+    const int last = plan.t.layers - 1;
+    bool alive = true;
+    bool wg_started = false, mma_pending = false;
+    uint32_t mma_parity = 0;
+    if (role == 0) {
+        // ---- producer (the two threads of a row are in different warps, so the branch is warp-uniform) ----
+        const WsShared sh{smem, sbase, full_bar, empty_bar};
+        alive = (t >> 7) ? ws_producer<F, 1>(P, vis, n_rows, plan, sh, row) : ws_producer<F, 0>(P, vis, n_rows, plan, sh, row);
+    } else {
+        // ---- consumer g: the CTA's tiles k = g, g + 2, ... on stage g ----
+        const uint32_t g = static_cast<uint32_t>(role - 1), bar_id = 1 + g;
+        const uint32_t cb = tb + g * 256u;
+        const uint32_t t_row = cb + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+        const uint32_t st = sbase + plan.stage0 + g * plan.stage_bytes;
+        unsigned char* const sg = smem + plan.stage0 + g * plan.stage_bytes;
+        const bool issuer = row == 0;
+        const bool relu = A.hidden_act == 1;
+        float* const fstage = reinterpret_cast<float*>(sg + plan.x_off);
+        uint32_t* const fprim = reinterpret_cast<uint32_t*>(sg + plan.x_off + static_cast<uint32_t>(F + 4) * kTcRows * 4);
+        const float* const trig = reinterpret_cast<const float*>(sg + plan.trig_off);
+        const WsRowInfo* const info = reinterpret_cast<const WsRowInfo*>(sg + plan.info_off);
+        for (uint32_t k = g, tile = blockIdx.x + g * G; tile < n_tiles; k += 2, tile += 2 * G) {
+            const bool ok = tc::mbar_wait(&full_bar[g], (k >> 1) & 1u);
+            if (tc::bar_or(bar_id, kTcRows, !ok)) {
+                alive = false;
+                break;
+            }
+            tc::fence_after_sync();
+            for (int l = last; l >= 0; l--) {
+                if (issuer) {
+                    ws_issue_backward(plan, sbase, st, cb, l, wg_started);
+                    tc::commit(&mma_bar[g]);
+                }
+                __syncwarp();
+                mma_pending = true;
+                const bool done = tc::mbar_wait(&mma_bar[g], mma_parity);
+                if (tc::bar_or(bar_id, kTcRows, !done)) {
+                    alive = false;
+                    break;
+                }
+                mma_pending = false;
+                mma_parity ^= 1u;
+                tc::fence_after_sync();
+                if (l > 0) {
+                    ws_hidden_grad(t_row, reinterpret_cast<uint4*>(sg + plan.h_off + static_cast<uint32_t>(l - 1) * kTcActLayerBytes +
+                                                                   tc::kmajor_offset(row, 0, kTcWidth)),
+                                   relu);
+                    tc::fence_smem_to_async();
+                    tc::fence_before_sync();
+                    tc::bar_sync(bar_id, kTcRows);
+                    tc::fence_after_sync();
+                }
+            }
+            if (!alive) break;
+            wg_started = true;
+            const WsRowInfo ri = info[row];
+            ws_input_grad<F>(A, O, t_row, ri, trig, row, deg, fstage + row * (F + 4));
+            fprim[row] = ri.i;
+            tc::fence_before_sync();
+            tc::bar_sync(bar_id, kTcRows);
+            // the staged feature gradients by whole rows
+#pragma unroll
+            for (int m = 0; m < F / 4; m++) {
+                const int c = row + kTcRows * m, r = c / (F / 4), q = c % (F / 4);
+                const uint32_t pi = fprim[r];
+                if (pi == 0xffffffffu) continue;
+                const float4 val = *reinterpret_cast<const float4*>(fstage + r * (F + 4) + 4 * q);
+                float4* dst = reinterpret_cast<float4*>(O.residual + static_cast<size_t>(pi) * F + 4 * q);
+                if (O.accumulate) atomicAdd(dst, val);  // one addition per element and launch (deterministic)
+                else *dst = val;
+            }
+            tc::mbar_arrive(&empty_bar[g]);
+        }
+        if (!alive && mma_pending) tc::mbar_wait(&mma_bar[g], mma_parity);  // no MMA in flight when the columns are freed
+        // weight gradients of this consumer (M = 64 accumulators: row m in lane (m % 16) + 32 (m / 16)), unscaled
+        if (wg_started && alive) {
+            const float inv = 1.0f / kLossScale;
+            const int m = (warp & 3) * 16 + lane;
+            for (int l = 0; l < plan.t.layers; l++) {
+                const int ncol = l == last ? plan.t.rows[l] : plan.t.cols[l];
+                for (int c0 = 0; c0 < ncol; c0 += 16) {
+                    float a[16];
+                    tc::ld16(t_row + plan.wg_col[l] + c0, a);
+                    if (lane < 16)
+                        for (int kk = 0; kk < 16; kk++) {
+                            const int c = c0 + kk;
+                            float* dst = l == last ? O.mlp + plan.t.w_off[l] + c * kTcWidth + m : O.mlp + plan.t.w_off[l] + m * plan.t.cols[l] + c;
+                            atomicAdd(dst, a[kk] * inv);
+                        }
+                }
+            }
+        }
+    }
+    if (!alive && row == 0) atomicExch(&g_tc_timeout, 1);
+    cp_async_wait();  // no activation copy outlives the CTA (only a timeout leaves one in flight)
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tb, 512);
+}
+
 bool make_plan(const AppearanceConfig& A, bool backward, TcPlan& p) {
     if (A.n_neurons != kTcWidth || A.n_hidden < 1 || A.n_hidden + 1 > kTcMaxLayers) return false;
     p = TcPlan{};
     p.layers = A.n_hidden + 1;
     p.kin = A.n_input_pad;
     p.backward = backward ? 1 : 0;
-    p.act_tile_bytes = static_cast<uint32_t>(p.layers - 1) * kTcActLayerBytes + kTcActOutBytes;
+    p.act_tile_bytes = static_cast<uint32_t>(p.layers - 1) * kTcActLayerBytes + kTcActOutBytes + kTcRows * kTcRowDataBytes;
     if (p.kin % 16 != 0 || p.kin > 256) return false;
     uint32_t off = 0, w = 0;
     for (int l = 0; l < p.layers; l++) {
@@ -959,6 +1384,17 @@ size_t tc_activation_bytes(const AppearanceConfig& A, uint64_t n_rows) {
     return static_cast<size_t>((n_rows + kTcRows - 1) / kTcRows) * p.act_tile_bytes;
 }
 
+bool tc_ws_layout(const Params& P, const AppearanceConfig& A, const GradOut& O, TcRowLayout* L) {
+    WsPlan w;
+    if (!P.mlp_act || !make_ws_plan(A, w) || (reinterpret_cast<uintptr_t>(P.residual) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(O.residual) & 15u) != 0)
+        return false;
+    L->tile_bytes = w.t.act_tile_bytes;
+    L->outputs_off = static_cast<uint32_t>(w.t.layers - 1) * kTcActLayerBytes;
+    L->rows_off = L->outputs_off + kTcActOutBytes;
+    return true;
+}
+
 size_t tc_mlp_smem_bytes(const AppearanceConfig& A) {
     TcPlan f, b;
     if (!make_plan(A, false, f) || !make_plan(A, true, b)) return 0;
@@ -982,8 +1418,25 @@ cudaError_t launch_tc_backward(const Params& P, const AppearanceConfig& A, const
     TcPlan p;
     if (!make_plan(A, true, p)) return cudaErrorInvalidConfiguration;
     if (n_visible == 0) return cudaSuccess;
+    const uint32_t n_tiles = (n_visible + kTcRows - 1) / kTcRows;
+    WsPlan w;
+    TcRowLayout L;
+    if (tc_ws_layout(P, A, O, &L) && make_ws_plan(A, w)) {
+        auto launch = [&](auto kernel) -> cudaError_t {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(w.smem_bytes));
+            if (e != cudaSuccess) return e;
+            const int grid = static_cast<int>(n_tiles < static_cast<uint32_t>(tc_sm_count()) ? n_tiles : tc_sm_count());
+            kernel<<<grid, kWsThreads, w.smem_bytes, s>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, w);
+            return cudaGetLastError();
+        };
+        switch (A.feature_dim) {
+            case 8: return launch(tc_bwd_ws_kernel<8>);
+            case 16: return launch(tc_bwd_ws_kernel<16>);
+            default: return launch(tc_bwd_ws_kernel<32>);
+        }
+    }
     int grid = 0;
-    cudaError_t e = tc_grid(tc_bwd_kernel, p, (n_visible + kTcRows - 1) / kTcRows, 2, &grid);
+    cudaError_t e = tc_grid(tc_bwd_kernel, p, n_tiles, 2, &grid);
     if (e != cudaSuccess) return e;
     tc_bwd_kernel<<<grid, kTcThreads, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O, p);
     return cudaGetLastError();

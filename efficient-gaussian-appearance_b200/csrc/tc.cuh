@@ -73,6 +73,28 @@ __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
+// one arrival of this thread (release: its earlier shared-memory writes are visible to the threads that observe the
+// completed phase)
+__device__ inline void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}\n" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// named barrier `id` (1..15) over `n` threads (whole warps)
+__device__ inline void bar_sync(uint32_t id, uint32_t n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// the same barrier, returning whether any of the `n` threads passed true
+__device__ inline bool bar_or(uint32_t id, uint32_t n, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred q, o;\n\t"
+        "setp.ne.b32 q, %1, 0;\n\t"
+        "bar.red.or.pred o, %2, %3, q;\n\t"
+        "selp.b32 %0, 1, 0, o;\n\t}\n"
+        : "=r"(r)
+        : "r"(p ? 1u : 0u), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
+
 // TMEM allocation (whole warp): the base address is written to *dst
 __device__ inline void tmem_alloc(uint32_t* dst, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)), "r"(ncols) : "memory");

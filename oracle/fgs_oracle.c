@@ -3,17 +3,21 @@
  * CPU restatement of the reference rasterizer (nerficg-project/efficient-gaussian-appearance,
  * FasterGSVDACudaBackend) used only as the checker by tests/, __graft_entry__.smoke() and the cpu_baseline
  * leg of bench.py. Built twice by oracle/Makefile:
- *   - ORC_REAL=float : the working-precision pipeline performs the same IEEE operations in the same order as
- *     the CUDA kernels (compiled with -ffp-contract=off, explicit fmaf where the kernels use fmaf, and the same
- *     polynomial exp / log), so culling, keys, tile lists, ranges and contributor counts are reproduced
- *     bit for bit; images are bit-exact wherever the colors are (precomputed colors, SH).
+ *   - ORC_REAL=float : the working-precision pipeline in the kernels' operation order with IEEE single-precision
+ *     arithmetic (compiled with -ffp-contract=off, explicit fmaf where the kernels use one, the single-rounding forms
+ *     of the reference's projection and tile test, and its exp2 fragment acceptance on the host's exp2). The GPU path
+ *     evaluates those steps with the reference build's fast-math approximations (division, square root, exp, log,
+ *     exp2), which C cannot reproduce, so the two agree within rounding and a decision within a rounding of its
+ *     threshold may go either way; the Neural MLP (encoding, SH inputs, tensor-core accumulation, orc_neural.h) is
+ *     restated exactly.
  *   - ORC_REAL=double: a smooth double-precision forward used for finite-difference checks of the backward.
  * The backward always evaluates values in double; the accept / terminate decisions come from the forward.
  *
  * Parity pinning: the appearance models are pinned against golden vectors produced by the reference's own
- * PyTorch modules (Appearance/SH.py, SV.py, NASG.py, NASGabor.py) under tests/golden/. The rasterizer
- * geometry, binning and blending are "parity unpinned": the reference ships no tests or fixtures and its CUDA
- * backend cannot be built here (tiny-cuda-nn submodule absent); gradients are checked by finite differences.
+ * PyTorch modules (Appearance/SH.py, SV.py, NASG.py, NASGabor.py) under tests/golden/. The rasterizer (geometry,
+ * binning, blending, backward) is pinned on the GPU against the reference's own kernels, built from its unmodified
+ * sources by oracle/ref_build.py (oracle/reference.py); this restatement is checked against those same runs within
+ * the bounds above, and its gradients against finite differences.
  *
  * Reference files followed (paths within the reference project):
  *   preprocess forward   FasterGSVDACudaBackend/FasterGSVDACudaBackend/rasterization/rtc/preprocess_forward.cu:12-278

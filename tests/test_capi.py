@@ -56,8 +56,9 @@ def test_workspace_queries():
 
 def test_workspace_activation_store_size():
     """A rasterizer whose Neural MLP runs on the tensor cores (64 neurons) sizes the primitive workspace with the
-    activation store: per 128-row tile one 16 KB block per hidden layer plus 1 KB of raw outputs, after the other
-    buffers (one 256-byte alignment step at most); NULL, SH and 16-wide networks size it without."""
+    activation store: per 128-row tile one 16 KB block per hidden layer, 1 KB of raw outputs and the 80-byte row block
+    of each row (filled by the geometry pass of the warp-specialised backward), after the other buffers (one 256-byte
+    alignment step at most); NULL, SH and 16-wide networks size it without."""
     import FasterGSVDACudaBackend as F
     from FasterGSVDACudaBackend._lib import lib, size_out
     from FasterGSVDACudaBackend import rasterization as R
@@ -70,7 +71,7 @@ def test_workspace_activation_store_size():
         with_store = size_out(lib.fgs_primitive_workspace_bytes, R._rasterizer.handle, n)
         without = size_out(lib.fgs_primitive_workspace_bytes, None, n)
         extra = with_store - without
-        store = tiles * (hidden * 128 * 64 * 2 + 128 * 8)
+        store = tiles * (hidden * 128 * 64 * 2 + 128 * 8 + 128 * 80)
         assert store <= extra < store + 256, (hidden, extra, store)
     F.initialize_residual_mlp(80, 3, {'otype': 'Identity'}, {'otype': 'FullyFusedMLP', 'activation': 'ReLU', 'output_activation': 'None',
                                                               'n_neurons': 16, 'n_hidden_layers': 2}, False, 1, [0, 1, 2, 3])

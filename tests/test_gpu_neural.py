@@ -167,13 +167,15 @@ def test_neural_accumulate_two_views(cuda):
         assert err <= 1e-5, f'{k}: relative error {err:.2e}'
 
 
-@pytest.mark.parametrize('cfg', [(16, 0, 64, 1, False, 'none'), (32, 1, 64, 2, False, 'tanh'), (8, 2, 64, 3, True, 'softplus')],
-                         ids=['1-hidden', '2-hidden', '3-hidden-base'])
+@pytest.mark.parametrize('cfg', [(16, 0, 64, 1, False, 'none'), (32, 1, 64, 2, False, 'tanh'), (8, 2, 64, 3, True, 'softplus'),
+                                 (16, 1, 64, 1, False, 'none'), (8, 1, 64, 2, False, 'softplus')],
+                         ids=['1-hidden', '2-hidden', '3-hidden-base', 'f16-1-hidden', 'f8-2-hidden'])
 def test_neural_stored_activations_match_recompute(cuda, cfg):
     """A training forward keeps the tensor-core MLP's activations for the backward (frame.mlp_activations); a forward
     whose workspace excludes the store (training=False) leaves the backward to recompute them. Both give the same
     image and the same gradients (up to the order of the fp32 atomics), over enough rows that every CTA fetches
-    several tiles' activations."""
+    several tiles' activations. In the cases with one octave and no base input ('2-hidden', 'f16-1-hidden',
+    'f8-2-hidden') the stored path runs the warp-specialised backward, so these also check it against the other kernel."""
     import FasterGSVDACudaBackend as F
     from FasterGSVDACudaBackend import rasterization as R, _lib
     feat, nf, nn, nh, base_input, res_act = cfg
