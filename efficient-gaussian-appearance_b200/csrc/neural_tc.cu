@@ -448,6 +448,8 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
     sync_tile();
     bool alive = true;
     const uint32_t tb = tbase, sbase = tc::smem_addr(smem);
+    const int wu = tc::warp_id_uniform();                 // warp-uniform operands for the elected MMA issue
+    const uint32_t tbu = __shfl_sync(0xffffffffu, tb, 0);
     const uint32_t t_row = tb + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int deg = min(v.degree, A.max_degree);
     uint32_t phase = 0;
@@ -468,11 +470,13 @@ __global__ void __launch_bounds__(kTcThreads, 3) tc_color_kernel(Params P, Appea
         write_input_row(P, A, v, deg, cur, fast, half, x_row, plan.kin, nullptr, row);
         sync_tile();
         for (int l = 0; l < plan.layers; l++) {
-            if (t == 0) {
-                issue_forward(plan, sbase, tb, l);
-                tc::commit(&bar);
+            if (wu == 0) {
+                if (tc::elect_one()) {
+                    issue_forward(plan, sbase, tbu, l);
+                    tc::commit(&bar);
+                }
+                __syncwarp();
             }
-            __syncwarp();
             if (l == 0 && more) load_row_params(P, A, fast, half, nullptr, nxt);
             alive = wait_all(&bar, phase);
             if (!alive) break;
@@ -711,6 +715,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
     sync_tile();
     bool alive = true;
     const uint32_t tb = tbase, sbase = tc::smem_addr(smem);
+    const int wu = tc::warp_id_uniform();                 // warp-uniform operands for the elected MMA issue
+    const uint32_t tbu = __shfl_sync(0xffffffffu, tb, 0);
     const uint32_t t_row = tb + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int deg = min(v.degree, A.max_degree);
     const int last = plan.layers - 1;
@@ -764,11 +770,13 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
         sync_tile();
         // recomputed forward (no activation store); the last layer's outputs become the scaled output gradient
         for (int l = 0; l < plan.layers && alive && !act; l++) {
-            if (t == 0) {
-                issue_forward(plan, sbase, tb, l);
-                tc::commit(&bar);
+            if (wu == 0) {
+                if (tc::elect_one()) {
+                    issue_forward(plan, sbase, tbu, l);
+                    tc::commit(&bar);
+                }
+                __syncwarp();
             }
-            __syncwarp();
             if (l == 0 && more) load_row_params(P, A, fast, half, rank_of, nxt);
             alive = wait_all(&bar, phase);
             if (!alive) break;
@@ -784,11 +792,13 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_bwd_kernel(Params P, Appeara
         }
         // layers last to first
         for (int l = last; l >= 0 && alive; l--) {
-            if (t == 0) {
-                issue_backward(plan, sbase, tb, l, wg_started);
-                tc::commit(&bar);
+            if (wu == 0) {
+                if (tc::elect_one()) {
+                    issue_backward(plan, sbase, tbu, l, wg_started);
+                    tc::commit(&bar);
+                }
+                __syncwarp();
             }
-            __syncwarp();
             if (more) {
                 if (!act) {
                     if (l == last) load_row_rank(sorted_rec, grads, nxt);
@@ -1201,12 +1211,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_bwd_ws_kernel(Params P, Appe
         alive = (t >> 7) ? ws_producer<F, 1>(P, vis, n_rows, plan, sh, row) : ws_producer<F, 0>(P, vis, n_rows, plan, sh, row);
     } else {
         // ---- consumer g: the CTA's tiles k = g, g + 2, ... on stage g ----
-        const uint32_t g = static_cast<uint32_t>(role - 1), bar_id = 1 + g;
-        const uint32_t cb = tb + g * 256u;
-        const uint32_t t_row = cb + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+        // the MMA operands derive from warp-uniform values only (warp index and TMEM base through a shuffle), so the
+        // elected lane issues them from uniform registers
+        const int wu = tc::warp_id_uniform();
+        const uint32_t g = static_cast<uint32_t>((wu - kWsProducers / 32) >> 2), bar_id = 1 + g;
+        const uint32_t cb = __shfl_sync(0xffffffffu, tb, 0) + g * 256u;
+        const uint32_t t_row = cb + (static_cast<uint32_t>((wu & 3) * 32) << 16);
         const uint32_t st = sbase + plan.stage0 + g * plan.stage_bytes;
         unsigned char* const sg = smem + plan.stage0 + g * plan.stage_bytes;
-        const bool issuer = row == 0;
+        const bool issuer_warp = (wu & 3) == 0;
         const bool relu = A.hidden_act == 1;
         float* const fstage = reinterpret_cast<float*>(sg + plan.x_off);
         uint32_t* const fprim = reinterpret_cast<uint32_t*>(sg + plan.x_off + static_cast<uint32_t>(F + 4) * kTcRows * 4);
@@ -1220,11 +1233,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_bwd_ws_kernel(Params P, Appe
             }
             tc::fence_after_sync();
             for (int l = last; l >= 0; l--) {
-                if (issuer) {
-                    ws_issue_backward(plan, sbase, st, cb, l, wg_started);
-                    tc::commit(&mma_bar[g]);
+                if (issuer_warp) {
+                    if (tc::elect_one()) {
+                        ws_issue_backward(plan, sbase, st, cb, l, wg_started);
+                        tc::commit(&mma_bar[g]);
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
                 mma_pending = true;
                 const bool done = tc::mbar_wait(&mma_bar[g], mma_parity);
                 if (tc::bar_or(bar_id, kTcRows, !done)) {

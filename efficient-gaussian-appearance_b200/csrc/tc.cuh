@@ -79,6 +79,20 @@ __device__ inline void mbar_arrive(uint64_t* bar) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}\n" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// true in exactly one lane of the (fully active) warp. Issue code placed under it with operands computed from
+// warp-uniform values keeps the MMA operands in uniform registers.
+__device__ inline bool elect_one() {
+    uint32_t p;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "elect.sync _|P, 0xffffffff;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}\n"
+        : "=r"(p));
+    return p != 0;
+}
+// the warp index as a value the compiler knows to be warp-uniform
+__device__ inline int warp_id_uniform() { return __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0); }
+
 // named barrier `id` (1..15) over `n` threads (whole warps)
 __device__ inline void bar_sync(uint32_t id, uint32_t n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 // the same barrier, returning whether any of the `n` threads passed true
