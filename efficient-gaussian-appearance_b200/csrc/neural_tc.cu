@@ -1307,6 +1307,268 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_bwd_ws_kernel(Params P, Appe
     if (warp == 0) tc::tmem_dealloc(tb, 512);
 }
 
+// ---------------------------------------------------------------------------------------------------
+// Warp-specialised colour pass (the forward MLP): one CTA per SM, 512 threads, four stages.
+//   warps 0-7    producer, two threads per row: the latent features of the row's tile, encoded into the stage's input
+//                slot (fp16, K-major); the second thread also the SH inputs and the row's primitive index and base colour.
+//   warps 8-11   consumer 0 (the CTA's even tiles, stages 0 and 2) and warps 12-15 consumer 1 (odd tiles, stages 1 and
+//                3), one thread per row: per layer the group's elected lane issues the MMAs into the group's TMEM
+//                columns, the group applies the activation and writes the fp16 activations over the stage's input slot
+//                (and, training, into the activation store); after the last layer the colour goes to the record.
+// A stage holds only the input slot and the row info, so four fit and the producer runs two tiles ahead of each
+// consumer. Same arithmetic as tc_color_kernel.
+constexpr int kCwStages = 4;
+
+struct CwRowInfo {   // per row of a stage: primitive index (0xffffffff past the end) and base-colour parameters
+    uint32_t i;
+    float bx, by, bz;
+};
+
+struct CwPlan {
+    TcPlan t;
+    uint32_t stage0, stage_bytes, info_off, smem_bytes;
+};
+
+bool make_cw_plan(const AppearanceConfig& A, CwPlan& w) {
+    if (!make_plan(A, false, w.t)) return false;
+    const int F = A.feature_dim;
+    if (!(A.n_freq == 1 && (F == 8 || F == 16 || F == 32) && !A.base_input && A.sh_mask == 15 && w.t.kin == 2 * F + 16)) return false;
+    uint32_t wbytes = 0;
+    for (int l = 0; l < w.t.layers; l++) wbytes += static_cast<uint32_t>(w.t.rows[l] * w.t.cols[l]) * 2;
+    w.stage0 = (wbytes + 127) & ~127u;
+    const uint32_t in_bytes = kTcRows * static_cast<uint32_t>(w.t.kin > kTcWidth ? w.t.kin : kTcWidth) * 2;  // input, then activations
+    w.info_off = in_bytes;
+    w.stage_bytes = in_bytes + kTcRows * static_cast<uint32_t>(sizeof(CwRowInfo));
+    w.smem_bytes = w.stage0 + kCwStages * w.stage_bytes;
+    return w.smem_bytes + 256 <= 227u * 1024u;
+}
+
+template <int F, int H>
+struct CwRow {
+    static constexpr int kN = H ? WsSplit<F>::kChunks - WsSplit<F>::kC0 : WsSplit<F>::kC0;
+    uint32_t i;
+    bool valid;
+    f3 mean, base;                 // second thread only
+    float4 f[kN > 0 ? kN : 1];
+};
+
+template <int F, int H>
+__device__ inline void cw_load(const Params& P, CwRow<F, H>& d) {
+    if (!d.valid) return;
+    const float4* src = reinterpret_cast<const float4*>(P.residual + static_cast<size_t>(d.i) * F) + (H ? WsSplit<F>::kC0 : 0);
+#pragma unroll
+    for (int q = 0; q < CwRow<F, H>::kN; q++) d.f[q] = src[q];
+    if (H) {
+        d.mean = ld3(P.means, d.i);
+        d.base = ld3(P.base, d.i);
+    }
+}
+
+// The colour pass's producer loop of half H; three row buffers rotate as in ws_producer. Returns false when a wait
+// ran out.
+template <int F, int H>
+__device__ bool cw_producer(const Params& P, const View& v, int deg, const uint32_t* __restrict__ vis, uint32_t n_rows, const CwPlan& plan,
+                            const WsShared& sh, int row) {
+    using S = WsSplit<F>;
+    constexpr int c_lo = H ? S::kC0 : 0;
+    const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows, G = gridDim.x;
+    auto index = [&](uint32_t tile, CwRow<F, H>& d) {
+        const uint32_t gi = tile * kTcRows + row;
+        d.valid = gi < n_rows;
+        d.i = d.valid ? vis[gi] : 0u;
+    };
+    CwRow<F, H> ra, rb, rc;
+    uint32_t tile = blockIdx.x;
+    if (tile < n_tiles) {
+        index(tile, ra);
+        cw_load(P, ra);
+    }
+    if (tile + G < n_tiles) {
+        index(tile + G, rb);
+        cw_load(P, rb);
+    }
+    if (tile + 2 * G < n_tiles) index(tile + 2 * G, rc);
+    auto produce = [&](uint32_t k, CwRow<F, H>& cur, CwRow<F, H>& n2) -> bool {
+        const uint32_t s = k % kCwStages;
+        if (k >= kCwStages && !tc::mbar_wait(&sh.empty_bar[s], ((k / kCwStages) - 1) & 1u)) return false;
+        unsigned char* const sg = sh.smem + plan.stage0 + s * plan.stage_bytes;
+        uint4* const xs = reinterpret_cast<uint4*>(sg + tc::kmajor_offset(row, 0, 2 * F + 16));
+        CwRowInfo* const info = reinterpret_cast<CwRowInfo*>(sg + plan.info_off);
+        if (!cur.valid) {
+#pragma unroll
+            for (int q = 0; q < CwRow<F, H>::kN; q++) xs[8 * (c_lo + q)] = make_uint4(0u, 0u, 0u, 0u);
+            if (H) {
+                xs[8 * S::kChunks] = make_uint4(0u, 0u, 0u, 0u);
+                xs[8 * (S::kChunks + 1)] = make_uint4(0u, 0u, 0u, 0u);
+                info[row] = CwRowInfo{0xffffffffu, 0.0f, 0.0f, 0.0f};
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < CwRow<F, H>::kN; q++) {
+                const float4 x = cur.f[q];
+                float s0, c0, s1, c1, s2, c2, s3, c3;
+                enc_sincos(x.x, &s0, &c0);
+                enc_sincos(x.y, &s1, &c1);
+                enc_sincos(x.z, &s2, &c2);
+                enc_sincos(x.w, &s3, &c3);
+                xs[8 * (c_lo + q)] = make_uint4(pack2(s0, c0), pack2(s1, c1), pack2(s2, c2), pack2(s3, c3));
+            }
+            if (H) {
+                const f3 dir = view_dir(v, cur.mean, nullptr);
+                float shv[16];
+                sh_band_values(15, deg, dir, [&](int kk, float val) { shv[kk] = val; });
+                xs[8 * S::kChunks] = make_uint4(pack2(shv[0], shv[1]), pack2(shv[2], shv[3]), pack2(shv[4], shv[5]), pack2(shv[6], shv[7]));
+                xs[8 * (S::kChunks + 1)] =
+                    make_uint4(pack2(shv[8], shv[9]), pack2(shv[10], shv[11]), pack2(shv[12], shv[13]), pack2(shv[14], shv[15]));
+                info[row] = CwRowInfo{cur.i, cur.base.x, cur.base.y, cur.base.z};
+            }
+        }
+        tc::fence_smem_to_async();
+        tc::mbar_arrive(&sh.full_bar[s]);
+        // loads after the arrival (which orders this thread's earlier memory accesses)
+        if (tile + 2 * G < n_tiles) cw_load(P, n2);
+        if (tile + 3 * G < n_tiles) index(tile + 3 * G, cur);
+        return true;
+    };
+    for (uint32_t k = 0; tile < n_tiles;) {
+        if (!produce(k, ra, rc)) return false;
+        k++;
+        if ((tile += G) >= n_tiles) break;
+        if (!produce(k, rb, ra)) return false;
+        k++;
+        if ((tile += G) >= n_tiles) break;
+        if (!produce(k, rc, rb)) return false;
+        k++;
+        tile += G;
+    }
+    return true;
+}
+
+template <int F>
+__global__ void __launch_bounds__(kWsThreads, 1) tc_color_ws_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis,
+                                                                    uint32_t n_rows, Record* __restrict__ rec, const __grid_constant__ CwPlan plan) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t full_bar[kCwStages], empty_bar[kCwStages], mma_bar[2];
+    __shared__ uint32_t tbase;
+    const int t = threadIdx.x, warp = t >> 5, row = t & (kTcRows - 1);
+    const bool producer = t < kWsProducers;
+    stage_weights_tc(plan.t, P.mlp, smem);
+    if (warp == 0) tc::tmem_alloc(&tbase, 256);
+    if (t == 0) {
+        for (int s = 0; s < kCwStages; s++) {
+            tc::mbar_init(&full_bar[s], kWsProducers);
+            tc::mbar_init(&empty_bar[s], kTcRows);
+        }
+        tc::mbar_init(&mma_bar[0], 1);
+        tc::mbar_init(&mma_bar[1], 1);
+    }
+    sync_tile();
+    const uint32_t sbase = tc::smem_addr(smem);
+    const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows, G = gridDim.x;
+    const int deg = min(v.degree, A.max_degree);
+    bool alive = true;
+    bool mma_pending = false;
+    uint32_t mma_parity = 0;
+    if (producer) {
+        const WsShared sh{smem, sbase, full_bar, empty_bar};
+        alive = (t >> 7) ? cw_producer<F, 1>(P, v, deg, vis, n_rows, plan, sh, row) : cw_producer<F, 0>(P, v, deg, vis, n_rows, plan, sh, row);
+    } else {
+        // ---- consumer g: the CTA's tiles k = g, g + 2, ... (stage k % 4) ----
+        const int wu = tc::warp_id_uniform();
+        const uint32_t g = static_cast<uint32_t>((wu - kWsProducers / 32) >> 2), bar_id = 1 + g;
+        const uint32_t cb = __shfl_sync(0xffffffffu, tbase, 0) + g * 128u;
+        const uint32_t t_row = cb + (static_cast<uint32_t>((wu & 3) * 32) << 16);
+        const bool issuer_warp = (wu & 3) == 0;
+        const bool relu = A.hidden_act == 1;
+        const int last = plan.t.layers - 1;
+        const uint32_t h_row = tc::kmajor_offset(row, 0, kTcWidth);
+        for (uint32_t k = g, tile = blockIdx.x + g * G; tile < n_tiles; k += 2, tile += 2 * G) {
+            const uint32_t s = k % kCwStages;
+            const bool ok = tc::mbar_wait(&full_bar[s], (k / kCwStages) & 1u);
+            if (tc::bar_or(bar_id, kTcRows, !ok)) {
+                alive = false;
+                break;
+            }
+            tc::fence_after_sync();
+            const uint32_t st = sbase + plan.stage0 + s * plan.stage_bytes;
+            unsigned char* const sg = smem + plan.stage0 + s * plan.stage_bytes;
+            const CwRowInfo ri = reinterpret_cast<const CwRowInfo*>(sg + plan.info_off)[row];
+            unsigned char* const act = P.mlp_act ? P.mlp_act + static_cast<size_t>(tile) * plan.t.act_tile_bytes : nullptr;
+            for (int l = 0; l <= last; l++) {
+                if (issuer_warp) {
+                    if (tc::elect_one()) {
+                        // the input (layer 0) or the previous activations, written over the input slot
+                        const uint32_t K = plan.t.cols[l], sbo = 16u * K, w = sbase + plan.t.w_smem[l];
+                        const uint32_t id = tc::idesc(128, plan.t.rows[l], 0, 0);
+                        const uint64_t a = tc::desc(st, 128, sbo), b = tc::desc(w, 128, sbo);
+                        for (uint32_t ks = 0; ks < K / 16; ks++) tc::mma(cb, tc::desc_advance(a, ks * 256), tc::desc_advance(b, ks * 256), id, ks > 0);
+                        tc::commit(&mma_bar[g]);
+                    }
+                    __syncwarp();
+                }
+                mma_pending = true;
+                const bool done = tc::mbar_wait(&mma_bar[g], mma_parity);
+                if (tc::bar_or(bar_id, kTcRows, !done)) {
+                    alive = false;
+                    break;
+                }
+                mma_pending = false;
+                mma_parity ^= 1u;
+                tc::fence_after_sync();
+                if (l < last) {
+                    float a[64];
+                    tc::ld64(t_row, a);
+                    uint4* const hs = reinterpret_cast<uint4*>(sg + h_row);
+                    uint4* const ga = act ? reinterpret_cast<uint4*>(act + static_cast<size_t>(l) * kTcActLayerBytes + h_row) : nullptr;
+#pragma unroll
+                    for (int q = 0; q < 8; q++) {
+                        float* x = a + 8 * q;
+                        if (relu)
+#pragma unroll
+                            for (int kk = 0; kk < 8; kk++) x[kk] = fmaxf(x[kk], 0.0f);
+                        const uint4 h = make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+                        hs[8 * q] = h;
+                        if (ga) ga[8 * q] = h;
+                    }
+                    tc::fence_smem_to_async();
+                    tc::fence_before_sync();
+                    tc::bar_sync(bar_id, kTcRows);
+                    tc::fence_after_sync();
+                } else {
+                    float y[16];
+                    tc::ld16(t_row, y);
+                    if (act)
+                        *reinterpret_cast<uint2*>(act + static_cast<size_t>(l) * kTcActLayerBytes + row * 8) =
+                            make_uint2(pack2(y[0], y[1]), pack2(y[2], 0.0f));
+                    if (ri.i != 0xffffffffu) {
+                        const f3 res = residual_act3(A.res_act, mk3(__half2float(__float2half_rn(y[0])), __half2float(__float2half_rn(y[1])),
+                                                                     __half2float(__float2half_rn(y[2]))));
+                        const f3 base = base_act3(A.base_act, mk3(ri.bx, ri.by, ri.bz));
+                        f3 color = color_act3(A.color_act, base + res);
+                        if (!v.render_base) {
+                            const f3 bc = color_act3(A.color_act, base);
+                            color = mk3(fabsf(color.x - bc.x), fabsf(color.y - bc.y), fabsf(color.z - bc.z));
+                        }
+                        float* q2 = reinterpret_cast<float*>(rec + ri.i) + 8;
+                        q2[0] = color.x;
+                        q2[1] = color.y;
+                        q2[2] = color.z;
+                    }
+                    tc::fence_before_sync();
+                }
+            }
+            if (!alive) break;
+            tc::mbar_arrive(&empty_bar[s]);
+        }
+        if (!alive && mma_pending) tc::mbar_wait(&mma_bar[g], mma_parity);  // no MMA in flight when the columns are freed
+    }
+    if (!alive && row == 0) atomicExch(&g_tc_timeout, 1);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tbase, 256);
+}
+
 bool make_plan(const AppearanceConfig& A, bool backward, TcPlan& p) {
     if (A.n_neurons != kTcWidth || A.n_hidden < 1 || A.n_hidden + 1 > kTcMaxLayers) return false;
     p = TcPlan{};
@@ -1421,8 +1683,24 @@ cudaError_t launch_tc_color(const Params& P, const AppearanceConfig& A, const Vi
     TcPlan p;
     if (!make_plan(A, false, p)) return cudaErrorInvalidConfiguration;
     if (n_visible == 0) return cudaSuccess;
+    const uint32_t n_tiles = (n_visible + kTcRows - 1) / kTcRows;
+    CwPlan w;
+    if (make_cw_plan(A, w) && (reinterpret_cast<uintptr_t>(P.residual) & 15u) == 0) {
+        auto launch = [&](auto kernel) -> cudaError_t {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(w.smem_bytes));
+            if (e != cudaSuccess) return e;
+            const int grid = static_cast<int>(n_tiles < static_cast<uint32_t>(tc_sm_count()) ? n_tiles : tc_sm_count());
+            kernel<<<grid, kWsThreads, w.smem_bytes, s>>>(P, A, v, vis, n_visible, rec, w);
+            return cudaGetLastError();
+        };
+        switch (A.feature_dim) {
+            case 8: return launch(tc_color_ws_kernel<8>);
+            case 16: return launch(tc_color_ws_kernel<16>);
+            default: return launch(tc_color_ws_kernel<32>);
+        }
+    }
     int grid = 0;
-    cudaError_t e = tc_grid(tc_color_kernel, p, (n_visible + kTcRows - 1) / kTcRows, 3, &grid);
+    cudaError_t e = tc_grid(tc_color_kernel, p, n_tiles, 3, &grid);
     if (e != cudaSuccess) return e;
     tc_color_kernel<<<grid, kTcThreads, p.smem_bytes, s>>>(P, A, v, vis, n_visible, rec, p);
     return cudaGetLastError();
