@@ -223,6 +223,14 @@ def stage_bytes(stage: str, s: dict) -> float:
     if stage == 'blend_backward':
         return I * 52 + P * 32 + V * 48
     if stage == 'preprocess_backward':
+        if neural and s['store_bytes']:
+            # tensor-core path, per visible row. Geometry pass: index, rank, blend sums (48) and record (48), geometry
+            # parameters (44) and base (12), stored raw outputs (8), the 80-byte row block written, gradients of the
+            # geometry parameters and base added (read + write). MLP backward: index, latent, the activation store and
+            # row block, latent gradient and mean gradient added (read + write). Untouched rows: zero gradients.
+            geometry = 4 + 4 + 48 + 48 + 44 + 12 + 8 + 80 + 2 * (44 + 12)
+            mlp = 4 + 4 * F + s['store_bytes'] + 80 + 8 * F + 24
+            return V * (geometry + mlp) + (N - V) * (56 + 4 * F) + N * 4
         if neural:  # touched rows: MLP backward + geometry backward; zero gradients of the untouched rows
             return V * (128 + 8 * F) + V * 192 + (N - V) * (56 + 4 * F) + N * 4
         return N * 4 + V * (44 + A + 96) + N * (44 + A)

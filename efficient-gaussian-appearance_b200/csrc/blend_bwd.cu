@@ -86,7 +86,8 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
                     alpha = __fmul_rn(a.w, G);
                     acc = !(alpha < kMinAlpha);
                 }
-                if (!__any_sync(0xffffffffu, acc)) continue;
+                const uint32_t accepting = __ballot_sync(0xffffffffu, acc);
+                if (!accepting) continue;
                 float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
                 float v8 = 0.0f, ax = 0.0f, ay = 0.0f;
                 if (acc) {
@@ -112,16 +113,26 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
                     tr = __fmul_rn(tr, oma);
                     if (tr < kTransmittanceThreshold) done = true;
                 }
-                const float s = butterfly8(v, lane);
-                const float s8 = warp_sum(v8);
-                float sax = 0.0f, say = 0.0f;
-                if (kAbs) { sax = warp_sum(ax); say = warp_sum(ay); }
                 const uint32_t r = __float_as_uint(h.w);
                 float* gp = reinterpret_cast<float*>(grads + r);
-                if ((lane & 3) == 0) atomicAdd(gp + (lane >> 2), s);
-                if (lane == 0) {
-                    atomicAdd(gp + 8, s8);
-                    if (kAbs) { atomicAdd(gp + 9, sax); atomicAdd(gp + 10, say); }
+                if (__popc(accepting) <= 3) {
+                    // few accepting lanes (a fifth of the visits): each adds its own terms, no warp reduction
+                    if (acc) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++) atomicAdd(gp + j, v[j]);
+                        atomicAdd(gp + 8, v8);
+                        if (kAbs) { atomicAdd(gp + 9, ax); atomicAdd(gp + 10, ay); }
+                    }
+                } else {
+                    const float s = butterfly8(v, lane);
+                    const float s8 = warp_sum(v8);
+                    float sax = 0.0f, say = 0.0f;
+                    if (kAbs) { sax = warp_sum(ax); say = warp_sum(ay); }
+                    if ((lane & 3) == 0) atomicAdd(gp + (lane >> 2), s);
+                    if (lane == 0) {
+                        atomicAdd(gp + 8, s8);
+                        if (kAbs) { atomicAdd(gp + 9, sax); atomicAdd(gp + 10, say); }
+                    }
                 }
                 if (__all_sync(0xffffffffu, done)) break;
             }

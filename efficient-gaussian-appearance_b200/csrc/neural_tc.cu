@@ -1310,7 +1310,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_bwd_ws_kernel(Params P, Appe
 // ---------------------------------------------------------------------------------------------------
 // Warp-specialised colour pass (the forward MLP): one CTA per SM, 512 threads, four stages.
 //   warps 0-7    producer, two threads per row: the latent features of the row's tile, encoded into the stage's input
-//                slot (fp16, K-major); the second thread also the SH inputs and the row's primitive index and base colour.
+//                slot (fp16, K-major); the second thread fewer features, and the SH inputs and the row's primitive index.
 //   warps 8-11   consumer 0 (the CTA's even tiles, stages 0 and 2) and warps 12-15 consumer 1 (odd tiles, stages 1 and
 //                3), one thread per row: per layer the group's elected lane issues the MMAs into the group's TMEM
 //                columns, the group applies the activation and writes the fp16 activations over the stage's input slot
@@ -1319,9 +1319,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_bwd_ws_kernel(Params P, Appe
 // consumer. Same arithmetic as tc_color_kernel.
 constexpr int kCwStages = 4;
 
-struct CwRowInfo {   // per row of a stage: primitive index (0xffffffff past the end) and base-colour parameters
-    uint32_t i;
-    float bx, by, bz;
+// Split of a row's encoding: the first thread chunks [0, kC0), the second the rest plus the view direction and SH inputs.
+template <int F>
+struct CwSplit {
+    static constexpr int kChunks = F / 4;
+    static constexpr int kC0 = (kChunks * 5 + 7) / 8;
 };
 
 struct CwPlan {
@@ -1338,30 +1340,27 @@ bool make_cw_plan(const AppearanceConfig& A, CwPlan& w) {
     w.stage0 = (wbytes + 127) & ~127u;
     const uint32_t in_bytes = kTcRows * static_cast<uint32_t>(w.t.kin > kTcWidth ? w.t.kin : kTcWidth) * 2;  // input, then activations
     w.info_off = in_bytes;
-    w.stage_bytes = in_bytes + kTcRows * static_cast<uint32_t>(sizeof(CwRowInfo));
+    w.stage_bytes = in_bytes + kTcRows * 4;  // then the rows' primitive indices (0xffffffff past the end)
     w.smem_bytes = w.stage0 + kCwStages * w.stage_bytes;
     return w.smem_bytes + 256 <= 227u * 1024u;
 }
 
 template <int F, int H>
 struct CwRow {
-    static constexpr int kN = H ? WsSplit<F>::kChunks - WsSplit<F>::kC0 : WsSplit<F>::kC0;
+    static constexpr int kN = H ? CwSplit<F>::kChunks - CwSplit<F>::kC0 : CwSplit<F>::kC0;
     uint32_t i;
     bool valid;
-    f3 mean, base;                 // second thread only
+    f3 mean;                       // second thread only
     float4 f[kN > 0 ? kN : 1];
 };
 
 template <int F, int H>
 __device__ inline void cw_load(const Params& P, CwRow<F, H>& d) {
     if (!d.valid) return;
-    const float4* src = reinterpret_cast<const float4*>(P.residual + static_cast<size_t>(d.i) * F) + (H ? WsSplit<F>::kC0 : 0);
+    const float4* src = reinterpret_cast<const float4*>(P.residual + static_cast<size_t>(d.i) * F) + (H ? CwSplit<F>::kC0 : 0);
 #pragma unroll
     for (int q = 0; q < CwRow<F, H>::kN; q++) d.f[q] = src[q];
-    if (H) {
-        d.mean = ld3(P.means, d.i);
-        d.base = ld3(P.base, d.i);
-    }
+    if (H) d.mean = ld3(P.means, d.i);
 }
 
 // The colour pass's producer loop of half H; three row buffers rotate as in ws_producer. Returns false when a wait
@@ -1369,7 +1368,7 @@ __device__ inline void cw_load(const Params& P, CwRow<F, H>& d) {
 template <int F, int H>
 __device__ bool cw_producer(const Params& P, const View& v, int deg, const uint32_t* __restrict__ vis, uint32_t n_rows, const CwPlan& plan,
                             const WsShared& sh, int row) {
-    using S = WsSplit<F>;
+    using S = CwSplit<F>;
     constexpr int c_lo = H ? S::kC0 : 0;
     const uint32_t n_tiles = (n_rows + kTcRows - 1) / kTcRows, G = gridDim.x;
     auto index = [&](uint32_t tile, CwRow<F, H>& d) {
@@ -1393,14 +1392,14 @@ __device__ bool cw_producer(const Params& P, const View& v, int deg, const uint3
         if (k >= kCwStages && !tc::mbar_wait(&sh.empty_bar[s], ((k / kCwStages) - 1) & 1u)) return false;
         unsigned char* const sg = sh.smem + plan.stage0 + s * plan.stage_bytes;
         uint4* const xs = reinterpret_cast<uint4*>(sg + tc::kmajor_offset(row, 0, 2 * F + 16));
-        CwRowInfo* const info = reinterpret_cast<CwRowInfo*>(sg + plan.info_off);
+        uint32_t* const info = reinterpret_cast<uint32_t*>(sg + plan.info_off);
         if (!cur.valid) {
 #pragma unroll
             for (int q = 0; q < CwRow<F, H>::kN; q++) xs[8 * (c_lo + q)] = make_uint4(0u, 0u, 0u, 0u);
             if (H) {
                 xs[8 * S::kChunks] = make_uint4(0u, 0u, 0u, 0u);
                 xs[8 * (S::kChunks + 1)] = make_uint4(0u, 0u, 0u, 0u);
-                info[row] = CwRowInfo{0xffffffffu, 0.0f, 0.0f, 0.0f};
+                info[row] = 0xffffffffu;
             }
         } else {
 #pragma unroll
@@ -1420,7 +1419,7 @@ __device__ bool cw_producer(const Params& P, const View& v, int deg, const uint3
                 xs[8 * S::kChunks] = make_uint4(pack2(shv[0], shv[1]), pack2(shv[2], shv[3]), pack2(shv[4], shv[5]), pack2(shv[6], shv[7]));
                 xs[8 * (S::kChunks + 1)] =
                     make_uint4(pack2(shv[8], shv[9]), pack2(shv[10], shv[11]), pack2(shv[12], shv[13]), pack2(shv[14], shv[15]));
-                info[row] = CwRowInfo{cur.i, cur.base.x, cur.base.y, cur.base.z};
+                info[row] = cur.i;
             }
         }
         tc::fence_smem_to_async();
@@ -1492,7 +1491,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_color_ws_kernel(Params P, Ap
             tc::fence_after_sync();
             const uint32_t st = sbase + plan.stage0 + s * plan.stage_bytes;
             unsigned char* const sg = smem + plan.stage0 + s * plan.stage_bytes;
-            const CwRowInfo ri = reinterpret_cast<const CwRowInfo*>(sg + plan.info_off)[row];
+            const uint32_t pi = reinterpret_cast<const uint32_t*>(sg + plan.info_off)[row];
+            // the base colour, needed after the last layer: loaded now so its latency passes under the MMAs
+            const f3 base_p = pi != 0xffffffffu ? ld3(P.base, pi) : mk3(0.0f, 0.0f, 0.0f);
             unsigned char* const act = P.mlp_act ? P.mlp_act + static_cast<size_t>(tile) * plan.t.act_tile_bytes : nullptr;
             for (int l = 0; l <= last; l++) {
                 if (issuer_warp) {
@@ -1540,16 +1541,16 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_color_ws_kernel(Params P, Ap
                     if (act)
                         *reinterpret_cast<uint2*>(act + static_cast<size_t>(l) * kTcActLayerBytes + row * 8) =
                             make_uint2(pack2(y[0], y[1]), pack2(y[2], 0.0f));
-                    if (ri.i != 0xffffffffu) {
+                    if (pi != 0xffffffffu) {
                         const f3 res = residual_act3(A.res_act, mk3(__half2float(__float2half_rn(y[0])), __half2float(__float2half_rn(y[1])),
                                                                      __half2float(__float2half_rn(y[2]))));
-                        const f3 base = base_act3(A.base_act, mk3(ri.bx, ri.by, ri.bz));
+                        const f3 base = base_act3(A.base_act, base_p);
                         f3 color = color_act3(A.color_act, base + res);
                         if (!v.render_base) {
                             const f3 bc = color_act3(A.color_act, base);
                             color = mk3(fabsf(color.x - bc.x), fabsf(color.y - bc.y), fabsf(color.z - bc.z));
                         }
-                        float* q2 = reinterpret_cast<float*>(rec + ri.i) + 8;
+                        float* q2 = reinterpret_cast<float*>(rec + pi) + 8;
                         q2[0] = color.x;
                         q2[1] = color.y;
                         q2[2] = color.z;
