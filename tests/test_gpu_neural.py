@@ -126,9 +126,15 @@ def test_neural_tensor_core_many_tiles(cuda):
     print(f'\n[neural many tiles] image max-abs {img_err.max():.3e} mean-abs {img_err.mean():.3e}')
     assert img_err.mean() <= 5e-6 and (img_err.max(0) > 1e-4).mean() <= 1e-3, (img_err.max(), img_err.mean())
     img.backward(grad_image.to(cuda))
+    torch.cuda.synchronize()
+    from FasterGSVDACudaBackend import _lib
+    flag = ctypes.c_int(-1)
+    _lib.check(_lib.lib.fgs_tc_timeout(ctypes.byref(flag), 0))
+    assert flag.value == 0, 'a tensor-core kernel gave up a bounded wait'
     for k, t in (('means', 1e-3), ('opacities', 1e-3), ('base_colors', 1e-3), ('residual_params', 1e-3), ('mlp_weights', 1e-3)):
         ref = o['grads'][k]
         err = rel_err(leaves[k].grad.cpu().numpy().reshape(ref.shape), ref)
+        print(f'[neural many tiles] grad {k} rel {err:.3e}')
         assert err <= t, f'{k}: relative error {err:.2e}'
 
 
