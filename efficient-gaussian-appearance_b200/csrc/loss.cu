@@ -31,12 +31,22 @@ constexpr float kC2 = 0.03f * 0.03f;
 
 struct Window { float w[2 * kR + 1]; };
 
-// stages a kE x kE tile of `src` (channel plane) with zero padding; row stride kE + 1
-__device__ inline void stage(const float* __restrict__ src, int H, int W, int x0, int y0, float* dst) {
-    for (int idx = threadIdx.x; idx < kE * kE; idx += kThreads) {
-        const int r = idx / kE, c = idx - r * kE;
-        const int gy = y0 - kR + r, gx = x0 - kR + c;
-        dst[r * (kE + 1) + c] = (gy >= 0 && gy < H && gx >= 0 && gx < W) ? src[static_cast<size_t>(gy) * W + gx] : 0.0f;
+// stages the kE x kE tiles of up to three channel planes (zero padding outside the image; row stride kE + 1): a warp
+// per staged row, its lanes along the row; tiles whose halo lies inside the image skip the bounds tests
+template <int N>
+__device__ inline void stage(const float* const (&src)[N], int H, int W, int x0, int y0, float* const (&dst)[N]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool interior = x0 >= kR && y0 >= kR && x0 + kT + kR <= W && y0 + kT + kR <= H;
+    for (int r = warp; r < kE; r += kThreads / 32) {
+        const int gy = y0 - kR + r;
+        const bool row_in = interior || (gy >= 0 && gy < H);
+        const size_t roff = static_cast<size_t>(gy) * W + (x0 - kR);
+        for (int c = lane; c < kE; c += 32) {
+            const int gx = x0 - kR + c;
+            const bool in = interior || (row_in && gx >= 0 && gx < W);
+#pragma unroll
+            for (int q = 0; q < N; q++) dst[q][r * (kE + 1) + c] = in ? src[q][roff + c] : 0.0f;
+        }
     }
 }
 
@@ -48,20 +58,25 @@ __global__ void __launch_bounds__(kThreads) ssim_stats_kernel(const float* __res
     __shared__ float red[2][kThreads / 32];
     const int x0 = blockIdx.x * kT, y0 = blockIdx.y * kT, ch = blockIdx.z;
     const size_t plane = static_cast<size_t>(H) * W;
-    const float* xp = x + ch * plane;
-    const float* tp = t + ch * plane;
-    stage(xp, H, W, x0, y0, xs);
-    stage(tp, H, W, x0, y0, ts);
+    {
+        const float* const src[2] = {x + ch * plane, t + ch * plane};
+        float* const dst[2] = {xs, ts};
+        stage<2>(src, H, W, x0, y0, dst);
+    }
     __syncthreads();
     // rows: five moments of every staged row at every output column; a thread takes 4 consecutive columns of a row
     // (14 staged values feed its 4 outputs)
     for (int job = threadIdx.x; job < kE * (kT / 4); job += kThreads) {
         const int r = job / (kT / 4), c0 = (job - r * (kT / 4)) * 4;
-        float xa[4 + 2 * kR], ta[4 + 2 * kR];
+        // the staged values and their products, once per staged element
+        float xa[4 + 2 * kR], ta[4 + 2 * kR], xx[4 + 2 * kR], tt[4 + 2 * kR], xt[4 + 2 * kR];
 #pragma unroll
         for (int j = 0; j < 4 + 2 * kR; j++) {
             xa[j] = xs[r * (kE + 1) + c0 + j];
             ta[j] = ts[r * (kE + 1) + c0 + j];
+            xx[j] = xa[j] * xa[j];
+            tt[j] = ta[j] * ta[j];
+            xt[j] = xa[j] * ta[j];
         }
         float m[5][4];
 #pragma unroll
@@ -71,12 +86,11 @@ __global__ void __launch_bounds__(kThreads) ssim_stats_kernel(const float* __res
             const float w = win.w[k];
 #pragma unroll
             for (int o = 0; o < 4; o++) {
-                const float a = xa[o + k], b = ta[o + k];
-                m[0][o] += w * a;
-                m[1][o] += w * b;
-                m[2][o] += w * (a * a);
-                m[3][o] += w * (b * b);
-                m[4][o] += w * (a * b);
+                m[0][o] += w * xa[o + k];
+                m[1][o] += w * ta[o + k];
+                m[2][o] += w * xx[o + k];
+                m[3][o] += w * tt[o + k];
+                m[4][o] += w * xt[o + k];
             }
         }
 #pragma unroll
@@ -154,9 +168,11 @@ __global__ void __launch_bounds__(kThreads) ssim_grad_kernel(const float* __rest
     __shared__ __align__(16) float hs[3][kE * kT];  // 16-byte aligned rows: float4 stores
     const int x0 = blockIdx.x * kT, y0 = blockIdx.y * kT, ch = blockIdx.z;
     const size_t plane = static_cast<size_t>(H) * W;
-    stage(A + ch * plane, H, W, x0, y0, as);
-    stage(B + ch * plane, H, W, x0, y0, bs);
-    stage(Cm + ch * plane, H, W, x0, y0, cs);
+    {
+        const float* const src[3] = {A + ch * plane, B + ch * plane, Cm + ch * plane};
+        float* const dst[3] = {as, bs, cs};
+        stage<3>(src, H, W, x0, y0, dst);
+    }
     __syncthreads();
     for (int job = threadIdx.x; job < kE * (kT / 4); job += kThreads) {
         const int r = job / (kT / 4), c0 = (job - r * (kT / 4)) * 4;
