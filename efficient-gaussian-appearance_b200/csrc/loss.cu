@@ -168,17 +168,6 @@ __global__ void __launch_bounds__(kThreads) ssim_grad_kernel(const float* __rest
     __shared__ __align__(16) float hs[3][kE * kT];  // 16-byte aligned rows: float4 stores
     const int x0 = blockIdx.x * kT, y0 = blockIdx.y * kT, ch = blockIdx.z;
     const size_t plane = static_cast<size_t>(H) * W;
-    // this thread's 4 output pixels (one column, 4 consecutive rows): image and target loaded now, used at the end
-    const int c = threadIdx.x & (kT - 1), r0 = (threadIdx.x / kT) * 4;
-    float xv[4], tv[4];
-#pragma unroll
-    for (int o = 0; o < 4; o++) {
-        const int gy = y0 + r0 + o, gx = x0 + c;
-        const bool in = gy < H && gx < W;
-        const size_t p = ch * plane + static_cast<size_t>(in ? gy : 0) * W + (in ? gx : 0);
-        xv[o] = in ? x[p] : 0.0f;
-        tv[o] = in ? t[p] : 0.0f;
-    }
     {
         const float* const src[3] = {A + ch * plane, B + ch * plane, Cm + ch * plane};
         float* const dst[3] = {as, bs, cs};
@@ -209,6 +198,7 @@ __global__ void __launch_bounds__(kThreads) ssim_grad_kernel(const float* __rest
             *reinterpret_cast<float4*>(&hs[q][r * kT + c0]) = make_float4(m[q][0], m[q][1], m[q][2], m[q][3]);
     }
     __syncthreads();
+    const int c = threadIdx.x & (kT - 1), r0 = (threadIdx.x / kT) * 4;
     float ga[4], gb[4], gc[4];
 #pragma unroll
     for (int o = 0; o < 4; o++) ga[o] = gb[o] = gc[o] = 0.0f;
@@ -231,9 +221,9 @@ __global__ void __launch_bounds__(kThreads) ssim_grad_kernel(const float* __rest
         const int gy = y0 + r0 + o, gx = x0 + c;
         if (gy >= H || gx >= W) continue;
         const size_t p = ch * plane + static_cast<size_t>(gy) * W + gx;
-        const float d = xv[o] - tv[o];
+        const float xv = x[p], tv = t[p], d = xv - tv;
         const float sgn = d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f);
-        grad[p] = l1_scale * sgn - ssim_scale * (ga[o] + 2.0f * xv[o] * gb[o] + tv[o] * gc[o]);
+        grad[p] = l1_scale * sgn - ssim_scale * (ga[o] + 2.0f * xv * gb[o] + tv * gc[o]);
     }
 }
 
