@@ -134,9 +134,11 @@ class Trainer:
     """Holds the flat parameter / gradient buffers of one replica and runs data-parallel steps."""
 
     def __init__(self, prims: dict[str, torch.Tensor], lrs: dict[str, float | list], device: torch.device, group=None,
-                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool = False, overlap_views: bool = True) -> None:
+                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool = False, overlap_views: bool = True,
+                 view_streams: int = 2) -> None:
         self.device = device
         self.overlap_views = overlap_views
+        self.view_streams = max(1, view_streams)
         self.pg = group
         self.world = torch.distributed.get_world_size(group) if group is not None else 1
         self.rank = torch.distributed.get_rank(group) if group is not None else 0
@@ -187,10 +189,10 @@ class Trainer:
                                 torch.zeros(self.mlp.numel, dtype=torch.float32, device=device))
         self.grad_shard = torch.empty(self.shard, dtype=torch.float32, device=device) if self.world > 1 else None
         self.step_count = 0
-        self.loss_fns = (FusedLoss(), FusedLoss())
-        self._images = [None, None]
-        self._grad_images = [None, None]
-        self._side_stream = None
+        self.loss_fns = [FusedLoss() for _ in range(self.view_streams)]
+        self._images = [None] * self.view_streams
+        self._grad_images = [None] * self.view_streams
+        self._side_streams = []
 
     def _setup_peer_buffers(self) -> None:
         """Flat buffers in symmetric memory: every rank's buffers mapped on every device (peer pointers), plus the
@@ -254,25 +256,27 @@ class Trainer:
     def backward_views(self, settings_list: list, targets: list, ready: list | None = None) -> torch.Tensor:
         """Renders the local views and accumulates their gradients into the flat gradient buffer; returns the summed loss.
 
-        With overlap_views (and more than one view) consecutive views alternate between the current stream and a side
-        stream, each with its own workspaces, image and loss buffers: the forward, loss and binning of view k + 1 run
-        while view k's backward runs. The backward passes stay chained in view order (each waits for the previous
-        one's event), so gradients accumulate view by view as in the sequential order. `ready` (optional, one CUDA
-        event per view) lets the targets arrive asynchronously: view k's loss waits for ready[k], its render does not."""
+        With overlap_views (and more than one view) consecutive views go round `view_streams` streams (the current
+        one and side streams), each with its own workspaces, image and loss buffers: the forward, loss and binning of
+        the next views run while view k's backward runs. The backward passes stay chained in view order (each waits
+        for the previous one's event), so gradients accumulate view by view as in the sequential order. `ready`
+        (optional, one CUDA event per view) lets the targets arrive asynchronously: view k's loss waits for ready[k],
+        its render does not."""
         cp = self._prims()
         cg = self._grads()
         main = torch.cuda.current_stream(self.device)
-        overlap = self.overlap_views and len(settings_list) > 1
-        if overlap and self._side_stream is None:
-            self._side_stream = torch.cuda.Stream(self.device)
-        streams = (main, self._side_stream if overlap else main)
-        totals = [torch.zeros((), device=self.device) for _ in range(2)]
-        if overlap:
-            streams[1].wait_stream(main)  # parameters, targets and totals are ready
+        S = self.view_streams if self.overlap_views and len(settings_list) > 1 else 1
+        overlap = S > 1
+        while len(self._side_streams) < S - 1:
+            self._side_streams.append(torch.cuda.Stream(self.device))
+        streams = [main] + self._side_streams[:S - 1]
+        totals = [torch.zeros((), device=self.device) for _ in range(S)]
+        for side in streams[1:]:
+            side.wait_stream(main)  # parameters, targets and totals are ready
         prev_backward = None
-        states = [None, None]  # a view's workspaces live until the next view on the same stream replaces them
+        states = [None] * S  # a view's workspaces live until the next view on the same stream replaces them
         for k, (settings, target) in enumerate(zip(settings_list, targets)):
-            j = k % 2
+            j = k % S
             with torch.cuda.stream(streams[j]):
                 st = R.ForwardState(R._rasterizer, cp, settings, self.device)
                 st.preprocess(cp)
@@ -292,9 +296,9 @@ class Trainer:
                     prev_backward = torch.cuda.Event()
                     prev_backward.record(streams[j])
                 states[j] = st
-        if overlap:
-            main.wait_stream(streams[1])
-        return totals[0] + totals[1]
+        for side in streams[1:]:
+            main.wait_stream(side)
+        return sum(totals[1:], totals[0])
 
     @torch.no_grad()
     def apply_morton_ordering(self) -> None:
