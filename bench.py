@@ -60,18 +60,18 @@ METRIC = {'c3': 'render FPS (inference, NASG 8 lobes, 3M Gaussians, 64 ring view
 # depth sort 4 passes x 3 (upsweep, row scan, downsweep), depth reorder 1, offset scan 3, emission 1, tile sort
 # 2 passes x 3 (end_bit 13 or 14 at these sizes), ranges + bucket scan 2, blend 1; training adds the fused loss 3
 # (c4), the backward blend 1 and the backward preprocess (SH: 1; Neural: tcgen05 backward + geometry 2), plus the
-# Neural colour pass 1 in the forward. Per step: c4 adds one zeroing of the untouched gradients and one fused Adam
-# (or the fused exchange kernel); c1 one fused Adam. NCCL and torch's own kernels are not counted.
+# Neural colour pass 1 in the forward. Per step: one fused Adam (or the fused exchange kernel). The first view's
+# gradient arrays are cleared with memsets; those, NCCL and torch's own kernels are not counted.
 RENDER_LAUNCHES_PER_VIEW = 1 + 4 + 12 + 1 + 3 + 1 + 6 + 2 + 1
 
 
 def own_launches(wl_name: str, views: int) -> int:
     if wl_name in RENDER:
         return RENDER_LAUNCHES_PER_VIEW * views
-    if wl_name == 'c4':
-        return (RENDER_LAUNCHES_PER_VIEW + 1 + 3 + 1 + 2) * views + 2
-    if WORKLOADS[wl_name]['model'] == 'neural':  # colour pass, blend backward, MLP backward + geometry + zeroing, Adam
-        return RENDER_LAUNCHES_PER_VIEW + 1 + 1 + 3 + 1
+    if wl_name == 'c4':  # per view: loss 3, colour pass, blend backward, MLP backward + geometry; per step: Adam
+        return (RENDER_LAUNCHES_PER_VIEW + 3 + 1 + 1 + 2) * views + 1
+    if WORKLOADS[wl_name]['model'] == 'neural':  # colour pass, blend backward, MLP backward + geometry, Adam
+        return RENDER_LAUNCHES_PER_VIEW + 1 + 1 + 2 + 1
     return RENDER_LAUNCHES_PER_VIEW + 1 + 1 + 1
 
 

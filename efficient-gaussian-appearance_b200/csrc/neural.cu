@@ -945,25 +945,19 @@ __global__ void __launch_bounds__(256) neural_base_bwd_kernel(Params P, Appearan
 
 // zero gradients of the primitives outside the view (overwrite mode of the visible-row backward); one thread per
 // primitive; vec4 bit 0: feature rows 16-byte aligned, bit 1: rotation rows 16-byte aligned (16-byte stores)
-__global__ void zero_invisible_kernel(const uint32_t* __restrict__ rank_of, uint32_t n, int F, int vec4, GradOut O) {
-    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
-        if (rank_of[i] != kInvalidRank) continue;
-        for (int k = 0; k < 3; k++) {
-            O.means[3 * i + k] = 0.0f;
-            O.scales[3 * i + k] = 0.0f;
-            O.base[3 * i + k] = 0.0f;
-        }
-        if (vec4 & 2) reinterpret_cast<float4*>(O.rotations)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        else
-            for (int k = 0; k < 4; k++) O.rotations[4 * i + k] = 0.0f;
-        O.opacities[i] = 0.0f;
-        float* row = O.residual + i * F;
-        if (vec4 & 1)
-            for (int k = 0; k < F; k += 4) *reinterpret_cast<float4*>(row + k) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        else
-            for (int k = 0; k < F; k++) row[k] = 0.0f;
+// Zero gradients of the first view (no accumulation): every per-Gaussian gradient array is cleared as a whole before
+// the view's kernels store the visible rows' values (or add to them), so the rows no view touches end at zero. Plain
+// memsets stream at full bandwidth, where clearing only the untouched rows took one scattered store per value.
+cudaError_t zero_gradients(const GradOut& O, uint32_t n, int F, cudaStream_t st) {
+    const size_t rows = n;
+    const struct { float* p; size_t floats; } arrays[] = {{O.means, 3 * rows}, {O.scales, 3 * rows}, {O.rotations, 4 * rows},
+                                                          {O.opacities, rows}, {O.base, 3 * rows}, {O.residual, rows * static_cast<size_t>(F)}};
+    for (const auto& a : arrays) {
+        if (!a.p || !a.floats) continue;
+        const cudaError_t e = cudaMemsetAsync(a.p, 0, a.floats * sizeof(float), st);
+        if (e != cudaSuccess) return e;
     }
+    return cudaSuccess;
 }
 
 int sm_count() {
@@ -1057,10 +1051,8 @@ cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig
     }
     if (std::min(v.degree, A.max_degree) <= 0) {
         if (!O.accumulate) {
-            const int blocks = std::max(1, std::min(static_cast<int>((P.n + 255) / 256), sm_count() * 8));
-            const int vec4 = ((A.feature_dim % 4 == 0 && reinterpret_cast<uintptr_t>(O.residual) % 16 == 0) ? 1 : 0) |
-                             (reinterpret_cast<uintptr_t>(O.rotations) % 16 == 0 ? 2 : 0);
-            zero_invisible_kernel<<<blocks, 256, 0, st>>>(rank_of, P.n, A.feature_dim, vec4, O);
+            cudaError_t e = zero_gradients(O, P.n, A.feature_dim, st);
+            if (e != cudaSuccess) return e;
         }
         if (n_visible > 0) {
             neural_base_bwd_kernel<<<(n_visible + 255) / 256, 256, 0, st>>>(P, A, v, vis, n_visible, rank_of, sorted_rec, grads, O);
@@ -1076,11 +1068,7 @@ cudaError_t launch_preprocess_bwd_neural(const Params& P, const AppearanceConfig
                       (n_tiles <= kFastWarps * kMaxTilesPerWarp && fast_smem + kBwdRows * 3 * sizeof(float) <= kSmemLimit);
     if (fast) {
         if (!O.accumulate) {
-            const int blocks = std::max(1, std::min(static_cast<int>((P.n + 255) / 256), sm_count() * 8));
-            const int vec4 = ((A.feature_dim % 4 == 0 && reinterpret_cast<uintptr_t>(O.residual) % 16 == 0) ? 1 : 0) |
-                             (reinterpret_cast<uintptr_t>(O.rotations) % 16 == 0 ? 2 : 0);
-            zero_invisible_kernel<<<blocks, 256, 0, st>>>(rank_of, P.n, A.feature_dim, vec4, O);
-            cudaError_t e = cudaGetLastError();
+            cudaError_t e = zero_gradients(O, P.n, A.feature_dim, st);
             if (e != cudaSuccess) return e;
         }
         if (n_visible == 0) return cudaSuccess;

@@ -149,16 +149,29 @@ __global__ void __launch_bounds__(kChunk) compact_kernel(const uint32_t* __restr
     }
 }
 
-// gathers records into depth order, records the rank of every visible primitive, and the tile counts
-__global__ void reorder_kernel(const uint32_t* __restrict__ sorted_idx, const Record* __restrict__ rec,
-                               const uint32_t* __restrict__ n_touched, Record* __restrict__ sorted_rec,
-                               uint32_t* __restrict__ counts, uint32_t* __restrict__ rank_of, uint32_t n_visible) {
-    const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= n_visible) return;
-    const uint32_t i = sorted_idx[r];
-    sorted_rec[r] = rec[i];
-    counts[r] = n_touched[i];
-    rank_of[i] = r;
+// gathers records into depth order, records the rank of every visible primitive, and the tile counts. A block takes
+// 256 consecutive ranks; the records are copied as 16-byte thirds with three consecutive lanes on one record, so a
+// warp instruction reads whole 48-byte records and the depth-ordered output is written contiguously.
+constexpr int kReorderRanks = 256;
+__global__ void __launch_bounds__(kReorderRanks) reorder_kernel(const uint32_t* __restrict__ sorted_idx, const Record* __restrict__ rec,
+                                                                const uint32_t* __restrict__ n_touched, Record* __restrict__ sorted_rec,
+                                                                uint32_t* __restrict__ counts, uint32_t* __restrict__ rank_of, uint32_t n_visible) {
+    __shared__ uint32_t prim[kReorderRanks];
+    const uint32_t r0 = blockIdx.x * kReorderRanks, t = threadIdx.x;
+    const uint32_t m = min(static_cast<uint32_t>(kReorderRanks), n_visible - r0);
+    if (t < m) {
+        const uint32_t i = sorted_idx[r0 + t];
+        prim[t] = i;
+        counts[r0 + t] = n_touched[i];
+        rank_of[i] = r0 + t;
+    }
+    __syncthreads();
+    const float4* src = reinterpret_cast<const float4*>(rec);
+    float4* dst = reinterpret_cast<float4*>(sorted_rec + r0);
+    for (uint32_t c = t; c < 3 * m; c += kReorderRanks) {
+        const uint32_t k = c / 3, part = c - 3 * k;
+        dst[c] = src[3ull * prim[k] + part];
+    }
 }
 
 // ----------------------------------------------------------------------------------------------------
@@ -274,7 +287,8 @@ cudaError_t launch_compaction(const PrimBuffers& B, uint32_t n, cudaStream_t s) 
 
 cudaError_t launch_reorder(const PrimBuffers& B, uint32_t n_visible, cudaStream_t s) {
     if (n_visible == 0) return cudaSuccess;
-    reorder_kernel<<<grid_of(n_visible, 256), 256, 0, s>>>(B.sorted_idx, B.rec, B.n_touched, B.sorted_rec, B.inst_off, B.rank_of, n_visible);
+    reorder_kernel<<<grid_of(n_visible, kReorderRanks), kReorderRanks, 0, s>>>(B.sorted_idx, B.rec, B.n_touched, B.sorted_rec, B.inst_off,
+                                                                              B.rank_of, n_visible);
     return cudaGetLastError();
 }
 
