@@ -715,7 +715,8 @@ def main() -> None:
     ap.add_argument('--cpu-sample', type=float, default=0.05)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--exchange', default='auto', choices=['auto', 'peer', 'nccl'], help='c4 data-parallel exchange (N > 1)')
-    ap.add_argument('--multicast', action='store_true', help='peer exchange through NVSwitch multicast (multimem)')
+    ap.add_argument('--no-multicast', dest='multicast', action='store_false',
+                    help='peer exchange by loads / stores instead of NVSwitch multicast (multimem, the default where the switch provides it)')
     ap.add_argument('--gaussians', type=int, default=0, help='override the workload\'s Gaussian count (small profiling cases)')
     ap.add_argument('--views', type=int, default=0, help='override the workload\'s global batch of views (c4)')
     ap.add_argument('--order', default='morton', choices=['morton', 'generated'],

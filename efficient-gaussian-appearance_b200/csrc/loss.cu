@@ -129,11 +129,12 @@ __global__ void __launch_bounds__(kThreads) ssim_stats_kernel(const float* __res
             const float sxx = exx[o] - mu_x[o] * mu_x[o], syy = eyy[o] - mu_y[o] * mu_y[o], sxy = exy[o] - mu_x[o] * mu_y[o];
             const float a1 = 2.0f * mu_x[o] * mu_y[o] + kC1, a2 = 2.0f * sxy + kC2;
             const float b1 = mu_x[o] * mu_x[o] + mu_y[o] * mu_y[o] + kC1, b2 = sxx + syy + kC2;
-            const float den = b1 * b2;
-            const float s = a1 * a2 / den;
-            const float ds_dmu = 2.0f * mu_y[o] * a2 / den - s * 2.0f * mu_x[o] / b1;
-            const float ds_dsxx = -s / b2;
-            const float ds_dsxy = 2.0f * a1 / den;
+            // one division: 1 / (b1 b2), and from it 1 / b1 = b2 / (b1 b2) and 1 / b2 = b1 / (b1 b2)
+            const float rden = 1.0f / (b1 * b2), rb1 = b2 * rden, rb2 = b1 * rden;
+            const float s = a1 * a2 * rden;
+            const float ds_dmu = 2.0f * mu_y[o] * a2 * rden - s * 2.0f * mu_x[o] * rb1;
+            const float ds_dsxx = -s * rb2;
+            const float ds_dsxy = 2.0f * a1 * rden;
             const size_t p = ch * plane + static_cast<size_t>(gy) * W + gx;
             A[p] = ds_dmu - 2.0f * mu_x[o] * ds_dsxx - mu_y[o] * ds_dsxy;
             B[p] = ds_dsxx;

@@ -22,8 +22,11 @@ all-reduce of the MLP gradient, and the fused Adam kernel; 'peer' keeps the flat
 into every rank) and runs steps 2-4 as one kernel (fgs_dp_shard_adam) that, for every element of the rank's
 segments, sums the gradients of all ranks over NVLink (or through the switch with multicast), applies Adam and writes
 the new parameter into every rank's buffer, between two device-side barriers. 'auto' picks 'peer' when symmetric
-memory can be set up on the group and falls back to 'nccl' otherwise. The switch-multicast variant (multimem) is
-opt-in (multicast=True).
+memory can be set up on the group and falls back to 'nccl' otherwise. In the 'peer' exchange the sum is read with
+one multimem.ld_reduce through the NVSwitch and the new parameters are written with one multimem.st where the switch
+provides multicast mappings (multicast=True, the default): the switch does the sum and the fan-out, so each GPU moves
+about (N - 1) / N of the vector per link direction and step instead of twice that (at 8 GPUs 1.1 against 1.9 GB;
+measured 2.37 against 2.92 ms); without the mappings, or with multicast=False, peer loads and stores.
 """
 from __future__ import annotations
 
@@ -134,7 +137,7 @@ class Trainer:
     """Holds the flat parameter / gradient buffers of one replica and runs data-parallel steps."""
 
     def __init__(self, prims: dict[str, torch.Tensor], lrs: dict[str, float | list], device: torch.device, group=None,
-                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool = False, overlap_views: bool = True,
+                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool = True, overlap_views: bool = True,
                  view_streams: int = 2) -> None:
         self.device = device
         self.overlap_views = overlap_views
