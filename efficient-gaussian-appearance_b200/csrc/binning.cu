@@ -66,8 +66,8 @@ __global__ void __launch_bounds__(256) emit_kernel(const Record* __restrict__ re
         const uint32_t qpos = __shfl_sync(0xffffffffu, w, owner) + __shfl_sync(0xffffffffu, emitted, owner);
         const uint32_t qlim = __shfl_sync(0xffffffffu, lim, owner);
         const bool valid = c < total;  // then the owner has candidates and qw >= 1
-        const uint32_t t = c - o_excl, qw1 = valid ? qw : 1u;
-        const uint32_t tx = qx0 + t % qw1, ty = qy0 + t / qw1;
+        const uint2 qr = divmod_small(valid ? c - o_excl : 0u, valid ? qw : 1u);
+        const uint32_t tx = qx0 + qr.y, ty = qy0 + qr.x;
         const bool hit = valid && tile_overlaps(qx, qy, qa, qb, qc, tx, ty, qt);
         const uint32_t hits = __ballot_sync(0xffffffffu, hit);
         // lanes of this round that belong to the owner: from the owner's first candidate in the round up to this lane

@@ -44,6 +44,20 @@ __device__ inline Mat3 quat_to_rot(float r, float x, float y, float z, float& no
 }
 
 // screen-space bounds (x_min, x_max, y_min, y_max) in pixels -> tile bounds [tx0, tx1) x [ty0, ty1)
+// t / w and t % w for w >= 1. For t < 2^21 (tile candidates of any image up to about 23k x 23k pixels) a float estimate
+// from the approximate reciprocal (relative error about 2^-22, so t * (1 / w) is within t * 2^-21 < 1 / w of t / w)
+// truncates to the quotient or one below it, and one correction step makes it exact; larger t divide as integers.
+__device__ inline uint2 divmod_small(uint32_t t, uint32_t w) {
+    if (t >= (1u << 21)) return make_uint2(t / w, t % w);
+    uint32_t q = static_cast<uint32_t>(static_cast<float>(t) * __fdividef(1.0f, static_cast<float>(w)));
+    uint32_t r = t - q * w;
+    if (r >= w) {
+        q += 1;
+        r -= w;
+    }
+    return make_uint2(q, r);
+}
+
 __device__ inline uint4 tile_bounds_of(uint32_t xmin, uint32_t xmax, uint32_t ymin, uint32_t ymax) {
     return make_uint4(xmin / kTileW, (xmax + kTileW - 1) / kTileW, ymin / kTileH, (ymax + kTileH - 1) / kTileH);
 }
@@ -210,8 +224,8 @@ __device__ inline Geometry project_primitive(const float* __restrict__ means, co
         const uint32_t qx0 = __shfl_sync(0xffffffffu, tb.x, owner), qy0 = __shfl_sync(0xffffffffu, tb.z, owner);
         const uint32_t qw = __shfl_sync(0xffffffffu, bw, owner);
         const bool valid = c < total;  // then the owner has candidates and qw >= 1
-        const uint32_t t = c - o_excl, qw1 = valid ? qw : 1u;
-        const bool hit = valid && tile_overlaps(qx, qy, qa, qb, qc, qx0 + t % qw1, qy0 + t / qw1, qt);
+        const uint2 qr = divmod_small(valid ? c - o_excl : 0u, valid ? qw : 1u);
+        const bool hit = valid && tile_overlaps(qx, qy, qa, qb, qc, qx0 + qr.y, qy0 + qr.x, qt);
         const uint32_t hits = __ballot_sync(0xffffffffu, hit);
         const uint32_t lo = excl > base ? excl - base : 0u, hi = incl > base ? incl - base : 0u;
         if (lo < 32 && hi > lo) {
