@@ -1505,10 +1505,18 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_color_ws_kernel(Params P, Ap
                         for (uint32_t ks = 0; ks < K / 16; ks++) tc::mma(cb, tc::desc_advance(a, ks * 256), tc::desc_advance(b, ks * 256), id, ks > 0);
                         tc::commit(&mma_bar[g]);
                     }
+                    // training: the previous layer's activations (the 16 KB K-major block in the slot) into the
+                    // activation store with one bulk copy, by the group's first thread
+                    if (act && l > 0 && row == 0) {
+                        tc::bulk_s2g(act + static_cast<size_t>(l - 1) * kTcActLayerBytes, st, kTcActLayerBytes);
+                        tc::bulk_commit();
+                    }
                     __syncwarp();
                 }
                 mma_pending = true;
                 const bool done = tc::mbar_wait(&mma_bar[g], mma_parity);
+                // the copy has read the slot before the epilogue below (or the next tile) writes it again
+                if (act && l > 0 && row == 0) tc::bulk_wait_read();
                 if (tc::bar_or(bar_id, kTcRows, !done)) {
                     alive = false;
                     break;
@@ -1520,16 +1528,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_color_ws_kernel(Params P, Ap
                     float a[64];
                     tc::ld64(t_row, a);
                     uint4* const hs = reinterpret_cast<uint4*>(sg + h_row);
-                    uint4* const ga = act ? reinterpret_cast<uint4*>(act + static_cast<size_t>(l) * kTcActLayerBytes + h_row) : nullptr;
 #pragma unroll
                     for (int q = 0; q < 8; q++) {
                         float* x = a + 8 * q;
                         if (relu)
 #pragma unroll
                             for (int kk = 0; kk < 8; kk++) x[kk] = fmaxf(x[kk], 0.0f);
-                        const uint4 h = make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
-                        hs[8 * q] = h;
-                        if (ga) ga[8 * q] = h;
+                        hs[8 * q] = make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
                     }
                     tc::fence_smem_to_async();
                     tc::fence_before_sync();
@@ -1562,6 +1567,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tc_color_ws_kernel(Params P, Ap
             tc::mbar_arrive(&empty_bar[s]);
         }
         if (!alive && mma_pending) tc::mbar_wait(&mma_bar[g], mma_parity);  // no MMA in flight when the columns are freed
+        if (row == 0) tc::bulk_wait();  // the activation-store copies have completed before the CTA ends
     }
     if (!alive && row == 0) atomicExch(&g_tc_timeout, 1);
     tc::fence_before_sync();

@@ -73,6 +73,15 @@ __device__ inline bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
+// bulk copy of `bytes` (a multiple of 16) from shared memory to global memory (both 16-byte aligned), in this thread's
+// current bulk group; the wait forms make the group's shared-memory reads, or the whole copies, complete
+__device__ inline void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes) : "memory");
+}
+__device__ inline void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ inline void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ inline void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // one arrival of this thread (release: its earlier shared-memory writes are visible to the threads that observe the
 // completed phase)
 __device__ inline void mbar_arrive(uint64_t* bar) {
