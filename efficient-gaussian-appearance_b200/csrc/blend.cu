@@ -103,8 +103,9 @@ __global__ void __launch_bounds__(kTilePixels) blend_kernel(BlendArgs A, float* 
 // its accepted fragments exactly as the forward did (the acceptance test and the transmittance updates are
 // the same operations), stopping at the pixel's contributor count. The color still to be composited behind a
 // fragment is the final color minus what was composited up to and including it. Per-fragment gradient terms
-// are summed over the warp with a transposing butterfly (8 sums in 9 shuffles) and added to the primitive's
-// gradient record with one atomic per value and warp. Stored sums (converted by the backward preprocess):
+// are added to the primitive's gradient record, per lane with 16-byte vector atomics when at most half the warp
+// accepts the fragment, else summed over the warp first with a transposing butterfly (8 sums in 9 shuffles) and
+// added with one atomic per value and warp. Stored sums (converted by the backward preprocess):
 //   g0 = (sum h dx, sum h dy, sum h dx^2, sum h dx dy), g1 = (sum h dy^2, sum w g_rgb),
 //   g2 = (sum G dL/dalpha, sum |dL/dmean2d.x|, sum |dL/dmean2d.y|, 0) with h = -alpha dL/dalpha.
 
