@@ -99,12 +99,12 @@ __global__ void __launch_bounds__(kTilePixels) blend_kernel(BlendArgs A, float* 
 }
 
 // ---------------------------------------------------------------------------------------------------
-// backward: same tile / subtile walk as the forward, front to back. Each thread owns one pixel and re-derives
-// its accepted fragments exactly as the forward did (the acceptance test and the transmittance updates are
-// the same operations), stopping at the pixel's contributor count. The color still to be composited behind a
-// fragment is the final color minus what was composited up to and including it. Per-fragment gradient terms
-// are added to the primitive's gradient record, per lane with 16-byte vector atomics when at most half the warp
-// accepts the fragment, else summed over the warp first with a transposing butterfly (8 sums in 9 shuffles) and
+// backward: the same tile walk as the forward, front to back, with warps owning 16x4 bands (two pixels per lane).
+// Each thread re-derives the accepted fragments of its pixels exactly as the forward did (the acceptance test and the
+// transmittance updates are the same operations), stopping at each pixel's contributor count. The colour still to be
+// composited behind a fragment is the final colour minus what was composited up to and including it. Per-fragment
+// gradient terms are added to the primitive's gradient record, per lane with 16-byte vector atomics when few lanes
+// accept the fragment, else summed over the warp first with a transposing butterfly (8 sums in 9 shuffles) and
 // added with one atomic per value and warp. Stored sums (converted by the backward preprocess):
 //   g0 = (sum h dx, sum h dy, sum h dx^2, sum h dx dy), g1 = (sum h dy^2, sum w g_rgb),
 //   g2 = (sum G dL/dalpha, sum |dL/dmean2d.x|, sum |dL/dmean2d.y|, 0) with h = -alpha dL/dalpha.

@@ -1,8 +1,9 @@
 // Backward of the tile blend: for every pixel, the fragments of its tile are walked front to back again (the same
 // acceptance and termination decisions as the forward: the exponent, alpha, 1 - alpha and the transmittance are
 // evaluated with the forward's operations, blend_common.cuh), and the gradient terms of each accepted fragment are
-// added to the primitive's gradient record: per lane with vector atomics when at most half the warp accepts it, else
-// summed over the warp first.
+// added to the primitive's gradient record: per lane with vector atomics when few lanes accept it, else summed over
+// the warp first. Each lane owns two pixels of a 16x4 band, so a staged record's loads, the warp vote and the
+// reduction serve both.
 //
 // Semantics: FasterGSVDACudaBackend/.../rasterization/include/kernels_backward.cuh:12-231 (the reference processes
 // buckets of 32 instances with the pixels pipelined through the lanes, which for small footprints spends most issue
@@ -23,108 +24,133 @@ __device__ inline float rcp_approx(float x) {
 }
 
 // Visits with at most this many accepting lanes add per lane (the same addresses then take that many atomic additions
-// in L2); above it the warp reduces first. Measured on the c4 view: 16 beats 3, 12 and 20, and every lane adding
+// in L2); above it the warp reduces first. Measured on the c4 step: 20 beats 12, 16 and 24, and every lane adding
 // directly (32) triples the kernel's time through same-address serialisation.
-constexpr int kDirectLanes = 16;
+constexpr int kDirectLanes = 20;
+
+// Each warp owns a 16x4 row band of the tile (two 8x4 subtiles side by side) and each lane two pixels of it, (x, y)
+// and (x + 8, y): a staged record's loads, the warp's vote and the per-record reduction or atomics serve both pixels.
+constexpr int kBwdWarps = kTileH / kSubtileH;       // 3
+constexpr int kBwdThreads = 32 * kBwdWarps;         // 96
+constexpr int kBandW = 2 * kSubtileW;               // 16
+
+__device__ inline bool overlaps_band(uint2 bnd, uint32_t bx0, uint32_t by0) {
+    const uint32_t xlo = bnd.x & 0xffffu, xhi = bnd.x >> 16, ylo = bnd.y & 0xffffu, yhi = bnd.y >> 16;
+    return xlo < bx0 + kBandW && bx0 < xhi && ylo < by0 + kSubtileH && by0 < yhi;
+}
 
 template <bool kAbs>
-__global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A, const float* __restrict__ image, const float* __restrict__ grad_image,
+__global__ void __launch_bounds__(kBwdThreads) blend_backward_kernel(BlendArgs A, const float* __restrict__ image, const float* __restrict__ grad_image,
                                                                      TileBuffers T, GradRecord* __restrict__ grads) {
     __shared__ StagedB st[kTilePixels];
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint32_t tile = blockIdx.y * A.grid_w + blockIdx.x;
-    const uint32_t sx0 = blockIdx.x * kTileW + (warp % 2) * kSubtileW;
-    const uint32_t sy0 = blockIdx.y * kTileH + (warp / 2) * kSubtileH;
-    const uint32_t px = sx0 + lane % kSubtileW, py = sy0 + lane / kSubtileW;
-    const uint32_t local = (py - blockIdx.y * kTileH) * kTileW + (px - blockIdx.x * kTileW);
-    const bool inside = px < static_cast<uint32_t>(A.width) && py < static_cast<uint32_t>(A.height);
-    const float pxf = static_cast<float>(px) + 0.5f, pyf = static_cast<float>(py) + 0.5f;
+    const uint32_t bx0 = blockIdx.x * kTileW, by0 = blockIdx.y * kTileH + warp * kSubtileH;
+    const uint32_t py = by0 + lane / kSubtileW;
+    const float pyf = static_cast<float>(py) + 0.5f;
     const uint2 range = A.ranges[tile];
     const uint32_t n = range.y - range.x;
-    uint32_t last = 0;
-    float gcf = 0.0f, gr = 0.0f, gg = 0.0f, gb = 0.0f, gac = 0.0f;
-    if (inside) {
-        const size_t pix = static_cast<size_t>(py) * A.width + px;
-        const size_t np = static_cast<size_t>(A.width) * A.height;
-        last = T.n_contrib[static_cast<size_t>(tile) * kTilePixels + local];
-        const float tf = T.final_T[static_cast<size_t>(tile) * kTilePixels + local];
-        const float bgr = A.bg[0], bgg = A.bg[1], bgb = A.bg[2];
-        const float cfr = image[pix] - tf * bgr;
-        const float cfg = image[np + pix] - tf * bgg;
-        const float cfb = image[2 * np + pix] - tf * bgb;
-        gr = grad_image[pix];
-        gg = grad_image[np + pix];
-        gb = grad_image[2 * np + pix];
-        gac = tf * -(gr * bgr + gg * bgg + gb * bgb);
-        gcf = cfr * gr + cfg * gg + cfb * gb;  // (final colour without background) . dL/dcolour
+    // per pixel j (x offset 8 j): contributor count, dL/dcolour, (final colour without background) . dL/dcolour,
+    // the background term, the transmittance and accd = (colour accumulated so far) . dL/dcolour, so that
+    // (final - accumulated) . dL/dcolour = gcf - accd
+    uint32_t last[2] = {0u, 0u};
+    float pxf[2], gcf[2] = {0.0f, 0.0f}, gr[2] = {0.0f, 0.0f}, gg[2] = {0.0f, 0.0f}, gb[2] = {0.0f, 0.0f}, gac[2] = {0.0f, 0.0f};
+    float tr[2] = {1.0f, 1.0f}, accd[2] = {0.0f, 0.0f};
+    bool done[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const uint32_t px = bx0 + lane % kSubtileW + kSubtileW * j;
+        pxf[j] = static_cast<float>(px) + 0.5f;
+        if (px < static_cast<uint32_t>(A.width) && py < static_cast<uint32_t>(A.height)) {
+            const uint32_t local = (py - blockIdx.y * kTileH) * kTileW + (px - bx0);
+            const size_t pix = static_cast<size_t>(py) * A.width + px;
+            const size_t np = static_cast<size_t>(A.width) * A.height;
+            last[j] = T.n_contrib[static_cast<size_t>(tile) * kTilePixels + local];
+            const float tf = T.final_T[static_cast<size_t>(tile) * kTilePixels + local];
+            const float bgr = A.bg[0], bgg = A.bg[1], bgb = A.bg[2];
+            const float cfr = image[pix] - tf * bgr;
+            const float cfg = image[np + pix] - tf * bgg;
+            const float cfb = image[2 * np + pix] - tf * bgb;
+            gr[j] = grad_image[pix];
+            gg[j] = grad_image[np + pix];
+            gb[j] = grad_image[2 * np + pix];
+            gac[j] = tf * -(gr[j] * bgr + gg[j] * bgg + gb[j] * bgb);
+            gcf[j] = cfr * gr[j] + cfg * gg[j] + cfb * gb[j];
+        }
+        done[j] = last[j] == 0;
     }
-    // accd = (colour accumulated so far) . dL/dcolour, so that (final - accumulated) . dL/dcolour = gcf - accd
-    float tr = 1.0f, accd = 0.0f;
-    bool done = last == 0;
     for (uint32_t start = 0; start < n; start += kTilePixels) {
-        if (__syncthreads_and(done)) break;
-        if (start + t < n) {
-            const uint32_t r = A.vals[range.x + start + t];
-            const Record q = A.rec[r];
-            StagedB& s = st[t];
-            s.a = make_float4(q.q0.x, q.q0.y, 0.0f, q.q0.z);
-            s.h = make_float4(kHalfConic * q.q1.x, kCrossConic * q.q1.y, kHalfConic * q.q1.z, __uint_as_float(r));
-            s.c = make_float4(q.q2.x, q.q2.y, q.q2.z, 0.0f);
-            s.bnd = make_uint2(__float_as_uint(q.q1.w), __float_as_uint(q.q2.w));
+        if (__syncthreads_and(done[0] && done[1])) break;
+        for (uint32_t u = t; u < kTilePixels; u += kBwdThreads) {
+            if (start + u < n) {
+                const uint32_t r = A.vals[range.x + start + u];
+                const Record q = A.rec[r];
+                StagedB& s = st[u];
+                s.a = make_float4(q.q0.x, q.q0.y, 0.0f, q.q0.z);
+                s.h = make_float4(kHalfConic * q.q1.x, kCrossConic * q.q1.y, kHalfConic * q.q1.z, __uint_as_float(r));
+                s.c = make_float4(q.q2.x, q.q2.y, q.q2.z, 0.0f);
+                s.bnd = make_uint2(__float_as_uint(q.q1.w), __float_as_uint(q.q2.w));
+            }
         }
         __syncthreads();
         const uint32_t bs = min(static_cast<uint32_t>(kTilePixels), n - start);
         for (uint32_t g = 0; g < bs; g += 32) {
-            const bool ov = g + lane < bs && overlaps_subtile(st[g + lane].bnd, sx0, sy0);
+            const bool ov = g + lane < bs && overlaps_band(st[g + lane].bnd, bx0, by0);
             // `done` changes only where a fragment is accepted, so the warp votes on it once per group of 32
             // records and after each accepted fragment
-            uint32_t pending = __all_sync(0xffffffffu, done) ? 0u : __ballot_sync(0xffffffffu, ov);
+            uint32_t pending = __all_sync(0xffffffffu, done[0] && done[1]) ? 0u : __ballot_sync(0xffffffffu, ov);
             while (pending) {
                 const uint32_t k = g + __ffs(pending) - 1;
                 pending &= pending - 1;
                 const float4 a = st[k].a;
                 const float4 h = st[k].h;
-                const float dx = a.x - pxf, dy = a.y - pyf;
-                bool acc = !done && start + k < last;
-                float G = 0.0f, alpha = 0.0f;
-                if (acc) {
-                    G = fragment_gaussian(gauss_exponent(dx, dy, h));
-                    alpha = __fmul_rn(a.w, G);
-                    acc = !(alpha < kMinAlpha);
-                }
-                const uint32_t accepting = __ballot_sync(0xffffffffu, acc);
-                if (!accepting) continue;
+                // the fragment's terms summed over this lane's accepting pixels
                 float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
                 float v8 = 0.0f, ax = 0.0f, ay = 0.0f;
-                if (acc) {
-                    const float4 c = st[k].c;
-                    const float w = tr * alpha;
-                    const float cg = c.x * gr + c.y * gg + c.z * gb;
-                    accd = fmaf(w, cg, accd);
-                    const float oma = __fsub_rn(1.0f, alpha);
-                    const float rcp = rcp_approx(fmaxf(oma, kOneMinusAlphaEps));
-                    // sum_c (tr c_c - (final_c - accumulated_c) / (1 - alpha)) g_c + gac / (1 - alpha)
-                    const float dl_da = fmaf(tr, cg, rcp * (gac - (gcf - accd)));
-                    const float hl = -alpha * dl_da;
-                    const float hx = hl * dx, hy = hl * dy;
-                    v[0] = hx; v[1] = hy; v[2] = hx * dx; v[3] = hx * dy;
-                    v[4] = hy * dy; v[5] = w * gr; v[6] = w * gg; v[7] = w * gb;
-                    v8 = G * dl_da;
-                    if (kAbs) {
-                        // |dL/dmean2d| of this fragment, with the raw conic recovered from the staged scaled conic
-                        const float ca = h.x / kHalfConic, cb = h.y / kCrossConic, cc = h.z / kHalfConic;
-                        ax = fabsf(ca * hx + cb * hy);
-                        ay = fabsf(cb * hx + cc * hy);
+                bool any = false;
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const float dx = a.x - pxf[j], dy = a.y - pyf;
+                    bool acc = !done[j] && start + k < last[j];
+                    float G = 0.0f, alpha = 0.0f;
+                    if (acc) {
+                        G = fragment_gaussian(gauss_exponent(dx, dy, h));
+                        alpha = __fmul_rn(a.w, G);
+                        acc = !(alpha < kMinAlpha);
                     }
-                    tr = __fmul_rn(tr, oma);
-                    if (tr < kTransmittanceThreshold) done = true;
+                    if (acc) {
+                        const float4 c = st[k].c;
+                        const float w = tr[j] * alpha;
+                        const float cg = c.x * gr[j] + c.y * gg[j] + c.z * gb[j];
+                        accd[j] = fmaf(w, cg, accd[j]);
+                        const float oma = __fsub_rn(1.0f, alpha);
+                        const float rcp = rcp_approx(fmaxf(oma, kOneMinusAlphaEps));
+                        // sum_c (tr c_c - (final_c - accumulated_c) / (1 - alpha)) g_c + gac / (1 - alpha)
+                        const float dl_da = fmaf(tr[j], cg, rcp * (gac[j] - (gcf[j] - accd[j])));
+                        const float hl = -alpha * dl_da;
+                        const float hx = hl * dx, hy = hl * dy;
+                        v[0] += hx; v[1] += hy; v[2] = fmaf(hx, dx, v[2]); v[3] = fmaf(hx, dy, v[3]);
+                        v[4] = fmaf(hy, dy, v[4]); v[5] = fmaf(w, gr[j], v[5]); v[6] = fmaf(w, gg[j], v[6]); v[7] = fmaf(w, gb[j], v[7]);
+                        v8 = fmaf(G, dl_da, v8);
+                        if (kAbs) {
+                            // |dL/dmean2d| of this fragment, with the raw conic recovered from the staged scaled conic
+                            const float ca = h.x / kHalfConic, cb = h.y / kCrossConic, cc = h.z / kHalfConic;
+                            ax += fabsf(ca * hx + cb * hy);
+                            ay += fabsf(cb * hx + cc * hy);
+                        }
+                        tr[j] = __fmul_rn(tr[j], oma);
+                        if (tr[j] < kTransmittanceThreshold) done[j] = true;
+                        any = true;
+                    }
                 }
+                const uint32_t accepting = __ballot_sync(0xffffffffu, any);
+                if (!accepting) continue;
                 const uint32_t r = __float_as_uint(h.w);
                 float* gp = reinterpret_cast<float*>(grads + r);
                 if (__popc(accepting) <= kDirectLanes) {
-                    // up to half the warp accepting: each lane adds its own terms with 16-byte vector atomics (three
-                    // warp instructions), no warp reduction
-                    if (acc) {
+                    // few enough lanes accepting: each adds its own terms with 16-byte vector atomics (three warp
+                    // instructions), no warp reduction
+                    if (any) {
                         GradRecord* const gq = grads + r;
                         atomicAdd(&gq->g0, make_float4(v[0], v[1], v[2], v[3]));
                         atomicAdd(&gq->g1, make_float4(v[4], v[5], v[6], v[7]));
@@ -142,7 +168,7 @@ __global__ void __launch_bounds__(kTilePixels) blend_backward_kernel(BlendArgs A
                         if (kAbs) { atomicAdd(gp + 9, sax); atomicAdd(gp + 10, say); }
                     }
                 }
-                if (__all_sync(0xffffffffu, done)) break;
+                if (__all_sync(0xffffffffu, done[0] && done[1])) break;
             }
         }
     }
@@ -242,8 +268,8 @@ cudaError_t launch_pruning_scores(const BlendArgs& a, const float* image, const 
 cudaError_t launch_blend_backward(const BlendArgs& a, const float* image, const float* grad_image, const TileBuffers& T, GradRecord* grads,
                                   int abs_grad, cudaStream_t s) {
     const dim3 grid(a.grid_w, a.grid_h);
-    if (abs_grad) blend_backward_kernel<true><<<grid, kTilePixels, 0, s>>>(a, image, grad_image, T, grads);
-    else blend_backward_kernel<false><<<grid, kTilePixels, 0, s>>>(a, image, grad_image, T, grads);
+    if (abs_grad) blend_backward_kernel<true><<<grid, kBwdThreads, 0, s>>>(a, image, grad_image, T, grads);
+    else blend_backward_kernel<false><<<grid, kBwdThreads, 0, s>>>(a, image, grad_image, T, grads);
     return cudaGetLastError();
 }
 
