@@ -865,7 +865,7 @@ __global__ void __launch_bounds__(256, 3) neural_geometry_bwd_kernel(Params P, V
 // index, 1 / distance and view direction; the base-colour gradient is written here. Same values as tc_bwd_kernel
 // computes (the same functions, compiled with the same flags). This kernel writes the mean gradient first; the MLP
 // backward adds its direction part.
-__global__ void __launch_bounds__(256, 3) neural_geometry_rows_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis,
+__global__ void __launch_bounds__(256, 4) neural_geometry_rows_kernel(Params P, AppearanceConfig A, View v, const uint32_t* __restrict__ vis,
                                                                    uint32_t n_rows, const uint32_t* __restrict__ rank_of,
                                                                    const Record* __restrict__ sorted_rec, const GradRecord* __restrict__ grads,
                                                                    GradOut O, TcRowLayout L) {
