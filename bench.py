@@ -3,9 +3,11 @@
 Default workload c4 (the headline "train steps/s @1080p"): one data-parallel training step of the Neural appearance
 model -- 6,000,000 Gaussians, 32 latent features per Gaussian, MLP 80 -> 64 -> 64 -> 3 (fp16 tensor cores) -- over a
 global batch of 8 views at 1920x1080. Every rank renders its share of the views (forward, loss 0.8 L1 + 0.2 (1 - SSIM)
-against a blurred random target, backward with gradients accumulated over its views); the flat gradient buffer is
-reduce-scattered, every rank runs the fused Adam on its slice, and the parameters are all-gathered (NCCL). The total
-work is fixed as N grows ("scaling": "strong").
+against a blurred random target, backward with gradients accumulated over its views); the gradients are summed by
+Gaussian range, every rank runs the fused Adam on its range, and the updated ranges go back to every rank (one fused
+kernel over NVLink, or NCCL with --exchange nccl). The total work is fixed as N grows ("scaling": "strong"). The
+line also carries "render": inference of configuration c3 (3M Gaussians, NASG 8 lobes, 64 ring views at 1920x1080,
+views split over the GPUs) in frames/s, timed the same way after the training step (--no-render skips it).
 
 Workload c1 (--workload c1): one SH-3 training step (forward, backward, fused Adam through the public autograd API)
 of 1,000,000 Gaussians on one 1280x720 view with a fixed upstream image gradient; with N GPUs every rank trains its
@@ -14,7 +16,7 @@ own replica (no exchange step, "scaling": "weak").
 value: steps/s with every input resident in HBM. e2e: the same step with the step's inputs (c4: the target images of
 the rank's views; c1: the upstream gradient) copied host->device from pinned memory and the step's result (c4: the
 loss; c1: the rendered image) copied back, every step. --impl reference times the CPU restatement of the reference
-path (oracle/, "port", one thread) on a bounded sample of the same workload.
+path (oracle/, "port", on every host core) on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -300,7 +302,9 @@ def _tensor_peak() -> float:
 # ------------------------------------------------------------------------------------------------------------
 # B200 arm
 
-def run_b200(args, wl_name: str) -> dict | None:
+def run_b200(args, wl_name: str, companion: bool = False) -> dict | None:
+    """One workload on this rank's GPU. With companion=True (the render measurement that follows the c4 training
+    step in the same process) only the timed and end-to-end loops run, and the process group is left open."""
     from FasterGSVDACudaBackend import _lib, rasterization as R
     import synthetic as S
     wl = WORKLOADS[wl_name]
@@ -311,8 +315,9 @@ def run_b200(args, wl_name: str) -> dict | None:
     dev = torch.device('cuda', local)
     pg = None
     if world > 1:
-        import datetime
-        torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
+        if not torch.distributed.is_initialized():
+            import datetime
+            torch.distributed.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
         pg = torch.distributed.group.WORLD
     configure(wl)
     prims = scene(wl)
@@ -487,6 +492,18 @@ def run_b200(args, wl_name: str) -> dict | None:
     barrier()
     ms_e2e = e2.elapsed_time(e3) / args.steps
 
+    if companion:
+        if world > 1:
+            t = torch.tensor([ms, ms_e2e], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms, ms_e2e = float(t[0]), float(t[1])
+        fps, fps_e2e = wl['views'] * 1000.0 / ms, wl['views'] * 1000.0 / ms_e2e
+        return {'metric': METRIC[wl_name], 'value': fps, 'unit': 'frames/s', 'ms_per_step': ms, 'steps': args.steps, 'warmup': args.warmup,
+                'scaling': 'strong', 'config': static_config(wl_name, world, args),
+                'mpix_per_s': fps * wl['width'] * wl['height'] / 1e6,
+                'e2e': {'value': fps_e2e, 'unit': 'frames/s', 'h2d_bytes_per_step': int(h2d), 'd2h_bytes_per_step': int(d2h)},
+                'gpu_launches': own_launches(wl_name, views_per_step) * args.steps, 'clocks': clocks} if rank == 0 else None
+
     # per-stage timing pass (CUDA events on the launching stream), averaged per step; the training step runs its views
     # one after another here (no second stream), so every stage's events bracket only that stage's kernels
     overlapped = wl_name == 'c4' and trainer.overlap_views
@@ -556,6 +573,13 @@ def run_b200(args, wl_name: str) -> dict | None:
                      'frac_by_stage': fracs, 'tensor_frac_by_stage': tensor_fracs, 'tensor_peak_tflops': tflops_peak,
                      'bound_by_stage': {k: BOUND.get(k, 'hbm') for k in per_view}},
     }
+    if wl_name == 'c4' and args.render:
+        # the other half of the headline metric (train steps/s and render FPS): inference of configuration c3 on the
+        # same GPUs, measured after the training step (the training state stays allocated: it is a few GB)
+        torch.cuda.synchronize()
+        r = run_b200(args, 'c3', companion=True)
+        if rank == 0:
+            out['render'] = r
     if world > 1:
         torch.distributed.destroy_process_group()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -714,6 +738,8 @@ def main() -> None:
     ap.add_argument('--workload', default='c4', choices=sorted(WORKLOADS))
     ap.add_argument('--cpu-sample', type=float, default=0.05)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-render', dest='render', action='store_false',
+                    help='c4: skip the render measurement of configuration c3 that the line carries under "render"')
     ap.add_argument('--exchange', default='auto', choices=['auto', 'peer', 'nccl'], help='c4 data-parallel exchange (N > 1)')
     ap.add_argument('--no-multicast', dest='multicast', action='store_false',
                     help='peer exchange by loads / stores instead of NVSwitch multicast (multimem, the default where the switch provides it)')
