@@ -226,16 +226,19 @@ def stage_bytes(stage: str, s: dict) -> float:
     if stage == 'blend_backward':
         return I * 52 + P * 32 + V * 48
     if stage == 'preprocess_backward':
+        # Neural: the gradient arrays of all N rows (geometry 44, base 12, latent 4F bytes) are cleared by memsets
+        # when a view does not accumulate (every view of c2; the first of the step's views in c4: clear_share)
+        clear = s['clear_share'] * N * (56 + 4 * F)
         if neural and s['store_bytes']:
             # tensor-core path, per visible row. Geometry pass: index, rank, blend sums (48) and record (48), geometry
             # parameters (44) and base (12), stored raw outputs (8), the 80-byte row block written, gradients of the
             # geometry parameters and base added (read + write). MLP backward: index, latent, the activation store and
-            # row block, latent gradient and mean gradient added (read + write). Untouched rows: zero gradients.
+            # row block, latent gradient and mean gradient added (read + write).
             geometry = 4 + 4 + 48 + 48 + 44 + 12 + 8 + 80 + 2 * (44 + 12)
             mlp = 4 + 4 * F + s['store_bytes'] + 80 + 8 * F + 24
-            return V * (geometry + mlp) + (N - V) * (56 + 4 * F) + N * 4
-        if neural:  # touched rows: MLP backward + geometry backward; zero gradients of the untouched rows
-            return V * (128 + 8 * F) + V * 192 + (N - V) * (56 + 4 * F) + N * 4
+            return V * (geometry + mlp) + clear
+        if neural:  # touched rows: MLP backward + geometry backward
+            return V * (128 + 8 * F) + V * 192 + clear
         return N * 4 + V * (44 + A + 96) + N * (44 + A)
     if stage == 'adam':
         return 28 * s['params']
@@ -254,14 +257,15 @@ def stage_flops(stage: str, s: dict) -> float:
     return 0.0
 
 
-def frame_stats(wl: dict, n_visible: int, n_instances: int, n_params: int) -> dict:
-    """The per-view units the byte and FLOP counts scale with."""
+def frame_stats(wl: dict, n_visible: int, n_instances: int, n_params: int, clear_share: float = 1.0) -> dict:
+    """The per-view units the byte and FLOP counts scale with (clear_share: the fraction of views that clear the
+    gradient arrays instead of accumulating into them)."""
     model = wl['model']
     stride = {'sh': 45, 'neural': wl.get('feature_dim', 0), 'nasg': 8 * wl['degree'], 'sv': 7 * wl['degree']}[model]
     tiles = ((wl['width'] + 15) // 16) * ((wl['height'] + 11) // 12)
     out = dict(N=wl['n'], V=n_visible, I=n_instances, pixels=wl['width'] * wl['height'], params=n_params, model=model,
                appearance_bytes=0 if model == 'neural' else 12 + 4 * stride, features=wl.get('feature_dim', 0),
-               key_bytes=2 if tiles <= 65536 else 4, tiles=tiles, store_bytes=0, mlp_flops=0)
+               key_bytes=2 if tiles <= 65536 else 4, tiles=tiles, store_bytes=0, mlp_flops=0, clear_share=clear_share)
     if model == 'neural':
         nn, hidden = wl['neurons'], wl['hidden']
         kin = (wl['feature_dim'] * 2 * wl['n_freq'] + 16 + 15) // 16 * 16
@@ -524,7 +528,7 @@ def run_b200(args, wl_name: str, companion: bool = False) -> dict | None:
     st.preprocess(stat_prims)
     fr = st.frame
     del st
-    stats = frame_stats(wl, fr.n_visible, fr.n_instances, n_params)
+    stats = frame_stats(wl, fr.n_visible, fr.n_instances, n_params, 1.0 / views_per_step if wl_name == 'c4' else 1.0)
     per_view = {k: (v if k == 'adam' else v / views_per_step) for k, v in stage_ms.items()}
     dominant = max(stage_ms, key=stage_ms.get)
     peak, peak_kind = _peaks()
@@ -571,7 +575,10 @@ def run_b200(args, wl_name: str, companion: bool = False) -> dict | None:
         'roofline': {'kernel': dominant, 'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'peak_kind': peak_kind, 'unit': 'GB/s',
                      'frac': achieved / peak, 'traffic': traffic, 'traffic_source': traffic_src, 'algorithmic_bytes': bytes_dom,
                      'frac_by_stage': fracs, 'tensor_frac_by_stage': tensor_fracs, 'tensor_peak_tflops': tflops_peak,
-                     'bound_by_stage': {k: BOUND.get(k, 'hbm') for k in per_view}},
+                     'bound_by_stage': {k: BOUND.get(k, 'hbm') for k in per_view},
+                     # training with the tensor-core MLP: the fp16 activations the colour pass writes and the MLP
+                     # backward reads back (inside both stages' algorithmic bytes), per view
+                     'activation_store_bytes_per_view': stats['V'] * stats['store_bytes']},
     }
     if wl_name == 'c4' and args.render:
         # the other half of the headline metric (train steps/s and render FPS): inference of configuration c3 on the
