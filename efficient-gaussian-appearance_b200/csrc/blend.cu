@@ -99,7 +99,8 @@ __global__ void __launch_bounds__(kTilePixels) blend_kernel(BlendArgs A, float* 
 }
 
 // ---------------------------------------------------------------------------------------------------
-// backward: the same tile walk as the forward, front to back, with warps owning 16x4 bands (two pixels per lane).
+// backward (blend_bwd.cu): the same tile walk as the forward, front to back, with warps owning 8x12 column bands
+// (three pixels per lane).
 // Each thread re-derives the accepted fragments of its pixels exactly as the forward did (the acceptance test and the
 // transmittance updates are the same operations), stopping at each pixel's contributor count. The colour still to be
 // composited behind a fragment is the final colour minus what was composited up to and including it. Per-fragment

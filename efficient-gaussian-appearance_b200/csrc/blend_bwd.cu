@@ -2,8 +2,8 @@
 // acceptance and termination decisions as the forward: the exponent, alpha, 1 - alpha and the transmittance are
 // evaluated with the forward's operations, blend_common.cuh), and the gradient terms of each accepted fragment are
 // added to the primitive's gradient record: per lane with vector atomics when few lanes accept it, else summed over
-// the warp first. Each lane owns two pixels of a 16x4 band, so a staged record's loads, the warp vote and the
-// reduction serve both.
+// the warp first. Each warp owns an 8x12 column half of the tile and each lane three pixels of it, one per 4-row
+// subtile, so a staged record's loads, the warp vote and the reduction serve all three.
 //
 // Semantics: FasterGSVDACudaBackend/.../rasterization/include/kernels_backward.cuh:12-231 (the reference processes
 // buckets of 32 instances with the pixels pipelined through the lanes, which for small footprints spends most issue
@@ -28,15 +28,20 @@ __device__ inline float rcp_approx(float x) {
 // directly (32) triples the kernel's time through same-address serialisation.
 constexpr int kDirectLanes = 20;
 
-// Each warp owns a 16x4 row band of the tile (two 8x4 subtiles side by side) and each lane two pixels of it, (x, y)
-// and (x + 8, y): a staged record's loads, the warp's vote and the per-record reduction or atomics serve both pixels.
-constexpr int kBwdWarps = kTileH / kSubtileH;       // 3
-constexpr int kBwdThreads = 32 * kBwdWarps;         // 96
-constexpr int kBandW = 2 * kSubtileW;               // 16
+// Each warp owns a band of (8 JX) x (4 JY) pixels of the tile and each lane JX x JY pixels of it, (x + 8 jx, y + 4 jy):
+// a staged record's loads, the warp's vote and the per-record reduction or atomics serve all of a lane's pixels.
+// Measured on the c4 step (blend backward per step): 8x4 subtiles, one pixel per lane, 8.07 ms; 16x4 bands, two
+// pixels, 7.62 ms; 8x12 column bands, three pixels, 7.25 ms; the whole 16x12 tile in one warp, six pixels, 10.6 ms.
+constexpr int kBandJX = 1, kBandJY = 3;  // 8x12 column bands, two warps per tile
+constexpr int kBandW = kSubtileW * kBandJX, kBandH = kSubtileH * kBandJY;
+constexpr int kBandsX = kTileW / kBandW;
+constexpr int kBwdWarps = kBandsX * (kTileH / kBandH);
+constexpr int kBwdThreads = 32 * kBwdWarps;
+constexpr int kLanePix = kBandJX * kBandJY;
 
 __device__ inline bool overlaps_band(uint2 bnd, uint32_t bx0, uint32_t by0) {
     const uint32_t xlo = bnd.x & 0xffffu, xhi = bnd.x >> 16, ylo = bnd.y & 0xffffu, yhi = bnd.y >> 16;
-    return xlo < bx0 + kBandW && bx0 < xhi && ylo < by0 + kSubtileH && by0 < yhi;
+    return xlo < bx0 + kBandW && bx0 < xhi && ylo < by0 + kBandH && by0 < yhi;
 }
 
 template <bool kAbs>
@@ -45,42 +50,52 @@ __global__ void __launch_bounds__(kBwdThreads) blend_backward_kernel(BlendArgs A
     __shared__ StagedB st[kTilePixels];
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const uint32_t tile = blockIdx.y * A.grid_w + blockIdx.x;
-    const uint32_t bx0 = blockIdx.x * kTileW, by0 = blockIdx.y * kTileH + warp * kSubtileH;
-    const uint32_t py = by0 + lane / kSubtileW;
-    const float pyf = static_cast<float>(py) + 0.5f;
+    const uint32_t bx0 = blockIdx.x * kTileW + (warp % kBandsX) * kBandW, by0 = blockIdx.y * kTileH + (warp / kBandsX) * kBandH;
     const uint2 range = A.ranges[tile];
     const uint32_t n = range.y - range.x;
-    // per pixel j (x offset 8 j): contributor count, dL/dcolour, (final colour without background) . dL/dcolour,
-    // the background term, the transmittance and accd = (colour accumulated so far) . dL/dcolour, so that
-    // (final - accumulated) . dL/dcolour = gcf - accd
-    uint32_t last[2] = {0u, 0u};
-    float pxf[2], gcf[2] = {0.0f, 0.0f}, gr[2] = {0.0f, 0.0f}, gg[2] = {0.0f, 0.0f}, gb[2] = {0.0f, 0.0f}, gac[2] = {0.0f, 0.0f};
-    float tr[2] = {1.0f, 1.0f}, accd[2] = {0.0f, 0.0f};
-    bool done[2];
+    // per pixel p = jy JX + jx: contributor count, dL/dcolour, (final colour without background) . dL/dcolour, the
+    // background term, the transmittance and accd = (colour accumulated so far) . dL/dcolour
+    uint32_t last[kLanePix];
+    float pxf[kBandJX], pyf[kBandJY];
+    float gcf[kLanePix], gr[kLanePix], gg[kLanePix], gb[kLanePix], gac[kLanePix], tr[kLanePix], accd[kLanePix];
+    bool done[kLanePix];
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
-        const uint32_t px = bx0 + lane % kSubtileW + kSubtileW * j;
-        pxf[j] = static_cast<float>(px) + 0.5f;
+    for (int jx = 0; jx < kBandJX; jx++) pxf[jx] = static_cast<float>(bx0 + lane % kSubtileW + kSubtileW * jx) + 0.5f;
+#pragma unroll
+    for (int jy = 0; jy < kBandJY; jy++) pyf[jy] = static_cast<float>(by0 + lane / kSubtileW + kSubtileH * jy) + 0.5f;
+#pragma unroll
+    for (int p = 0; p < kLanePix; p++) {
+        const uint32_t px = bx0 + lane % kSubtileW + kSubtileW * (p % kBandJX), py = by0 + lane / kSubtileW + kSubtileH * (p / kBandJX);
+        last[p] = 0u;
+        gcf[p] = gr[p] = gg[p] = gb[p] = gac[p] = 0.0f;
+        tr[p] = 1.0f;
+        accd[p] = 0.0f;
         if (px < static_cast<uint32_t>(A.width) && py < static_cast<uint32_t>(A.height)) {
-            const uint32_t local = (py - blockIdx.y * kTileH) * kTileW + (px - bx0);
+            const uint32_t local = (py - blockIdx.y * kTileH) * kTileW + (px - blockIdx.x * kTileW);
             const size_t pix = static_cast<size_t>(py) * A.width + px;
             const size_t np = static_cast<size_t>(A.width) * A.height;
-            last[j] = T.n_contrib[static_cast<size_t>(tile) * kTilePixels + local];
+            last[p] = T.n_contrib[static_cast<size_t>(tile) * kTilePixels + local];
             const float tf = T.final_T[static_cast<size_t>(tile) * kTilePixels + local];
             const float bgr = A.bg[0], bgg = A.bg[1], bgb = A.bg[2];
             const float cfr = image[pix] - tf * bgr;
             const float cfg = image[np + pix] - tf * bgg;
             const float cfb = image[2 * np + pix] - tf * bgb;
-            gr[j] = grad_image[pix];
-            gg[j] = grad_image[np + pix];
-            gb[j] = grad_image[2 * np + pix];
-            gac[j] = tf * -(gr[j] * bgr + gg[j] * bgg + gb[j] * bgb);
-            gcf[j] = cfr * gr[j] + cfg * gg[j] + cfb * gb[j];
+            gr[p] = grad_image[pix];
+            gg[p] = grad_image[np + pix];
+            gb[p] = grad_image[2 * np + pix];
+            gac[p] = tf * -(gr[p] * bgr + gg[p] * bgg + gb[p] * bgb);
+            gcf[p] = cfr * gr[p] + cfg * gg[p] + cfb * gb[p];
         }
-        done[j] = last[j] == 0;
+        done[p] = last[p] == 0;
     }
+    auto all_done = [&]() {
+        bool d = true;
+#pragma unroll
+        for (int p = 0; p < kLanePix; p++) d = d && done[p];
+        return d;
+    };
     for (uint32_t start = 0; start < n; start += kTilePixels) {
-        if (__syncthreads_and(done[0] && done[1])) break;
+        if (__syncthreads_and(all_done())) break;
         for (uint32_t u = t; u < kTilePixels; u += kBwdThreads) {
             if (start + u < n) {
                 const uint32_t r = A.vals[range.x + start + u];
@@ -96,22 +111,24 @@ __global__ void __launch_bounds__(kBwdThreads) blend_backward_kernel(BlendArgs A
         const uint32_t bs = min(static_cast<uint32_t>(kTilePixels), n - start);
         for (uint32_t g = 0; g < bs; g += 32) {
             const bool ov = g + lane < bs && overlaps_band(st[g + lane].bnd, bx0, by0);
-            // `done` changes only where a fragment is accepted, so the warp votes on it once per group of 32
-            // records and after each accepted fragment
-            uint32_t pending = __all_sync(0xffffffffu, done[0] && done[1]) ? 0u : __ballot_sync(0xffffffffu, ov);
+            uint32_t pending = __all_sync(0xffffffffu, all_done()) ? 0u : __ballot_sync(0xffffffffu, ov);
             while (pending) {
                 const uint32_t k = g + __ffs(pending) - 1;
                 pending &= pending - 1;
                 const float4 a = st[k].a;
                 const float4 h = st[k].h;
-                // the fragment's terms summed over this lane's accepting pixels
                 float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
                 float v8 = 0.0f, ax = 0.0f, ay = 0.0f;
                 bool any = false;
+                float dxs[kBandJX], dys[kBandJY];
 #pragma unroll
-                for (int j = 0; j < 2; j++) {
-                    const float dx = a.x - pxf[j], dy = a.y - pyf;
-                    bool acc = !done[j] && start + k < last[j];
+                for (int jx = 0; jx < kBandJX; jx++) dxs[jx] = a.x - pxf[jx];
+#pragma unroll
+                for (int jy = 0; jy < kBandJY; jy++) dys[jy] = a.y - pyf[jy];
+#pragma unroll
+                for (int p = 0; p < kLanePix; p++) {
+                    const float dx = dxs[p % kBandJX], dy = dys[p / kBandJX];
+                    bool acc = !done[p] && start + k < last[p];
                     float G = 0.0f, alpha = 0.0f;
                     if (acc) {
                         G = fragment_gaussian(gauss_exponent(dx, dy, h));
@@ -120,26 +137,24 @@ __global__ void __launch_bounds__(kBwdThreads) blend_backward_kernel(BlendArgs A
                     }
                     if (acc) {
                         const float4 c = st[k].c;
-                        const float w = tr[j] * alpha;
-                        const float cg = c.x * gr[j] + c.y * gg[j] + c.z * gb[j];
-                        accd[j] = fmaf(w, cg, accd[j]);
+                        const float w = tr[p] * alpha;
+                        const float cg = c.x * gr[p] + c.y * gg[p] + c.z * gb[p];
+                        accd[p] = fmaf(w, cg, accd[p]);
                         const float oma = __fsub_rn(1.0f, alpha);
                         const float rcp = rcp_approx(fmaxf(oma, kOneMinusAlphaEps));
-                        // sum_c (tr c_c - (final_c - accumulated_c) / (1 - alpha)) g_c + gac / (1 - alpha)
-                        const float dl_da = fmaf(tr[j], cg, rcp * (gac[j] - (gcf[j] - accd[j])));
+                        const float dl_da = fmaf(tr[p], cg, rcp * (gac[p] - (gcf[p] - accd[p])));
                         const float hl = -alpha * dl_da;
                         const float hx = hl * dx, hy = hl * dy;
                         v[0] += hx; v[1] += hy; v[2] = fmaf(hx, dx, v[2]); v[3] = fmaf(hx, dy, v[3]);
-                        v[4] = fmaf(hy, dy, v[4]); v[5] = fmaf(w, gr[j], v[5]); v[6] = fmaf(w, gg[j], v[6]); v[7] = fmaf(w, gb[j], v[7]);
+                        v[4] = fmaf(hy, dy, v[4]); v[5] = fmaf(w, gr[p], v[5]); v[6] = fmaf(w, gg[p], v[6]); v[7] = fmaf(w, gb[p], v[7]);
                         v8 = fmaf(G, dl_da, v8);
                         if (kAbs) {
-                            // |dL/dmean2d| of this fragment, with the raw conic recovered from the staged scaled conic
                             const float ca = h.x / kHalfConic, cb = h.y / kCrossConic, cc = h.z / kHalfConic;
                             ax += fabsf(ca * hx + cb * hy);
                             ay += fabsf(cb * hx + cc * hy);
                         }
-                        tr[j] = __fmul_rn(tr[j], oma);
-                        if (tr[j] < kTransmittanceThreshold) done[j] = true;
+                        tr[p] = __fmul_rn(tr[p], oma);
+                        if (tr[p] < kTransmittanceThreshold) done[p] = true;
                         any = true;
                     }
                 }
@@ -148,8 +163,6 @@ __global__ void __launch_bounds__(kBwdThreads) blend_backward_kernel(BlendArgs A
                 const uint32_t r = __float_as_uint(h.w);
                 float* gp = reinterpret_cast<float*>(grads + r);
                 if (__popc(accepting) <= kDirectLanes) {
-                    // few enough lanes accepting: each adds its own terms with 16-byte vector atomics (three warp
-                    // instructions), no warp reduction
                     if (any) {
                         GradRecord* const gq = grads + r;
                         atomicAdd(&gq->g0, make_float4(v[0], v[1], v[2], v[3]));
@@ -168,7 +181,7 @@ __global__ void __launch_bounds__(kBwdThreads) blend_backward_kernel(BlendArgs A
                         if (kAbs) { atomicAdd(gp + 9, sax); atomicAdd(gp + 10, say); }
                     }
                 }
-                if (__all_sync(0xffffffffu, done[0] && done[1])) break;
+                if (__all_sync(0xffffffffu, all_done())) break;
             }
         }
     }

@@ -6,10 +6,11 @@ and the oracle's C restatement (fgs_testutil.compare_forward bounds; colours and
 
 - c1 (SH-3, 1,000,000 Gaussians, 1280x720): forward against the restatement, the backward through the public autograd
   API within 1e-3 relative L2 per gradient tensor (the reference comparison of c1 is in test_gpu_reference.py).
-- c3 (NASG-8 inference, 3,000,000 Gaussians, 1920x1080): forward stages against the reference kernels, the clamped HWC
-  inference image bit for bit against the reference's inference outside tiles with reordered depth ties, and against
-  the restatement within its bounds.
-- c2 (Neural 80-64-64-3, 1,000,000 Gaussians, 1264x832): the MLP colours of every visible primitive against the
+- c3 (NASG-8 and SV-8 inference, 3,000,000 Gaussians, 1920x1080): forward stages against the reference kernels, the clamped HWC
+  inference image against the reference's inference outside tiles with reordered depth ties (NASG bit for bit, SV
+  within 2e-6: its colours are evaluated in another operation order), and against the restatement within its bounds.
+- c2 (Neural 80-64-64-3 on the tensor-core kernels, and the paper's default 32-16-16-3 on the mma.sync kernels,
+  1,000,000 Gaussians, 1264x832): the MLP colours of every visible primitive against the
   restatement's fp16-semantics MLP (tensor-core accumulation restated exactly) within 1e-5, every gradient within 1e-3
   relative L2; the forward stages and the image bit for bit against the reference kernels given these colours as
   precomputed colours (the reference's Neural path needs tiny-cuda-nn, which is absent), and against the restatement
@@ -83,11 +84,13 @@ def test_c1_full_size_forward_and_backward(cuda, oracle_threads):
         assert err <= 1e-3, f'{k}: relative error {err:.2e}'
 
 
-def test_c3_full_size_nasg_inference(cuda, oracle_threads):
+@pytest.mark.parametrize('model', ['nasg', 'sv'])
+def test_c3_full_size_inference(cuda, oracle_threads, model):
+    """Configuration c3 at full size, NASG with 8 lobes and Spherical Voronoi with 8 sites."""
     import FasterGSVDACudaBackend as F
     n, W, H, lobes = 3_000_000, 1920, 1080, 8
-    F.initialize_appearance('nasg', lobes, 'none', 'none', 'relu', True)
-    prims = {**S.geometry(n), **S.nasg_appearance(n, lobes)}
+    F.initialize_appearance(model, lobes, 'none', 'none', 'relu', True)
+    prims = {**S.geometry(n), **(S.nasg_appearance(n, lobes) if model == 'nasg' else S.sv_appearance(n, lobes))}
     cam = S.ring_cameras(64, W, H)[0]
     settings = settings_for(F, cam, lobes, cuda)
     dev = to_dev(prims, cuda)
@@ -95,22 +98,27 @@ def test_c3_full_size_nasg_inference(cuda, oracle_threads):
                       base_colors=dev['base_colors'], residual_params=dev['residual_params']).cpu().numpy()
     g = gpu_forward_stages(F, dev, settings)
     if REF.available():
-        ref = REF.Reference('nasg8_none_none_relu')
+        ref = REF.Reference(f'{model}8_none_none_relu')
         img_ref = ref.forward(dev, settings)
         ties, mask = assert_matches_reference(g, ref.buffers(), img_ref)
         inf_ref = ref.inference(dev, settings, False, True).cpu().numpy()
-        np.testing.assert_array_equal(img.transpose(2, 0, 1)[:, mask], inf_ref.transpose(2, 0, 1)[:, mask])
-        print(f'\n[c3] tiles with reordered depth ties: {ties}')
+        mine, theirs = img.transpose(2, 0, 1)[:, mask], inf_ref.transpose(2, 0, 1)[:, mask]
+        d = float(np.abs(mine - theirs).max())
+        print(f'\n[c3 {model}] tiles with reordered depth ties: {ties}; inference image max-abs difference {d:.2e}')
+        if model == 'nasg':  # measured bit for bit
+            np.testing.assert_array_equal(mine, theirs)
+        else:  # the Voronoi colours are evaluated in another operation order (last-bit differences)
+            assert d <= 2e-6, d
         ref.close()
-    o = O.run(O.make_appearance('nasg', lobes, 0, 0, 1, True), O.make_view(cam, lobes), prims)
+    o = O.run(O.make_appearance(model, lobes, 0, 0, 1, True), O.make_view(cam, lobes), prims)
     assert o['n_visible'] > 1_000_000 and o['n_instances'] > 4_000_000
     compare_forward(g, o)
     d = np.abs(img - np.clip(o['image'], 0.0, 1.0).transpose(1, 2, 0))
     assert d.mean() <= 5e-6 and (d.max(2) > 1e-4).mean() <= 1e-3, (d.mean(), d.max())
 
 
-def _neural_c4(F):
-    feat, n_freq, neurons, hidden = 32, 1, 64, 2
+def _neural_c4(F, feat: int = 32, neurons: int = 64):
+    n_freq, hidden = 1, 2
     n_in = feat * 2 * n_freq + 16
     pad = (n_in + 15) // 16 * 16
     F.initialize_appearance('neural', 0, 'none', 'tanh', 'relu', True)
@@ -132,11 +140,15 @@ def _colors_against_oracle(g, o, prims_idx=None):
     return np.abs(colors_g - colors_o), int(both.sum())
 
 
-def test_c2_full_size_neural_forward_backward(cuda, oracle_threads):
+@pytest.mark.parametrize('net', [(32, 64), (8, 16)], ids=['f32-n2x64', 'paper-f8-n2x16'])
+def test_c2_full_size_neural_forward_backward(cuda, oracle_threads, net):
+    """Configuration c2 at full size with the 64-wide network (tensor-core kernels) and with the paper's default
+    network (8 features, 2 hidden layers of 16 neurons: the mma.sync kernels)."""
     import FasterGSVDACudaBackend as F
     n, W, H = 1_000_000, 1264, 832
-    neural, shapes = _neural_c4(F)
-    prims = {**S.geometry(n), **S.neural_appearance(n, 32, layer_shapes=shapes)}
+    feat, neurons = net
+    neural, shapes = _neural_c4(F, feat, neurons)
+    prims = {**S.geometry(n), **S.neural_appearance(n, feat, layer_shapes=shapes)}
     cam = S.ring_cameras(1, W, H)[0]
     settings = settings_for(F, cam, 3, cuda)
     dev = to_dev(prims, cuda)
