@@ -14,8 +14,10 @@
 
 namespace fgs {
 
+// The training forward is compiled for eight CTAs per SM (40 registers; measured on the c4 step: 3.60 -> 3.40 ms per
+// step against the unconstrained 44 registers and seven CTAs); the inference forward keeps its unconstrained allocation.
 template <bool kTrain>
-__global__ void __launch_bounds__(kTilePixels) blend_kernel(BlendArgs A, float* __restrict__ image, TileBuffers T, int chw, int clamp_out) {
+__global__ void __launch_bounds__(kTilePixels, kTrain ? 8 : 0) blend_kernel(BlendArgs A, float* __restrict__ image, TileBuffers T, int chw, int clamp_out) {
     __shared__ Staged st[kTilePixels];
     __shared__ uint32_t warp_max[kTilePixels / 32];
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
