@@ -14,10 +14,11 @@
 
 namespace fgs {
 
-// The training forward is compiled for eight CTAs per SM (40 registers; measured on the c4 step: 3.60 -> 3.40 ms per
-// step against the unconstrained 44 registers and seven CTAs); the inference forward keeps its unconstrained allocation.
+// The training forward is compiled for nine CTAs per SM (32 registers, 16 bytes spilled; measured on the c4 step: 3.60
+// ms per step with the unconstrained 44 registers and seven CTAs, 3.40 at eight CTAs, 3.29 at nine); the inference
+// forward keeps its unconstrained allocation.
 template <bool kTrain>
-__global__ void __launch_bounds__(kTilePixels, kTrain ? 8 : 0) blend_kernel(BlendArgs A, float* __restrict__ image, TileBuffers T, int chw, int clamp_out) {
+__global__ void __launch_bounds__(kTilePixels, kTrain ? 9 : 0) blend_kernel(BlendArgs A, float* __restrict__ image, TileBuffers T, int chw, int clamp_out) {
     __shared__ Staged st[kTilePixels];
     __shared__ uint32_t warp_max[kTilePixels / 32];
     const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
