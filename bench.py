@@ -188,7 +188,7 @@ def settings_of(cam, degree: int, dev):
 # visible rows, 3,455,838 instances), per visible row and per instance: backward preprocess = warp-specialised MLP
 # backward (566.6 MB) + its geometry pass (274.3 MB), per visible row; blend backward (170.6 MB) over the instances.
 # Scaled by the view's visible rows and instances.
-TRAFFIC_PER_UNIT = {('c4', 'preprocess_backward'): ((566.6e6 + 274.3e6) / 945338, 0.0), ('c4', 'blend_backward'): (0.0, 170.6e6 / 3455838)}
+TRAFFIC_PER_UNIT = {('c4', 'preprocess_backward'): ((566.6e6 + 274.3e6) / 945338, 0.0), ('c4', 'blend_backward'): (0.0, (157.0e6 + 13.2e6) / 3455837)}
 # how each stage is bound at these sizes (ncu): the blends issue-bound (warps walking subtiles or bands of the tile),
 # the tensor-core MLP stages latency-bound on their per-tile MMA -> epilogue chains; the rest streams HBM
 BOUND = {'blend_forward': 'issue', 'blend_inference': 'issue', 'blend_backward': 'issue', 'appearance_mlp': 'latency',
