@@ -16,7 +16,7 @@ namespace fgs {
 
 // The training forward is compiled for nine CTAs per SM (32 registers, 16 bytes spilled; measured on the c4 step: 3.60
 // ms per step with the unconstrained 44 registers and seven CTAs, 3.40 at eight CTAs, 3.29 at nine); the inference
-// forward keeps its unconstrained allocation.
+// forward keeps its unconstrained allocation (a minimum of 0 CTAs per SM sets no bound).
 template <bool kTrain>
 __global__ void __launch_bounds__(kTilePixels, kTrain ? 9 : 0) blend_kernel(BlendArgs A, float* __restrict__ image, TileBuffers T, int chw, int clamp_out) {
     __shared__ Staged st[kTilePixels];

@@ -40,7 +40,7 @@ __device__ inline f3 fused_color(const Params& P, const AppearanceConfig& A, con
 
 // The Neural preprocess (geometry only: the colour pass evaluates the appearance) is compiled for eight CTAs per SM
 // (32 registers, a few bytes spilled; measured on the c4 step: 1.53 -> 1.46 ms per step against 47 registers and five
-// CTAs); the other models keep their unconstrained allocation.
+// CTAs); the other models keep their unconstrained allocation (a minimum of 0 CTAs per SM sets no bound).
 template <int MODEL>
 __global__ void __launch_bounds__(kChunk, MODEL == kNeural ? 8 : 0) preprocess_fwd_kernel(Params P, AppearanceConfig A, View v, PrimBuffers B) {
     const uint32_t i = blockIdx.x * kChunk + threadIdx.x;
