@@ -748,8 +748,10 @@ def main() -> None:
     ap.add_argument('--no-render', dest='render', action='store_false',
                     help='c4: skip the render measurement of configuration c3 that the line carries under "render"')
     ap.add_argument('--exchange', default='auto', choices=['auto', 'peer', 'nccl'], help='c4 data-parallel exchange (N > 1)')
-    ap.add_argument('--no-multicast', dest='multicast', action='store_false',
-                    help='peer exchange by loads / stores instead of NVSwitch multicast (multimem, the default where the switch provides it)')
+    ap.add_argument('--no-multicast', dest='multicast', action='store_const', const=False, default='auto',
+                    help='c4 peer exchange by loads / stores only (by default NVSwitch multicast from trainer.MULTICAST_MIN_RANKS GPUs on)')
+    ap.add_argument('--multicast', dest='multicast', action='store_const', const=True,
+                    help='c4 peer exchange through NVSwitch multicast (multimem) at any GPU count where the switch provides it')
     ap.add_argument('--gaussians', type=int, default=0, help='override the workload\'s Gaussian count (small profiling cases)')
     ap.add_argument('--views', type=int, default=0, help='override the workload\'s global batch of views (c4)')
     ap.add_argument('--order', default='morton', choices=['morton', 'generated'],

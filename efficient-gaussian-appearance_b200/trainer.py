@@ -24,9 +24,12 @@ segments, sums the gradients of all ranks over NVLink (or through the switch wit
 the new parameter into every rank's buffer, between two device-side barriers. 'auto' picks 'peer' when symmetric
 memory can be set up on the group and falls back to 'nccl' otherwise. In the 'peer' exchange the sum is read with
 one multimem.ld_reduce through the NVSwitch and the new parameters are written with one multimem.st where the switch
-provides multicast mappings (multicast=True, the default): the switch does the sum and the fan-out, so each GPU moves
-about (N - 1) / N of the vector per link direction and step instead of twice that (at 8 GPUs 1.1 against 1.9 GB;
-measured 2.37 against 2.92 ms); without the mappings, or with multicast=False, peer loads and stores.
+provides multicast mappings: the switch does the sum and the fan-out, so each GPU moves about the vector's size per
+link direction and step instead of 2 (N - 1) / N of it (at 8 GPUs 1.1 against 1.9 GB). The multicast loads run at a
+lower rate than peer loads, so the fewer bytes pay only at larger N: measured on the c4 step, 2 GPUs 62.5 steps/s with
+peer loads / stores against 58.2 with multicast (exchange 1.64 against 2.83 ms), 8 GPUs 133.3 against 144.3 (2.92
+against 2.37 ms). multicast='auto' (the default) uses multicast from MULTICAST_MIN_RANKS ranks on, True wherever the
+switch provides the mappings, False never.
 """
 from __future__ import annotations
 
@@ -40,6 +43,11 @@ import torch.nn.functional as tf
 
 from FasterGSVDACudaBackend import rasterization as R, _lib
 from FasterGSVDACudaBackend.adam import _segment, adam_step_segments
+
+# ranks from which the 'auto' exchange reads and writes through NVSwitch multicast: the peer exchange moves
+# 2 (N - 1) / N of the vector per link direction at about 0.67 TB/s (measured at 2 and 8 GPUs), the multicast one
+# the vector's size at 0.39-0.46 TB/s, so multicast pays from about 5 ranks on
+MULTICAST_MIN_RANKS = 5
 
 GROUP_ORDER = ('means', 'scales', 'rotations', 'opacities', 'base_colors', 'residual_params', 'mlp_weights')
 
@@ -137,7 +145,7 @@ class Trainer:
     """Holds the flat parameter / gradient buffers of one replica and runs data-parallel steps."""
 
     def __init__(self, prims: dict[str, torch.Tensor], lrs: dict[str, float | list], device: torch.device, group=None,
-                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool = True, overlap_views: bool = True,
+                 mlp_betas: tuple = (0.9, 0.99), exchange: str = 'nccl', multicast: bool | str = 'auto', overlap_views: bool = True,
                  view_streams: int = 2) -> None:
         self.device = device
         self.overlap_views = overlap_views
@@ -219,7 +227,8 @@ class Trainer:
             pb.params[r] = self.h_params.buffer_ptrs[r]
         pb.local_params = self.params.data_ptr()
         mg, mp = int(getattr(self.h_grads, 'multicast_ptr', 0) or 0), int(getattr(self.h_params, 'multicast_ptr', 0) or 0)
-        self.multicast = bool(mg and mp) and self.use_multicast
+        want = self.world >= MULTICAST_MIN_RANKS if self.use_multicast == 'auto' else bool(self.use_multicast)
+        self.multicast = bool(mg and mp) and want
         pb.multicast_grads = mg if self.multicast else None
         pb.multicast_params = mp if self.multicast else None
         self.peers = pb
