@@ -49,6 +49,16 @@ from FasterGSVDACudaBackend.adam import _segment, adam_step_segments
 # the vector's size at 0.39-0.46 TB/s, so multicast pays from about 5 ranks on
 MULTICAST_MIN_RANKS = 5
 
+
+def multicast_wanted(multicast: bool | str, world: int) -> bool:
+    """Whether the peer exchange of `world` ranks reads and writes through NVSwitch multicast (where the switch provides
+    the mappings): multicast='auto' from MULTICAST_MIN_RANKS ranks on, True always, False never."""
+    if multicast == 'auto':
+        return world >= MULTICAST_MIN_RANKS
+    if isinstance(multicast, bool):
+        return multicast
+    raise ValueError(f"multicast must be True, False or 'auto', not {multicast!r}")
+
 GROUP_ORDER = ('means', 'scales', 'rotations', 'opacities', 'base_colors', 'residual_params', 'mlp_weights')
 
 
@@ -177,6 +187,7 @@ class Trainer:
         self.mlp_owner = self.world - 1
         self.exchange = 'nccl'
         self.peers = None
+        multicast_wanted(multicast, 1)  # argument check
         self.use_multicast = multicast
         if self.world > 1 and exchange in ('peer', 'auto'):
             try:
@@ -227,8 +238,7 @@ class Trainer:
             pb.params[r] = self.h_params.buffer_ptrs[r]
         pb.local_params = self.params.data_ptr()
         mg, mp = int(getattr(self.h_grads, 'multicast_ptr', 0) or 0), int(getattr(self.h_params, 'multicast_ptr', 0) or 0)
-        want = self.world >= MULTICAST_MIN_RANKS if self.use_multicast == 'auto' else bool(self.use_multicast)
-        self.multicast = bool(mg and mp) and want
+        self.multicast = bool(mg and mp) and multicast_wanted(self.use_multicast, self.world)
         pb.multicast_grads = mg if self.multicast else None
         pb.multicast_params = mp if self.multicast else None
         self.peers = pb

@@ -2,7 +2,7 @@
 per parameter group, an all-reduce of the MLP weights), Adam on each rank's Gaussian range (the checker's float Adam,
 same operations as the kernel) and the ranges gathered back give bit-identical parameters to a single process applying
 Adam to the summed gradients. Also a rank that fails before the collective makes the others fail with an error
-instead of hanging (short process-group timeout)."""
+instead of hanging (short process-group timeout); and the rank-count rule of the multicast exchange."""
 import os
 import socket
 import sys
@@ -189,3 +189,15 @@ def test_morton_ordering_two_ranks_matches_single_process(tmp_path):
             assert torch.equal(dist, ref.shard_view(buf, g.name)[:n]), (key, g.name)
     means = _prims()['means']
     assert torch.equal(ref.view(ref.params, 'means'), means[_position_order(means)])
+
+
+def test_multicast_choice_by_rank_count():
+    """The peer exchange reads and writes through NVSwitch multicast from trainer.MULTICAST_MIN_RANKS ranks on by
+    default (measured: peer loads and stores faster at 2 GPUs, multicast at 8); True and False force either."""
+    sys.path.insert(0, str(ROOT / 'efficient-gaussian-appearance_b200'))
+    import trainer as T
+    assert T.MULTICAST_MIN_RANKS == 5
+    assert [T.multicast_wanted('auto', w) for w in (1, 2, 4, 5, 8)] == [False, False, False, True, True]
+    assert T.multicast_wanted(True, 2) and not T.multicast_wanted(False, 8)
+    with pytest.raises(ValueError):
+        T.multicast_wanted('yes', 8)
