@@ -7,7 +7,7 @@
 //
 // Semantics: FasterGSVDACudaBackend/.../rasterization/include/kernels_backward.cuh:12-231 (the reference processes
 // buckets of 32 instances with the pixels pipelined through the lanes, which for small footprints spends most issue
-// slots on pairs that do not overlap); here each warp walks its subtile's fragments front to back like the forward.
+// slots on pairs that do not overlap); here each warp walks its band's fragments front to back like the forward.
 // This translation unit is compiled with -use_fast_math like the forward (its gradients are checked within a
 // tolerance); the decisions above use the forward's explicit operations so they do not depend on contraction.
 #include "blend_common.cuh"
@@ -24,14 +24,17 @@ __device__ inline float rcp_approx(float x) {
 }
 
 // Visits with at most this many accepting lanes add per lane (the same addresses then take that many atomic additions
-// in L2); above it the warp reduces first. Measured on the c4 step: 20 beats 12, 16 and 24, and every lane adding
-// directly (32) triples the kernel's time through same-address serialisation.
+// in L2); above it the warp reduces first. Measured on the c4 step with 16x4 bands: 20 beats 12, 16 and 24, and every
+// lane adding directly (32) triples the kernel's time through same-address serialisation; with the 8x12 bands 16 is
+// slower and 24 the same.
 constexpr int kDirectLanes = 20;
 
 // Each warp owns a band of (8 JX) x (4 JY) pixels of the tile and each lane JX x JY pixels of it, (x + 8 jx, y + 4 jy):
 // a staged record's loads, the warp's vote and the per-record reduction or atomics serve all of a lane's pixels.
 // Measured on the c4 step (blend backward per step): 8x4 subtiles, one pixel per lane, 8.07 ms; 16x4 bands, two
 // pixels, 7.62 ms; 8x12 column bands, three pixels, 7.25 ms; the whole 16x12 tile in one warp, six pixels, 10.6 ms.
+// A lane's pixels 4 rows (8 columns) apart beat adjacent ones (three consecutive rows: 7.80 ms): a small footprint then
+// spreads its accepting pixels over more lanes instead of making a few lanes walk several of them one after another.
 constexpr int kBandJX = 1, kBandJY = 3;  // 8x12 column bands, two warps per tile
 constexpr int kBandW = kSubtileW * kBandJX, kBandH = kSubtileH * kBandJY;
 constexpr int kBandsX = kTileW / kBandW;
